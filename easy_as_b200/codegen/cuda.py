@@ -1,0 +1,668 @@
+"""Lower traced IR to CUDA C++ for sm_100a (compiled at run time by NVRTC).
+
+This replaces the reference's Metal emitter (easy_as ``eas/codegen/msl.py``)
+and keeps its execution semantics, re-mapped onto the CUDA machine:
+
+Mode inference (``msl.py:59-95``)
+    ``mk.arange(0, BLOCK)`` makes an SPMD kernel, ``mk.tid(0, BLOCK)`` a
+    thread kernel; the two never mix and only one size is allowed.
+
+SPMD kernels (Metal: one thread walks a ``BLOCK``-lane array, ``msl.py:98-350``)
+    One *program* is one CTA.  Its ``BLOCK`` lanes are spread over ``T``
+    threads, ``V`` consecutive lanes per thread per chunk, chunks ``T*V``
+    lanes apart, so a warp touches 32*V consecutive elements per chunk.
+    A load or store whose offset is ``scalar + arange`` (unit lane stride)
+    becomes one 16-byte vector access per chunk when the address is aligned
+    and all ``V`` lane masks are set, else per-lane predicated accesses.
+    Scalar (lane-uniform) stores are done by thread 0 only, and a
+    ``__syncthreads()`` follows any store that later memory operations could
+    observe, so the program still behaves as one sequential instruction
+    stream.
+
+Thread kernels (one Metal thread per ``tid``, ``msl.py:353-1433``)
+    One CUDA thread per DSL thread, ``blockDim.x = BLOCK``.  A 1D launch
+    without ``_grid`` runs exactly ``N`` threads in Metal (partial last group,
+    ``metal.py:283-288``): threads past ``N`` return at once when the kernel
+    has no barriers, block memory or matrix ops, and otherwise stay alive as
+    inert "ghosts" that join barriers and warp matrix ops but never touch
+    memory.
+
+Operations
+    ``mul``/``add`` stay separately rounded (NVRTC ``--fmad=false``); ``fma``
+    is ``fmaf``; f16 values are carried as their bit pattern and computed in
+    f32 with one round-to-nearest-even at the end (exactly rounded for
+    ``+``/``*``, as in ``msl.py:885-897`` for ``fma``); ``dot`` is the strict
+    ``k``-order ``fmaf`` chain from 0 (``msl.py:920-952``); ``mma`` is one
+    warp-wide ``mma.sync.m16n8k8`` (f16 operands, f32 accumulate) holding the
+    8x8 fragment in rows 0-7, or an FFMA loop for f32 operands.
+
+Hidden parameters follow the IR arguments: ``eas_ntx`` (active threads along
+x, thread mode) and ``eas_pid_{x,y,z}`` (program-id offsets, used to split a
+grid into several launches or across GPUs).
+"""
+
+from __future__ import annotations
+
+import struct
+from dataclasses import dataclass, field
+from typing import Any
+
+import numpy as np
+
+from ..ir import DType, IRModule, Inst, ValueRef
+
+# ---------------------------------------------------------------------------
+# launch description shared with the runtime
+# ---------------------------------------------------------------------------
+
+
+@dataclass(frozen=True, slots=True)
+class Param:
+    name: str          # C identifier in the kernel signature
+    kind: str          # "buffer" | "scalar" | "hidden"
+    dtype: DType | None
+    arg: str | None    # IR argument name (None for hidden params)
+
+
+@dataclass(slots=True)
+class Lowered:
+    src: str
+    kernel_name: str
+    block_size: int      # DSL BLOCK (spmd lanes per program / thread-mode threads per block)
+    mode: str            # "spmd" | "thread"
+    cuda_threads: int    # CUDA threads per CTA
+    params: list[Param]
+    dyn_smem: int        # bytes of dynamic shared memory per CTA
+    native: Any = field(default=None)   # pattern-lowered native plan (see codegen.patterns)
+
+
+HIDDEN = ("eas_ntx", "eas_pid_x", "eas_pid_y", "eas_pid_z")
+
+_CXX_RESERVED = {
+    "auto", "bool", "break", "case", "char", "class", "const", "continue", "default", "delete", "do",
+    "double", "else", "enum", "extern", "float", "for", "goto", "if", "inline", "int", "long", "new",
+    "operator", "private", "protected", "public", "register", "return", "short", "signed", "sizeof",
+    "static", "struct", "switch", "template", "this", "throw", "try", "typedef", "union", "unsigned",
+    "virtual", "void", "volatile", "while", "half", "dim3", "uint", "asm", "namespace", "using",
+    "threadIdx", "blockIdx", "blockDim", "gridDim", "warpSize", "true", "false", "nullptr",
+}
+
+
+def c_ident(name: str) -> str:
+    if name in _CXX_RESERVED or name.startswith("eas_") or name.startswith("__") or (
+            name[:1] == "v" and name[1:].isdigit()):
+        return f"{name}_p"
+    return name
+
+
+_CTYPE = {DType.F32: "float", DType.F16: "eas_h", DType.U32: "uint32_t", DType.BOOL: "bool",
+          DType.SG_F32_8X8: "float2"}
+
+
+def ctype(dt: DType) -> str:
+    return _CTYPE[dt]
+
+
+def f32_literal(v: float) -> str:
+    bits = struct.unpack("<I", struct.pack("<f", float(np.float32(v))))[0]
+    return f"__int_as_float(0x{bits:08x})"
+
+
+def infer_block_and_mode(ir: IRModule) -> tuple[int, str]:
+    sizes = {"arange": set(), "tid": set()}
+    for inst in ir.insts:
+        if inst.op in sizes:
+            sizes[inst.op].add(int(inst.args[1]))
+    for op, s in sizes.items():
+        if len(s) > 1:
+            raise ValueError(f"multiple {op} sizes not supported in MVP")
+    if sizes["arange"] and sizes["tid"]:
+        raise ValueError("kernel must not mix mk.arange(...) and mk.tid(...) in MVP")
+    if sizes["arange"]:
+        return next(iter(sizes["arange"])), "spmd"
+    if sizes["tid"]:
+        return next(iter(sizes["tid"])), "thread"
+    raise ValueError("kernel must use mk.arange(0, BLOCK) (spmd) or mk.tid(0, BLOCK) (thread) to define BLOCK")
+
+
+PRELUDE = r"""
+typedef unsigned int uint32_t;
+typedef unsigned long long uint64_t;
+typedef unsigned short eas_h;
+struct __align__(8) eas_h4 { eas_h x, y, z, w; };
+static __device__ __forceinline__ float eas_h2f(eas_h h) { float f; asm("cvt.f32.f16 %0, %1;" : "=f"(f) : "h"(h)); return f; }
+static __device__ __forceinline__ eas_h eas_f2h(float f) { eas_h h; asm("cvt.rn.f16.f32 %0, %1;" : "=h"(h) : "f"(f)); return h; }
+static __device__ __forceinline__ eas_h eas_u2h(uint32_t u) { eas_h h; asm("cvt.rn.f16.u32 %0, %1;" : "=h"(h) : "r"(u)); return h; }
+static __device__ __forceinline__ uint32_t eas_h2u(eas_h h) { uint32_t u; asm("cvt.rzi.sat.u32.f16 %0, %1;" : "=r"(u) : "h"(h)); return u; }
+static __device__ __forceinline__ uint32_t eas_f2u(float f) { uint32_t u; asm("cvt.rzi.sat.u32.f32 %0, %1;" : "=r"(u) : "f"(f)); return u; }
+static __device__ __forceinline__ float eas_u2f(uint32_t u) { float f; asm("cvt.rn.f32.u32 %0, %1;" : "=f"(f) : "r"(u)); return f; }
+static __device__ __forceinline__ uint32_t eas_pack2(eas_h lo, eas_h hi) { return (uint32_t)lo | ((uint32_t)hi << 16); }
+static __device__ __forceinline__ float2 eas_mma_f16(uint32_t a01, uint32_t b01, float2 c) {
+  float d0, d1, d2, d3;
+  asm volatile("mma.sync.aligned.m16n8k8.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%8,%9,%10};"
+               : "=f"(d0), "=f"(d1), "=f"(d2), "=f"(d3)
+               : "r"(a01), "r"(0u), "r"(b01), "f"(c.x), "f"(c.y), "f"(0.0f), "f"(0.0f));
+  return make_float2(d0, d1);
+}
+"""
+
+# ---------------------------------------------------------------------------
+# helpers for value expressions
+# ---------------------------------------------------------------------------
+
+
+def _zero(dt: DType) -> str:
+    return {DType.F32: "0.0f", DType.F16: "(eas_h)0", DType.U32: "0u", DType.BOOL: "false"}[dt]
+
+
+def _cast_expr(x: str, src: DType, dst: DType) -> str:
+    if src == dst:
+        return x
+    if dst == DType.BOOL:
+        return {DType.U32: f"({x} != 0u)", DType.F32: f"({x} != 0.0f)", DType.F16: f"(eas_h2f({x}) != 0.0f)"}[src]
+    if src == DType.BOOL:
+        return {DType.U32: f"({x} ? 1u : 0u)", DType.F32: f"({x} ? 1.0f : 0.0f)",
+                DType.F16: f"({x} ? (eas_h)0x3c00 : (eas_h)0)"}[dst]
+    table = {
+        (DType.U32, DType.F32): f"eas_u2f({x})",
+        (DType.U32, DType.F16): f"eas_u2h({x})",
+        (DType.F32, DType.U32): f"eas_f2u({x})",
+        (DType.F32, DType.F16): f"eas_f2h({x})",
+        (DType.F16, DType.F32): f"eas_h2f({x})",
+        (DType.F16, DType.U32): f"eas_h2u({x})",
+    }
+    return table[(src, dst)]
+
+
+def _binop_expr(op: str, dt: DType, a: str, b: str) -> str:
+    if op in ("add", "mul"):
+        sym = "+" if op == "add" else "*"
+        if dt == DType.F16:
+            return f"eas_f2h(eas_h2f({a}) {sym} eas_h2f({b}))"
+        if dt == DType.F32:
+            return f"__f{'add' if op == 'add' else 'mul'}_rn({a}, {b})"
+        return f"({a} {sym} {b})"
+    if op == "floordiv":
+        return f"({a} / {b})"
+    if op == "mod":
+        return f"({a} % {b})"
+    if op == "lt":
+        if dt == DType.F16:
+            return f"(eas_h2f({a}) < eas_h2f({b}))"
+        return f"({a} < {b})"
+    if op == "and":
+        return f"({a} && {b})"
+    if op == "or":
+        return f"({a} || {b})"
+    raise ValueError(op)
+
+
+def _fma_expr(dt: DType, x: str, y: str, z: str) -> str:
+    if dt == DType.F16:
+        return f"eas_f2h(fmaf(eas_h2f({x}), eas_h2f({y}), eas_h2f({z})))"
+    return f"fmaf({x}, {y}, {z})"
+
+
+def _as_float(dt: DType, x: str) -> str:
+    return f"eas_h2f({x})" if dt == DType.F16 else x
+
+
+# ---------------------------------------------------------------------------
+# emitter
+# ---------------------------------------------------------------------------
+
+
+class _Emitter:
+    def __init__(self, ir: IRModule):
+        self.ir = ir
+        self.block, self.mode = infer_block_and_mode(ir)
+        self.defs: dict[int, Inst] = {i.out.id: i for i in ir.insts if i.out is not None}
+        self.arg_c: dict[int, str] = {}       # value id of an arg -> C identifier
+        self.arg_dtype: dict[int, DType] = {}
+        self.writes: set[str] = set()
+        self.tg: dict[int, tuple[int, int]] = {}   # alloc_tg value id -> (byte offset, elements)
+        self.lines: list[str] = []
+        self.uses: dict[int, int] = {}
+        for inst in ir.insts:
+            for a in inst.args:
+                if isinstance(a, ValueRef):
+                    self.uses[a.id] = self.uses.get(a.id, 0) + 1
+        for inst in ir.insts:
+            if inst.op == "arg":
+                self.arg_c[inst.out.id] = c_ident(str(inst.args[0]))
+                self.arg_dtype[inst.out.id] = inst.out.dtype
+            elif inst.op in ("store", "mma_store"):
+                buf = inst.args[0]
+                if buf.id in self.arg_c:
+                    self.writes.add(self.arg_c[buf.id])
+        self.cooperative = any(i.op in ("barrier", "alloc_tg", "mma_zero", "mma", "mma_store") for i in ir.insts)
+        if self.mode == "spmd":
+            forbidden = {"tid", "local_id", "lane_id", "sg_id", "dot", "mma_zero", "mma", "mma_store"}
+            for inst in ir.insts:
+                if inst.op in forbidden:
+                    raise ValueError(f"op {inst.op!r} is not supported in spmd mode "
+                                     "(use mk.tid for thread-level kernels)")
+            self.V = 4 if self.block % 4 == 0 else 1
+            per_chunk = self.block // self.V
+            self.T = per_chunk if per_chunk <= 256 else 256
+            self.J = -(-per_chunk // self.T)
+            self.L = self.J * self.V
+            self.lane_guard = (self.J * self.T * self.V) != self.block
+            self.cuda_threads = self.T
+            # unit-stride lane vectors: value id -> C expression of the scalar base
+            self.unit: dict[int, str] = {}
+        else:
+            if self.block > 1024:
+                raise ValueError(f"thread mode BLOCK={self.block} exceeds 1024 threads per block")
+            self.cuda_threads = self.block
+        smem = 0
+        for inst in ir.insts:
+            if inst.op == "alloc_tg":
+                nbytes = int(inst.args[0]) * (4 if inst.out.dtype == DType.F32 else 2)
+                self.tg[inst.out.id] = (smem, int(inst.args[0]))
+                smem += -(-nbytes // 16) * 16
+        self.smem = smem
+
+    # -- naming ---------------------------------------------------------------
+    def name(self, ref: ValueRef) -> str:
+        return self.arg_c.get(ref.id, f"v{ref.id}")
+
+    def lane(self, ref: ValueRef, i: str) -> str:
+        n = self.name(ref)
+        return f"{n}[{i}]" if ref.lanes > 1 else n
+
+    def is_const_true(self, ref: ValueRef) -> bool:
+        d = self.defs.get(ref.id)
+        return d is not None and d.op == "const" and d.args[0] is True and ref.dtype == DType.BOOL
+
+    def buf_dtype(self, ref: ValueRef) -> DType:
+        return ref.dtype
+
+    def emit(self, line: str, indent: int = 1) -> None:
+        self.lines.append("  " * indent + line)
+
+    # -- signature -------------------------------------------------------------
+    def params(self) -> list[Param]:
+        ps = []
+        for a in self.ir.args:
+            ps.append(Param(c_ident(a.name), a.kind, a.dtype, a.name))
+        ps += [Param(h, "hidden", DType.U32, None) for h in HIDDEN]
+        return ps
+
+    def signature(self) -> str:
+        parts = []
+        for a in self.ir.args:
+            cn = c_ident(a.name)
+            if a.kind == "buffer":
+                t = ctype(a.dtype)
+                if cn in self.writes:
+                    parts.append(f"{t}* {cn}")
+                else:
+                    parts.append(f"const {t}* __restrict__ {cn}")
+            else:
+                parts.append(f"const {ctype(a.dtype)} {cn}")
+        parts += [f"const uint32_t {h}" for h in HIDDEN]
+        return ",\n    ".join(parts)
+
+    # -- main -------------------------------------------------------------------
+    def run(self) -> Lowered:
+        body = self._spmd() if self.mode == "spmd" else self._thread()
+        name = c_ident(self.ir.name) if self.ir.name else "eas_kernel"
+        src = "\n".join([
+            f"// generated by easy_as_b200.codegen.cuda for sm_100a ({self.mode} mode, BLOCK={self.block})",
+            PRELUDE,
+            f'extern "C" __global__ void __launch_bounds__({self.cuda_threads}) {name}(',
+            "    " + self.signature() + ") {",
+            *body,
+            "}",
+            "",
+        ])
+        return Lowered(src=src, kernel_name=name, block_size=self.block, mode=self.mode,
+                       cuda_threads=self.cuda_threads, params=self.params(), dyn_smem=self.smem)
+
+    def _smem_decls(self) -> None:
+        if not self.tg:
+            return
+        self.emit("extern __shared__ __align__(16) unsigned char eas_smem[];")
+        for vid, (off, _n) in self.tg.items():
+            dt = self.defs[vid].out.dtype
+            self.emit(f"{ctype(dt)}* const v{vid} = reinterpret_cast<{ctype(dt)}*>(eas_smem + {off});")
+
+    # ======================================================================
+    # SPMD
+    # ======================================================================
+    def _lane_index(self, i: int) -> str:
+        j, e = divmod(i, self.V)
+        return f"({j * self.T * self.V}u + threadIdx.x * {self.V}u + {e}u)"
+
+    def _spmd(self) -> list[str]:
+        L = self.L
+        self.emit(f"// {self.T} threads x {self.L} lanes each ({self.J} chunk(s) of {self.V})")
+        self._smem_decls()
+        if self.lane_guard:
+            self.emit(f"bool eas_lv[{L}];")
+            for i in range(L):
+                self.emit(f"eas_lv[{i}] = {self._lane_index(i)} < {self.block}u;")
+        insts = self.ir.insts
+        mem_after = [False] * len(insts)
+        seen = False
+        for k in range(len(insts) - 1, -1, -1):
+            mem_after[k] = seen
+            if insts[k].op in ("load", "store"):
+                seen = True
+        for k, inst in enumerate(insts):
+            self._spmd_inst(inst)
+            if inst.op == "store" and mem_after[k]:
+                self.emit("__syncthreads();")
+        return self.lines
+
+    def _vec_decl(self, out: ValueRef) -> str:
+        return f"{ctype(out.dtype)} v{out.id}[{self.L}];"
+
+    def _spmd_elementwise(self, out: ValueRef, expr_of_i) -> None:
+        if out.lanes == 1:
+            self.emit(f"const {ctype(out.dtype)} v{out.id} = {expr_of_i('0')};")
+            return
+        self.emit(self._vec_decl(out))
+        self.emit(f"#pragma unroll\nfor (int i = 0; i < {self.L}; ++i) v{out.id}[i] = {expr_of_i('i')};")
+
+    def _spmd_inst(self, inst: Inst) -> None:
+        op, out, args = inst.op, inst.out, inst.args
+        if op in ("arg", "alloc_tg"):
+            return
+        if op == "const":
+            self.emit(f"const {ctype(out.dtype)} v{out.id} = {self._const(out.dtype, args[0])};")
+            return
+        if op in ("program_id", "thread_id"):
+            ax = "xyz"[int(args[0])]
+            self.emit(f"const uint32_t v{out.id} = blockIdx.{ax} + eas_pid_{ax};")
+            return
+        if op == "arange":
+            start = int(args[0])
+            self.emit(self._vec_decl(out))
+            for i in range(self.L):
+                self.emit(f"v{out.id}[{i}] = {start}u + {self._lane_index(i)};")
+            self.unit[out.id] = f"{start}u"
+            return
+        if op in ("add", "mul", "floordiv", "mod", "lt", "and", "or"):
+            a, b = args
+            dt = a.dtype
+            self._spmd_elementwise(out, lambda i: _binop_expr(op, dt, self.lane(a, i), self.lane(b, i)))
+            if op == "add" and out.lanes > 1:
+                if a.id in self.unit and b.lanes == 1:
+                    self.unit[out.id] = f"({self.unit[a.id]} + {self.name(b)})"
+                elif b.id in self.unit and a.lanes == 1:
+                    self.unit[out.id] = f"({self.name(a)} + {self.unit[b.id]})"
+            return
+        if op == "not":
+            (x,) = args
+            self._spmd_elementwise(out, lambda i: f"(!{self.lane(x, i)})")
+            return
+        if op == "where":
+            c, a, b = args
+            self._spmd_elementwise(out, lambda i: f"({self.lane(c, i)} ? {self.lane(a, i)} : {self.lane(b, i)})")
+            return
+        if op == "cast":
+            x, dst = args
+            self._spmd_elementwise(out, lambda i: _cast_expr(self.lane(x, i), x.dtype, dst))
+            return
+        if op == "fma":
+            x, y, z = args
+            self._spmd_elementwise(out, lambda i: _fma_expr(out.dtype, self.lane(x, i), self.lane(y, i),
+                                                            self.lane(z, i)))
+            return
+        if op == "load":
+            self._spmd_load(inst)
+            return
+        if op == "store":
+            self._spmd_store(inst)
+            return
+        if op == "barrier":
+            self.emit("__syncthreads();")
+            return
+        raise ValueError(f"unsupported op in spmd codegen: {op!r}")
+
+    def _lane_mask(self, mask: ValueRef, i: int | str) -> str:
+        m = "true" if self.is_const_true(mask) else self.lane(mask, str(i))
+        if self.lane_guard:
+            m = f"(eas_lv[{i}] && {m})" if m != "true" else f"eas_lv[{i}]"
+        return m
+
+    def _vector_ok(self, buf: ValueRef, off: ValueRef) -> bool:
+        return self.V == 4 and off.lanes > 1 and off.id in self.unit and buf.id in self.arg_c
+
+    def _spmd_load(self, inst: Inst) -> None:
+        buf, off, mask = inst.args
+        out = inst.out
+        bn = self.name(buf)
+        z = _zero(out.dtype)
+        if out.lanes == 1:
+            m = "true" if self.is_const_true(mask) else self.name(mask)
+            self.emit(f"const {ctype(out.dtype)} v{out.id} = {m} ? {bn}[{self.name(off)}] : {z};")
+            return
+        self.emit(self._vec_decl(out))
+        if self._vector_ok(buf, off):
+            base = self.unit[off.id]
+            vt, bytes_ = ("float4", 16) if out.dtype == DType.F32 else ("eas_h4", 8)
+            self.emit("{")
+            self.emit(f"const uint32_t eas_b = {base};", 2)
+            self.emit(f"const bool eas_al = ((eas_b & 3u) == 0u) && ((((uint64_t){bn}) & {bytes_ - 1}ull) == 0ull);", 2)
+            for j in range(self.J):
+                ms = [self._lane_mask(mask, j * 4 + e) for e in range(4)]
+                allm = " && ".join(ms)
+                i0 = j * 4
+                self.emit(f"if (eas_al && {allm}) {{", 2)
+                self.emit(f"const {vt} t = *reinterpret_cast<const {vt}*>({bn} + {self.lane(off, str(i0))});", 3)
+                for e, comp in enumerate("xyzw"):
+                    self.emit(f"v{out.id}[{i0 + e}] = t.{comp};", 3)
+                self.emit("} else {", 2)
+                for e in range(4):
+                    i = i0 + e
+                    self.emit(f"v{out.id}[{i}] = {ms[e]} ? {bn}[{self.lane(off, str(i))}] : {z};", 3)
+                self.emit("}", 2)
+            self.emit("}")
+            return
+        for i in range(self.L):
+            self.emit(f"v{out.id}[{i}] = {self._lane_mask(mask, i)} ? {bn}[{self.lane(off, str(i))}] : {z};")
+
+    def _spmd_store(self, inst: Inst) -> None:
+        buf, off, val, mask = inst.args
+        bn = self.name(buf)
+        if off.lanes == 1:
+            m = "true" if self.is_const_true(mask) else self.name(mask)
+            self.emit(f"if (threadIdx.x == 0 && {m}) {bn}[{self.name(off)}] = {self.name(val)};")
+            return
+        if self._vector_ok(buf, off):
+            base = self.unit[off.id]
+            vt, bytes_ = ("float4", 16) if buf.dtype == DType.F32 else ("eas_h4", 8)
+            self.emit("{")
+            self.emit(f"const uint32_t eas_b = {base};", 2)
+            self.emit(f"const bool eas_al = ((eas_b & 3u) == 0u) && ((((uint64_t){bn}) & {bytes_ - 1}ull) == 0ull);", 2)
+            for j in range(self.J):
+                i0 = j * 4
+                ms = [self._lane_mask(mask, i0 + e) for e in range(4)]
+                self.emit(f"if (eas_al && {' && '.join(ms)}) {{", 2)
+                vals = ", ".join(self.lane(val, str(i0 + e)) for e in range(4))
+                self.emit(f"*reinterpret_cast<{vt}*>({bn} + {self.lane(off, str(i0))}) = {vt}{{{vals}}};", 3)
+                self.emit("} else {", 2)
+                for e in range(4):
+                    i = i0 + e
+                    self.emit(f"if ({ms[e]}) {bn}[{self.lane(off, str(i))}] = {self.lane(val, str(i))};", 3)
+                self.emit("}", 2)
+            self.emit("}")
+            return
+        for i in range(self.L):
+            self.emit(f"if ({self._lane_mask(mask, i)}) {bn}[{self.lane(off, str(i))}] = {self.lane(val, str(i))};")
+
+    @staticmethod
+    def _const(dt: DType, v: Any) -> str:
+        if dt == DType.BOOL:
+            return "true" if v else "false"
+        if dt == DType.U32:
+            return f"{int(v) % (1 << 32)}u"
+        if dt == DType.F32:
+            return f32_literal(float(v))
+        raise ValueError(f"unsupported const dtype {dt}")
+
+    # ======================================================================
+    # thread mode
+    # ======================================================================
+    def _thread(self) -> list[str]:
+        self._smem_decls()
+        self.emit("const uint32_t eas_gx = (blockIdx.x + eas_pid_x) * blockDim.x + threadIdx.x;")
+        if self.cooperative:
+            self.emit("const bool eas_on = eas_gx < eas_ntx;")
+            self.ghost = "eas_on"
+        else:
+            self.emit("if (eas_gx >= eas_ntx) return;")
+            self.ghost = None
+        needs_lane = any(i.op in ("mma", "mma_store", "lane_id") for i in self.ir.insts)
+        if needs_lane:
+            self.emit("const uint32_t eas_lane = threadIdx.x & 31u;")
+        for inst in self.ir.insts:
+            self._thread_inst(inst)
+        return self.lines
+
+    def _guard(self, cond: str) -> str:
+        if self.ghost is None:
+            return cond
+        return self.ghost if cond == "true" else f"({self.ghost} && {cond})"
+
+    def _thread_inst(self, inst: Inst) -> None:
+        op, out, args = inst.op, inst.out, inst.args
+        if op in ("arg", "alloc_tg"):
+            return
+        if out is not None and self.uses.get(out.id, 0) == 0 and op not in ("store", "mma_store"):
+            return  # e.g. the tid that only defines BLOCK
+        if op == "const":
+            self.emit(f"const {ctype(out.dtype)} v{out.id} = {self._const(out.dtype, args[0])};")
+        elif op == "program_id":
+            ax = "xyz"[int(args[0])]
+            self.emit(f"const uint32_t v{out.id} = blockIdx.{ax} + eas_pid_{ax};")
+        elif op == "thread_id":
+            ax = int(args[0])
+            if ax == 0:
+                self.emit(f"const uint32_t v{out.id} = eas_gx;")
+            else:
+                a = "xyz"[ax]
+                self.emit(f"const uint32_t v{out.id} = blockIdx.{a} + eas_pid_{a};")
+        elif op == "local_id":
+            self.emit(f"const uint32_t v{out.id} = {'threadIdx.x' if int(args[0]) == 0 else '0u'};")
+        elif op == "lane_id":
+            self.emit(f"const uint32_t v{out.id} = eas_lane;")
+        elif op == "sg_id":
+            self.emit(f"const uint32_t v{out.id} = threadIdx.x >> 5;")
+        elif op == "tid":
+            self.emit(f"const uint32_t v{out.id} = {int(args[0])}u + threadIdx.x;")
+        elif op == "arange":
+            raise ValueError("arange is not supported in thread mode codegen; use mk.tid(...) for thread-level kernels")
+        elif op in ("add", "mul", "floordiv", "mod", "lt", "and", "or"):
+            a, b = args
+            self.emit(f"const {ctype(out.dtype)} v{out.id} = {_binop_expr(op, a.dtype, self.name(a), self.name(b))};")
+        elif op == "not":
+            self.emit(f"const bool v{out.id} = !{self.name(args[0])};")
+        elif op == "where":
+            c, a, b = args
+            self.emit(f"const {ctype(out.dtype)} v{out.id} = {self.name(c)} ? {self.name(a)} : {self.name(b)};")
+        elif op == "cast":
+            x, dst = args
+            self.emit(f"const {ctype(out.dtype)} v{out.id} = {_cast_expr(self.name(x), x.dtype, dst)};")
+        elif op == "fma":
+            x, y, z = args
+            self.emit(f"const {ctype(out.dtype)} v{out.id} = "
+                      f"{_fma_expr(out.dtype, self.name(x), self.name(y), self.name(z))};")
+        elif op == "load":
+            buf, off, mask = args
+            m = self._guard("true" if self.is_const_true(mask) else self.name(mask))
+            rhs = f"{self.name(buf)}[{self.name(off)}]"
+            if m == "true":
+                self.emit(f"const {ctype(out.dtype)} v{out.id} = {rhs};")
+            else:
+                self.emit(f"const {ctype(out.dtype)} v{out.id} = {m} ? {rhs} : {_zero(out.dtype)};")
+        elif op == "store":
+            buf, off, val, mask = args
+            m = self._guard("true" if self.is_const_true(mask) else self.name(mask))
+            st = f"{self.name(buf)}[{self.name(off)}] = {self.name(val)};"
+            self.emit(st if m == "true" else f"if ({m}) {st}")
+        elif op == "barrier":
+            self.emit("__syncthreads();")
+        elif op == "dot":
+            self._dot(inst)
+        elif op == "mma_zero":
+            self.emit(f"float2 v{out.id} = make_float2(0.0f, 0.0f);")
+        elif op == "mma":
+            self._mma(inst)
+        elif op == "mma_store":
+            buf, base, stride, frag = args
+            g = self._guard("true")
+            b, s, f = self.name(base), self.name(stride), self.name(frag)
+            self.emit("{")
+            self.emit(f"const uint32_t eas_o = {b} + (eas_lane >> 2) * {s} + (eas_lane & 3u) * 2u;", 2)
+            pre = "" if g == "true" else f"if ({g}) "
+            self.emit(f"{pre}{{ {self.name(buf)}[eas_o] = {f}.x; {self.name(buf)}[eas_o + 1u] = {f}.y; }}", 2)
+            self.emit("}")
+        else:
+            raise ValueError(f"unsupported op: {op}")
+
+    def _dot(self, inst: Inst) -> None:
+        a_buf, a_base, a_stride, b_buf, b_base, b_stride, k_ref = inst.args
+        o = inst.out.id
+        kd = self.defs.get(k_ref.id)
+        unroll = "#pragma unroll" if kd is not None and kd.op == "const" and 1 <= int(kd.args[0]) <= 32 else ""
+        self.emit(f"float v{o} = 0.0f;")
+        body_guard = self._guard("true")
+        self.emit("{" if body_guard == "true" else f"if ({body_guard}) {{")
+        self.emit(f"uint32_t ai = {self.name(a_base)}, bi = {self.name(b_base)};", 2)
+        if unroll:
+            self.emit(unroll, 2)
+        self.emit(f"for (uint32_t k = 0; k < {self.name(k_ref)}; ++k) {{", 2)
+        av = _as_float(a_buf.dtype, f"{self.name(a_buf)}[ai]")
+        bv = _as_float(b_buf.dtype, f"{self.name(b_buf)}[bi]")
+        self.emit(f"v{o} = fmaf({av}, {bv}, v{o});", 3)
+        self.emit(f"ai += {self.name(a_stride)}; bi += {self.name(b_stride)};", 3)
+        self.emit("}", 2)
+        self.emit("}")
+
+    def _mma(self, inst: Inst) -> None:
+        a_buf, a_base, a_stride, b_buf, b_base, b_stride, acc = inst.args
+        o = inst.out.id
+        A, B = self.name(a_buf), self.name(b_buf)
+        ab, as_, bb, bs = self.name(a_base), self.name(a_stride), self.name(b_base), self.name(b_stride)
+        on = self._guard("true")
+        self.emit(f"float2 v{o};")
+        self.emit("{")
+        self.emit("const uint32_t eas_g = eas_lane >> 2, eas_t = eas_lane & 3u;", 2)
+        if a_buf.dtype == DType.F16 and b_buf.dtype == DType.F16:
+            ai = f"{ab} + eas_g * {as_} + eas_t * 2u"
+            bi0 = f"{bb} + (eas_t * 2u) * {bs} + eas_g"
+            if on == "true":
+                self.emit(f"const uint32_t eas_a = eas_pack2({A}[{ai}], {A}[{ai} + 1u]);", 2)
+                self.emit(f"const uint32_t eas_b = eas_pack2({B}[{bi0}], {B}[{bi0} + {bs}]);", 2)
+            else:
+                self.emit(f"const uint32_t eas_a = {on} ? eas_pack2({A}[{ai}], {A}[{ai} + 1u]) : 0u;", 2)
+                self.emit(f"const uint32_t eas_b = {on} ? eas_pack2({B}[{bi0}], {B}[{bi0} + {bs}]) : 0u;", 2)
+            self.emit(f"v{o} = eas_mma_f16(eas_a, eas_b, {self.name(acc)});", 2)
+        else:
+            self.emit(f"float d0 = {self.name(acc)}.x, d1 = {self.name(acc)}.y;", 2)
+            pre = "" if on == "true" else f"if ({on}) "
+            self.emit(f"{pre}{{", 2)
+            self.emit("#pragma unroll", 3)
+            self.emit("for (uint32_t k = 0; k < 8u; ++k) {", 3)
+            av = _as_float(a_buf.dtype, f"{A}[{ab} + eas_g * {as_} + k]")
+            b0 = _as_float(b_buf.dtype, f"{B}[{bb} + k * {bs} + eas_t * 2u]")
+            b1 = _as_float(b_buf.dtype, f"{B}[{bb} + k * {bs} + eas_t * 2u + 1u]")
+            self.emit(f"const float a = {av};", 4)
+            self.emit(f"d0 = fmaf(a, {b0}, d0); d1 = fmaf(a, {b1}, d1);", 4)
+            self.emit("}", 3)
+            self.emit("}", 2)
+            self.emit(f"v{o} = make_float2(d0, d1);", 2)
+        self.emit("}")
+
+
+def ir_to_cuda(ir: IRModule) -> Lowered:
+    """Lower validated, optimised IR to one CUDA kernel (plus an optional native plan)."""
+    lowered = _Emitter(ir).run()
+    from .patterns import match_native
+
+    lowered.native = match_native(ir, lowered)
+    return lowered

@@ -1,0 +1,24 @@
+// eas_internal.h — declarations shared by the .cu files of libeas_cuda.so.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include "../../include/eas_cuda.h"
+
+// Driver-API entry points resolved at runtime (no link against libcuda).
+struct DriverApi {
+  decltype(&::cuModuleLoadData) moduleLoadData = nullptr;
+  decltype(&::cuModuleUnload) moduleUnload = nullptr;
+  decltype(&::cuModuleGetFunction) moduleGetFunction = nullptr;
+  decltype(&::cuLaunchKernel) launchKernel = nullptr;
+  decltype(&::cuFuncSetAttribute) funcSetAttribute = nullptr;
+  decltype(&::cuFuncGetAttribute) funcGetAttribute = nullptr;
+  decltype(&::cuGetErrorString) getErrorString = nullptr;
+  decltype(&::cuTensorMapEncodeTiled) tensorMapEncodeTiled = nullptr;
+};
+extern DriverApi g_drv;
+
+int eas_driver_init();
+int eas_fail(int code, const char* fmt, ...);
+int eas_cuda_check(cudaError_t e, const char* what, int code);
+int eas_drv_check(CUresult r, const char* what, int code);

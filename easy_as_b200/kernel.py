@@ -1,0 +1,211 @@
+"""``@eas.kernel``: argument binding, compile cache, autotune and dispatch.
+
+Behaviour follows easy_as ``eas/kernel.py``:
+
+* constexpr parameters are split from runtime ones by annotation (``:14-29``);
+* the compile cache key is ``(sorted meta items, runtime_arg_signature)`` so
+  scalar *values* never trigger a recompile (``:242-255``);
+* launch options ``_sync, _grid, _tptg, _shape, _nthreads`` are popped from
+  the keyword arguments and normalised (``:129-240``); ``_grid`` may be a
+  callable ``(meta, runtime_args) -> dims``;
+* ``_tptg`` must equal ``(block, 1, 1)`` in thread mode and ``(1, 1, 1)`` in
+  SPMD mode, else ``ValueError`` (``:306-319``);
+* ``@eas.autotune`` times every config once per key with the runtime's
+  ``benchmark`` and caches the winner (``:73-127``).
+"""
+
+from __future__ import annotations
+
+import inspect
+from typing import Any, Callable, Mapping
+
+from .autotune import AutotuneSpec, Config
+from .compiler import CompiledKernel, compile as _compile, runtime_arg_signature
+from .meta import constexpr
+from .runtime import get_runtime
+
+_LAUNCH_OPTIONS = ("_sync", "_shape", "_grid", "_tptg", "_nthreads")
+
+
+def _dims(value: Any, what: str, *, lo: int, hi: int, pad: bool, min_value: int) -> tuple[int, ...]:
+    if isinstance(value, int):
+        dims = [int(value)]
+    elif isinstance(value, (tuple, list)):
+        dims = [int(x) for x in value]
+    else:
+        raise TypeError(f"{what} must be int or tuple/list of ints, got {type(value)!r}")
+    if not (lo <= len(dims) <= hi):
+        raise ValueError(f"{what} must have {lo}..{hi} dims" if hi < 99 else f"{what} must have >= {lo} dim")
+    if pad:
+        dims += [1] * (3 - len(dims))
+    if any(d < min_value for d in dims):
+        raise ValueError(f"{what} dims must be {'>= 0' if min_value == 0 else '> 0'}")
+    return tuple(dims)
+
+
+class Kernel:
+    def __init__(self, fn: Callable[..., Any]):
+        self.fn = fn
+        self.name = fn.__name__
+        self.sig = inspect.signature(fn)
+        ann = inspect.get_annotations(fn, eval_str=True)
+        self.meta_params = {n for n, p in self.sig.parameters.items()
+                            if ann.get(n, p.annotation) is constexpr}
+        self._cache: dict[tuple[Any, Any], CompiledKernel] = {}
+        self._autotune_spec: AutotuneSpec | None = None
+        self._tuned_cache: dict[tuple[Any, ...], Config] = {}
+
+    def _set_autotune_spec(self, spec: AutotuneSpec) -> None:
+        self._autotune_spec = spec
+
+    # -- launch options ------------------------------------------------------
+    def _extract_runtime_options(self, kwargs: dict[str, Any]) -> dict[str, Any]:
+        sync = kwargs.pop("_sync", True)
+        if not isinstance(sync, bool):
+            raise TypeError(f"_sync must be bool, got {type(sync)!r}")
+        shape = kwargs.pop("_shape", None)
+        grid = kwargs.pop("_grid", None)
+        tptg = kwargs.pop("_tptg", None)
+        nthreads = kwargs.pop("_nthreads", None)
+        if nthreads is not None:
+            try:
+                nthreads = int(nthreads)
+            except Exception as e:
+                raise TypeError(f"_nthreads must be an int-like value, got {type(nthreads)!r}") from e
+            if nthreads < 0:
+                raise ValueError("_nthreads must be >= 0")
+        return {"sync": sync, "nthreads": nthreads, "grid": grid, "shape": shape, "tptg": tptg}
+
+    def _normalize_runtime_options(self, raw: dict[str, Any], meta: dict[str, Any],
+                                   runtime_args: dict[str, Any]) -> dict[str, Any]:
+        shape = raw.get("shape")
+        if shape is not None:
+            if not isinstance(shape, (int, tuple, list)):
+                raise TypeError(f"_shape must be int or tuple/list of ints, got {type(shape)!r}")
+            shape = _dims(shape, "_shape", lo=1, hi=99, pad=False, min_value=0)
+        grid = raw.get("grid")
+        if callable(grid):
+            grid = grid(meta, runtime_args)
+        if grid is not None:
+            if not isinstance(grid, (int, tuple, list)):
+                raise TypeError(f"_grid must be int/tuple/list or callable, got {type(grid)!r}")
+            grid = _dims(grid, "_grid", lo=1, hi=3, pad=True, min_value=0)
+        tptg = raw.get("tptg")
+        if tptg is not None:
+            tptg = _dims(tptg, "_tptg", lo=1, hi=3, pad=True, min_value=1)
+        return {"sync": bool(raw["sync"]), "nthreads": raw["nthreads"], "grid": grid,
+                "shape": shape, "tptg": tptg}
+
+    @staticmethod
+    def _check_tptg(ck: CompiledKernel, tptg: tuple[int, int, int] | None) -> None:
+        if tptg is None:
+            raise RuntimeError("internal error: normalized tptg must not be None")
+        expected = (int(ck.block_size), 1, 1) if ck.launch_mode == "thread" else (1, 1, 1)
+        if tuple(int(x) for x in tptg) != expected:
+            raise ValueError(f"_tptg must match kernel launch mode: expected {expected}, "
+                             f"got ({tptg[0]}, {tptg[1]}, {tptg[2]})")
+
+    # -- autotune --------------------------------------------------------------
+    def _autotune_key(self, spec: AutotuneSpec, meta: Mapping[str, Any],
+                      runtime_args: Mapping[str, Any]) -> tuple[Any, ...]:
+        def norm(v: Any) -> Any:
+            if isinstance(v, (bool, int, float, str, type(None))):
+                return v
+            if isinstance(v, (tuple, list)):
+                return tuple(norm(x) for x in v)
+            if isinstance(v, dict):
+                return tuple(sorted((str(k), norm(x)) for k, x in v.items()))
+            for conv in (int, float):
+                try:
+                    return conv(v)
+                except Exception:
+                    pass
+            if hasattr(v, "shape"):
+                try:
+                    return ("shape", tuple(int(x) for x in v.shape))
+                except Exception:
+                    pass
+            raise TypeError(f"autotune key value must be hashable/normalizable, got {type(v)!r}")
+
+        key = []
+        for name in spec.key:
+            if name in meta:
+                key.append(norm(meta[name]))
+            elif name in runtime_args:
+                key.append(norm(runtime_args[name]))
+            else:
+                raise KeyError(f"autotune key {name!r} not found in args/meta")
+        return tuple(key)
+
+    def _autotune_select(self, spec: AutotuneSpec, meta: dict[str, Any], runtime_args: dict[str, Any],
+                         raw_opts: dict[str, Any]) -> tuple[dict[str, Any], dict[str, Any]]:
+        key = self._autotune_key(spec, meta, runtime_args)
+        best = self._tuned_cache.get(key)
+        if best is None:
+            bench = getattr(get_runtime(), "benchmark", None)
+            if not callable(bench):
+                raise RuntimeError("autotune requires a runtime with benchmark(); use the CUDA runtime")
+            best_t = None
+            for cfg in spec.configs:
+                m = {**meta, **dict(cfg.meta)}
+                opts = self._normalize_runtime_options(raw_opts, m, runtime_args)
+                ck = self._compile_from_split(m, runtime_args)
+                t = float(bench(ck, runtime_args, m, repeat=spec.repeat, warmup=spec.warmup,
+                                nthreads=opts["nthreads"], grid=opts["grid"], tptg=opts["tptg"],
+                                shape=opts["shape"]))
+                if best_t is None or t < best_t:
+                    best, best_t = cfg, t
+            if best is None:  # pragma: no cover
+                raise RuntimeError("autotune failed to select a config")
+            self._tuned_cache[key] = best
+        m = {**meta, **dict(best.meta)}
+        return m, self._normalize_runtime_options(raw_opts, m, runtime_args)
+
+    # -- compile / launch -----------------------------------------------------------
+    def _compile_from_split(self, meta: dict[str, Any], runtime_args: dict[str, Any]) -> CompiledKernel:
+        key = (tuple(sorted(meta.items())), runtime_arg_signature(runtime_args))
+        ck = self._cache.get(key)
+        if ck is None:
+            ck = _compile(self.fn, runtime_args, meta)
+            self._cache[key] = ck
+        return ck
+
+    def _bind_and_split(self, /, *args: Any, **kwargs: Any) -> tuple[dict[str, Any], dict[str, Any]]:
+        bound = self.sig.bind(*args, **kwargs)
+        bound.apply_defaults()
+        meta = {k: bound.arguments.pop(k) for k in list(bound.arguments) if k in self.meta_params}
+        return meta, dict(bound.arguments)
+
+    def _prepare(self, args: tuple[Any, ...], kwargs: dict[str, Any]):
+        raw = self._extract_runtime_options(kwargs)
+        meta, runtime_args = self._bind_and_split(*args, **kwargs)
+        if self._autotune_spec is not None:
+            meta, opts = self._autotune_select(self._autotune_spec, meta, runtime_args, raw)
+        else:
+            opts = self._normalize_runtime_options(raw, meta, runtime_args)
+        ck = self._compile_from_split(meta, runtime_args)
+        if raw.get("tptg") is not None:
+            self._check_tptg(ck, opts.get("tptg"))
+        return ck, meta, runtime_args, opts
+
+    def compile(self, /, *args: Any, **kwargs: Any) -> CompiledKernel:
+        return self._prepare(args, dict(kwargs))[0]
+
+    def __call__(self, /, *args: Any, **kwargs: Any) -> None:
+        ck, meta, runtime_args, opts = self._prepare(args, dict(kwargs))
+        get_runtime().run(ck, runtime_args, meta, **opts)
+
+    def to_cuda(self, /, *args: Any, **kwargs: Any) -> str:
+        """Generated CUDA C++ source for this specialisation."""
+        return self.compile(*args, **kwargs).src
+
+    # the reference's name for the same query; returns the CUDA source here
+    to_msl = to_cuda
+
+
+def kernel(fn: Callable[..., Any]) -> Kernel:
+    k = Kernel(fn)
+    spec = getattr(fn, "__eas_autotune_spec__", None)
+    if isinstance(spec, AutotuneSpec):
+        k._set_autotune_spec(spec)
+    return k

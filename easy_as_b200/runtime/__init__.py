@@ -1,0 +1,42 @@
+"""Runtime selection.
+
+There is one backend, CUDA on sm_100a.  ``EAS_BACKEND`` accepts ``auto`` and
+``cuda``; the reference's names for its GPU backend (``mps``/``metal``) are
+refused with a message, and ``cpu`` is refused as in the reference
+(easy_as ``eas/runtime/__init__.py:18-44``): there is no CPU fallback.
+"""
+
+from __future__ import annotations
+
+import os
+from typing import Any
+
+from .base import Runtime
+
+__all__ = ["get_runtime", "Runtime"]
+
+_cuda: Any = None
+
+
+def _cuda_runtime() -> Any:
+    global _cuda
+    if _cuda is None:
+        from .cuda import CudaRuntime
+
+        _cuda = CudaRuntime()
+    return _cuda
+
+
+def get_runtime(backend: str | None = None) -> Runtime:
+    name = (backend or os.environ.get("EAS_BACKEND", "auto")).lower()
+    if name in ("auto", "cuda"):
+        rt = _cuda_runtime()
+        if not rt.is_available():
+            raise RuntimeError("CUDA runtime is not available: " + rt.unavailable_reason()
+                               + ". Build the native library with `python -m easy_as_b200.build`.")
+        return rt
+    if name == "cpu":
+        raise ValueError("unsupported backend: 'cpu' (there is no CPU runtime; use 'cuda' or 'auto')")
+    if name in ("mps", "metal"):
+        raise ValueError(f"unsupported backend: {name!r} (this build targets CUDA sm_100a; use 'cuda' or 'auto')")
+    raise ValueError(f"unsupported backend: {name!r} (expected 'auto'|'cuda')")

@@ -1,0 +1,507 @@
+"""CUDA runtime: the B200 counterpart of the reference's ``MetalRuntime``.
+
+Same public methods and launch semantics as easy_as ``eas/runtime/metal.py``:
+
+* ``run(ck, runtime_args, meta, *, sync, nthreads, grid, tptg, shape)``
+  (``metal.py:244-352``): checks ``tptg`` against the launch mode, derives the
+  grid with the reference's rules (``grid.py``; thread mode 1D without
+  ``_grid`` runs exactly ``N`` threads), resolves every buffer argument to a
+  device pointer, packs the kernel parameters, launches, and either waits
+  (``sync=True``) or queues an event, keeping at most ``EAS_MAX_IN_FLIGHT``
+  (default 256) launches in flight (``metal.py:52-67,346-352``).
+* ``synchronize()`` drains the queue (``metal.py:354-360``).
+* ``benchmark(...)`` times ``repeat`` launches after ``warmup`` with CUDA
+  events on the launch stream and returns seconds per launch
+  (``metal.py:362-506`` used wall-clock time around a command buffer).
+
+Buffer arguments may be torch CUDA tensors (zero copy, launched on torch's
+current stream), ``eas.Tensor(device="cuda")``, or host arrays (numpy, torch
+CPU, ``eas.Tensor(device="cpu")``), which are bridged through temporary device
+buffers and copied back when written (``metal.py:209-233,337-344``).
+
+There is no CPU fallback: without the native library or a GPU every entry
+point raises.
+"""
+
+from __future__ import annotations
+
+import hashlib
+import math
+import os
+import struct
+import time
+from collections import deque
+from pathlib import Path
+from typing import Any, Mapping
+
+import numpy as np
+
+from ..ir import DType
+from . import cuda_ext
+from .grid import infer_1d_grid, infer_grid, infer_nthreads
+
+ALL_THREADS = 0xFFFFFFFF
+MAX_GRID_YZ = 65535
+
+
+def _torch() -> Any:
+    try:
+        import torch  # type: ignore
+
+        return torch
+    except Exception:
+        return None
+
+
+class DeviceBuffer:
+    """Owning handle of one ``cudaMalloc`` allocation on one device."""
+
+    __slots__ = ("ptr", "nbytes", "device", "__weakref__")
+
+    def __init__(self, nbytes: int, device: int = 0):
+        lib = cuda_ext.load()
+        p = cuda_ext.ctypes.c_void_p()
+        cuda_ext.check(lib.eas_alloc_buffer(int(device), int(nbytes), cuda_ext.ctypes.byref(p)), "alloc_buffer")
+        self.ptr = int(p.value or 0)
+        self.nbytes = int(nbytes)
+        self.device = int(device)
+
+    def free(self) -> None:
+        if self.ptr:
+            lib = cuda_ext.load(require=False)
+            if lib is not None:
+                lib.eas_free_buffer(self.ptr)
+            self.ptr = 0
+
+    def __del__(self) -> None:  # pragma: no cover - interpreter shutdown order varies
+        try:
+            self.free()
+        except Exception:
+            pass
+
+    def copy_from_host(self, arr: Any, stream: int = 0) -> None:
+        a = np.ascontiguousarray(arr)
+        if a.nbytes > self.nbytes:
+            raise ValueError(f"copy_from_host: {a.nbytes} bytes do not fit a {self.nbytes}-byte buffer")
+        lib = cuda_ext.load()
+        cuda_ext.check(lib.eas_copy_from_host(self.ptr, a.ctypes.data, a.nbytes, stream), "copy_from_host")
+
+    def copy_to_host(self, out: np.ndarray, stream: int = 0) -> None:
+        if not out.flags.c_contiguous:
+            raise ValueError("copy_to_host needs a C-contiguous destination")
+        if out.nbytes > self.nbytes:
+            raise ValueError(f"copy_to_host: {out.nbytes} bytes exceed the {self.nbytes}-byte buffer")
+        lib = cuda_ext.load()
+        cuda_ext.check(lib.eas_copy_to_host(out.ctypes.data, self.ptr, out.nbytes, stream), "copy_to_host")
+
+
+# ---------------------------------------------------------------------------
+# kernel parameter packing
+# ---------------------------------------------------------------------------
+
+_SCALAR_FMT = {DType.U32: ("<I", 4), DType.F32: ("<f", 4), DType.F16: ("<H", 2), DType.BOOL: ("<?", 1)}
+
+
+class ParamLayout:
+    """Byte layout of a generated kernel's parameters (natural alignment, in order)."""
+
+    def __init__(self, params: list[Any]):
+        self.entries: list[tuple[Any, int, str]] = []
+        off = 0
+        for p in params:
+            if p.kind == "buffer":
+                fmt, size = "<Q", 8
+            else:
+                fmt, size = _SCALAR_FMT[p.dtype]
+            off = -(-off // size) * size
+            self.entries.append((p, off, fmt))
+            off += size
+        self.size = -(-off // 8) * 8
+
+    def pack(self, values: Mapping[str, Any], pointers: Mapping[str, int], hidden: Mapping[str, int]) -> bytearray:
+        buf = bytearray(self.size)
+        for p, off, fmt in self.entries:
+            if p.kind == "buffer":
+                struct.pack_into(fmt, buf, off, pointers[p.arg])
+            elif p.kind == "hidden":
+                struct.pack_into(fmt, buf, off, hidden[p.name])
+            else:
+                struct.pack_into(fmt, buf, off, _scalar_bits(p.dtype, values[p.arg], p.arg))
+        return buf
+
+
+def _scalar_bits(dt: DType, v: Any, name: str) -> Any:
+    if dt == DType.U32:
+        iv = int(v)
+        if not 0 <= iv < (1 << 32):
+            raise ValueError(f"scalar {name!r}={iv} does not fit u32")
+        return iv
+    if dt == DType.F32:
+        return float(v)
+    if dt == DType.F16:
+        return int(np.array(v, dtype=np.float16).view(np.uint16))
+    return bool(v)
+
+
+# ---------------------------------------------------------------------------
+# launch geometry
+# ---------------------------------------------------------------------------
+
+
+def launch_geometry(ck: Any, runtime_args: Mapping[str, Any], *, nthreads: int | None,
+                    grid: tuple[int, int, int] | None, tptg: tuple[int, int, int] | None,
+                    shape: tuple[int, ...] | None) -> tuple[tuple[int, int, int], int] | None:
+    """Programs per axis and active-thread count, or None when there is nothing to run.
+
+    Thread mode: one program = one block of ``block_size`` threads.
+    SPMD mode: one program = ``block_size`` lanes.  Follows ``metal.py:257-326``.
+    """
+    bs = int(ck.block_size)
+    thread_mode = ck.launch_mode == "thread"
+    expected = (bs, 1, 1) if thread_mode else (1, 1, 1)
+    if tptg is not None and tuple(int(x) for x in tptg) != expected:
+        raise ValueError(f"tptg must match kernel launch mode: expected {expected}, "
+                         f"got ({tptg[0]}, {tptg[1]}, {tptg[2]})")
+    if grid is None:
+        inferred = infer_grid(ck.ir, runtime_args, bs, shape=shape)
+        if inferred is None:
+            n = infer_nthreads(runtime_args, nthreads=nthreads)
+            if n == 0:
+                return None
+            if thread_mode:
+                return (math.ceil(n / bs), 1, 1), n
+            return (infer_1d_grid(runtime_args, bs, nthreads=nthreads), 1, 1), ALL_THREADS
+        dims = tuple(int(x) for x in inferred)
+    else:
+        dims = tuple(int(x) for x in grid)
+        if min(dims) < 0:
+            raise ValueError("grid dims must be >= 0")
+    if min(dims) == 0:
+        return None
+    return dims, ALL_THREADS  # type: ignore[return-value]
+
+
+# ---------------------------------------------------------------------------
+# runtime
+# ---------------------------------------------------------------------------
+
+
+def _cache_dir() -> Path | None:
+    d = os.environ.get("EAS_CACHE_DIR", str(Path.home() / ".cache" / "easy_as_b200"))
+    if d in ("", "0", "off", "none"):
+        return None
+    return Path(d)
+
+
+class _Arg:
+    """A buffer argument resolved to a device pointer."""
+
+    __slots__ = ("ptr", "device", "keep", "host", "dev_buf", "torch_stream")
+
+    def __init__(self, ptr: int, device: int | None, keep: Any = None, host: np.ndarray | None = None,
+                 dev_buf: DeviceBuffer | None = None, torch_stream: bool = False):
+        self.ptr, self.device, self.keep, self.host = ptr, device, keep, host
+        self.dev_buf, self.torch_stream = dev_buf, torch_stream
+
+
+class CudaRuntime:
+    def __init__(self) -> None:
+        self._available: bool | None = None
+        self._reason = ""
+        self._pipelines: dict[tuple[str, str, int, int], int] = {}
+        self._layouts: dict[int, ParamLayout] = {}
+        self._pending: deque[tuple[int, Any]] = deque()
+        self._max_in_flight: int | None = None
+        self._staging: dict[tuple[int, int], list[DeviceBuffer]] = {}
+        self.launch_count = 0  # kernels launched through this runtime (generic + native)
+
+    # -- availability ----------------------------------------------------------
+    def is_available(self) -> bool:
+        if self._available is None:
+            lib = cuda_ext.load(require=False)
+            if lib is None:
+                self._available, self._reason = False, cuda_ext.load_error() or "native library missing"
+            else:
+                self._available = bool(lib.eas_is_available())
+                self._reason = "" if self._available else cuda_ext.last_error()
+        return self._available
+
+    def unavailable_reason(self) -> str:
+        self.is_available()
+        return self._reason
+
+    @staticmethod
+    def lib() -> Any:
+        return cuda_ext.load()
+
+    def default_device(self) -> int:
+        t = _torch()
+        if t is not None and t.cuda.is_available() and t.cuda.is_initialized():
+            return int(t.cuda.current_device())
+        return int(os.environ.get("EAS_DEVICE", "0"))
+
+    def _max_flight(self) -> int:
+        if self._max_in_flight is None:
+            try:
+                v = int(os.environ.get("EAS_MAX_IN_FLIGHT", "256").strip() or 256)
+            except ValueError:
+                v = 256
+            self._max_in_flight = max(v, 0)
+        return self._max_in_flight
+
+    # -- compile / pipelines ---------------------------------------------------------
+    def compile_cubin(self, src: str, name: str) -> bytes:
+        lib = self.lib()
+        drv, nvrtc = cuda_ext.ctypes.c_int(), cuda_ext.ctypes.c_int()
+        lib.eas_versions(cuda_ext.ctypes.byref(drv), cuda_ext.ctypes.byref(nvrtc))
+        key = hashlib.sha256(f"sm_100a|nvrtc{nvrtc.value}|{name}|".encode() + src.encode()).hexdigest()
+        cdir = _cache_dir()
+        if cdir is not None:
+            f = cdir / f"{key}.cubin"
+            if f.exists():
+                return f.read_bytes()
+        img, size = cuda_ext.ctypes.c_void_p(), cuda_ext.ctypes.c_size_t()
+        rc = lib.eas_compile(src.encode(), f"{name}.cu".encode(), None, 0, cuda_ext.ctypes.byref(img),
+                             cuda_ext.ctypes.byref(size))
+        if rc != cuda_ext.EAS_OK:
+            msg = cuda_ext.last_error()
+            if rc == cuda_ext.EAS_ERR_COMPILE:
+                raise RuntimeError(f"CUDA compile failed: {msg}")
+            cuda_ext.check(rc, "compile")
+        try:
+            data = cuda_ext.ctypes.string_at(img.value, size.value)
+        finally:
+            lib.eas_free_host(img)
+        if cdir is not None:
+            try:
+                cdir.mkdir(parents=True, exist_ok=True)
+                tmp = cdir / f"{key}.{os.getpid()}.tmp"
+                tmp.write_bytes(data)
+                os.replace(tmp, cdir / f"{key}.cubin")
+            except OSError:
+                pass
+        return data
+
+    def pipeline(self, src: str, name: str, device: int, dyn_smem: int) -> int:
+        key = (src, name, device, dyn_smem)
+        p = self._pipelines.get(key)
+        if p is None:
+            cubin = self.compile_cubin(src, name)
+            lib = self.lib()
+            h = cuda_ext.ctypes.c_void_p()
+            cuda_ext.check(lib.eas_pipeline_load(device, cubin, len(cubin), name.encode(),
+                                                 dyn_smem if dyn_smem > 48 * 1024 else 0,
+                                                 cuda_ext.ctypes.byref(h)), "pipeline_load")
+            p = int(h.value)
+            self._pipelines[key] = p
+        return p
+
+    def _pipeline_for(self, ck: Any, device: int) -> int:
+        plan = ck.plan
+        return self.pipeline(ck.src, plan.kernel_name, device, plan.dyn_smem)
+
+    # -- arguments ---------------------------------------------------------------------
+    def _resolve(self, ck: Any, runtime_args: Mapping[str, Any], *, allow_host: bool = True
+                 ) -> tuple[dict[str, _Arg], int, int]:
+        torch = _torch()
+        resolved: dict[str, _Arg] = {}
+        device: int | None = None
+        torch_stream = False
+        host_pending: list[tuple[str, np.ndarray]] = []
+        for a in ck.ir.args:
+            if a.kind != "buffer":
+                continue
+            v = runtime_args[a.name]
+            want = np.float32 if a.dtype == DType.F32 else np.float16
+            if torch is not None and isinstance(v, torch.Tensor):
+                t = v.detach()
+                tdt = torch.float32 if a.dtype == DType.F32 else torch.float16
+                if t.dtype != tdt:
+                    raise TypeError(f"{a.name!r} must be {tdt}, got {t.dtype}")
+                if t.device.type == "cuda":
+                    if not t.is_contiguous():
+                        if a.name in ck.writes:
+                            raise ValueError(f"{a.name!r} is written by the kernel and must be contiguous")
+                        t = t.contiguous()
+                    dev = int(t.device.index or 0)
+                    if device is not None and dev != device:
+                        raise ValueError(f"buffers on different devices: {device} and {dev}")
+                    device = dev
+                    resolved[a.name] = _Arg(int(t.data_ptr()), dev, keep=t)
+                    torch_stream = True
+                    continue
+                if t.device.type != "cpu":
+                    raise TypeError(f"unsupported torch device for {a.name!r}: {t.device!s}")
+                v = t.contiguous().numpy()
+            if getattr(v, "__eas_tensor__", False):
+                if np.dtype(v.dtype) != np.dtype(want):
+                    raise TypeError(f"{a.name!r} dtype mismatch: expected {np.dtype(want)}, got {v.dtype}")
+                if v.device == "cuda":
+                    dev = v._cuda_device()
+                    if device is not None and dev != device:
+                        raise ValueError(f"buffers on different devices: {device} and {dev}")
+                    device = dev
+                    resolved[a.name] = _Arg(v._cuda_ptr(), dev, keep=v)
+                    continue
+                v = v.numpy()
+            if isinstance(v, np.ndarray):
+                if v.dtype != want:
+                    raise TypeError(f"{a.name!r} must be {np.dtype(want)}, got {v.dtype}")
+                if not v.flags.c_contiguous:
+                    raise ValueError(f"{a.name!r} must be C-contiguous for MVP")
+                if not allow_host:
+                    raise ValueError("benchmark() with numpy inputs is not supported; use eas.Tensor(device='cuda') "
+                                     "or torch CUDA tensors for device-native timing")
+                host_pending.append((a.name, v))
+                continue
+            raise TypeError(f"expected numpy.ndarray, torch.Tensor or eas.Tensor for {a.name!r}, got {type(v)!r}")
+        if device is None:
+            device = self.default_device()
+        stream = 0
+        if torch_stream and torch is not None:
+            stream = int(torch.cuda.current_stream(device).cuda_stream)
+        # host arrays: one temporary device buffer per distinct array object
+        staged: dict[int, DeviceBuffer] = {}
+        for name, arr in host_pending:
+            buf = staged.get(id(arr))
+            if buf is None:
+                buf = self._stage(device, max(arr.nbytes, 1))
+                buf.copy_from_host(arr, stream)
+                staged[id(arr)] = buf
+            resolved[name] = _Arg(buf.ptr, device, keep=arr, host=arr if name in ck.writes else None,
+                                  dev_buf=buf)
+        return resolved, device, stream
+
+    # -- host staging buffers ----------------------------------------------------------
+    def _stage(self, device: int, nbytes: int) -> DeviceBuffer:
+        free = self._staging.get((device, nbytes))
+        return free.pop() if free else DeviceBuffer(nbytes, device)
+
+    def _unstage(self, args: dict[str, _Arg]) -> None:
+        """Return staging buffers of host arguments to the pool (after the launch has completed)."""
+        seen: set[int] = set()
+        for a in args.values():
+            b = a.dev_buf
+            if b is not None and id(b) not in seen:
+                seen.add(id(b))
+                free = self._staging.setdefault((b.device, b.nbytes), [])
+                if len(free) < 4:
+                    free.append(b)
+                a.dev_buf = None
+
+    # -- launch -------------------------------------------------------------------------
+    def _launch_generic(self, ck: Any, runtime_args: Mapping[str, Any], args: dict[str, _Arg], device: int,
+                        stream: int, programs: tuple[int, int, int], ntx: int) -> None:
+        plan = ck.plan
+        pipe = self._pipeline_for(ck, device)
+        layout = self._layouts.get(id(plan))
+        if layout is None:
+            layout = ParamLayout(plan.params)
+            self._layouts[id(plan)] = layout
+        ptrs = {n: a.ptr for n, a in args.items()}
+        lib = self.lib()
+        gx, gy, gz = programs
+        block = (cuda_ext.ctypes.c_uint32 * 3)(plan.cuda_threads, 1, 1)
+        for z0 in range(0, gz, MAX_GRID_YZ):
+            for y0 in range(0, gy, MAX_GRID_YZ):
+                hidden = {"eas_ntx": ntx, "eas_pid_x": 0, "eas_pid_y": y0, "eas_pid_z": z0}
+                blob = layout.pack(runtime_args, ptrs, hidden)
+                cblob = (cuda_ext.ctypes.c_char * len(blob)).from_buffer(blob)
+                g = (cuda_ext.ctypes.c_uint32 * 3)(gx, min(MAX_GRID_YZ, gy - y0), min(MAX_GRID_YZ, gz - z0))
+                cuda_ext.check(lib.eas_launch(pipe, g, block, plan.dyn_smem, stream, cblob, len(blob)),
+                               f"launch {plan.kernel_name}")
+                self.launch_count += 1
+
+    def _dispatch(self, ck: Any, runtime_args: Mapping[str, Any], args: dict[str, _Arg], device: int, stream: int,
+                  programs: tuple[int, int, int], ntx: int) -> None:
+        native = getattr(ck.plan, "native", None)
+        if native is not None and native.try_launch(self, ck, runtime_args, args, device, stream, programs, ntx):
+            return
+        self._launch_generic(ck, runtime_args, args, device, stream, programs, ntx)
+
+    def run(self, ck: Any, runtime_args: Mapping[str, Any], meta: Mapping[str, Any], *, sync: bool = True,
+            nthreads: int | None = None, grid: tuple[int, int, int] | None = None,
+            tptg: tuple[int, int, int] | None = None, shape: tuple[int, ...] | None = None) -> None:
+        _ = meta
+        geo = launch_geometry(ck, runtime_args, nthreads=nthreads, grid=grid, tptg=tptg, shape=shape)
+        if geo is None:
+            return
+        if not self.is_available():
+            raise RuntimeError("CUDA runtime is not available: " + self._reason)
+        args, device, stream = self._resolve(ck, runtime_args)
+        host_copies = [(a.dev_buf, a.host) for a in args.values() if a.host is not None]
+        self._dispatch(ck, runtime_args, args, device, stream, *geo)
+        lib = self.lib()
+        if sync or host_copies:
+            cuda_ext.check(lib.eas_stream_synchronize(stream), "kernel execution")
+            done: set[int] = set()
+            for buf, arr in host_copies:
+                if id(arr) not in done:
+                    buf.copy_to_host(arr, stream)
+                    done.add(id(arr))
+            self._unstage(args)
+            return
+        ev = cuda_ext.ctypes.c_void_p()
+        cuda_ext.check(lib.eas_event_create(cuda_ext.ctypes.byref(ev)), "event_create")
+        cuda_ext.check(lib.eas_event_record(ev, stream), "event_record")
+        self._pending.append((int(ev.value), (args, runtime_args)))
+        limit = self._max_flight()
+        if limit and len(self._pending) > limit:
+            self._wait_one()
+
+    def _wait_one(self) -> None:
+        ev, _keep = self._pending.popleft()
+        lib = self.lib()
+        try:
+            cuda_ext.check(lib.eas_event_synchronize(ev), "kernel execution")
+        finally:
+            lib.eas_event_destroy(ev)
+
+    def synchronize(self) -> None:
+        while self._pending:
+            self._wait_one()
+
+    def in_flight(self) -> int:
+        return len(self._pending)
+
+    # -- timing ---------------------------------------------------------------------------
+    def benchmark(self, ck: Any, runtime_args: Mapping[str, Any], meta: Mapping[str, Any], *, repeat: int,
+                  warmup: int = 0, nthreads: int | None = None, grid: tuple[int, int, int] | None = None,
+                  tptg: tuple[int, int, int] | None = None, shape: tuple[int, ...] | None = None,
+                  **_ignored: Any) -> float:
+        """Mean seconds per launch over ``repeat`` launches (CUDA events), after ``warmup``."""
+        _ = meta
+        if repeat <= 0:
+            raise ValueError("repeat must be > 0")
+        if warmup < 0:
+            raise ValueError("warmup must be >= 0")
+        self.synchronize()
+        geo = launch_geometry(ck, runtime_args, nthreads=nthreads, grid=grid, tptg=tptg, shape=shape)
+        if geo is None:
+            return 0.0
+        args, device, stream = self._resolve(ck, runtime_args, allow_host=False)
+        for _ in range(warmup):
+            self._dispatch(ck, runtime_args, args, device, stream, *geo)
+        lib = self.lib()
+        e0, e1 = cuda_ext.ctypes.c_void_p(), cuda_ext.ctypes.c_void_p()
+        cuda_ext.check(lib.eas_event_create(cuda_ext.ctypes.byref(e0)), "event_create")
+        cuda_ext.check(lib.eas_event_create(cuda_ext.ctypes.byref(e1)), "event_create")
+        try:
+            cuda_ext.check(lib.eas_event_record(e0, stream), "event_record")
+            for _ in range(repeat):
+                self._dispatch(ck, runtime_args, args, device, stream, *geo)
+            cuda_ext.check(lib.eas_event_record(e1, stream), "event_record")
+            cuda_ext.check(lib.eas_event_synchronize(e1), "kernel execution")
+            ms = cuda_ext.ctypes.c_float()
+            cuda_ext.check(lib.eas_event_elapsed_ms(e0, e1, cuda_ext.ctypes.byref(ms)), "elapsed")
+        finally:
+            lib.eas_event_destroy(e0)
+            lib.eas_event_destroy(e1)
+        return float(ms.value) * 1e-3 / repeat
+
+    def wall_benchmark(self, fn: Any, repeat: int) -> float:  # pragma: no cover - helper for examples
+        t0 = time.perf_counter()
+        for _ in range(repeat):
+            fn()
+        self.synchronize()
+        return (time.perf_counter() - t0) / repeat

@@ -1,0 +1,129 @@
+/*
+ * eas_cuda.h — C ABI of libeas_cuda.so, the native device layer of easy_as_b200.
+ *
+ * The reference binds its device layer as the CPython extension `eas._metal`
+ * (easy_as eas/runtime/_metal.mm, method table at _metal.mm:1436-1461; the
+ * required subset is checked by eas/runtime/metal_ext.py:22-33).  This header
+ * replaces that module with plain C entry points — pointers, sizes and status
+ * codes, no Python or torch types — bound from Python with ctypes
+ * (easy_as_b200/runtime/cuda_ext.py).  Each entry point names the `eas._metal`
+ * method it replaces.
+ *
+ * Conventions
+ *   - Every function returns an int status (EAS_OK == 0).  On failure
+ *     eas_last_error() returns a thread-local, human-readable message.
+ *   - Device pointers are CUdeviceptr values carried as void*.
+ *   - `stream` is a cudaStream_t / CUstream (NULL = legacy default stream,
+ *     which is also torch's default stream).
+ *   - Nothing here traps, asserts or spins without bound on the device.
+ */
+#ifndef EAS_CUDA_H
+#define EAS_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define EAS_OK 0
+#define EAS_ERR_UNAVAILABLE 1 /* no driver, no device, or NVRTC missing           */
+#define EAS_ERR_COMPILE 2     /* NVRTC rejected the source (log in last_error)     */
+#define EAS_ERR_LAUNCH 3      /* launch or asynchronous kernel failure             */
+#define EAS_ERR_VALUE 4       /* bad argument (sizes, dims, alignment)             */
+#define EAS_ERR_MEMORY 5      /* allocation or copy failure                        */
+#define EAS_ERR_INJECTED 6    /* failure injected by eas_fault_inject()            */
+#define EAS_ERR_TIMEOUT 7     /* a bounded device-side wait gave up                */
+
+/* ---- errors / availability -------------------------------------------- */
+
+/* Message for the last failing call on this thread ("" if none). */
+const char* eas_last_error(void);
+
+/* 1 if a CUDA driver and at least one device are usable, else 0.
+ * Replaces `eas._metal.is_available` (_metal.mm:168-183). */
+int eas_is_available(void);
+
+/* Number of visible CUDA devices. */
+int eas_device_count(int* count);
+
+/* Make `dev` current on this thread and initialise its primary context. */
+int eas_set_device(int dev);
+
+/* Compute capability of `dev` (e.g. 10, 0 for sm_100). */
+int eas_device_capability(int dev, int* major, int* minor);
+
+/* Runtime versions: CUDA driver, NVRTC major*1000+minor*10. */
+int eas_versions(int* driver_version, int* nvrtc_version);
+
+/* ---- compile (replaces `eas._metal.compile`, _metal.mm:185-260) ------- */
+
+/* Compile CUDA C++ `src` with NVRTC for sm_100a and return a CUBIN image
+ * (never PTX).  `opts` are extra NVRTC options.  The image is malloc'd and
+ * must be released with eas_free_host().  On EAS_ERR_COMPILE the NVRTC log is
+ * in eas_last_error(). */
+int eas_compile(const char* src, const char* name, const char* const* opts, int nopts,
+                void** image, size_t* image_size);
+
+void eas_free_host(void* p);
+
+/* Load a CUBIN on `dev` and resolve kernel `name`.  `max_dyn_smem` > 0 raises
+ * the function's dynamic shared-memory limit (needed above 48 KiB).
+ * Returns an opaque pipeline handle. */
+int eas_pipeline_load(int dev, const void* image, size_t image_size, const char* name,
+                      int max_dyn_smem, void** pipeline);
+
+int eas_pipeline_free(void* pipeline);
+
+/* Registers per thread / static shared bytes of a loaded pipeline. */
+int eas_pipeline_attrs(void* pipeline, int* num_regs, int* static_smem, int* max_threads);
+
+/* ---- launch (replaces `eas._metal.launch/launch_async`, _metal.mm:1013-1395) ---- */
+
+/* Enqueue one launch.  `params` is the packed kernel-parameter block (each
+ * parameter at its natural alignment, as the generated kernel declares
+ * them).  Asynchronous: pair with eas_stream_synchronize / events. */
+int eas_launch(void* pipeline, const uint32_t grid[3], const uint32_t block[3], uint32_t dyn_smem,
+               void* stream, const void* params, size_t params_size);
+
+/* ---- memory (replaces alloc_buffer / copy_from_host / copy_to_host,
+ *      _metal.mm:262-455) -------------------------------------------------- */
+
+int eas_alloc_buffer(int dev, size_t nbytes, void** dptr);
+int eas_free_buffer(void* dptr);
+/* host -> device; waits until the host buffer may be reused */
+int eas_copy_from_host(void* dst, const void* src, size_t nbytes, void* stream);
+/* device -> host; returns when `dst` holds the data */
+int eas_copy_to_host(void* dst, const void* src, size_t nbytes, void* stream);
+/* device -> device (same or peer device over NVLink), asynchronous */
+int eas_copy_device(void* dst, const void* src, size_t nbytes, void* stream);
+int eas_memset_d8(void* dst, int value, size_t nbytes, void* stream);
+
+/* ---- synchronisation (replaces synchronize / queue_synchronize,
+ *      _metal.mm:1397-1434) ------------------------------------------------ */
+
+int eas_stream_synchronize(void* stream);
+int eas_device_synchronize(int dev);
+int eas_stream_create(int dev, void** stream);
+int eas_stream_destroy(void* stream);
+int eas_event_create(void** event);
+int eas_event_destroy(void* event);
+int eas_event_record(void* event, void* stream);
+int eas_event_synchronize(void* event);
+/* 1 if complete, 0 if pending */
+int eas_event_query(void* event, int* done);
+int eas_event_elapsed_ms(void* start, void* end, float* ms);
+
+/* ---- host-side fault injection (tests; no device fault is ever made) --- */
+
+/* Make the `nth` (1-based) next call of kind "compile", "alloc", "launch" or
+ * "copy" fail with EAS_ERR_INJECTED.  nth <= 0 clears the injection. */
+int eas_fault_inject(const char* kind, int nth);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* EAS_CUDA_H */
