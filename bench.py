@@ -24,13 +24,10 @@ oracle interpreting the reference front end's IR of the same kernel, on all
 host threads) and prints the same metric.
 """
 
-from __future__ import annotations
-
 import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import threading
 import time
@@ -72,52 +69,59 @@ def profile_traffic(name: str) -> float | None:
 
 
 class ClockSampler:
-    """nvidia-smi clocks/throttle sampling during the timed region."""
+    """SM clock and throttle reasons sampled through NVML (read-only) every 100 ms in the timed region."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+               "sw_power_cap": 0x4}
 
     def __init__(self, gpu: int):
         self.gpu = gpu
-        self.proc = None
-        self.out = ""
+        self.samples: list[float] = []
+        self.max_mhz = None
+        self.reasons: set[str] = set()
+        self._stop = threading.Event()
+        self._ready = threading.Event()
+        self._thread = None
+        self.error = None
+
+    def _loop(self):
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+            while True:
+                self.samples.append(float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)))
+                r = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                for name, bit in self.REASONS.items():
+                    if r & bit:
+                        self.reasons.add(name)
+                self._ready.set()
+                if self._stop.wait(0.05):
+                    break
+        except Exception as e:  # NVML missing: report no samples rather than failing the bench
+            self.error = repr(e)
+        finally:
+            self._ready.set()
 
     def __enter__(self):
-        try:
-            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
-                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except OSError:
-            self.proc = None
+        self._thread = threading.Thread(target=self._loop, daemon=True)
+        self._thread.start()
+        self._ready.wait(timeout=10)
         return self
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.out, _ = self.proc.communicate(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-                self.out, _ = self.proc.communicate()
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join(timeout=5)
 
     def summary(self) -> dict:
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.out.splitlines():
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx = float(parts[2])
-            except ValueError:
-                continue
-            for n, v in zip(names, parts[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        out = {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.max_mhz,
+               "reasons": sorted(self.reasons), "samples": len(self.samples)}
+        if self.error:
+            out["error"] = self.error
+        return out
 
 
 def dist_setup():
@@ -207,7 +211,7 @@ def run_eas(args) -> None:
 
     rt = get_runtime()
     add_kernel = make_add_kernel()
-    lo, hi = shard(N_TOTAL, BLOCK, world, rank)
+    lo, hi = shard(args.n, BLOCK, world, rank)
     n = hi - lo
     gen = torch.Generator(device="cuda").manual_seed(1234 + rank)
     a = torch.randn(n, device="cuda", dtype=torch.float32, generator=gen)
@@ -221,8 +225,13 @@ def run_eas(args) -> None:
         raise SystemExit("bench: add result differs from a + b")
 
     stream = torch.cuda.current_stream()
-    for _ in range(max(args.warmup, 3)):
+    t_warm = time.perf_counter()
+    w = 0
+    while w < max(args.warmup, 3) or (not args.quick and time.perf_counter() - t_warm < 0.5):
         add_kernel(a, b, c, n, BLOCK=BLOCK, _sync=False)
+        w += 1
+        if w % 64 == 0:
+            rt.synchronize()
     rt.synchronize()
     torch.cuda.synchronize()
     barrier(world)
@@ -241,24 +250,29 @@ def run_eas(args) -> None:
     launches = rt.launch_count - launches0
     ms = e0.elapsed_time(e1) / args.steps
     ms_max = max_over_ranks(ms, world)
-    gbs = BYTES_PER_ELEM * N_TOTAL / (ms_max * 1e-3) / 1e9
+    gbs = BYTES_PER_ELEM * args.n / (ms_max * 1e-3) / 1e9
     kernel_gbs_local = BYTES_PER_ELEM * n / (ms * 1e-3) / 1e9
 
     # end to end through the public API with pinned host buffers
-    ha = a.cpu().pin_memory()
-    hb = b.cpu().pin_memory()
-    hc = torch.empty(n, dtype=torch.float32).pin_memory()
-    add_kernel(ha, hb, hc, n, BLOCK=BLOCK)
-    barrier(world)
-    t0 = time.perf_counter()
-    e2e_steps = max(1, min(args.steps, 5))
-    for _ in range(e2e_steps):
-        add_kernel(ha, hb, hc, n, BLOCK=BLOCK)  # sync launch: H2D copies, kernel, D2H copy of c
-    t_e2e = (time.perf_counter() - t0) / e2e_steps
-    t_e2e = max_over_ranks(t_e2e, world)
-    if not torch.equal(hc, ha + hb):
-        raise SystemExit("bench: e2e add result differs from a + b")
-    e2e_gbs = BYTES_PER_ELEM * N_TOTAL / t_e2e / 1e9
+    e2e = None
+    if not args.quick:
+        ha = a.cpu().pin_memory()
+        hb = b.cpu().pin_memory()
+        hc = torch.empty(n, dtype=torch.float32).pin_memory()
+        add_kernel(ha, hb, hc, n, BLOCK=BLOCK)
+        barrier(world)
+        t0 = time.perf_counter()
+        e2e_steps = max(1, min(args.steps, 5))
+        for _ in range(e2e_steps):
+            add_kernel(ha, hb, hc, n, BLOCK=BLOCK)  # sync launch: H2D copies, kernel, D2H copy of c
+        t_e2e = (time.perf_counter() - t0) / e2e_steps
+        t_e2e = max_over_ranks(t_e2e, world)
+        if not torch.equal(hc, ha + hb):
+            raise SystemExit("bench: e2e add result differs from a + b")
+        e2e = {"value": round(BYTES_PER_ELEM * args.n / t_e2e / 1e9, 2), "unit": "GB/s",
+               "h2d_bytes_per_step": 3 * 4 * args.n, "d2h_bytes_per_step": 4 * args.n,
+               "how": "public API with pinned torch CPU tensors (a, b, c copied in, c copied out) inside the "
+                      "timed region; wall clock, max over ranks"}
 
     if rank != 0:
         return
@@ -269,11 +283,9 @@ def run_eas(args) -> None:
         "warmup": max(args.warmup, 3), "ms_per_step": round(ms_max, 4), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (torch.randn, seeded)",
         "config": {"workload": "C2 add_kernel N=2^28 f32, BLOCK=1024, program-id ranges split across GPUs",
-                   "N": N_TOTAL, "BLOCK": BLOCK, "per_gpu_elements": n, "parallelism": f"pid-shard x{world}",
+                   "N": args.n, "BLOCK": BLOCK, "per_gpu_elements": n, "parallelism": f"pid-shard x{world}",
                    "l2": "inputs 3 GiB/step > 126 MB L2 (no flush needed)"},
-        "e2e": {"value": round(e2e_gbs, 2), "unit": "GB/s",
-                "h2d_bytes_per_step": 3 * 4 * N_TOTAL, "d2h_bytes_per_step": 4 * N_TOTAL,
-                "how": "public API with pinned torch CPU tensors; copies in the timed region"},
+        "e2e": e2e,
         "roofline": {"bound": "hbm", "achieved": round(kernel_gbs_local, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                      "frac": round(kernel_gbs_local / pk["hbm_gbs"], 4),
                      "traffic": traffic, "peak_source": pk["source"] + " (MEASURED_PEAKS.json hbm_gbs)"
@@ -281,7 +293,7 @@ def run_eas(args) -> None:
         "gpu_launches": launches,
         "clocks": clk.summary(),
     }
-    if world == 1 and not args.no_cpu_baseline:
+    if world == 1 and not args.no_cpu_baseline and not args.quick:
         line["cpu_baseline"] = cpu_add_baseline(args.cpu_seconds)
     print(json.dumps(line), flush=True)
 
@@ -336,11 +348,14 @@ def run_reference(args) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="eas", choices=["eas", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--n", type=int, default=N_TOTAL, help="total elements (profiling runs use a smaller case)")
+    ap.add_argument("--quick", action="store_true",
+                    help="profiling mode: no clock warm-up loop, no e2e arm, no CPU baseline")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)

@@ -74,6 +74,7 @@ class Lowered:
     params: list[Param]
     dyn_smem: int        # bytes of dynamic shared memory per CTA
     native: Any = field(default=None)   # pattern-lowered native plan (see codegen.patterns)
+    layout: Any = field(default=None)   # runtime parameter layout, built on first launch
 
 
 HIDDEN = ("eas_ntx", "eas_pid_x", "eas_pid_y", "eas_pid_z")

@@ -15,6 +15,7 @@ struct DriverApi {
   decltype(&::cuFuncGetAttribute) funcGetAttribute = nullptr;
   decltype(&::cuGetErrorString) getErrorString = nullptr;
   decltype(&::cuTensorMapEncodeTiled) tensorMapEncodeTiled = nullptr;
+  decltype(&::cuFuncGetParamInfo) funcGetParamInfo = nullptr;  // optional (driver >= 12.4)
 };
 extern DriverApi g_drv;
 

@@ -164,6 +164,7 @@ int eas_driver_init() {
       g_drv_error = "could not resolve CUDA driver entry points";
       return;
     }
+    fetch("cuFuncGetParamInfo", g_drv.funcGetParamInfo);
     g_drv_status = EAS_OK;
   });
   if (g_drv_status != EAS_OK) return eas_fail(g_drv_status, "%s", g_drv_error.c_str());
@@ -187,12 +188,23 @@ extern "C" int eas_device_count(int* count) {
   return eas_cuda_check(cudaGetDeviceCount(count), "cudaGetDeviceCount", EAS_ERR_UNAVAILABLE);
 }
 
+static std::atomic<uint64_t> g_ctx_ready{0};  // bit d: primary context of device d initialised
+
 extern "C" int eas_set_device(int dev) {
   int rc = eas_driver_init();
   if (rc) return rc;
-  rc = eas_cuda_check(cudaSetDevice(dev), "cudaSetDevice", EAS_ERR_VALUE);
-  if (rc) return rc;
-  return eas_cuda_check(cudaFree(nullptr), "primary context init", EAS_ERR_UNAVAILABLE);
+  int cur = -1;
+  if (cudaGetDevice(&cur) != cudaSuccess || cur != dev) {
+    rc = eas_cuda_check(cudaSetDevice(dev), "cudaSetDevice", EAS_ERR_VALUE);
+    if (rc) return rc;
+  }
+  uint64_t bit = (dev >= 0 && dev < 64) ? (1ull << dev) : 0;
+  if (!bit || !(g_ctx_ready.load() & bit)) {
+    rc = eas_cuda_check(cudaFree(nullptr), "primary context init", EAS_ERR_UNAVAILABLE);
+    if (rc) return rc;
+    g_ctx_ready.fetch_or(bit);
+  }
+  return EAS_OK;
 }
 
 extern "C" int eas_device_capability(int dev, int* major, int* minor) {
@@ -335,7 +347,17 @@ struct Pipeline {
   int dev;
   CUmodule mod;
   CUfunction fn;
+  int nparams;  // -1 when the driver cannot report it
 };
+
+int count_params(CUfunction fn) {
+  if (!g_drv.funcGetParamInfo) return -1;
+  for (int i = 0; i < 4096; ++i) {
+    size_t off = 0, size = 0;
+    if (g_drv.funcGetParamInfo(fn, (size_t)i, &off, &size) != CUDA_SUCCESS) return i;
+  }
+  return -1;
+}
 }  // namespace
 
 extern "C" int eas_pipeline_load(int dev, const void* image, size_t image_size, const char* name, int max_dyn_smem,
@@ -361,7 +383,7 @@ extern "C" int eas_pipeline_load(int dev, const void* image, size_t image_size, 
       return rc;
     }
   }
-  *pipeline = new Pipeline{dev, mod, fn};
+  *pipeline = new Pipeline{dev, mod, fn, count_params(fn)};
   return EAS_OK;
 }
 
@@ -387,20 +409,23 @@ extern "C" int eas_pipeline_attrs(void* pipeline, int* num_regs, int* static_sme
 }
 
 extern "C" int eas_launch(void* pipeline, const uint32_t grid[3], const uint32_t block[3], uint32_t dyn_smem,
-                          void* stream, const void* params, size_t params_size) {
+                          void* stream, const void* params, const uint32_t* offsets, uint32_t nparams) {
   if (!pipeline || !grid || !block) return eas_fail(EAS_ERR_VALUE, "eas_launch: null argument");
+  if (nparams && (!params || !offsets)) return eas_fail(EAS_ERR_VALUE, "eas_launch: null parameter block");
+  if (nparams > 256) return eas_fail(EAS_ERR_VALUE, "eas_launch: %u parameters (max 256)", nparams);
   EAS_INJECT(kLaunch, "eas_launch");
   Pipeline* p = static_cast<Pipeline*>(pipeline);
+  if (p->nparams >= 0 && (uint32_t)p->nparams != nparams)
+    return eas_fail(EAS_ERR_VALUE, "eas_launch: kernel takes %d parameters, %u given", p->nparams, nparams);
   if (block[0] * block[1] * block[2] > 1024u || block[0] == 0)
     return eas_fail(EAS_ERR_VALUE, "eas_launch: block (%u,%u,%u) exceeds 1024 threads", block[0], block[1], block[2]);
   if (grid[1] > 65535u || grid[2] > 65535u)
     return eas_fail(EAS_ERR_VALUE, "eas_launch: grid.y/z (%u,%u) exceed 65535", grid[1], grid[2]);
   if (grid[0] == 0 || grid[1] == 0 || grid[2] == 0) return EAS_OK;
-  size_t size = params_size;
-  void* extra[] = {CU_LAUNCH_PARAM_BUFFER_POINTER, const_cast<void*>(params), CU_LAUNCH_PARAM_BUFFER_SIZE, &size,
-                   CU_LAUNCH_PARAM_END};
+  void* argv[256];
+  for (uint32_t i = 0; i < nparams; ++i) argv[i] = const_cast<char*>(static_cast<const char*>(params) + offsets[i]);
   CUresult r = g_drv.launchKernel(p->fn, grid[0], grid[1], grid[2], block[0], block[1], block[2], dyn_smem,
-                                    (CUstream)stream, nullptr, params_size ? extra : nullptr);
+                                  (CUstream)stream, nparams ? argv : nullptr, nullptr);
   return eas_drv_check(r, "cuLaunchKernel", EAS_ERR_LAUNCH);
 }
 

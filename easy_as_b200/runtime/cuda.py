@@ -117,6 +117,8 @@ class ParamLayout:
             self.entries.append((p, off, fmt))
             off += size
         self.size = -(-off // 8) * 8
+        self.offsets = (cuda_ext.ctypes.c_uint32 * max(len(self.entries), 1))(*[o for _p, o, _f in self.entries])
+        self.count = len(self.entries)
 
     def pack(self, values: Mapping[str, Any], pointers: Mapping[str, int], hidden: Mapping[str, int]) -> bytearray:
         buf = bytearray(self.size)
@@ -209,7 +211,6 @@ class CudaRuntime:
         self._available: bool | None = None
         self._reason = ""
         self._pipelines: dict[tuple[str, str, int, int], int] = {}
-        self._layouts: dict[int, ParamLayout] = {}
         self._pending: deque[tuple[int, Any]] = deque()
         self._max_in_flight: int | None = None
         self._staging: dict[tuple[int, int], list[DeviceBuffer]] = {}
@@ -394,10 +395,9 @@ class CudaRuntime:
                         stream: int, programs: tuple[int, int, int], ntx: int) -> None:
         plan = ck.plan
         pipe = self._pipeline_for(ck, device)
-        layout = self._layouts.get(id(plan))
+        layout = plan.layout
         if layout is None:
-            layout = ParamLayout(plan.params)
-            self._layouts[id(plan)] = layout
+            layout = plan.layout = ParamLayout(plan.params)
         ptrs = {n: a.ptr for n, a in args.items()}
         lib = self.lib()
         gx, gy, gz = programs
@@ -408,7 +408,7 @@ class CudaRuntime:
                 blob = layout.pack(runtime_args, ptrs, hidden)
                 cblob = (cuda_ext.ctypes.c_char * len(blob)).from_buffer(blob)
                 g = (cuda_ext.ctypes.c_uint32 * 3)(gx, min(MAX_GRID_YZ, gy - y0), min(MAX_GRID_YZ, gz - z0))
-                cuda_ext.check(lib.eas_launch(pipe, g, block, plan.dyn_smem, stream, cblob, len(blob)),
+                cuda_ext.check(lib.eas_launch(pipe, g, block, plan.dyn_smem, stream, cblob, layout.offsets, layout.count),
                                f"launch {plan.kernel_name}")
                 self.launch_count += 1
 

@@ -82,11 +82,12 @@ int eas_pipeline_attrs(void* pipeline, int* num_regs, int* static_smem, int* max
 
 /* ---- launch (replaces `eas._metal.launch/launch_async`, _metal.mm:1013-1395) ---- */
 
-/* Enqueue one launch.  `params` is the packed kernel-parameter block (each
- * parameter at its natural alignment, as the generated kernel declares
- * them).  Asynchronous: pair with eas_stream_synchronize / events. */
+/* Enqueue one launch.  `params` is a block holding the kernel's parameter
+ * values; parameter i starts at byte offsets[i] (nparams entries, in the
+ * kernel's declaration order).  Asynchronous: pair with
+ * eas_stream_synchronize / events. */
 int eas_launch(void* pipeline, const uint32_t grid[3], const uint32_t block[3], uint32_t dyn_smem,
-               void* stream, const void* params, size_t params_size);
+               void* stream, const void* params, const uint32_t* offsets, uint32_t nparams);
 
 /* ---- memory (replaces alloc_buffer / copy_from_host / copy_to_host,
  *      _metal.mm:262-455) -------------------------------------------------- */

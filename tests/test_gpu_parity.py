@@ -18,6 +18,10 @@ from oracle.interp import execute
 pytestmark = pytest.mark.gpu
 CASES = goldens.cases()
 TOLERANT = {"matmul_simdgroup": 5e-3}
+# kernels whose output is undefined in the reference too: t_many_dot sums dots over
+# threadgroup memory it never writes (reference tests/test_dot_codegen_unique_vars.py only
+# inspects its generated source), so only compile + launch is checked
+UNDEFINED = {"t_many_dot"}
 
 
 def _run_both(rt, c, seed, to_torch=False):
@@ -43,6 +47,8 @@ def test_reference_kernel_matches_oracle(cuda_rt, c):
     for seed in (0, 1):
         gpu, cpu = _run_both(cuda_rt, c, seed)
         for name in c["writes"]:
+            if c["id"] in UNDEFINED:
+                continue
             if c["id"] in TOLERANT:
                 np.testing.assert_allclose(gpu[name], cpu[name], rtol=TOLERANT[c["id"]], atol=TOLERANT[c["id"]])
             else:
