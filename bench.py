@@ -176,6 +176,89 @@ def make_add_kernel():
     return add_kernel
 
 
+GEMM_CONFIGS = {
+    # name: (batch, M, N, K, how the work is split across ranks)
+    "C4": (1, 8192, 8192, 8192, "rows of A/C split across ranks, B replicated"),
+    "C5": (64, 4096, 4096, 2088, "batch split across ranks"),
+}
+
+
+def gemm_shard(name: str, world: int, rank: int) -> tuple[int, int, int, int]:
+    batch, M, N, K, _ = GEMM_CONFIGS[name]
+    if name == "C4":
+        r0, r1 = M * rank // world, M * (rank + 1) // world
+        return batch, r1 - r0, N, K
+    b0, b1 = batch * rank // world, batch * (rank + 1) // world
+    return b1 - b0, M, N, K
+
+
+def run_gemm(name: str, args, world: int, rank: int, rt) -> dict:
+    """fp16 mk.dot GEMM (examples/matmul_dot_f16.py) on this rank's shard; TFLOP/s aggregated over ranks."""
+    import torch
+
+    from examples.matmul_dot_f16 import grid, matmul_dot_f16
+
+    batch, M, N, K = gemm_shard(name, world, rank)
+    tb, TM, TN, TK, split = GEMM_CONFIGS[name]
+    g = torch.Generator(device="cuda").manual_seed(3 + rank)
+    a = (torch.randn(batch, M, K, device="cuda", generator=g) / K ** 0.5).half()
+    b = (torch.randn(batch, K, N, device="cuda", generator=g) / K ** 0.5).half()
+    c = torch.empty(batch, M, N, device="cuda")
+    bn = 256
+
+    def step(sync=False):
+        matmul_dot_f16(a.reshape(-1), b.reshape(-1), c.reshape(-1), M, N, K, BLOCK_M=128, BLOCK_N=bn, BLOCK_K=64,
+                       _grid=grid(batch), _sync=sync)
+
+    native0 = rt.native_launches
+    step(sync=True)
+    if rt.native_launches == native0:
+        raise SystemExit(f"bench: {name} did not take the tcgen05 path")
+    # parity spot check: rows 0..3 of the first batch against float64
+    ref = a[0, :4].double() @ b[0].double()
+    err = ((c[0, :4].double() - ref).abs().max() / ref.abs().max()).item()
+    if err > 1e-4:
+        raise SystemExit(f"bench: {name} result off by {err:.2e}")
+    steps = max(2, min(args.steps, args.gemm_steps))
+    for _ in range(max(args.warmup, 3)):
+        step()
+    rt.synchronize()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    launches0 = rt.launch_count
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        e0.record(stream)
+        for _ in range(steps):
+            step()
+        e1.record(stream)
+        e1.synchronize()
+        rt.synchronize()
+    barrier(world)
+    ms = e0.elapsed_time(e1) / steps
+    ms_max = max_over_ranks(ms, world)
+    flops_total = 2.0 * tb * TM * TN * TK
+    flops_local = 2.0 * batch * M * N * K
+    pk = peaks()
+    local_tf = flops_local / (ms * 1e-3) / 1e12
+    return {
+        "metric": "fp16 mk.dot GEMM TFLOP/s", "value": round(flops_total / (ms_max * 1e-3) / 1e12, 1),
+        "unit": "TFLOP/s", "ms_per_step": round(ms_max, 4), "steps": steps,
+        "config": {"workload": f"{name} batch={tb} M={TM} N={TN} K={TK} f16 in, f32 acc/out", "split": split,
+                   "kernel": f"tcgen05 cta_group::1, tile 128x{bn}x64", "spot_check_rel_err": err},
+        "roofline": {"bound": "tensor", "achieved": round(local_tf, 1), "peak": pk["bf16_tflops"],
+                     "unit": "TFLOP/s", "frac": round(local_tf / pk["bf16_tflops"], 4),
+                     "peak_source": ("measured burst cuBLAS bf16 (MEASURED_PEAKS.json bf16_tflops)"
+                                     if pk["source"] == "measured" else "fallback"),
+                     "frac_of_nominal_2250": round(local_tf / 2250.0, 4),
+                     "traffic": profile_traffic(f"gemm_{name.lower()}_n1")},
+        "gpu_launches": rt.launch_count - launches0,
+        "clocks": clk.summary(),
+    }
+
+
 def cpu_add_baseline(seconds: float = 10.0) -> dict:
     """numpy add on the host cores over 2**24-element chunks for ~``seconds`` (all threads)."""
     cores = os.cpu_count() or 1
@@ -274,6 +357,12 @@ def run_eas(args) -> None:
                "how": "public API with pinned torch CPU tensors (a, b, c copied in, c copied out) inside the "
                       "timed region; wall clock, max over ranks"}
 
+    gemm = {}
+    if not args.quick and not args.no_gemm:
+        del a, b, c
+        torch.cuda.empty_cache()
+        for name in ("C4", "C5"):
+            gemm[name] = run_gemm(name, args, world, rank, rt)
     if rank != 0:
         return
     pk = peaks()
@@ -293,6 +382,8 @@ def run_eas(args) -> None:
         "gpu_launches": launches,
         "clocks": clk.summary(),
     }
+    if gemm:
+        line["gemm"] = gemm
     if world == 1 and not args.no_cpu_baseline and not args.quick:
         line["cpu_baseline"] = cpu_add_baseline(args.cpu_seconds)
     print(json.dumps(line), flush=True)
@@ -354,6 +445,8 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--n", type=int, default=N_TOTAL, help="total elements (profiling runs use a smaller case)")
+    ap.add_argument("--no-gemm", action="store_true", help="skip the fp16 GEMM configs (C4, C5)")
+    ap.add_argument("--gemm-steps", type=int, default=20)
     ap.add_argument("--quick", action="store_true",
                     help="profiling mode: no clock warm-up loop, no e2e arm, no CPU baseline")
     args = ap.parse_args()

@@ -1,0 +1,481 @@
+// gemm_tcgen05.cu — native sm_100a kernel for the fp16 `mk.dot` GEMM pattern.
+//
+// Computes the strided batched product the DSL expresses as one `mk.dot` per
+// output element (reference dot lowering: easy_as eas/codegen/msl.py:920-952,
+// an f32 `fma` chain over f16 inputs):
+//
+//   C[b][m][n] = sum_k A[b][m][k] * B[b][k][n]        f16 x f16 -> f32
+//
+//   A[b][m][k] at a + b*a_bstride + m*lda + k                    (K-major)
+//   B[b][k][n] at b + b*b_bstride + k*ldb + n   (b_kmajor == 0, N-major)
+//            or b + b*b_bstride + n*ldb + k     (b_kmajor == 1, K-major)
+//   C[b][m][n] at c + b*c_bstride + m*ldc + n                    (f32)
+//
+// Design (one persistent CTA per SM, 6 warps):
+//   warp 0      TMA producer: 128B-swizzled A (128 x 64) and B (BN x 64) tiles
+//               into a STAGES-deep shared-memory ring, mbarrier complete_tx.
+//   warp 1      allocates TMEM (2 x BN f32 columns: double-buffered
+//               accumulators) and issues tcgen05.mma.cta_group::1.kind::f16
+//               (M=128, N=BN, K=16) from one lane; tcgen05.commit frees ring
+//               slots and publishes finished accumulators.
+//   warps 2..5  epilogue: tcgen05.ld 32x32b rows of the accumulator, masked
+//               f32 stores to C, then release the accumulator buffer.
+// K, M and N tails are zero-filled by TMA (out-of-range box elements read 0),
+// so they add nothing to the sums; stores are masked to m < M, n < N.
+//
+// Every mbarrier wait is bounded (clock64 budget).  On expiry the kernel sets
+// a shared abort flag, every role leaves its loop, TMEM is freed, and the
+// code EAS_ERR_TIMEOUT is written to the host-mapped status word.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <mutex>
+
+#include "eas_internal.h"
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int BK = 64;                       // one 128-byte swizzle row of f16
+constexpr int kThreads = 192;                // 6 warps
+constexpr long long kWaitBudget = 4000000000LL;  // cycles (~2 s) before a wait is declared hung
+constexpr int kGroupM = 16;                  // tile-order swizzle for L2 reuse
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: false when the budget ran out or another role aborted.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (clock64() - t0 > kWaitBudget) {
+      *abort_flag = 1;
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::
+          "r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int x, int y, int z) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Shared-memory matrix descriptor (tcgen05), 128-byte swizzle:
+//   [0,14) start address >> 4, [16,30) leading byte offset >> 4,
+//   [32,46) stride byte offset >> 4, [46,48) version = 1,
+//   [49,52) base offset = 0 (atoms are 1024-byte aligned), [61,64) layout = 2 (SWIZZLE_128B).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16) |
+         ((uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
+}
+
+// Instruction descriptor, kind::f16: D = f32 (bits 4-5 = 1), A = B = f16 (0),
+// A K-major (bit 15 = 0), B major per b_mn (bit 16), N >> 3 at bits 17-22, M >> 4 at bits 24-28.
+__host__ __device__ constexpr uint32_t instr_desc(int n, bool b_mn_major) {
+  return (1u << 4) | ((b_mn_major ? 1u : 0u) << 16) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+struct TileCoord {
+  int b, m0, n0;
+};
+
+struct Sched {
+  int mt, nt, tiles_per_batch, total;
+  __device__ TileCoord at(int t) const {
+    TileCoord c;
+    c.b = t / tiles_per_batch;
+    int r = t - c.b * tiles_per_batch;
+    const int per_group = kGroupM * nt;
+    const int g = r / per_group;
+    const int first_m = g * kGroupM;
+    const int gsize = min(kGroupM, mt - first_m);
+    const int rr = r - g * per_group;
+    c.m0 = (first_m + rr % gsize) * BM;
+    c.n0 = rr / gsize;  // tile index along N (times BN at the call site)
+    return c;
+  }
+};
+
+template <int BN, int STAGES, bool B_MN>
+struct Smem {
+  static constexpr int kABytes = BM * BK * 2;
+  static constexpr int kBBytes = BN * BK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kEpiOffset = STAGES * kStageBytes;       // 4 warps x 32x32 f32 staging boxes
+  static constexpr int kEpiBytes = 4 * 32 * 32 * 4;
+  static constexpr int kBarOffset = kEpiOffset + kEpiBytes;
+  static constexpr int kTotal = kBarOffset + (2 * STAGES + 4) * 8 + 16 + 1024;  // + alignment slack
+};
+
+template <int BN, int STAGES, bool B_MN, bool TMA_C>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_f16_tcgen05_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                            const __grid_constant__ CUtensorMap map_c, float* __restrict__ c, int M, int N, int K,
+                            int batch, long long ldc, long long c_bstride, int* status) {
+  using L = Smem<BN, STAGES, B_MN>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  constexpr uint32_t kTmemCols = 2 * BN;  // power of two: 256 or 512
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 4);  // one arrival per epilogue warp
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  Sched sched;
+  sched.mt = (M + BM - 1) / BM;
+  sched.nt = (N + BN - 1) / BN;
+  sched.tiles_per_batch = sched.mt * sched.nt;
+  sched.total = sched.tiles_per_batch * batch;
+  const int kblocks = (K + BK - 1) / BK;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      for (int t = blockIdx.x; t < sched.total && !*abort_flag; t += gridDim.x) {
+        const TileCoord tc = sched.at(t);
+        const int n0 = tc.n0 * BN;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) break;
+          uint8_t* sa = smem + s * L::kStageBytes;
+          uint8_t* sb = sa + L::kABytes;
+          mbar_expect_tx(&full[s], L::kStageBytes);
+          tma_load_3d(sa, &map_a, &full[s], kb * BK, tc.m0, tc.b);
+          if (B_MN) {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) tma_load_3d(sb + j * (BK * 128), &map_b, &full[s], n0 + 64 * j, kb * BK, tc.b);
+          } else {
+            tma_load_3d(sb, &map_b, &full[s], kb * BK, n0, tc.b);
+          }
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t idesc = instr_desc(BN, B_MN);
+      int s = 0;
+      uint32_t ph = 0;
+      int local = 0;
+      for (int t = blockIdx.x; t < sched.total && !*abort_flag; t += gridDim.x, ++local) {
+        const int buf = local & 1;
+        const uint32_t acc_ph = (local >> 1) & 1;
+        if (!mbar_wait(&acc_empty[buf], acc_ph ^ 1, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * BN;
+        bool ok = true;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&full[s], ph, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + s * L::kStageBytes);
+          const uint32_t b_addr = a_addr + L::kABytes;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t adesc = smem_desc(a_addr + kk * 32, 16, 1024);
+            const uint64_t bdesc = B_MN ? smem_desc(b_addr + kk * 2048, BK * 128, 1024)
+                                        : smem_desc(b_addr + kk * 32, 16, 1024);
+            tc_mma(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          tc_commit(&empty[s]);  // slot s is free once these MMAs have read it
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+        if (!ok) break;
+        tc_commit(&acc_full[buf]);  // accumulator complete
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const bool vec_ok = ((ldc & 3) == 0) && ((c_bstride & 3) == 0) && ((reinterpret_cast<uintptr_t>(c) & 15) == 0);
+    // TMA_C: this warp's 32x32 f32 box, 128B-swizzled (16-byte chunk j of row r lives at chunk j ^ (r & 7))
+    uint8_t* box = smem + L::kEpiOffset + q * (32 * 32 * 4);
+    int local = 0;
+    for (int t = blockIdx.x; t < sched.total && !*abort_flag; t += gridDim.x, ++local) {
+      const int buf = local & 1;
+      const uint32_t acc_ph = (local >> 1) & 1;
+      if (!mbar_wait(&acc_full[buf], acc_ph, abort_flag)) break;
+      tc_fence_after();
+      const TileCoord tc = sched.at(t);
+      const int n0 = tc.n0 * BN;
+      const int m = tc.m0 + q * 32 + lane;
+      float* crow = c + (long long)tc.b * c_bstride + (long long)m * ldc;
+#pragma unroll 1
+      for (int cc = 0; cc < BN / 32; ++cc) {
+        uint32_t r[32];
+        tmem_ld32(tmem_base + buf * BN + cc * 32 + ((uint32_t)(q * 32) << 16), r);
+        const int nb = n0 + cc * 32;
+        if (TMA_C) {
+          if (nb < N && tc.m0 + q * 32 < M) {  // boxes wholly outside C are skipped; partial ones are clipped
+            if (lane == 0) bulk_wait_read0();  // previous box has been read out of shared memory
+            __syncwarp();
+            uint8_t* row = box + lane * 128;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              float4 v = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                     __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+              *reinterpret_cast<float4*>(row + ((j ^ (lane & 7)) << 4)) = v;
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_3d(&map_c, box, nb, tc.m0 + q * 32, tc.b);
+              bulk_commit();
+            }
+          }
+        } else if (m < M) {
+          if (vec_ok && nb + 32 <= N) {
+            float4* dst = reinterpret_cast<float4*>(crow + nb);
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              dst[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                   __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (nb + j < N) crow[nb + j] = __uint_as_float(r[j]);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+    }
+    if (TMA_C && lane == 0) bulk_wait_all0();  // stores complete before the CTA's shared memory goes away
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols) : "memory");
+  }
+  if (threadIdx.x == 0 && *abort_flag && status) *status = EAS_ERR_TIMEOUT;
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+
+int encode_map(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t stride1_bytes,
+               uint64_t stride2_bytes, uint32_t box0, uint32_t box1,
+               CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT16) {
+  const cuuint64_t dims[3] = {d0, d1, d2};
+  const cuuint64_t strides[2] = {stride1_bytes, stride2_bytes};
+  const cuuint32_t box[3] = {box0, box1, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = g_drv.tensorMapEncodeTiled(map, dt, 3, const_cast<void*>(base), dims,
+                                          strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return eas_drv_check(r, "cuTensorMapEncodeTiled", EAS_ERR_VALUE);
+}
+
+template <int BN, int STAGES, bool B_MN, bool TMA_C>
+int launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, float* c, int M, int N, int K,
+                   int batch, long long ldc, long long cbs, int* status, cudaStream_t stream, int num_sms) {
+  using L = Smem<BN, STAGES, B_MN>;
+  auto kern = gemm_f16_tcgen05_kernel<BN, STAGES, B_MN, TMA_C>;
+  int rc = eas_cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal),
+                          "gemm: set smem attribute", EAS_ERR_LAUNCH);
+  if (rc) return rc;
+  const long long tiles = (long long)((M + BM - 1) / BM) * ((N + BN - 1) / BN) * batch;
+  const int grid = (int)(tiles < num_sms ? tiles : num_sms);
+  kern<<<grid, kThreads, L::kTotal, stream>>>(ma, mb, mc, c, M, N, K, batch, ldc, cbs, status);
+  return eas_cuda_check(cudaGetLastError(), "gemm: launch", EAS_ERR_LAUNCH);
+}
+
+int* g_status_host = nullptr;  // host-mapped status words, one per device
+int* g_status_dev = nullptr;
+std::once_flag g_status_once;
+
+}  // namespace
+
+extern "C" int eas_gemm_status(int dev, int* code) {
+  if (!code) return eas_fail(EAS_ERR_VALUE, "eas_gemm_status: null pointer");
+  *code = (g_status_host && dev >= 0 && dev < 64) ? g_status_host[dev] : 0;
+  if (g_status_host && dev >= 0 && dev < 64) g_status_host[dev] = 0;
+  return EAS_OK;
+}
+
+extern "C" int eas_gemm_f16(const void* a, const void* b, float* c, uint32_t M, uint32_t N, uint32_t K,
+                            uint32_t batch, uint64_t lda, uint64_t a_bstride, uint64_t ldb, uint64_t b_bstride,
+                            int b_kmajor, uint64_t ldc, uint64_t c_bstride, int block_n, void* stream) {
+  int rc = eas_driver_init();
+  if (rc) return rc;
+  if (!a || !b || !c) return eas_fail(EAS_ERR_VALUE, "eas_gemm_f16: null operand");
+  if (M == 0 || N == 0 || batch == 0) return EAS_OK;
+  if (K == 0) return eas_fail(EAS_ERR_VALUE, "eas_gemm_f16: K == 0 (nothing to accumulate)");
+  if (block_n != 128 && block_n != 256) return eas_fail(EAS_ERR_VALUE, "eas_gemm_f16: block_n must be 128 or 256");
+  if (M > 0x7fffffffu || N > 0x7fffffffu || K > 0x7fffffffu)
+    return eas_fail(EAS_ERR_VALUE, "eas_gemm_f16: dimension exceeds 2^31-1");
+  // TMA rules: 16-byte aligned bases, 16-byte multiple strides
+  if ((reinterpret_cast<uintptr_t>(a) & 15) || (reinterpret_cast<uintptr_t>(b) & 15))
+    return eas_fail(EAS_ERR_VALUE, "eas_gemm_f16: A/B base must be 16-byte aligned");
+  if ((lda * 2) % 16 || (ldb * 2) % 16 || (batch > 1 && ((a_bstride * 2) % 16 || (b_bstride * 2) % 16)))
+    return eas_fail(EAS_ERR_VALUE, "eas_gemm_f16: A/B strides must be multiples of 8 elements");
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::call_once(g_status_once, [] {
+    void* h = nullptr;
+    if (cudaHostAlloc(&h, 64 * sizeof(int), cudaHostAllocMapped | cudaHostAllocPortable) == cudaSuccess) {
+      g_status_host = static_cast<int*>(h);
+      for (int i = 0; i < 64; ++i) g_status_host[i] = 0;
+      void* d = nullptr;
+      if (cudaHostGetDevicePointer(&d, h, 0) == cudaSuccess) g_status_dev = static_cast<int*>(d);
+    }
+    cudaGetLastError();
+  });
+  int* status = (g_status_dev && dev < 64) ? g_status_dev + dev : nullptr;
+  int num_sms = 148;
+  cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev);
+
+  const uint64_t ab = batch > 1 ? a_bstride * 2 : (uint64_t)M * lda * 2;
+  const uint64_t bb = batch > 1 ? b_bstride * 2 : (uint64_t)(b_kmajor ? N : K) * ldb * 2;
+  CUtensorMap ma, mb;
+  rc = encode_map(&ma, a, K, M, batch, lda * 2, ab ? ab : 16, BK, BM);
+  if (rc) return rc;
+  const bool b_mn = !b_kmajor;
+  if (b_mn)
+    rc = encode_map(&mb, b, N, K, batch, ldb * 2, bb ? bb : 16, 64, BK);
+  else
+    rc = encode_map(&mb, b, K, N, batch, ldb * 2, bb ? bb : 16, BK, (uint32_t)block_n);
+  if (rc) return rc;
+  // C through TMA stores when its rows/batches are 16-byte strided and the base is aligned
+  CUtensorMap mc;
+  const bool tma_c = (reinterpret_cast<uintptr_t>(c) & 15) == 0 && (ldc * 4) % 16 == 0 &&
+                     (batch == 1 || (c_bstride * 4) % 16 == 0) && ldc >= N;
+  if (tma_c) {
+    const uint64_t cb = batch > 1 ? c_bstride * 4 : (uint64_t)M * ldc * 4;
+    rc = encode_map(&mc, c, N, M, batch, ldc * 4, cb ? cb : 16, 32, 32, CU_TENSOR_MAP_DATA_TYPE_FLOAT32);
+    if (rc) return rc;
+  } else {
+    mc = ma;  // unused by the direct-store variant
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const long long ldc_l = (long long)ldc, cbs = (long long)c_bstride;
+#define EAS_GEMM_VARIANT(BN_, ST_)                                                                              \
+  (b_mn ? (tma_c ? launch_variant<BN_, ST_, true, true>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s, num_sms) \
+                 : launch_variant<BN_, ST_, true, false>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s,      \
+                                                         num_sms))                                               \
+        : (tma_c ? launch_variant<BN_, ST_, false, true>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s,     \
+                                                         num_sms)                                                \
+                 : launch_variant<BN_, ST_, false, false>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s,    \
+                                                          num_sms)))
+  if (block_n == 256) return EAS_GEMM_VARIANT(256, 4);
+  return EAS_GEMM_VARIANT(128, 6);
+#undef EAS_GEMM_VARIANT
+}

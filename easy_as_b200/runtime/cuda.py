@@ -215,6 +215,7 @@ class CudaRuntime:
         self._max_in_flight: int | None = None
         self._staging: dict[tuple[int, int], list[DeviceBuffer]] = {}
         self.launch_count = 0  # kernels launched through this runtime (generic + native)
+        self.native_launches = 0  # of which pattern-lowered native kernels
 
     # -- availability ----------------------------------------------------------
     def is_available(self) -> bool:
@@ -434,6 +435,7 @@ class CudaRuntime:
         lib = self.lib()
         if sync or host_copies:
             cuda_ext.check(lib.eas_stream_synchronize(stream), "kernel execution")
+            self._check_native_status(device)
             done: set[int] = set()
             for buf, arr in host_copies:
                 if id(arr) not in done:
@@ -460,6 +462,18 @@ class CudaRuntime:
     def synchronize(self) -> None:
         while self._pending:
             self._wait_one()
+        if self.native_launches:
+            for dev in range(8):
+                self._check_native_status(dev)
+
+    def _check_native_status(self, device: int) -> None:
+        if not self.native_launches:
+            return
+        code = cuda_ext.ctypes.c_int()
+        self.lib().eas_gemm_status(device, cuda_ext.ctypes.byref(code))
+        if code.value:
+            raise RuntimeError(f"native kernel on device {device} reported status {code.value} "
+                               "(a bounded pipeline wait expired; results are incomplete)")
 
     def in_flight(self) -> int:
         return len(self._pending)

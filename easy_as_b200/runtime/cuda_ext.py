@@ -66,6 +66,9 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "eas_event_query": (_int, [_vp, _PINT]),
     "eas_event_elapsed_ms": (_int, [_vp, _vp, ctypes.POINTER(ctypes.c_float)]),
     "eas_fault_inject": (_int, [ctypes.c_char_p, _int]),
+    "eas_gemm_f16": (_int, [_vp, _vp, _vp, _u32, _u32, _u32, _u32, ctypes.c_uint64, ctypes.c_uint64,
+                            ctypes.c_uint64, ctypes.c_uint64, _int, ctypes.c_uint64, ctypes.c_uint64, _int, _vp]),
+    "eas_gemm_status": (_int, [_int, _PINT]),
 }
 
 _lib: ctypes.CDLL | None = None

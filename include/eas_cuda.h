@@ -117,6 +117,29 @@ int eas_event_synchronize(void* event);
 int eas_event_query(void* event, int* done);
 int eas_event_elapsed_ms(void* start, void* end, float* ms);
 
+/* ---- native kernels (pattern-lowered DSL kernels) --------------------- */
+
+/* Strided batched GEMM, f16 x f16 -> f32 accumulate -> f32, on tcgen05/TMEM
+ * tensor cores (sm_100a).  Replaces the launch of the generated kernel for the
+ * `mk.dot` GEMM pattern (reference: dot lowering eas/codegen/msl.py:920-952,
+ * dispatched through eas._metal.launch, _metal.mm:1013-1222):
+ *   C[b][m][n] = sum_{k<K} A[b][m][k] * B[b][k][n]
+ *   A at a + b*a_bstride + m*lda + k                       (elements)
+ *   B at b + b*b_bstride + k*ldb + n  (b_kmajor = 0)  or  + n*ldb + k  (1)
+ *   C at c + b*c_bstride + m*ldc + n
+ * A and B must be 16-byte aligned with strides that are multiples of 8
+ * elements (TMA); otherwise EAS_ERR_VALUE (the caller then runs the generic
+ * kernel).  block_n is the N tile (128 or 256).  Asynchronous on `stream`.
+ * A pipeline wait that exceeds its budget ends the kernel early and is
+ * reported by eas_gemm_status(). */
+int eas_gemm_f16(const void* a, const void* b, float* c, uint32_t M, uint32_t N, uint32_t K, uint32_t batch,
+                 uint64_t lda, uint64_t a_bstride, uint64_t ldb, uint64_t b_bstride, int b_kmajor, uint64_t ldc,
+                 uint64_t c_bstride, int block_n, void* stream);
+
+/* Read and clear the status word of native kernels on `dev` (0 = ok,
+ * EAS_ERR_TIMEOUT = a bounded wait expired).  Valid after the stream synced. */
+int eas_gemm_status(int dev, int* code);
+
 /* ---- host-side fault injection (tests; no device fault is ever made) --- */
 
 /* Make the `nth` (1-based) next call of kind "compile", "alloc", "launch" or
