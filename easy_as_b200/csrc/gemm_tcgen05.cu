@@ -30,6 +30,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "eas_internal.h"
@@ -478,4 +479,120 @@ extern "C" int eas_gemm_f16(const void* a, const void* b, float* c, uint32_t M, 
   if (block_n == 256) return EAS_GEMM_VARIANT(256, 4);
   return EAS_GEMM_VARIANT(128, 6);
 #undef EAS_GEMM_VARIANT
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant
+// ---------------------------------------------------------------------------
+//
+// eas_gemm_f16 keeps the kernel's status word in pinned, host-mapped memory
+// that the library allocates with cudaHostAlloc on its first call.  Some
+// callers cannot let a library allocate: code that owns every allocation in
+// the process (a custom device allocator or a fixed memory budget), or code
+// that must not trigger an allocation at an arbitrary point.  For them the
+// status word lives in the array below instead, a file-scope device variable
+// that every GPU loading this library holds until the process exits.
+//
+// Its size is fixed: one 4-byte word per device, whatever the problem size.
+// In host code `g_noalloc_status` is only a stand-in symbol, not a device
+// address; the real address comes from cudaGetSymbolAddress, looked up once
+// per device with that device current, on the first call made on it.
+
+namespace {
+constexpr int kNoAllocStatusWords = 1;  // the whole scratch: one status word
+static __device__ __align__(256) int g_noalloc_status[kNoAllocStatusWords];
+
+int* g_noalloc_ptr[64];                    // device address of g_noalloc_status, per device
+std::atomic<uint64_t> g_noalloc_ready{0};  // bit d: g_noalloc_ptr[d] is valid
+std::mutex g_noalloc_mu;
+
+int noalloc_status_ptr(int dev, int** out) {
+  if (dev < 0 || dev >= 64) return eas_fail(EAS_ERR_VALUE, "eas_gemm_f16_noalloc: device %d out of range", dev);
+  const uint64_t bit = 1ull << dev;
+  if (!(g_noalloc_ready.load() & bit)) {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!(g_noalloc_ready.load() & bit)) {
+      void* p = nullptr;
+      int rc = eas_cuda_check(cudaGetSymbolAddress(&p, g_noalloc_status), "eas_gemm_f16_noalloc: cudaGetSymbolAddress",
+                              EAS_ERR_UNAVAILABLE);
+      if (rc) return rc;
+      g_noalloc_ptr[dev] = static_cast<int*>(p);
+      g_noalloc_ready.fetch_or(bit);
+    }
+  }
+  *out = g_noalloc_ptr[dev];
+  return EAS_OK;
+}
+}  // namespace
+
+extern "C" int eas_gemm_f16_noalloc(const void* a, const void* b, float* c, uint32_t M, uint32_t N, uint32_t K,
+                                    uint32_t batch, uint64_t lda, uint64_t a_bstride, uint64_t ldb,
+                                    uint64_t b_bstride, int b_kmajor, uint64_t ldc, uint64_t c_bstride, int block_n,
+                                    void* stream, int* status_out) {
+  if (status_out) *status_out = 0;
+  int rc = eas_driver_init();
+  if (rc) return rc;
+  if (!a || !b || !c) return eas_fail(EAS_ERR_VALUE, "eas_gemm_f16_noalloc: null operand");
+  if (M == 0 || N == 0 || batch == 0) return EAS_OK;
+  if (K == 0) return eas_fail(EAS_ERR_VALUE, "eas_gemm_f16_noalloc: K == 0 (nothing to accumulate)");
+  if (block_n != 128 && block_n != 256)
+    return eas_fail(EAS_ERR_VALUE, "eas_gemm_f16_noalloc: block_n must be 128 or 256");
+  if (M > 0x7fffffffu || N > 0x7fffffffu || K > 0x7fffffffu || batch > 0x7fffffffu)
+    return eas_fail(EAS_ERR_VALUE,
+                    "eas_gemm_f16_noalloc: M, N, K and batch must each be below 2^31 (the fixed status word "
+                    "covers any size within these limits)");
+  if ((reinterpret_cast<uintptr_t>(a) & 15) || (reinterpret_cast<uintptr_t>(b) & 15))
+    return eas_fail(EAS_ERR_VALUE, "eas_gemm_f16_noalloc: A/B base must be 16-byte aligned");
+  if ((lda * 2) % 16 || (ldb * 2) % 16 || (batch > 1 && ((a_bstride * 2) % 16 || (b_bstride * 2) % 16)))
+    return eas_fail(EAS_ERR_VALUE, "eas_gemm_f16_noalloc: A/B strides must be multiples of 8 elements");
+  int dev = 0;
+  rc = eas_cuda_check(cudaGetDevice(&dev), "eas_gemm_f16_noalloc: cudaGetDevice", EAS_ERR_UNAVAILABLE);
+  if (rc) return rc;
+  int* status = nullptr;
+  rc = noalloc_status_ptr(dev, &status);
+  if (rc) return rc;
+  int num_sms = 148;
+  cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev);
+
+  const uint64_t ab = batch > 1 ? a_bstride * 2 : (uint64_t)M * lda * 2;
+  const uint64_t bb = batch > 1 ? b_bstride * 2 : (uint64_t)(b_kmajor ? N : K) * ldb * 2;
+  CUtensorMap ma, mb, mc;
+  rc = encode_map(&ma, a, K, M, batch, lda * 2, ab ? ab : 16, BK, BM);
+  if (rc) return rc;
+  const bool b_mn = !b_kmajor;
+  rc = b_mn ? encode_map(&mb, b, N, K, batch, ldb * 2, bb ? bb : 16, 64, BK)
+            : encode_map(&mb, b, K, N, batch, ldb * 2, bb ? bb : 16, BK, (uint32_t)block_n);
+  if (rc) return rc;
+  const bool tma_c = (reinterpret_cast<uintptr_t>(c) & 15) == 0 && (ldc * 4) % 16 == 0 &&
+                     (batch == 1 || (c_bstride * 4) % 16 == 0) && ldc >= N;
+  if (tma_c) {
+    const uint64_t cb = batch > 1 ? c_bstride * 4 : (uint64_t)M * ldc * 4;
+    rc = encode_map(&mc, c, N, M, batch, ldc * 4, cb ? cb : 16, 32, 32, CU_TENSOR_MAP_DATA_TYPE_FLOAT32);
+    if (rc) return rc;
+  } else {
+    mc = ma;
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // the word keeps the previous call's value: clear it before this call's kernel
+  rc = eas_cuda_check(cudaMemsetAsync(status, 0, sizeof(int), s), "eas_gemm_f16_noalloc: clear status",
+                      EAS_ERR_LAUNCH);
+  if (rc) return rc;
+  const long long ldc_l = (long long)ldc, cbs = (long long)c_bstride;
+  if (block_n == 256) {
+    rc = b_mn ? (tma_c ? launch_variant<256, 4, true, true>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s, num_sms)
+                       : launch_variant<256, 4, true, false>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s, num_sms))
+              : (tma_c ? launch_variant<256, 4, false, true>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s, num_sms)
+                       : launch_variant<256, 4, false, false>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s, num_sms));
+  } else {
+    rc = b_mn ? (tma_c ? launch_variant<128, 6, true, true>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s, num_sms)
+                       : launch_variant<128, 6, true, false>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s, num_sms))
+              : (tma_c ? launch_variant<128, 6, false, true>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s, num_sms)
+                       : launch_variant<128, 6, false, false>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s, num_sms));
+  }
+  if (rc || !status_out) return rc;
+  // the caller asked for the status: wait for the kernel and copy the word out
+  rc = eas_cuda_check(cudaMemcpyAsync(status_out, status, sizeof(int), cudaMemcpyDeviceToHost, s),
+                      "eas_gemm_f16_noalloc: read status", EAS_ERR_LAUNCH);
+  if (rc) return rc;
+  return eas_cuda_check(cudaStreamSynchronize(s), "eas_gemm_f16_noalloc: kernel execution", EAS_ERR_LAUNCH);
 }

@@ -140,6 +140,31 @@ int eas_gemm_f16(const void* a, const void* b, float* c, uint32_t M, uint32_t N,
  * EAS_ERR_TIMEOUT = a bounded wait expired).  Valid after the stream synced. */
 int eas_gemm_status(int dev, int* code);
 
+/* Allocation-free form of eas_gemm_f16, for callers that cannot let a library
+ * allocate memory: code that owns every allocation in its process (its own
+ * device allocator or a fixed memory budget), or code that must not allocate
+ * at the point where it launches work.  No counterpart in the reference.
+ *
+ * Same arguments and results as eas_gemm_f16.  The kernel's only scratch, one
+ * 4-byte status word, lives in a file-scope __device__ array of this library
+ * (one word per GPU that loads it, held until the process exits) instead of
+ * memory allocated on first use; this call never calls cudaMalloc, cudaFree
+ * or cudaHostAlloc.  Any size within the limits of eas_gemm_f16 fits (M, N,
+ * K and batch each below 2^31); larger values are rejected with
+ * EAS_ERR_VALUE.
+ *
+ * The first call on a device looks the word's device address up
+ * (cudaGetSymbolAddress) with that device current; make that first call
+ * before any stream capture.  Every call clears the word, then runs the
+ * kernel.  All calls on a device share the word, so calls that overlap on the
+ * GPU race on it.  With status_out != NULL the call waits for the kernel and
+ * stores the status there (0 = ok, EAS_ERR_TIMEOUT = a bounded wait expired);
+ * with NULL it returns at once. */
+int eas_gemm_f16_noalloc(const void* a, const void* b, float* c, uint32_t M, uint32_t N, uint32_t K,
+                         uint32_t batch, uint64_t lda, uint64_t a_bstride, uint64_t ldb, uint64_t b_bstride,
+                         int b_kmajor, uint64_t ldc, uint64_t c_bstride, int block_n, void* stream,
+                         int* status_out);
+
 /* ---- host-side fault injection (tests; no device fault is ever made) --- */
 
 /* Make the `nth` (1-based) next call of kind "compile", "alloc", "launch" or
