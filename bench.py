@@ -293,6 +293,12 @@ def run_eas(args) -> None:
     from easy_as_b200.runtime import get_runtime
 
     rt = get_runtime()
+    if args.only in ("C4", "C5"):
+        # profiling mode: one GEMM workload only
+        res = run_gemm(args.only, args, world, rank, rt)
+        if rank == 0:
+            print(json.dumps(res), flush=True)
+        return
     add_kernel = make_add_kernel()
     lo, hi = shard(args.n, BLOCK, world, rank)
     n = hi - lo
@@ -446,6 +452,8 @@ def main() -> None:
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--n", type=int, default=N_TOTAL, help="total elements (profiling runs use a smaller case)")
     ap.add_argument("--no-gemm", action="store_true", help="skip the fp16 GEMM configs (C4, C5)")
+    ap.add_argument("--only", choices=["all", "C4", "C5"], default="all",
+                    help="run a single GEMM workload (profiling)")
     ap.add_argument("--gemm-steps", type=int, default=20)
     ap.add_argument("--quick", action="store_true",
                     help="profiling mode: no clock warm-up loop, no e2e arm, no CPU baseline")

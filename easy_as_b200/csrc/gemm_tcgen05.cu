@@ -31,6 +31,7 @@
 #include <stdint.h>
 
 #include <atomic>
+#include <cstdlib>
 #include <mutex>
 
 #include "eas_internal.h"
@@ -101,7 +102,7 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void*
 }
 
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
@@ -176,8 +177,8 @@ struct Smem {
   static constexpr int kABytes = BM * BK * 2;
   static constexpr int kBBytes = BN * BK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kEpiOffset = STAGES * kStageBytes;       // 4 warps x 32x32 f32 staging boxes
-  static constexpr int kEpiBytes = 4 * 32 * 32 * 4;
+  static constexpr int kEpiOffset = STAGES * kStageBytes;       // 4 warps x 2 x 32x32 f32 staging boxes
+  static constexpr int kEpiBytes = 4 * 2 * 32 * 32 * 4;
   static constexpr int kBarOffset = kEpiOffset + kEpiBytes;
   static constexpr int kTotal = kBarOffset + (2 * STAGES + 4) * 8 + 16 + 1024;  // + alignment slack
 };
@@ -303,7 +304,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const bool vec_ok = ((ldc & 3) == 0) && ((c_bstride & 3) == 0) && ((reinterpret_cast<uintptr_t>(c) & 15) == 0);
     // TMA_C: this warp's 32x32 f32 box, 128B-swizzled (16-byte chunk j of row r lives at chunk j ^ (r & 7))
-    uint8_t* box = smem + L::kEpiOffset + q * (32 * 32 * 4);
+    uint8_t* boxes = smem + L::kEpiOffset + q * (2 * 32 * 32 * 4);
+    int nbox = 0;  // boxes issued by this warp so far; box nbox & 1 is the next to fill
     int local = 0;
     for (int t = blockIdx.x; t < sched.total && !*abort_flag; t += gridDim.x, ++local) {
       const int buf = local & 1;
@@ -321,7 +323,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int nb = n0 + cc * 32;
         if (TMA_C) {
           if (nb < N && tc.m0 + q * 32 < M) {  // boxes wholly outside C are skipped; partial ones are clipped
-            if (lane == 0) bulk_wait_read0();  // previous box has been read out of shared memory
+            uint8_t* box = boxes + (nbox & 1) * (32 * 32 * 4);
+            if (lane == 0) bulk_wait_read1();  // the store that last used this box has read it
             __syncwarp();
             uint8_t* row = box + lane * 128;
 #pragma unroll
@@ -336,6 +339,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               tma_store_3d(&map_c, box, nb, tc.m0 + q * 32, tc.b);
               bulk_commit();
             }
+            ++nbox;
           }
         } else if (m < M) {
           if (vec_ok && nb + 32 <= N) {
@@ -363,6 +367,291 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols) : "memory");
+  }
+  if (threadIdx.x == 0 && *abort_flag && status) *status = EAS_ERR_TIMEOUT;
+}
+
+// ---------------------------------------------------------------------------
+// 2-SM variant: a cluster of two CTAs computes a 256 x 256 tile with
+// tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 16).  CTA rank r of the pair
+// stages rows [128r, 128r+128) of the A tile and columns [128r, 128r+128) of
+// the B tile, so each SM holds half of B; the leader (rank 0) issues the MMAs
+// and its accumulators span both CTAs' TMEM (each CTA holds its 128 rows).
+//   * both CTAs' TMA loads complete on the leader's `full` barrier, which the
+//     leader alone arms with the pair's byte count (a CTA loads a slot only
+//     after the leader's commit freed it, so the peer's bytes always land in
+//     the phase the leader armed);
+//   * the leader's commits arrive on `empty` / `acc_full` in both CTAs
+//     (multicast commit, mask 0b11);
+//   * all 8 epilogue warps of the pair arrive on the leader's `acc_empty`.
+// No TMA multicast is used: every CTA loads only what it keeps.
+// ---------------------------------------------------------------------------
+
+constexpr int kStages2 = 6;
+
+__device__ __forceinline__ uint32_t mapa_rank(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ bool mbar_try_wait_cl(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ bool mbar_wait_cl(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  const uint32_t a = smem_u32(bar);
+  if (mbar_try_wait_cl(a, parity)) return true;
+  const long long t0 = clock64();
+  while (true) {
+    if (mbar_try_wait_cl(a, parity)) return true;
+    if (*abort_flag) return false;
+    if (clock64() - t0 > kWaitBudget) {
+      *abort_flag = 1;
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_3d_pair(void* dst, const CUtensorMap* map, uint32_t bar_cluster, int x, int y,
+                                                 int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, "
+      "%5}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+struct Smem2 {
+  static constexpr int kABytes = 128 * BK * 2;   // this CTA's half of the A tile
+  static constexpr int kBBytes = 128 * BK * 2;   // this CTA's half of the B tile
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kEpiOffset = kStages2 * kStageBytes;
+  static constexpr int kEpiBytes = 4 * 2 * 32 * 32 * 4;
+  static constexpr int kBarOffset = kEpiOffset + kEpiBytes;
+  static constexpr int kTotal = kBarOffset + (2 * kStages2 + 4) * 8 + 16 + 1024;
+};
+
+template <bool B_MN, bool TMA_C>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    gemm_f16_tcgen05_2sm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                                const __grid_constant__ CUtensorMap map_c, float* __restrict__ c, int M, int N, int K,
+                                int batch, long long ldc, long long c_bstride, int* status) {
+  using L = Smem2;
+  constexpr int BN = 256;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
+  uint64_t* empty = full + kStages2;
+  uint64_t* acc_full = empty + kStages2;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  uint32_t rank;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
+  constexpr uint32_t kTmemCols = 2 * BN;  // 512: two accumulators of 128 lanes x 256 columns per CTA
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages2; ++s) {
+      mbar_init(&full[s], 1);  // armed by the leader with both CTAs' bytes (leader's copy is used)
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 8);  // 4 epilogue warps x 2 CTAs (leader's copy is used)
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // peer barriers are initialised before anyone signals them
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  Sched sched;
+  sched.mt = (M + 255) / 256;
+  sched.nt = (N + BN - 1) / BN;
+  sched.tiles_per_batch = sched.mt * sched.nt;
+  sched.total = sched.tiles_per_batch * batch;
+  const int kblocks = (K + BK - 1) / BK;
+  const int cid = blockIdx.x >> 1;
+  const int ncl = gridDim.x >> 1;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      for (int t = cid; t < sched.total && !*abort_flag; t += ncl) {
+        const TileCoord tc = sched.at(t);  // m0 in units of 128: pair tiles are 256 rows
+        const int m0 = (tc.m0 / BM) * 256 + 128 * (int)rank;
+        const int n0 = tc.n0 * BN + 128 * (int)rank;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) break;
+          uint8_t* sa = smem + s * L::kStageBytes;
+          uint8_t* sb = sa + L::kABytes;
+          const uint32_t fl = mapa_rank(smem_u32(&full[s]), 0);
+          if (rank == 0) mbar_expect_tx(&full[s], 2 * L::kStageBytes);
+          tma_load_3d_pair(sa, &map_a, fl, kb * BK, m0, tc.b);
+          if (B_MN) {
+            tma_load_3d_pair(sb, &map_b, fl, n0, kb * BK, tc.b);
+            tma_load_3d_pair(sb + BK * 128, &map_b, fl, n0 + 64, kb * BK, tc.b);
+          } else {
+            tma_load_3d_pair(sb, &map_b, fl, kb * BK, n0, tc.b);
+          }
+          if (++s == kStages2) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = (1u << 4) | ((B_MN ? 1u : 0u) << 16) | ((uint32_t)(BN >> 3) << 17) |
+                                 ((uint32_t)(256 >> 4) << 24);
+      int s = 0;
+      uint32_t ph = 0;
+      int local = 0;
+      for (int t = cid; t < sched.total && !*abort_flag; t += ncl, ++local) {
+        const int buf = local & 1;
+        const uint32_t acc_ph = (local >> 1) & 1;
+        if (!mbar_wait_cl(&acc_empty[buf], acc_ph ^ 1, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * BN;
+        bool ok = true;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&full[s], ph, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + s * L::kStageBytes);
+          const uint32_t b_addr = a_addr + L::kABytes;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t adesc = smem_desc(a_addr + kk * 32, 16, 1024);
+            const uint64_t bdesc = B_MN ? smem_desc(b_addr + kk * 2048, BK * 128, 1024)
+                                        : smem_desc(b_addr + kk * 32, 16, 1024);
+            asm volatile(
+                "{\n\t.reg .pred p;\n\t"
+                "setp.ne.b32 p, %4, 0;\n\t"
+                "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+                "l"(adesc), "l"(bdesc), "r"(idesc), "r"((kb | kk) != 0 ? 1u : 0u)
+                : "memory");
+          }
+          asm volatile(
+              "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+                  smem_u32(&empty[s])),
+              "h"((uint16_t)3)
+              : "memory");
+          if (++s == kStages2) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+        if (!ok) break;
+        asm volatile(
+            "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+                smem_u32(&acc_full[buf])),
+            "h"((uint16_t)3)
+            : "memory");
+      }
+    }
+  } else {
+    const int q = warp & 3;
+    uint8_t* boxes = smem + L::kEpiOffset + q * (2 * 32 * 32 * 4);
+    int nbox = 0;
+    const bool vec_ok = ((ldc & 3) == 0) && ((c_bstride & 3) == 0) && ((reinterpret_cast<uintptr_t>(c) & 15) == 0);
+    const uint32_t acc_empty_leader[2] = {mapa_rank(smem_u32(&acc_empty[0]), 0), mapa_rank(smem_u32(&acc_empty[1]), 0)};
+    int local = 0;
+    for (int t = cid; t < sched.total && !*abort_flag; t += ncl, ++local) {
+      const int buf = local & 1;
+      const uint32_t acc_ph = (local >> 1) & 1;
+      if (!mbar_wait(&acc_full[buf], acc_ph, abort_flag)) break;
+      tc_fence_after();
+      const TileCoord tc = sched.at(t);
+      const int n0 = tc.n0 * BN;
+      const int mrow0 = (tc.m0 / BM) * 256 + 128 * (int)rank + q * 32;
+      const int m = mrow0 + lane;
+      float* crow = c + (long long)tc.b * c_bstride + (long long)m * ldc;
+#pragma unroll 1
+      for (int cc = 0; cc < BN / 32; ++cc) {
+        uint32_t r[32];
+        tmem_ld32(tmem_base + buf * BN + cc * 32 + ((uint32_t)(q * 32) << 16), r);
+        const int nb = n0 + cc * 32;
+        if (TMA_C) {
+          if (nb < N && mrow0 < M) {
+            uint8_t* box = boxes + (nbox & 1) * (32 * 32 * 4);
+            if (lane == 0) bulk_wait_read1();
+            __syncwarp();
+            uint8_t* row = box + lane * 128;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              float4 v = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                     __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+              *reinterpret_cast<float4*>(row + ((j ^ (lane & 7)) << 4)) = v;
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_3d(&map_c, box, nb, mrow0, tc.b);
+              bulk_commit();
+            }
+            ++nbox;
+          }
+        } else if (m < M) {
+          if (vec_ok && nb + 32 <= N) {
+            float4* dst = reinterpret_cast<float4*>(crow + nb);
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              dst[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                   __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (nb + j < N) crow[nb + j] = __uint_as_float(r[j]);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0)
+        asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(acc_empty_leader[buf])
+                     : "memory");
+    }
+    if (TMA_C && lane == 0) bulk_wait_all0();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // the pair leaves together: no MMA still targets the peer's TMEM
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols)
+                 : "memory");
   }
   if (threadIdx.x == 0 && *abort_flag && status) *status = EAS_ERR_TIMEOUT;
 }
@@ -397,6 +686,45 @@ int launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorM
   const int grid = (int)(tiles < num_sms ? tiles : num_sms);
   kern<<<grid, kThreads, L::kTotal, stream>>>(ma, mb, mc, c, M, N, K, batch, ldc, cbs, status);
   return eas_cuda_check(cudaGetLastError(), "gemm: launch", EAS_ERR_LAUNCH);
+}
+
+template <bool B_MN, bool TMA_C>
+int launch_2sm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, float* c, int M, int N, int K,
+               int batch, long long ldc, long long cbs, int* status, cudaStream_t stream, int num_sms) {
+  auto kern = gemm_f16_tcgen05_2sm_kernel<B_MN, TMA_C>;
+  int rc = eas_cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Smem2::kTotal),
+                          "gemm(2sm): set smem attribute", EAS_ERR_LAUNCH);
+  if (rc) return rc;
+  const long long tiles = (long long)((M + 255) / 256) * ((N + 255) / 256) * batch;
+  // persistent grid: only as many pairs as can be resident at once (GPC boundaries can leave SMs unpaired)
+  static int resident_pairs[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (resident_pairs[dev] == 0) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * (num_sms / 2), 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = Smem2::kTotal;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = num_sms / 2;
+    }
+    resident_pairs[dev] = n;
+  }
+  const long long pairs = resident_pairs[dev];
+  const int grid = 2 * (int)(tiles < pairs ? tiles : pairs);
+  kern<<<grid, kThreads, Smem2::kTotal, stream>>>(ma, mb, mc, c, M, N, K, batch, ldc, cbs, status);
+  return eas_cuda_check(cudaGetLastError(), "gemm(2sm): launch", EAS_ERR_LAUNCH);
+}
+
+bool use_2sm(int block_n, uint32_t M) {
+  static const bool enabled = [] {
+    const char* e = getenv("EAS_GEMM_2SM");
+    return !(e && e[0] == '0');
+  }();
+  return enabled && block_n == 256 && M > 128;
 }
 
 int* g_status_host = nullptr;  // host-mapped status words, one per device
@@ -450,10 +778,11 @@ extern "C" int eas_gemm_f16(const void* a, const void* b, float* c, uint32_t M, 
   rc = encode_map(&ma, a, K, M, batch, lda * 2, ab ? ab : 16, BK, BM);
   if (rc) return rc;
   const bool b_mn = !b_kmajor;
+  const bool pair = use_2sm(block_n, M);
   if (b_mn)
     rc = encode_map(&mb, b, N, K, batch, ldb * 2, bb ? bb : 16, 64, BK);
   else
-    rc = encode_map(&mb, b, K, N, batch, ldb * 2, bb ? bb : 16, BK, (uint32_t)block_n);
+    rc = encode_map(&mb, b, K, N, batch, ldb * 2, bb ? bb : 16, BK, pair ? 128u : (uint32_t)block_n);
   if (rc) return rc;
   // C through TMA stores when its rows/batches are 16-byte strided and the base is aligned
   CUtensorMap mc;
@@ -476,6 +805,12 @@ extern "C" int eas_gemm_f16(const void* a, const void* b, float* c, uint32_t M, 
                                                          num_sms)                                                \
                  : launch_variant<BN_, ST_, false, false>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s,    \
                                                           num_sms)))
+  if (pair) {
+    return b_mn ? (tma_c ? launch_2sm<true, true>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s, num_sms)
+                         : launch_2sm<true, false>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s, num_sms))
+                : (tma_c ? launch_2sm<false, true>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s, num_sms)
+                         : launch_2sm<false, false>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s, num_sms));
+  }
   if (block_n == 256) return EAS_GEMM_VARIANT(256, 4);
   return EAS_GEMM_VARIANT(128, 6);
 #undef EAS_GEMM_VARIANT
