@@ -247,7 +247,7 @@ def run_gemm(name: str, args, world: int, rank: int, rt) -> dict:
         "metric": "fp16 mk.dot GEMM TFLOP/s", "value": round(flops_total / (ms_max * 1e-3) / 1e12, 1),
         "unit": "TFLOP/s", "ms_per_step": round(ms_max, 4), "steps": steps,
         "config": {"workload": f"{name} batch={tb} M={TM} N={TN} K={TK} f16 in, f32 acc/out", "split": split,
-                   "kernel": f"tcgen05 cta_group::1, tile 128x{bn}x64", "spot_check_rel_err": err},
+                   "kernel": "tcgen05 cta_group::2 (CTA pair), tile 256x256x64, 6 stages", "spot_check_rel_err": err},
         "roofline": {"bound": "tensor", "achieved": round(local_tf, 1), "peak": pk["bf16_tflops"],
                      "unit": "TFLOP/s", "frac": round(local_tf / pk["bf16_tflops"], 4),
                      "peak_source": ("measured burst cuBLAS bf16 (MEASURED_PEAKS.json bf16_tflops)"
