@@ -462,6 +462,12 @@ def main() -> None:
         run_reference(args)
     else:
         run_eas(args)
+        if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+            import torch.distributed as dist
+
+            if dist.is_initialized():
+                dist.barrier()
+                dist.destroy_process_group()
 
 
 if __name__ == "__main__":

@@ -393,7 +393,8 @@ class CudaRuntime:
 
     # -- launch -------------------------------------------------------------------------
     def _launch_generic(self, ck: Any, runtime_args: Mapping[str, Any], args: dict[str, _Arg], device: int,
-                        stream: int, programs: tuple[int, int, int], ntx: int) -> None:
+                        stream: int, programs: tuple[int, int, int], ntx: int,
+                        pid_base: tuple[int, int, int] = (0, 0, 0)) -> None:
         plan = ck.plan
         pipe = self._pipeline_for(ck, device)
         layout = plan.layout
@@ -405,7 +406,8 @@ class CudaRuntime:
         block = (cuda_ext.ctypes.c_uint32 * 3)(plan.cuda_threads, 1, 1)
         for z0 in range(0, gz, MAX_GRID_YZ):
             for y0 in range(0, gy, MAX_GRID_YZ):
-                hidden = {"eas_ntx": ntx, "eas_pid_x": 0, "eas_pid_y": y0, "eas_pid_z": z0}
+                hidden = {"eas_ntx": ntx, "eas_pid_x": pid_base[0], "eas_pid_y": pid_base[1] + y0,
+                          "eas_pid_z": pid_base[2] + z0}
                 blob = layout.pack(runtime_args, ptrs, hidden)
                 cblob = (cuda_ext.ctypes.c_char * len(blob)).from_buffer(blob)
                 g = (cuda_ext.ctypes.c_uint32 * 3)(gx, min(MAX_GRID_YZ, gy - y0), min(MAX_GRID_YZ, gz - z0))
@@ -450,6 +452,44 @@ class CudaRuntime:
         limit = self._max_flight()
         if limit and len(self._pending) > limit:
             self._wait_one()
+
+    def run_range(self, ck: Any, runtime_args: Mapping[str, Any], meta: Mapping[str, Any], *, axis: int,
+                  lo: int, hi: int, grid: tuple[int, int, int] | None = None, nthreads: int | None = None,
+                  shape: tuple[int, ...] | None = None, buffer_base: Mapping[str, int] | None = None,
+                  sync: bool = True) -> None:
+        """Run only programs ``lo <= program_id(axis) < hi`` of the launch ``run`` would make.
+
+        The programs keep their global ids (the kernel's hidden program-id
+        offsets), so an unmodified kernel computes exactly its share.  With
+        ``buffer_base={name: e}`` buffer ``name`` holds only the elements from
+        global index ``e`` on: the kernel receives its pointer moved back by
+        ``e`` elements, and must only touch indices ``>= e`` in it (true for a
+        program-id shard whose programs address disjoint element ranges).
+        Used by :mod:`easy_as_b200.shard` to split a grid across GPUs.
+        """
+        geo = launch_geometry(ck, runtime_args, nthreads=nthreads, grid=grid, tptg=None, shape=shape)
+        if geo is None:
+            return
+        programs, ntx = geo
+        if not 0 <= axis <= 2:
+            raise ValueError("axis must be 0, 1 or 2")
+        lo, hi = max(0, int(lo)), min(int(hi), programs[axis])
+        if hi <= lo:
+            return
+        sub = list(programs)
+        sub[axis] = hi - lo
+        base = [0, 0, 0]
+        base[axis] = lo
+        args, device, stream = self._resolve(ck, runtime_args)
+        for name, e in (buffer_base or {}).items():
+            item = 4 if next(a for a in ck.ir.args if a.name == name).dtype == DType.F32 else 2
+            args[name].ptr -= int(e) * item
+        host_copies = [(a.dev_buf, a.host) for a in args.values() if a.host is not None]
+        if host_copies:
+            raise ValueError("run_range needs device buffers (torch CUDA tensors or eas.Tensor on cuda)")
+        self._launch_generic(ck, runtime_args, args, device, stream, tuple(sub), ntx, tuple(base))
+        if sync:
+            cuda_ext.check(self.lib().eas_stream_synchronize(stream), "kernel execution")
 
     def _wait_one(self) -> None:
         ev, _keep = self._pending.popleft()
