@@ -520,9 +520,112 @@ class _Emitter:
         needs_lane = any(i.op in ("mma", "mma_store", "lane_id") for i in self.ir.insts)
         if needs_lane:
             self.emit("const uint32_t eas_lane = threadIdx.x & 31u;")
-        for inst in self.ir.insts:
+        groups = self._dot_groups()
+        for k, inst in enumerate(self.ir.insts):
+            if k in groups:
+                if groups[k]:
+                    self._dot_group([self.ir.insts[j] for j in groups[k]])
+                continue
             self._thread_inst(inst)
         return self.lines
+
+    _PURE = frozenset({"const", "add", "mul", "floordiv", "mod", "lt", "and", "or", "not", "where", "cast", "fma",
+                       "program_id", "thread_id", "local_id", "lane_id", "sg_id", "tid"})
+
+    def _dot_groups(self) -> dict[int, list[int]]:
+        """Dots sharing (A buffer, A base, A stride, B buffer, B stride, K), up to 8, separated only by
+        pure instructions that do not read them; {index of last member: members, other members: []}."""
+        insts = self.ir.insts
+        out: dict[int, list[int]] = {}
+        taken: set[int] = set()
+
+        def sig(i: Inst) -> tuple[int, ...]:
+            a_buf, a_base, a_stride, b_buf, _b_base, b_stride, k = i.args
+            return (a_buf.id, a_base.id, a_stride.id, b_buf.id, b_stride.id, k.id)
+
+        for i, inst in enumerate(insts):
+            if inst.op != "dot" or i in taken:
+                continue
+            members = [i]
+            outs = {inst.out.id}
+            s0 = sig(inst)
+            for j in range(i + 1, min(len(insts), i + 64)):
+                nxt = insts[j]
+                if nxt.op == "dot" and sig(nxt) == s0 and len(members) < 8:
+                    members.append(j)
+                    outs.add(nxt.out.id)
+                    continue
+                if nxt.op in self._PURE and not any(isinstance(a, ValueRef) and a.id in outs for a in nxt.args):
+                    continue
+                break
+            if len(members) > 1:
+                for m in members:
+                    taken.add(m)
+                    out[m] = []
+                out[members[-1]] = members
+        return out
+
+    def _dot_group(self, dots: list[Inst]) -> None:
+        """One k loop for several dots: A is loaded once per k; when four B bases are X+0..3 the
+        four B values come from one vector load whenever that address is aligned.  Each dot keeps
+        its own strict k-order fma chain, so results equal the separate loops bit for bit."""
+        a_buf, a_base, a_stride, b_buf, _bb, b_stride, k_ref = dots[0].args
+        outs = [d.out.id for d in dots]
+        for o in outs:
+            self.emit(f"float v{o} = 0.0f;")
+        # vector candidate: first four members with B base = X + 0, 1, 2, 3
+        vec = None
+        if len(dots) >= 4:
+            bases = []
+            for d in dots[:4]:
+                bref = d.args[4]
+                bd = self.defs.get(bref.id)
+                if bd is not None and bd.op == "add":
+                    x, y = bd.args
+                    cy, cx = self.defs.get(y.id), self.defs.get(x.id)
+                    if cy is not None and cy.op == "const" and cy.out.dtype == DType.U32:
+                        bases.append((x.id, int(cy.args[0]), bref))
+                        continue
+                    if cx is not None and cx.op == "const" and cx.out.dtype == DType.U32:
+                        bases.append((y.id, int(cx.args[0]), bref))
+                        continue
+                bases.append((bref.id, 0, bref))
+            if len({b[0] for b in bases}) == 1 and [b[1] for b in bases] == [0, 1, 2, 3]:
+                vec = bases[0][2]
+        guard = self._guard("true")
+        self.emit("{" if guard == "true" else f"if ({guard}) {{")
+        self.emit(f"uint32_t ai = {self.name(a_base)};", 2)
+        for n, d in enumerate(dots):
+            self.emit(f"uint32_t bi{n} = {self.name(d.args[4])};", 2)
+        kd = self.defs.get(k_ref.id)
+        if kd is not None and kd.op == "const" and 1 <= int(kd.args[0]) <= 32:
+            self.emit("#pragma unroll", 2)
+        self.emit(f"for (uint32_t k = 0; k < {self.name(k_ref)}; ++k) {{", 2)
+        A, B = self.name(a_buf), self.name(b_buf)
+        self.emit(f"const float av = {_as_float(a_buf.dtype, f'{A}[ai]')};", 3)
+
+        def scalar(n: int, o: int) -> str:
+            return f"v{o} = fmaf(av, {_as_float(b_buf.dtype, f'{B}[bi{n}]')}, v{o});"
+
+        if vec is not None:
+            vt, comps = ("float4", "xyzw") if b_buf.dtype == DType.F32 else ("eas_h4", "xyzw")
+            self.emit("if ((bi0 & 3u) == 0u) {", 3)
+            self.emit(f"const {vt} bv = *reinterpret_cast<const {vt}*>({B} + bi0);", 4)
+            for n in range(4):
+                self.emit(f"v{outs[n]} = fmaf(av, {_as_float(b_buf.dtype, f'bv.{comps[n]}')}, v{outs[n]});", 4)
+            self.emit("} else {", 3)
+            for n in range(4):
+                self.emit(scalar(n, outs[n]), 4)
+            self.emit("}", 3)
+            for n in range(4, len(dots)):
+                self.emit(scalar(n, outs[n]), 3)
+        else:
+            for n, o in enumerate(outs):
+                self.emit(scalar(n, o), 3)
+        self.emit(f"ai += {self.name(a_stride)};" + "".join(f" bi{n} += {self.name(b_stride)};"
+                                                             for n in range(len(dots))), 3)
+        self.emit("}", 2)
+        self.emit("}")
 
     def _guard(self, cond: str) -> str:
         if self.ghost is None:
