@@ -175,7 +175,9 @@ def _cast_expr(x: str, src: DType, dst: DType) -> str:
     return table[(src, dst)]
 
 
-def _binop_expr(op: str, dt: DType, a: str, b: str) -> str:
+def _binop_expr(op: str, dt: DType, a: str, b: str, nonzero_b: bool = False) -> str:
+    """C expression of a binary IR op.  u32 ``x // 0`` is 0xFFFFFFFF and ``x % 0`` is ``x``
+    (the reference leaves these undefined; the oracle uses the same definition)."""
     if op in ("add", "mul"):
         sym = "+" if op == "add" else "*"
         if dt == DType.F16:
@@ -184,9 +186,9 @@ def _binop_expr(op: str, dt: DType, a: str, b: str) -> str:
             return f"__f{'add' if op == 'add' else 'mul'}_rn({a}, {b})"
         return f"({a} {sym} {b})"
     if op == "floordiv":
-        return f"({a} / {b})"
+        return f"({a} / {b})" if nonzero_b else f"(({b}) ? ({a} / {b}) : 0xFFFFFFFFu)"
     if op == "mod":
-        return f"({a} % {b})"
+        return f"({a} % {b})" if nonzero_b else f"(({b}) ? ({a} % {b}) : ({a}))"
     if op == "lt":
         if dt == DType.F16:
             return f"(eas_h2f({a}) < eas_h2f({b}))"
@@ -271,6 +273,10 @@ class _Emitter:
     def lane(self, ref: ValueRef, i: str) -> str:
         n = self.name(ref)
         return f"{n}[{i}]" if ref.lanes > 1 else n
+
+    def _nonzero_const(self, ref: ValueRef) -> bool:
+        d = self.defs.get(ref.id)
+        return d is not None and d.op == "const" and not isinstance(d.args[0], bool) and int(d.args[0]) % (1 << 32) != 0
 
     def is_const_true(self, ref: ValueRef) -> bool:
         d = self.defs.get(ref.id)
@@ -378,6 +384,9 @@ class _Emitter:
             ax = "xyz"[int(args[0])]
             self.emit(f"const uint32_t v{out.id} = blockIdx.{ax} + eas_pid_{ax};")
             return
+        if op == "arange" and out.lanes == 1:
+            self.emit(f"const uint32_t v{out.id} = {int(args[0])}u;")  # BLOCK == 1: one lane, held by thread 0
+            return
         if op == "arange":
             start = int(args[0])
             self.emit(self._vec_decl(out))
@@ -388,7 +397,8 @@ class _Emitter:
         if op in ("add", "mul", "floordiv", "mod", "lt", "and", "or"):
             a, b = args
             dt = a.dtype
-            self._spmd_elementwise(out, lambda i: _binop_expr(op, dt, self.lane(a, i), self.lane(b, i)))
+            nz = self._nonzero_const(b)
+            self._spmd_elementwise(out, lambda i: _binop_expr(op, dt, self.lane(a, i), self.lane(b, i), nz))
             if op == "add" and out.lanes > 1:
                 if a.id in self.unit and b.lanes == 1:
                     self.unit[out.id] = f"({self.unit[a.id]} + {self.name(b)})"
@@ -662,7 +672,8 @@ class _Emitter:
             raise ValueError("arange is not supported in thread mode codegen; use mk.tid(...) for thread-level kernels")
         elif op in ("add", "mul", "floordiv", "mod", "lt", "and", "or"):
             a, b = args
-            self.emit(f"const {ctype(out.dtype)} v{out.id} = {_binop_expr(op, a.dtype, self.name(a), self.name(b))};")
+            expr = _binop_expr(op, a.dtype, self.name(a), self.name(b), self._nonzero_const(b))
+            self.emit(f"const {ctype(out.dtype)} v{out.id} = {expr};")
         elif op == "not":
             self.emit(f"const bool v{out.id} = !{self.name(args[0])};")
         elif op == "where":
