@@ -491,6 +491,14 @@ extern "C" int eas_stream_synchronize(void* stream) {
                         EAS_ERR_LAUNCH);
 }
 
+extern "C" int eas_stream_is_capturing(void* stream, int* capturing) {
+  if (!capturing) return eas_fail(EAS_ERR_VALUE, "eas_stream_is_capturing: null pointer");
+  cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+  int rc = eas_cuda_check(cudaStreamIsCapturing((cudaStream_t)stream, &st), "cudaStreamIsCapturing", EAS_ERR_VALUE);
+  *capturing = (st == cudaStreamCaptureStatusActive) ? 1 : 0;
+  return rc;
+}
+
 extern "C" int eas_device_synchronize(int dev) {
   int rc = eas_set_device(dev);
   if (rc) return rc;

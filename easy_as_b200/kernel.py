@@ -141,6 +141,14 @@ class Kernel:
                          raw_opts: dict[str, Any]) -> tuple[dict[str, Any], dict[str, Any]]:
         key = self._autotune_key(spec, meta, runtime_args)
         best = self._tuned_cache.get(key)
+        disk_key = None
+        if best is None:
+            disk_key = _disk_key(self, spec, key, runtime_args)
+            stored = _disk_load(disk_key)
+            if stored is not None:
+                best = next((c for c in spec.configs if dict(c.meta) == stored), None)
+                if best is not None:
+                    self._tuned_cache[key] = best
         if best is None:
             bench = getattr(get_runtime(), "benchmark", None)
             if not callable(bench):
@@ -158,6 +166,7 @@ class Kernel:
             if best is None:  # pragma: no cover
                 raise RuntimeError("autotune failed to select a config")
             self._tuned_cache[key] = best
+            _disk_store(disk_key, dict(best.meta))
         m = {**meta, **dict(best.meta)}
         return m, self._normalize_runtime_options(raw_opts, m, runtime_args)
 
@@ -201,6 +210,66 @@ class Kernel:
 
     # the reference's name for the same query; returns the CUDA source here
     to_msl = to_cuda
+
+
+# ---------------------------------------------------------------------------
+# on-disk autotune results (EAS_CACHE_DIR/autotune.json; EAS_AUTOTUNE_CACHE=0 disables)
+# ---------------------------------------------------------------------------
+
+
+def _autotune_file() -> Any:
+    import os
+    from pathlib import Path
+
+    if os.environ.get("EAS_AUTOTUNE_CACHE", "1") in ("0", "off", "false"):
+        return None
+    d = os.environ.get("EAS_CACHE_DIR", str(Path.home() / ".cache" / "easy_as_b200"))
+    if d in ("", "0", "off", "none"):
+        return None
+    return Path(d) / "autotune.json"
+
+
+def _disk_key(k: "Kernel", spec: AutotuneSpec, key: tuple[Any, ...], runtime_args: Mapping[str, Any]) -> str | None:
+    import hashlib
+
+    try:
+        src = inspect.getsource(k.fn)
+    except (OSError, TypeError):
+        return None
+    sig = runtime_arg_signature(runtime_args)
+    blob = repr((k.fn.__module__, k.fn.__qualname__, src, [sorted(dict(c.meta).items()) for c in spec.configs],
+                 key, sig, "sm_100a"))
+    return hashlib.sha256(blob.encode()).hexdigest()
+
+
+def _disk_load(dkey: str | None) -> dict[str, Any] | None:
+    import json
+
+    f = _autotune_file()
+    if dkey is None or f is None or not f.exists():
+        return None
+    try:
+        return json.loads(f.read_text()).get(dkey)
+    except (OSError, ValueError):
+        return None
+
+
+def _disk_store(dkey: str | None, meta: dict[str, Any]) -> None:
+    import json
+    import os
+
+    f = _autotune_file()
+    if dkey is None or f is None:
+        return
+    try:
+        f.parent.mkdir(parents=True, exist_ok=True)
+        data = json.loads(f.read_text()) if f.exists() else {}
+        data[dkey] = meta
+        tmp = f.with_name(f"autotune.{os.getpid()}.tmp")
+        tmp.write_text(json.dumps(data))
+        os.replace(tmp, f)
+    except (OSError, ValueError):
+        pass
 
 
 def kernel(fn: Callable[..., Any]) -> Kernel:

@@ -433,8 +433,17 @@ class CudaRuntime:
             raise RuntimeError("CUDA runtime is not available: " + self._reason)
         args, device, stream = self._resolve(ck, runtime_args)
         host_copies = [(a.dev_buf, a.host) for a in args.values() if a.host is not None]
-        self._dispatch(ck, runtime_args, args, device, stream, *geo)
         lib = self.lib()
+        capturing = cuda_ext.ctypes.c_int(0)
+        if stream:
+            lib.eas_stream_is_capturing(stream, cuda_ext.ctypes.byref(capturing))
+        if capturing.value:
+            # inside CUDA graph capture: enqueue only (the graph keeps raw pointers: callers keep buffers alive)
+            if sync or host_copies:
+                raise ValueError("inside CUDA graph capture launch with _sync=False and device buffers only")
+            self._dispatch(ck, runtime_args, args, device, stream, *geo)
+            return
+        self._dispatch(ck, runtime_args, args, device, stream, *geo)
         if sync or host_copies:
             cuda_ext.check(lib.eas_stream_synchronize(stream), "kernel execution")
             self._check_native_status(device)

@@ -57,6 +57,7 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "eas_memset_d8": (_int, [_vp, _int, _sz, _vp]),
     "eas_stream_synchronize": (_int, [_vp]),
     "eas_device_synchronize": (_int, [_int]),
+    "eas_stream_is_capturing": (_int, [_vp, _PINT]),
     "eas_stream_create": (_int, [_int, ctypes.POINTER(_vp)]),
     "eas_stream_destroy": (_int, [_vp]),
     "eas_event_create": (_int, [ctypes.POINTER(_vp)]),

@@ -106,6 +106,8 @@ int eas_memset_d8(void* dst, int value, size_t nbytes, void* stream);
  *      _metal.mm:1397-1434) ------------------------------------------------ */
 
 int eas_stream_synchronize(void* stream);
+/* *capturing = 1 while `stream` is being captured into a CUDA graph. */
+int eas_stream_is_capturing(void* stream, int* capturing);
 int eas_device_synchronize(int dev);
 int eas_stream_create(int dev, void** stream);
 int eas_stream_destroy(void* stream);
