@@ -156,15 +156,15 @@ struct TileCoord {
 };
 
 struct Sched {
-  int mt, nt, tiles_per_batch, total;
+  int mt, nt, tiles_per_batch, total, group_m = kGroupM;
   __device__ TileCoord at(int t) const {
     TileCoord c;
     c.b = t / tiles_per_batch;
     int r = t - c.b * tiles_per_batch;
-    const int per_group = kGroupM * nt;
+    const int per_group = group_m * nt;
     const int g = r / per_group;
-    const int first_m = g * kGroupM;
-    const int gsize = min(kGroupM, mt - first_m);
+    const int first_m = g * group_m;
+    const int gsize = min(group_m, mt - first_m);
     const int rr = r - g * per_group;
     c.m0 = (first_m + rr % gsize) * BM;
     c.n0 = rr / gsize;  // tile index along N (times BN at the call site)
@@ -387,7 +387,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 // No TMA multicast is used: every CTA loads only what it keeps.
 // ---------------------------------------------------------------------------
 
-constexpr int kStages2 = 6;
 
 __device__ __forceinline__ uint32_t mapa_rank(uint32_t addr, uint32_t rank) {
   uint32_t r;
@@ -434,22 +433,23 @@ __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
+template <int kStages2, bool TMA_C>
 struct Smem2 {
   static constexpr int kABytes = 128 * BK * 2;   // this CTA's half of the A tile
   static constexpr int kBBytes = 128 * BK * 2;   // this CTA's half of the B tile
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kEpiOffset = kStages2 * kStageBytes;
-  static constexpr int kEpiBytes = 4 * 2 * 32 * 32 * 4;
+  static constexpr int kEpiBytes = TMA_C ? 4 * 2 * 32 * 32 * 4 : 0;
   static constexpr int kBarOffset = kEpiOffset + kEpiBytes;
   static constexpr int kTotal = kBarOffset + (2 * kStages2 + 4) * 8 + 16 + 1024;
 };
 
-template <bool B_MN, bool TMA_C>
+template <int kStages2, bool B_MN, bool TMA_C>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_f16_tcgen05_2sm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                                 const __grid_constant__ CUtensorMap map_c, float* __restrict__ c, int M, int N, int K,
                                 int batch, long long ldc, long long c_bstride, int* status) {
-  using L = Smem2;
+  using L = Smem2<kStages2, TMA_C>;
   constexpr int BN = 256;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -688,34 +688,36 @@ int launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorM
   return eas_cuda_check(cudaGetLastError(), "gemm: launch", EAS_ERR_LAUNCH);
 }
 
-template <bool B_MN, bool TMA_C>
+template <int STAGES, bool B_MN, bool TMA_C>
 int launch_2sm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, float* c, int M, int N, int K,
                int batch, long long ldc, long long cbs, int* status, cudaStream_t stream, int num_sms) {
-  auto kern = gemm_f16_tcgen05_2sm_kernel<B_MN, TMA_C>;
-  int rc = eas_cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Smem2::kTotal),
+  using L = Smem2<STAGES, TMA_C>;
+  auto kern = gemm_f16_tcgen05_2sm_kernel<STAGES, B_MN, TMA_C>;
+  int rc = eas_cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal),
                           "gemm(2sm): set smem attribute", EAS_ERR_LAUNCH);
   if (rc) return rc;
   const long long tiles = (long long)((M + 255) / 256) * ((N + 255) / 256) * batch;
   // persistent grid: only as many pairs as can be resident at once (GPC boundaries can leave SMs unpaired)
-  static int resident_pairs[64] = {0};
+  static int resident_pairs[2][64] = {{0}};
+  const int which = TMA_C ? 1 : 0;
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) dev = 0;
-  if (resident_pairs[dev] == 0) {
+  if (resident_pairs[which][dev] == 0) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * (num_sms / 2), 1, 1);
     cfg.blockDim = dim3(kThreads, 1, 1);
-    cfg.dynamicSmemBytes = Smem2::kTotal;
+    cfg.dynamicSmemBytes = L::kTotal;
     int n = 0;
     if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
       cudaGetLastError();
       n = num_sms / 2;
     }
-    resident_pairs[dev] = n;
+    resident_pairs[which][dev] = n;
   }
-  const long long pairs = resident_pairs[dev];
+  const long long pairs = resident_pairs[which][dev];
   const int grid = 2 * (int)(tiles < pairs ? tiles : pairs);
-  kern<<<grid, kThreads, Smem2::kTotal, stream>>>(ma, mb, mc, c, M, N, K, batch, ldc, cbs, status);
+  kern<<<grid, kThreads, L::kTotal, stream>>>(ma, mb, mc, c, M, N, K, batch, ldc, cbs, status);
   return eas_cuda_check(cudaGetLastError(), "gemm(2sm): launch", EAS_ERR_LAUNCH);
 }
 
@@ -806,10 +808,11 @@ extern "C" int eas_gemm_f16(const void* a, const void* b, float* c, uint32_t M, 
                  : launch_variant<BN_, ST_, false, false>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s,    \
                                                           num_sms)))
   if (pair) {
-    return b_mn ? (tma_c ? launch_2sm<true, true>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s, num_sms)
-                         : launch_2sm<true, false>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s, num_sms))
-                : (tma_c ? launch_2sm<false, true>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s, num_sms)
-                         : launch_2sm<false, false>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s, num_sms));
+    if (!tma_c)  // C not TMA-storable: direct stores, and the smem freed by the staging boxes buys a 7th stage
+      return b_mn ? launch_2sm<7, true, false>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s, num_sms)
+                  : launch_2sm<7, false, false>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s, num_sms);
+    return b_mn ? launch_2sm<6, true, true>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s, num_sms)
+                : launch_2sm<6, false, true>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s, num_sms);
   }
   if (block_n == 256) return EAS_GEMM_VARIANT(256, 4);
   return EAS_GEMM_VARIANT(128, 6);
