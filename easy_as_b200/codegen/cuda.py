@@ -74,6 +74,7 @@ class Lowered:
     params: list[Param]
     dyn_smem: int        # bytes of dynamic shared memory per CTA
     native: Any = field(default=None)   # pattern-lowered native plan (see codegen.patterns)
+    elementwise: Any = field(default=None)  # ElementwiseInfo when program p touches only elements [p*B, p*B+B)
     layout: Any = field(default=None)   # runtime parameter layout, built on first launch
 
 
@@ -774,10 +775,95 @@ class _Emitter:
         self.emit("}")
 
 
+@dataclass(frozen=True, slots=True)
+class ElementwiseInfo:
+    """Every memory access of the kernel is at the global element index X (= program_id(0)*BLOCK +
+    lane/thread), masked by ``X < bound`` or not at all.  Program p then touches only elements
+    [p*BLOCK, p*BLOCK + BLOCK), so any split of the programs splits the buffers the same way."""
+
+    block: int
+    reads: frozenset[str]                 # buffer args that are loaded
+    writes: frozenset[str]                # buffer args that are stored
+    store_bounds: tuple[tuple[str, Any], ...]  # (buffer, bound): ("arg", name), ("const", v) or None (unmasked)
+
+
+def elementwise_info(ir: IRModule, block: int, mode: str) -> ElementwiseInfo | None:
+    defs = {i.out.id: i for i in ir.insts if i.out is not None}
+    if any(i.op in ("program_id", "thread_id") and int(i.args[0]) != 0 for i in ir.insts):
+        return None
+    if any(i.op in ("dot", "mma", "mma_store", "alloc_tg", "barrier", "local_id", "lane_id", "sg_id") for i in ir.insts):
+        return None
+
+    def op(ref: ValueRef) -> Inst | None:
+        return defs.get(ref.id)
+
+    def is_const(ref: ValueRef, v: int) -> bool:
+        d = op(ref)
+        return d is not None and d.op == "const" and not isinstance(d.args[0], bool) and int(d.args[0]) == v
+
+    def is_index(ref: ValueRef) -> bool:
+        d = op(ref)
+        if d is None:
+            return False
+        if mode == "thread" and d.op == "thread_id":
+            return True
+        if d.op != "add":
+            return False
+        for x, y in (d.args, d.args[::-1]):
+            dx, dy = op(x), op(y)
+            if dx is None or dy is None or dx.op != "mul":
+                continue
+            local_ok = (dy.op == "arange" if mode == "spmd" else dy.op == "tid") and tuple(
+                int(v) for v in dy.args) == (0, block)
+            p, q = dx.args
+            pid_ok = any((op(u) is not None and op(u).op == "program_id" and is_const(w, block))
+                         for u, w in ((p, q), (q, p)))
+            if local_ok and pid_ok:
+                return True
+        return False
+
+    def bound(mask: ValueRef, idx: ValueRef) -> Any:
+        d = op(mask)
+        if d is not None and d.op == "const" and d.args[0] is True:
+            return None
+        if d is not None and d.op == "lt" and d.args[0].id == idx.id:
+            b = op(d.args[1])
+            if b is not None and b.op == "arg":
+                return ("arg", str(b.args[0]))
+            if b is not None and b.op == "const" and not isinstance(b.args[0], bool):
+                return ("const", int(b.args[0]))
+        return "bad"
+
+    arg_names = {i.out.id: str(i.args[0]) for i in ir.insts if i.op == "arg"}
+    reads, writes, bounds = set(), set(), []
+    for inst in ir.insts:
+        if inst.op not in ("load", "store"):
+            continue
+        buf, off = inst.args[0], inst.args[1]
+        mask = inst.args[2] if inst.op == "load" else inst.args[3]
+        if buf.id not in arg_names or not is_index(off):
+            return None
+        b = bound(mask, off)
+        if b == "bad":
+            return None
+        name = arg_names[buf.id]
+        if inst.op == "load":
+            reads.add(name)
+        else:
+            if inst.args[2].lanes not in (1, off.lanes):
+                return None
+            writes.add(name)
+            bounds.append((name, b))
+    if not writes:
+        return None
+    return ElementwiseInfo(block, frozenset(reads), frozenset(writes), tuple(bounds))
+
+
 def ir_to_cuda(ir: IRModule) -> Lowered:
     """Lower validated, optimised IR to one CUDA kernel (plus an optional native plan)."""
     lowered = _Emitter(ir).run()
     from .patterns import match_native
 
     lowered.native = match_native(ir, lowered)
+    lowered.elementwise = elementwise_info(ir, lowered.block_size, lowered.mode)
     return lowered

@@ -477,6 +477,34 @@ extern "C" int eas_copy_device(void* dst, const void* src, size_t nbytes, void* 
                         "copy device->device", EAS_ERR_MEMORY);
 }
 
+extern "C" int eas_copy_from_host_async(void* dst, const void* src, size_t nbytes, void* stream) {
+  EAS_INJECT(kCopy, "eas_copy_from_host_async");
+  if (!nbytes) return EAS_OK;
+  return eas_cuda_check(cudaMemcpyAsync(dst, src, nbytes, cudaMemcpyHostToDevice, (cudaStream_t)stream),
+                        "copy host->device (async)", EAS_ERR_MEMORY);
+}
+
+extern "C" int eas_copy_to_host_async(void* dst, const void* src, size_t nbytes, void* stream) {
+  EAS_INJECT(kCopy, "eas_copy_to_host_async");
+  if (!nbytes) return EAS_OK;
+  return eas_cuda_check(cudaMemcpyAsync(dst, src, nbytes, cudaMemcpyDeviceToHost, (cudaStream_t)stream),
+                        "copy device->host (async)", EAS_ERR_MEMORY);
+}
+
+extern "C" int eas_host_is_pinned(const void* ptr, int* pinned) {
+  if (!pinned) return eas_fail(EAS_ERR_VALUE, "eas_host_is_pinned: null pointer");
+  *pinned = 0;
+  int rc = eas_driver_init();
+  if (rc) return rc;
+  cudaPointerAttributes at;
+  if (cudaPointerGetAttributes(&at, ptr) != cudaSuccess) {
+    cudaGetLastError();
+    return EAS_OK;
+  }
+  *pinned = at.type == cudaMemoryTypeHost ? 1 : 0;
+  return EAS_OK;
+}
+
 extern "C" int eas_memset_d8(void* dst, int value, size_t nbytes, void* stream) {
   if (!nbytes) return EAS_OK;
   return eas_cuda_check(cudaMemsetAsync(dst, value, nbytes, (cudaStream_t)stream), "memset", EAS_ERR_MEMORY);
@@ -535,6 +563,11 @@ extern "C" int eas_event_destroy(void* event) {
 
 extern "C" int eas_event_record(void* event, void* stream) {
   return eas_cuda_check(cudaEventRecord((cudaEvent_t)event, (cudaStream_t)stream), "cudaEventRecord",
+                        EAS_ERR_LAUNCH);
+}
+
+extern "C" int eas_stream_wait_event(void* stream, void* event) {
+  return eas_cuda_check(cudaStreamWaitEvent((cudaStream_t)stream, (cudaEvent_t)event, 0), "cudaStreamWaitEvent",
                         EAS_ERR_LAUNCH);
 }
 

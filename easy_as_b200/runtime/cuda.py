@@ -431,6 +431,10 @@ class CudaRuntime:
             return
         if not self.is_available():
             raise RuntimeError("CUDA runtime is not available: " + self._reason)
+        hosts = self._pipeline_candidates(ck, runtime_args, geo)
+        if hosts is not None:
+            self._run_pipelined(ck, runtime_args, geo, hosts)
+            return
         args, device, stream = self._resolve(ck, runtime_args)
         host_copies = [(a.dev_buf, a.host) for a in args.values() if a.host is not None]
         lib = self.lib()
@@ -461,6 +465,146 @@ class CudaRuntime:
         limit = self._max_flight()
         if limit and len(self._pending) > limit:
             self._wait_one()
+
+    # -- pipelined host-buffer path ----------------------------------------------------
+    PIPELINE_CHUNK_ELEMS = 1 << 23      # elements per operand per chunk (32 MiB of f32)
+    PIPELINE_SLOTS = 3
+
+    def _pipeline_candidates(self, ck: Any, runtime_args: Mapping[str, Any], geo: Any) -> dict[str, np.ndarray] | None:
+        """Host arrays of an elementwise kernel, when the pipelined copy path applies.
+
+        Applies when every buffer argument is a page-locked host array (a
+        pinned torch CPU tensor, or memory registered with CUDA), the kernel is
+        elementwise (program p touches only elements [p*BLOCK, (p+1)*BLOCK)),
+        the launch is 1D and the data is large enough to be worth splitting.
+        """
+        ew = getattr(ck.plan, "elementwise", None)
+        if ew is None or os.environ.get("EAS_PIPELINE", "1") in ("0", "off"):
+            return None
+        (gx, gy, gz), _ntx = geo
+        if gy != 1 or gz != 1:
+            return None
+        torch = _torch()
+        hosts: dict[str, np.ndarray] = {}
+        total = 0
+        lib = self.lib()
+        for a in ck.ir.args:
+            if a.kind != "buffer":
+                continue
+            v = runtime_args[a.name]
+            if torch is not None and isinstance(v, torch.Tensor):
+                if v.device.type != "cpu" or not v.is_contiguous():
+                    return None
+                v = v.detach().numpy()
+            elif getattr(v, "__eas_tensor__", False):
+                if v.device != "cpu":
+                    return None
+                v = v.numpy()
+            if not isinstance(v, np.ndarray) or not v.flags.c_contiguous:
+                return None
+            want = np.float32 if a.dtype == DType.F32 else np.float16
+            if v.dtype != want:
+                return None
+            pinned = cuda_ext.ctypes.c_int(0)
+            lib.eas_host_is_pinned(v.ctypes.data, cuda_ext.ctypes.byref(pinned))
+            if not pinned.value:
+                return None
+            hosts[a.name] = v
+            total += v.nbytes
+        if not hosts or total < int(os.environ.get("EAS_PIPELINE_MIN_BYTES", str(64 << 20))):
+            return None
+        return hosts
+
+    def _streams(self, device: int) -> tuple[int, int, int]:
+        key = ("pipeline_streams", device)
+        st = self._pipelines.get(key)  # type: ignore[arg-type]
+        if st is None:
+            lib = self.lib()
+            out = []
+            for _ in range(3):
+                h = cuda_ext.ctypes.c_void_p()
+                cuda_ext.check(lib.eas_stream_create(device, cuda_ext.ctypes.byref(h)), "stream_create")
+                out.append(int(h.value))
+            st = tuple(out)
+            self._pipelines[key] = st  # type: ignore[index]
+        return st  # type: ignore[return-value]
+
+    def _run_pipelined(self, ck: Any, runtime_args: Mapping[str, Any], geo: Any, hosts: dict[str, np.ndarray]) -> None:
+        """H2D copy, kernel and D2H copy of successive program ranges overlap on three streams.
+
+        Buffers the kernel never loads are not copied in; only the elements a
+        store can reach (below its mask bound) are copied back, so host
+        elements the kernel leaves alone are untouched.  Returns after the
+        last copy has landed (the launch is synchronous).
+        """
+        ew = ck.plan.elementwise
+        (gx, _, _), ntx = geo
+        B = ew.block
+        device = self.default_device()
+        lib = self.lib()
+        s_in, s_run, s_out = self._streams(device)
+        progs = max(1, self.PIPELINE_CHUNK_ELEMS // B)
+        chunk = progs * B
+        distinct: dict[tuple[int, int], tuple[np.ndarray, bool, bool, list[str]]] = {}
+        for name, arr in hosts.items():
+            arr_id = (arr.ctypes.data, arr.nbytes)  # the same memory passed twice is staged once
+            _, r, w, names = distinct.get(arr_id, (arr, False, False, []))
+            distinct[arr_id] = (arr, r or name in ew.reads, w or name in ew.writes, names + [name])
+        write_limit: dict[str, int] = {}
+        for name, b in ew.store_bounds:
+            lim = hosts[name].size if b is None else (
+                int(runtime_args[b[1]]) if b[0] == "arg" else int(b[1]))
+            write_limit[name] = max(write_limit.get(name, 0), min(lim, hosts[name].size))
+        R = self.PIPELINE_SLOTS
+        slots: dict[tuple[int, int], list[DeviceBuffer]] = {}
+        for key, (arr, _r, _w, _n) in distinct.items():
+            slots[key] = [self._stage(device, chunk * arr.itemsize) for _ in range(R)]
+        evs = []
+        for _ in range(3 * R):
+            e = cuda_ext.ctypes.c_void_p()
+            cuda_ext.check(lib.eas_event_create(cuda_ext.ctypes.byref(e)), "event_create")
+            evs.append(int(e.value))
+        ev_in, ev_run, ev_free = evs[:R], evs[R:2 * R], evs[2 * R:]
+        try:
+            for i, p0 in enumerate(range(0, gx, progs)):
+                p1 = min(gx, p0 + progs)
+                s = i % R
+                lo = p0 * B
+                if i >= R:
+                    cuda_ext.check(lib.eas_stream_wait_event(s_in, ev_free[s]), "stream_wait_event")
+                for key, (arr, reads, _w, _n) in distinct.items():
+                    n = min(p1 * B, arr.size) - lo
+                    if reads and n > 0:
+                        cuda_ext.check(lib.eas_copy_from_host_async(slots[key][s].ptr, arr.ctypes.data + lo * arr.itemsize,
+                                                                    n * arr.itemsize, s_in), "pipelined copy in")
+                cuda_ext.check(lib.eas_event_record(ev_in[s], s_in), "event_record")
+                cuda_ext.check(lib.eas_stream_wait_event(s_run, ev_in[s]), "stream_wait_event")
+                args = {}
+                for key, (arr, _r, _w, names) in distinct.items():
+                    for name in names:
+                        args[name] = _Arg(slots[key][s].ptr - lo * arr.itemsize, device)
+                self._launch_generic(ck, runtime_args, args, device, s_run, (p1 - p0, 1, 1), ntx, (p0, 0, 0))
+                cuda_ext.check(lib.eas_event_record(ev_run[s], s_run), "event_record")
+                cuda_ext.check(lib.eas_stream_wait_event(s_out, ev_run[s]), "stream_wait_event")
+                for key, (arr, _r, writes, names) in distinct.items():
+                    if not writes:
+                        continue
+                    lim = max(write_limit.get(nm, 0) for nm in names)
+                    n = min(p1 * B, lim) - lo
+                    if n > 0:
+                        cuda_ext.check(lib.eas_copy_to_host_async(arr.ctypes.data + lo * arr.itemsize, slots[key][s].ptr,
+                                                                  n * arr.itemsize, s_out), "pipelined copy out")
+                cuda_ext.check(lib.eas_event_record(ev_free[s], s_out), "event_record")
+            cuda_ext.check(lib.eas_stream_synchronize(s_out), "kernel execution")
+            cuda_ext.check(lib.eas_stream_synchronize(s_run), "kernel execution")
+        finally:
+            for e in evs:
+                lib.eas_event_destroy(e)
+            for key, bufs in slots.items():
+                for b in bufs:
+                    free = self._staging.setdefault((b.device, b.nbytes), [])
+                    if len(free) < 4 * R:
+                        free.append(b)
 
     def run_range(self, ck: Any, runtime_args: Mapping[str, Any], meta: Mapping[str, Any], *, axis: int,
                   lo: int, hi: int, grid: tuple[int, int, int] | None = None, nthreads: int | None = None,

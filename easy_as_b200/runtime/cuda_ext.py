@@ -55,6 +55,10 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "eas_copy_to_host": (_int, [_vp, _vp, _sz, _vp]),
     "eas_copy_device": (_int, [_vp, _vp, _sz, _vp]),
     "eas_memset_d8": (_int, [_vp, _int, _sz, _vp]),
+    "eas_copy_from_host_async": (_int, [_vp, _vp, _sz, _vp]),
+    "eas_copy_to_host_async": (_int, [_vp, _vp, _sz, _vp]),
+    "eas_host_is_pinned": (_int, [_vp, _PINT]),
+    "eas_stream_wait_event": (_int, [_vp, _vp]),
     "eas_stream_synchronize": (_int, [_vp]),
     "eas_device_synchronize": (_int, [_int]),
     "eas_stream_is_capturing": (_int, [_vp, _PINT]),

@@ -101,6 +101,12 @@ int eas_copy_to_host(void* dst, const void* src, size_t nbytes, void* stream);
 /* device -> device (same or peer device over NVLink), asynchronous */
 int eas_copy_device(void* dst, const void* src, size_t nbytes, void* stream);
 int eas_memset_d8(void* dst, int value, size_t nbytes, void* stream);
+/* Asynchronous host <-> device copies for page-locked host memory: they return
+ * at once; the host buffer must stay untouched until the stream reaches them. */
+int eas_copy_from_host_async(void* dst, const void* src, size_t nbytes, void* stream);
+int eas_copy_to_host_async(void* dst, const void* src, size_t nbytes, void* stream);
+/* *pinned = 1 when `ptr` lies in page-locked host memory known to CUDA. */
+int eas_host_is_pinned(const void* ptr, int* pinned);
 
 /* ---- synchronisation (replaces synchronize / queue_synchronize,
  *      _metal.mm:1397-1434) ------------------------------------------------ */
@@ -114,6 +120,8 @@ int eas_stream_destroy(void* stream);
 int eas_event_create(void** event);
 int eas_event_destroy(void* event);
 int eas_event_record(void* event, void* stream);
+/* Make `stream` wait (on the device) until `event` has completed. */
+int eas_stream_wait_event(void* stream, void* event);
 int eas_event_synchronize(void* event);
 /* 1 if complete, 0 if pending */
 int eas_event_query(void* event, int* done);
