@@ -196,7 +196,7 @@ def run_gemm(name: str, args, world: int, rank: int, rt) -> dict:
     """fp16 mk.dot GEMM (examples/matmul_dot_f16.py) on this rank's shard; TFLOP/s aggregated over ranks."""
     import torch
 
-    from examples.matmul_dot_f16 import grid, matmul_dot_f16
+    from examples.matmul_dot_f16 import grid, matmul_dot_f16_tuned
 
     batch, M, N, K = gemm_shard(name, world, rank)
     tb, TM, TN, TK, split = GEMM_CONFIGS[name]
@@ -204,14 +204,15 @@ def run_gemm(name: str, args, world: int, rank: int, rt) -> dict:
     a = (torch.randn(batch, M, K, device="cuda", generator=g) / K ** 0.5).half()
     b = (torch.randn(batch, K, N, device="cuda", generator=g) / K ** 0.5).half()
     c = torch.empty(batch, M, N, device="cuda")
-    bn = 256
 
     def step(sync=False):
-        matmul_dot_f16(a.reshape(-1), b.reshape(-1), c.reshape(-1), M, N, K, BLOCK_M=128, BLOCK_N=bn, BLOCK_K=64,
-                       _grid=grid(batch), _sync=sync)
+        # autotuned over BLOCK_M/N in {128, 256} x BLOCK_K in {64, 128} (first call per shape tunes)
+        matmul_dot_f16_tuned(a.reshape(-1), b.reshape(-1), c.reshape(-1), M, N, K, _grid=grid(batch), _sync=sync)
 
     native0 = rt.native_launches
     step(sync=True)
+    cfg = matmul_dot_f16_tuned._tuned_cache.get((M, N, K))
+    tuned = dict(cfg.meta) if cfg is not None else {}
     if rt.native_launches == native0:
         raise SystemExit(f"bench: {name} did not take the tcgen05 path")
     # parity spot check: rows 0..3 of the first batch against float64
@@ -247,7 +248,8 @@ def run_gemm(name: str, args, world: int, rank: int, rt) -> dict:
         "metric": "fp16 mk.dot GEMM TFLOP/s", "value": round(flops_total / (ms_max * 1e-3) / 1e12, 1),
         "unit": "TFLOP/s", "ms_per_step": round(ms_max, 4), "steps": steps,
         "config": {"workload": f"{name} batch={tb} M={TM} N={TN} K={TK} f16 in, f32 acc/out", "split": split,
-                   "kernel": "tcgen05 cta_group::2 (CTA pair), tile 256x256x64, 6 stages", "spot_check_rel_err": err},
+                   "kernel": ("tcgen05 cta_group::2 (CTA pair), tile 256x256x64, 6 stages" if tuned.get("BLOCK_N") == 256
+                              else "tcgen05 cta_group::1, tile 128x128x64, 6 stages"), "autotuned": tuned, "spot_check_rel_err": err},
         "roofline": {"bound": "tensor", "achieved": round(local_tf, 1), "peak": pk["bf16_tflops"],
                      "unit": "TFLOP/s", "frac": round(local_tf / pk["bf16_tflops"], 4),
                      "peak_source": ("measured burst cuBLAS bf16 (MEASURED_PEAKS.json bf16_tflops)"

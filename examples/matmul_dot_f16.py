@@ -26,7 +26,8 @@ def _cdiv(a, b):
 
 
 @eas.kernel
-def matmul_dot_f16(a, b, c, M, N, K, BLOCK_M: eas.constexpr, BLOCK_N: eas.constexpr, BLOCK_K: eas.constexpr):
+def matmul_dot_f16(a, b, c, M, N, K, BLOCK_M: eas.constexpr = 128, BLOCK_N: eas.constexpr = 256,
+                   BLOCK_K: eas.constexpr = 64):
     col = mk.program_id(0) * BLOCK_N + mk.tid(0, BLOCK_N)
     row = mk.program_id(1)
     bat = mk.program_id(2)
