@@ -319,7 +319,7 @@ class _Emitter:
         src = "\n".join([
             f"// generated by easy_as_b200.codegen.cuda for sm_100a ({self.mode} mode, BLOCK={self.block})",
             PRELUDE,
-            f'extern "C" __global__ void __launch_bounds__({self.cuda_threads}) {name}(',
+            f'extern "C" __global__ void __launch_bounds__({self.cuda_threads}, {self._min_blocks()}) {name}(',
             "    " + self.signature() + ") {",
             *body,
             "}",
@@ -327,6 +327,14 @@ class _Emitter:
         ])
         return Lowered(src=src, kernel_name=name, block_size=self.block, mode=self.mode,
                        cuda_threads=self.cuda_threads, params=self.params(), dyn_smem=self.smem)
+
+    def _min_blocks(self) -> int:
+        """CTAs per SM to plan registers for: enough for 2048 resident threads (<= 64 registers each),
+        as far as the block's shared memory allows."""
+        want = max(1, 2048 // self.cuda_threads)
+        if self.smem:
+            want = min(want, max(1, (200 * 1024) // self.smem))
+        return min(want, 32)
 
     def _smem_decls(self) -> None:
         if not self.tg:
@@ -610,7 +618,7 @@ class _Emitter:
             self.emit(f"uint32_t bi{n} = {self.name(d.args[4])};", 2)
         kd = self.defs.get(k_ref.id)
         if kd is not None and kd.op == "const" and 1 <= int(kd.args[0]) <= 32:
-            self.emit("#pragma unroll", 2)
+            self.emit("#pragma unroll 4", 2)
         self.emit(f"for (uint32_t k = 0; k < {self.name(k_ref)}; ++k) {{", 2)
         A, B = self.name(a_buf), self.name(b_buf)
         self.emit(f"const float av = {_as_float(a_buf.dtype, f'{A}[ai]')};", 3)

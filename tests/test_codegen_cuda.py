@@ -21,7 +21,7 @@ def src(cid):
 def test_spmd_program_is_a_cta_with_vector_accesses():
     s = src("add_c1")
     assert "blockIdx.x + eas_pid_x" in s
-    assert "float4" in s and "__launch_bounds__(64)" in s  # 256 lanes = 64 threads x 4
+    assert "float4" in s and "__launch_bounds__(64, 32)" in s  # 256 lanes = 64 threads x 4
 
 
 def test_f16_buffers_are_half_bit_patterns():
