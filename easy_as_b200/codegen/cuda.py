@@ -76,6 +76,7 @@ class Lowered:
     native: Any = field(default=None)   # pattern-lowered native plan (see codegen.patterns)
     elementwise: Any = field(default=None)  # ElementwiseInfo when program p touches only elements [p*B, p*B+B)
     layout: Any = field(default=None)   # runtime parameter layout, built on first launch
+    grid_rank: Any = field(default=None)  # 1 + highest program_id/thread_id axis, cached by the runtime
 
 
 HIDDEN = ("eas_ntx", "eas_pid_x", "eas_pid_y", "eas_pid_z")

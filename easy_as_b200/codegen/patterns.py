@@ -241,7 +241,7 @@ class DotGemmPlan:
                    stream: int, programs: tuple[int, int, int], ntx: int) -> bool:
         import os
 
-        if os.environ.get("EAS_DISABLE_NATIVE", "") not in ("", "0"):
+        if os.environ.get("EAS_DISABLE_NATIVE", "0") not in ("", "0"):
             self.last_reason = "disabled by EAS_DISABLE_NATIVE"
             return False
         scalars = {f"${a.name}": int(runtime_args[a.name]) for a in self.ir.args if a.kind == "scalar"}

@@ -123,6 +123,25 @@ def _arg_sig(v: Any) -> RuntimeArgSig:
     return RuntimeArgSig("scalar", scalar_dtype(v), None)
 
 
+_SCALAR_SIGS = {bool: ("scalar", DType.BOOL, None), int: ("scalar", DType.U32, None),
+                float: ("scalar", DType.F32, None)}
+
+
+def fast_arg_sig(v: Any) -> tuple[Any, ...]:
+    """(kind, dtype, device) of one runtime argument; the launch-path form of ``_arg_sig``."""
+    s = _SCALAR_SIGS.get(type(v))
+    if s is not None:
+        return s
+    t = _torch()
+    if t is not None and isinstance(v, t.Tensor):
+        if v.dtype == t.float32:
+            return ("buffer", DType.F32, v.device.type)
+        if v.dtype == t.float16:
+            return ("buffer", DType.F16, v.device.type)
+    sig = _arg_sig(v)
+    return (sig.kind, sig.dtype, sig.device)
+
+
 def runtime_arg_signature(runtime_args: Mapping[str, Any]) -> tuple[tuple[str, Any], ...]:
     """Cache key part for runtime arguments: kinds/dtypes/devices, never scalar values."""
     return tuple(sorted((name, (s.kind, s.dtype, s.device))

@@ -20,7 +20,7 @@ import inspect
 from typing import Any, Callable, Mapping
 
 from .autotune import AutotuneSpec, Config
-from .compiler import CompiledKernel, compile as _compile, runtime_arg_signature
+from .compiler import CompiledKernel, compile as _compile, fast_arg_sig, runtime_arg_signature
 from .meta import constexpr
 from .runtime import get_runtime
 
@@ -52,6 +52,12 @@ class Kernel:
         self.meta_params = {n for n, p in self.sig.parameters.items()
                             if ann.get(n, p.annotation) is constexpr}
         self._cache: dict[tuple[Any, Any], CompiledKernel] = {}
+        # fast argument binding when every parameter is a plain positional-or-keyword one
+        kinds = {p.kind for p in self.sig.parameters.values()}
+        self._simple = kinds <= {inspect.Parameter.POSITIONAL_OR_KEYWORD}
+        self._names = tuple(self.sig.parameters)
+        self._name_set = frozenset(self._names)
+        self._defaults = {n: p.default for n, p in self.sig.parameters.items() if p.default is not p.empty}
         self._autotune_spec: AutotuneSpec | None = None
         self._tuned_cache: dict[tuple[Any, ...], Config] = {}
 
@@ -172,7 +178,10 @@ class Kernel:
 
     # -- compile / launch -----------------------------------------------------------
     def _compile_from_split(self, meta: dict[str, Any], runtime_args: dict[str, Any]) -> CompiledKernel:
-        key = (tuple(sorted(meta.items())), runtime_arg_signature(runtime_args))
+        # kinds/dtypes/devices of the runtime args, never scalar values (same distinctions as
+        # runtime_arg_signature, computed without sorting on the launch path)
+        key = (tuple(sorted(meta.items())) if len(meta) > 1 else tuple(meta.items()),
+               tuple((n, fast_arg_sig(v)) for n, v in runtime_args.items()))
         ck = self._cache.get(key)
         if ck is None:
             ck = _compile(self.fn, runtime_args, meta)
@@ -180,7 +189,27 @@ class Kernel:
         return ck
 
     def _bind_and_split(self, /, *args: Any, **kwargs: Any) -> tuple[dict[str, Any], dict[str, Any]]:
-        bound = self.sig.bind(*args, **kwargs)
+        if self._simple and len(args) <= len(self._names):
+            values = dict(zip(self._names, args))
+            ok = True
+            for k, v in kwargs.items():
+                if k not in self._name_set or k in values:
+                    ok = False
+                    break
+                values[k] = v
+            if ok:
+                for n in self._names[len(args):]:
+                    if n not in values:
+                        if n not in self._defaults:
+                            ok = False
+                            break
+                        values[n] = self._defaults[n]
+            if ok:
+                meta, rt = {}, {}
+                for n in self._names:
+                    (meta if n in self.meta_params else rt)[n] = values[n]
+                return meta, rt
+        bound = self.sig.bind(*args, **kwargs)  # slow path: produces the standard error messages
         bound.apply_defaults()
         meta = {k: bound.arguments.pop(k) for k in list(bound.arguments) if k in self.meta_params}
         return meta, dict(bound.arguments)

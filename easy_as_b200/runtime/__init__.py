@@ -29,6 +29,8 @@ def _cuda_runtime() -> Any:
 
 def get_runtime(backend: str | None = None) -> Runtime:
     name = (backend or os.environ.get("EAS_BACKEND", "auto")).lower()
+    if name in ("auto", "cuda") and _cuda is not None and _cuda._available:
+        return _cuda  # launch-path shortcut: already probed and available
     if name in ("auto", "cuda"):
         rt = _cuda_runtime()
         if not rt.is_available():

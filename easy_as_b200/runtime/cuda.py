@@ -38,7 +38,7 @@ import numpy as np
 
 from ..ir import DType
 from . import cuda_ext
-from .grid import infer_1d_grid, infer_grid, infer_nthreads
+from .grid import grid_rank, infer_1d_grid, infer_grid, infer_nthreads
 
 ALL_THREADS = 0xFFFFFFFF
 MAX_GRID_YZ = 65535
@@ -119,17 +119,25 @@ class ParamLayout:
         self.size = -(-off // 8) * 8
         self.offsets = (cuda_ext.ctypes.c_uint32 * max(len(self.entries), 1))(*[o for _p, o, _f in self.entries])
         self.count = len(self.entries)
+        # one struct for the whole block: explicit pad bytes reproduce the natural alignment above
+        fmt, pos = "<", 0
+        for _p, o, f in self.entries:
+            fmt += "x" * (o - pos) + f[1:]
+            pos = o + struct.calcsize(f)
+        fmt += "x" * (self.size - pos)
+        self._struct = struct.Struct(fmt)
+        self.block = None  # ctypes uint32[3] of the CUDA block shape, set by the runtime
 
-    def pack(self, values: Mapping[str, Any], pointers: Mapping[str, int], hidden: Mapping[str, int]) -> bytearray:
-        buf = bytearray(self.size)
-        for p, off, fmt in self.entries:
+    def pack(self, values: Mapping[str, Any], pointers: Mapping[str, int], hidden: Mapping[str, int]) -> bytes:
+        vals = []
+        for p, _off, _fmt in self.entries:
             if p.kind == "buffer":
-                struct.pack_into(fmt, buf, off, pointers[p.arg])
+                vals.append(pointers[p.arg])
             elif p.kind == "hidden":
-                struct.pack_into(fmt, buf, off, hidden[p.name])
+                vals.append(hidden[p.name])
             else:
-                struct.pack_into(fmt, buf, off, _scalar_bits(p.dtype, values[p.arg], p.arg))
-        return buf
+                vals.append(_scalar_bits(p.dtype, values[p.arg], p.arg))
+        return self._struct.pack(*vals)
 
 
 def _scalar_bits(dt: DType, v: Any, name: str) -> Any:
@@ -165,7 +173,11 @@ def launch_geometry(ck: Any, runtime_args: Mapping[str, Any], *, nthreads: int |
         raise ValueError(f"tptg must match kernel launch mode: expected {expected}, "
                          f"got ({tptg[0]}, {tptg[1]}, {tptg[2]})")
     if grid is None:
-        inferred = infer_grid(ck.ir, runtime_args, bs, shape=shape)
+        plan = getattr(ck, "plan", None)
+        rank = getattr(plan, "grid_rank", None) if plan is not None else None
+        if plan is not None and rank is None:
+            rank = plan.grid_rank = grid_rank(ck.ir)
+        inferred = infer_grid(ck.ir, runtime_args, bs, shape=shape, rank=rank)
         if inferred is None:
             n = infer_nthreads(runtime_args, nthreads=nthreads)
             if n == 0:
@@ -211,9 +223,14 @@ class CudaRuntime:
         self._available: bool | None = None
         self._reason = ""
         self._pipelines: dict[tuple[str, str, int, int], int] = {}
-        self._pending: deque[tuple[int, Any]] = deque()
+        self._pending: deque[tuple[int, int, Any]] = deque()
         self._max_in_flight: int | None = None
         self._staging: dict[tuple[int, int], list[DeviceBuffer]] = {}
+        self._bucket_keep: list[Any] = []
+        self._pending_n = 0
+        self._bucket_n = 0
+        self._bucket_stream = 0
+        self._event_pool: list[int] = []
         self.launch_count = 0  # kernels launched through this runtime (generic + native)
         self.native_launches = 0  # of which pattern-lowered native kernels
 
@@ -315,6 +332,16 @@ class CudaRuntime:
                 continue
             v = runtime_args[a.name]
             want = np.float32 if a.dtype == DType.F32 else np.float16
+            if torch is not None and type(v) is torch.Tensor and v.is_cuda and not v.requires_grad:
+                # common case first: a contiguous CUDA tensor of the right dtype
+                if v.dtype == (torch.float32 if a.dtype == DType.F32 else torch.float16) and v.is_contiguous():
+                    dev = v.get_device()
+                    if device is not None and dev != device:
+                        raise ValueError(f"buffers on different devices: {device} and {dev}")
+                    device = dev
+                    resolved[a.name] = _Arg(v.data_ptr(), dev, keep=v)
+                    torch_stream = True
+                    continue
             if torch is not None and isinstance(v, torch.Tensor):
                 t = v.detach()
                 tdt = torch.float32 if a.dtype == DType.F32 else torch.float16
@@ -361,7 +388,8 @@ class CudaRuntime:
             device = self.default_device()
         stream = 0
         if torch_stream and torch is not None:
-            stream = int(torch.cuda.current_stream(device).cuda_stream)
+            raw = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+            stream = int(raw(device)) if raw is not None else int(torch.cuda.current_stream(device).cuda_stream)
         # host arrays: one temporary device buffer per distinct array object
         staged: dict[int, DeviceBuffer] = {}
         for name, arr in host_pending:
@@ -400,18 +428,18 @@ class CudaRuntime:
         layout = plan.layout
         if layout is None:
             layout = plan.layout = ParamLayout(plan.params)
+            layout.block = (cuda_ext.ctypes.c_uint32 * 3)(plan.cuda_threads, 1, 1)
         ptrs = {n: a.ptr for n, a in args.items()}
         lib = self.lib()
         gx, gy, gz = programs
-        block = (cuda_ext.ctypes.c_uint32 * 3)(plan.cuda_threads, 1, 1)
+        block = layout.block
         for z0 in range(0, gz, MAX_GRID_YZ):
             for y0 in range(0, gy, MAX_GRID_YZ):
                 hidden = {"eas_ntx": ntx, "eas_pid_x": pid_base[0], "eas_pid_y": pid_base[1] + y0,
                           "eas_pid_z": pid_base[2] + z0}
                 blob = layout.pack(runtime_args, ptrs, hidden)
-                cblob = (cuda_ext.ctypes.c_char * len(blob)).from_buffer(blob)
                 g = (cuda_ext.ctypes.c_uint32 * 3)(gx, min(MAX_GRID_YZ, gy - y0), min(MAX_GRID_YZ, gz - z0))
-                cuda_ext.check(lib.eas_launch(pipe, g, block, plan.dyn_smem, stream, cblob, layout.offsets, layout.count),
+                cuda_ext.check(lib.eas_launch(pipe, g, block, plan.dyn_smem, stream, blob, layout.offsets, layout.count),
                                f"launch {plan.kernel_name}")
                 self.launch_count += 1
 
@@ -458,13 +486,54 @@ class CudaRuntime:
                     done.add(id(arr))
             self._unstage(args)
             return
-        ev = cuda_ext.ctypes.c_void_p()
-        cuda_ext.check(lib.eas_event_create(cuda_ext.ctypes.byref(ev)), "event_create")
-        cuda_ext.check(lib.eas_event_record(ev, stream), "event_record")
-        self._pending.append((int(ev.value), (args, runtime_args)))
+        # asynchronous launch: keep the arguments alive until a completion event covers it.
+        # One (pooled) event per group of launches; at most EAS_MAX_IN_FLIGHT stay unfinished.
+        if self._bucket_n and stream != self._bucket_stream:
+            self._close_bucket()
+        self._bucket_keep.append((args, runtime_args))
+        self._bucket_n += 1
+        self._bucket_stream = stream
         limit = self._max_flight()
-        if limit and len(self._pending) > limit:
+        if self._bucket_n >= (max(1, limit // 16) if limit else 64):
+            self._close_bucket()
+        while limit and self.in_flight() > limit:
+            if not self._pending:
+                self._close_bucket()
             self._wait_one()
+
+    def _close_bucket(self) -> None:
+        if not self._bucket_n:
+            return
+        lib = self.lib()
+        if self._event_pool:
+            ev = self._event_pool.pop()
+        else:
+            e = cuda_ext.ctypes.c_void_p()
+            cuda_ext.check(lib.eas_event_create(cuda_ext.ctypes.byref(e)), "event_create")
+            ev = int(e.value)
+        cuda_ext.check(lib.eas_event_record(ev, self._bucket_stream), "event_record")
+        self._pending.append((ev, self._bucket_n, self._bucket_keep))
+        self._pending_n += self._bucket_n
+        self._bucket_keep, self._bucket_n = [], 0
+
+    def _wait_one(self) -> None:
+        ev, n, _keep = self._pending.popleft()
+        self._pending_n -= n
+        try:
+            cuda_ext.check(self.lib().eas_event_synchronize(ev), "kernel execution")
+        finally:
+            self._event_pool.append(ev)
+
+    def synchronize(self) -> None:
+        self._close_bucket()
+        while self._pending:
+            self._wait_one()
+        if self.native_launches:
+            for dev in range(8):
+                self._check_native_status(dev)
+
+    def in_flight(self) -> int:
+        return self._pending_n + self._bucket_n
 
     # -- pipelined host-buffer path ----------------------------------------------------
     PIPELINE_CHUNK_ELEMS = 1 << 23      # elements per operand per chunk (32 MiB of f32)
@@ -479,12 +548,17 @@ class CudaRuntime:
         the launch is 1D and the data is large enough to be worth splitting.
         """
         ew = getattr(ck.plan, "elementwise", None)
-        if ew is None or os.environ.get("EAS_PIPELINE", "1") in ("0", "off"):
+        if ew is None:
+            return None
+        torch = _torch()
+        first = next((runtime_args[a.name] for a in ck.ir.args if a.kind == "buffer"), None)
+        if torch is not None and type(first) is torch.Tensor and first.is_cuda:
+            return None  # device tensors: nothing to copy
+        if os.environ.get("EAS_PIPELINE", "1") in ("0", "off"):
             return None
         (gx, gy, gz), _ntx = geo
         if gy != 1 or gz != 1:
             return None
-        torch = _torch()
         hosts: dict[str, np.ndarray] = {}
         total = 0
         lib = self.lib()
@@ -644,21 +718,6 @@ class CudaRuntime:
         if sync:
             cuda_ext.check(self.lib().eas_stream_synchronize(stream), "kernel execution")
 
-    def _wait_one(self) -> None:
-        ev, _keep = self._pending.popleft()
-        lib = self.lib()
-        try:
-            cuda_ext.check(lib.eas_event_synchronize(ev), "kernel execution")
-        finally:
-            lib.eas_event_destroy(ev)
-
-    def synchronize(self) -> None:
-        while self._pending:
-            self._wait_one()
-        if self.native_launches:
-            for dev in range(8):
-                self._check_native_status(dev)
-
     def _check_native_status(self, device: int) -> None:
         if not self.native_launches:
             return
@@ -667,9 +726,6 @@ class CudaRuntime:
         if code.value:
             raise RuntimeError(f"native kernel on device {device} reported status {code.value} "
                                "(a bounded pipeline wait expired; results are incomplete)")
-
-    def in_flight(self) -> int:
-        return len(self._pending)
 
     # -- timing ---------------------------------------------------------------------------
     def benchmark(self, ck: Any, runtime_args: Mapping[str, Any], meta: Mapping[str, Any], *, repeat: int,

@@ -46,8 +46,10 @@ def grid_rank(ir: IRModule) -> int:
 
 
 def infer_grid(ir: IRModule, runtime_args: Mapping[str, Any], threadgroup_size: int, *,
-               shape: tuple[int, ...] | None = None) -> tuple[int, int, int] | None:
-    rank = grid_rank(ir)
+               shape: tuple[int, ...] | None = None, rank: int | None = None) -> tuple[int, int, int] | None:
+    """``rank`` may pass a precomputed ``grid_rank(ir)`` (the runtime caches it per kernel)."""
+    if rank is None:
+        rank = grid_rank(ir)
     if rank <= 1:
         return None
     if rank > 3:
