@@ -1,0 +1,84 @@
+"""Parity at the BASELINE configurations' full sizes, through size-independent properties.
+
+C2: N = 2^28 f32 add, bit-exact against c = a + b.
+C3: the reference's unmodified tiled fp32 kernel (IR from the reference front end, K = 2048
+    constexpr, 32x32x32 tiles, NT = 256): bit-exact against the CPU oracle on a one-tile launch
+    of the same IR, and the full 2048^3 product within rtol 1e-4 of float64 (north_star bar).
+C4/C5: the fp16 mk.dot GEMM at 8192^3 and 64 x 4096 x 4096 x 2088, sampled rows against
+    float64 (rtol 2e-2 is the north_star bar; the tensor-core result holds 1e-5 * sqrt(K/2048) normwise).
+"""
+
+import numpy as np
+import pytest
+
+import goldens
+from easy_as_b200.compiler import compile_ir
+from examples.matmul_dot_f16 import grid, matmul_dot_f16
+from oracle.interp import execute
+
+pytestmark = pytest.mark.gpu
+
+
+def test_c2_add_full_size(cuda_rt):
+    import torch
+
+    c = goldens.case("add_block1024")
+    ck = compile_ir(goldens.ir_from_json(c["opt"]))
+    n = 1 << 28
+    g = torch.Generator(device="cuda").manual_seed(1)
+    a = torch.randn(n, device="cuda", generator=g)
+    b = torch.randn(n, device="cuda", generator=g)
+    out = torch.empty_like(a)
+    cuda_rt.run(ck, {"a": a, "b": b, "c": out, "N": n}, {"BLOCK": 1024})
+    assert torch.equal(out, a + b)
+
+
+def test_c3_tiled_fp32_one_tile_bit_exact(cuda_rt):
+    c = goldens.case("matmul_tiled_c3_full")
+    ir = goldens.ir_from_json(c["opt"])
+    ck = compile_ir(ir)
+    M = N = 32
+    K = 2048
+    rng = np.random.default_rng(2)
+    a = rng.uniform(-1, 1, M * K).astype(np.float32)
+    b = rng.uniform(-1, 1, K * N).astype(np.float32)
+    gpu = np.zeros(M * N, np.float32)
+    cpu = np.zeros(M * N, np.float32)
+    cuda_rt.run(ck, {"a": a, "b": b, "c": gpu, "M": M, "N": N}, c["meta"], grid=(1, 1, 1))
+    execute(ir, {"a": a, "b": b, "c": cpu, "M": M, "N": N}, grid=(1, 1, 1))
+    np.testing.assert_array_equal(gpu, cpu)
+
+
+def test_c3_tiled_fp32_full_size(cuda_rt):
+    import torch
+
+    c = goldens.case("matmul_tiled_c3_full")
+    ck = compile_ir(goldens.ir_from_json(c["opt"]))
+    M = N = K = 2048
+    g = torch.Generator(device="cuda").manual_seed(2)
+    a = torch.rand(M * K, device="cuda", generator=g) * 2 - 1
+    b = torch.rand(K * N, device="cuda", generator=g) * 2 - 1
+    out = torch.zeros(M * N, device="cuda")
+    cuda_rt.run(ck, {"a": a, "b": b, "c": out, "M": M, "N": N}, c["meta"], grid=(64, 64, 1))
+    ref = a.double().reshape(M, K) @ b.double().reshape(K, N)
+    torch.testing.assert_close(out.double().reshape(M, N), ref, rtol=1e-4, atol=1e-4)
+
+
+@pytest.mark.parametrize("batch,M,N,K", [(1, 8192, 8192, 8192), (64, 4096, 4096, 2088)])
+def test_fp16_gemm_full_size_sampled(cuda_rt, batch, M, N, K):
+    import torch
+
+    g = torch.Generator(device="cuda").manual_seed(3)
+    a = (torch.randn(batch, M, K, device="cuda", generator=g) / K ** 0.5).half()
+    b = (torch.randn(batch, K, N, device="cuda", generator=g) / K ** 0.5).half()
+    c = torch.empty(batch, M, N, device="cuda")
+    before = cuda_rt.native_launches
+    matmul_dot_f16(a.reshape(-1), b.reshape(-1), c.reshape(-1), M, N, K, _grid=grid(batch))
+    assert cuda_rt.native_launches == before + 1
+    rows = torch.tensor([0, 1, M // 2, M - 1], device="cuda")
+    for bi in sorted({0, batch // 2, batch - 1}):
+        ref = a[bi, rows].double() @ b[bi].double()
+        got = c[bi, rows].double()
+        torch.testing.assert_close(got, ref, rtol=2e-2, atol=2e-2 * ref.abs().max().item())
+        # f32 accumulation error grows like sqrt(K): 1e-5 normwise at K = 2048
+        assert ((got - ref).abs().max() / ref.abs().max()).item() <= 1e-5 * max(1.0, (K / 2048) ** 0.5)
