@@ -532,6 +532,13 @@ class CudaRuntime:
             for dev in range(8):
                 self._check_native_status(dev)
 
+    def stream_wait_pending(self, stream: int) -> None:
+        """Make ``stream`` wait (device side, no host block) for every launch queued so far."""
+        self._close_bucket()
+        lib = self.lib()
+        for ev, _n, _keep in self._pending:
+            cuda_ext.check(lib.eas_stream_wait_event(stream, ev), "stream_wait_event")
+
     def in_flight(self) -> int:
         return self._pending_n + self._bucket_n
 

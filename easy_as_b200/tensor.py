@@ -169,10 +169,23 @@ class Tensor:
 
     # -- DLPack ----------------------------------------------------------------------
     def __dlpack__(self, stream: Any | None = None, **_kw: Any) -> Any:
-        _ = stream
+        """Export for a DLPack consumer.
+
+        CUDA tensors: with ``stream=None`` all queued launches are waited for on
+        the host.  With a consumer stream (DLPack convention: 1 = legacy default
+        stream, 2 = per-thread default stream, otherwise a ``cudaStream_t``) the
+        consumer stream is made to wait on the device for every queued launch,
+        so the export does not block the host; ``stream=-1`` asks for no
+        synchronisation at all.
+        """
         if self._device == "cpu":
             return self._cpu.__dlpack__()  # type: ignore[union-attr]
-        _runtime().synchronize()
+        rt = _runtime()
+        if stream is None:
+            rt.synchronize()
+        elif int(stream) != -1:
+            s = int(stream)
+            rt.stream_wait_pending({1: 0, 2: 2}.get(s, s))
         return export_capsule(self._cuda.ptr, self._shape, self._dtype.itemsize, KDL_CUDA, self._cuda.device, self)
 
     def __dlpack_device__(self) -> tuple[int, int]:

@@ -147,3 +147,23 @@ def test_injected_launch_failure_then_recovery(cuda_rt):
 def test_compile_error_is_runtime_error(cuda_rt):
     with pytest.raises(RuntimeError, match="CUDA compile failed"):
         cuda_rt.compile_cubin('extern "C" __global__ void k() { nope; }', "k")
+
+
+def test_dlpack_export_orders_consumer_stream_without_host_sync(cuda_rt, monkeypatch):
+    import torch
+
+    monkeypatch.setattr(cuda_rt, "_max_in_flight", 1 << 20)
+    n = 1 << 22
+    a = eas.tensor(np.ones(n, np.float32), device="cuda")
+    b = eas.tensor(np.full(n, 2.0, np.float32), device="cuda")
+    c = eas.empty_like(a)
+    for _ in range(20):
+        add_kernel(a, b, c, n, BLOCK=1024, _sync=False)  # queued on the legacy default stream
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        t = torch.from_dlpack(c)  # torch passes stream s; eas makes it wait on the device
+        assert cuda_rt.in_flight() > 0  # no host synchronisation happened
+        d = t * 2
+    s.synchronize()
+    assert torch.equal(d, torch.full((n,), 6.0, device="cuda"))
+    cuda_rt.synchronize()
