@@ -11,9 +11,9 @@ with the device ``"cuda"`` in place of ``"mps"``:
   its producer (a torch CUDA tensor, or an imported DLPack capsule) whose
   lifetime the tensor extends;
 * ``__dlpack_device__`` answers ``(2, device_index)`` (``kDLCUDA``), and
-  ``__dlpack__`` exports the device pointer zero-copy after draining queued
-  asynchronous launches (the reference synchronised its whole queue,
-  ``_metal.mm:788-793``).
+  ``__dlpack__`` exports the device pointer zero-copy, ordering the
+  consumer's stream after queued launches on the device (the reference
+  synchronised its whole queue on the host, ``_metal.mm:788-793``).
 
 ``"cuda:N"`` selects device ``N``; ``"mps"``/``"metal"`` are rejected.
 """
