@@ -43,6 +43,7 @@ grid into several launches or across GPUs).
 
 from __future__ import annotations
 
+import os
 import struct
 from dataclasses import dataclass, field
 from typing import Any
@@ -50,6 +51,7 @@ from typing import Any
 import numpy as np
 
 from ..ir import DType, IRModule, Inst, ValueRef
+from .reroll import Run, find_runs
 
 # ---------------------------------------------------------------------------
 # launch description shared with the runtime
@@ -227,6 +229,8 @@ class _Emitter:
         self.writes: set[str] = set()
         self.tg: dict[int, tuple[int, int]] = {}   # alloc_tg value id -> (byte offset, elements)
         self.lines: list[str] = []
+        self.depth = 0                         # extra indentation (inside re-rolled loops)
+        self.alias: dict[int, str] = {}        # value id -> C expression (loop-carried / affine operands)
         self.uses: dict[int, int] = {}
         for inst in ir.insts:
             for a in inst.args:
@@ -270,6 +274,9 @@ class _Emitter:
 
     # -- naming ---------------------------------------------------------------
     def name(self, ref: ValueRef) -> str:
+        a = self.alias.get(ref.id)
+        if a is not None:
+            return a
         return self.arg_c.get(ref.id, f"v{ref.id}")
 
     def lane(self, ref: ValueRef, i: str) -> str:
@@ -288,7 +295,7 @@ class _Emitter:
         return ref.dtype
 
     def emit(self, line: str, indent: int = 1) -> None:
-        self.lines.append("  " * indent + line)
+        self.lines.append("  " * (indent + self.depth) + line)
 
     # -- signature -------------------------------------------------------------
     def params(self) -> list[Param]:
@@ -541,13 +548,85 @@ class _Emitter:
         if needs_lane:
             self.emit("const uint32_t eas_lane = threadIdx.x & 31u;")
         groups = self._dot_groups()
-        for k, inst in enumerate(self.ir.insts):
+        insts = self.ir.insts
+        runs = []
+        if os.environ.get("EAS_REROLL", "1") != "0":
+            runs = find_runs(insts, keep_together=tuple(frozenset(m) for m in groups.values() if m))
+        run_at = {r.first[0]: r for r in runs}
+        in_run: set[int] = set()
+        for r in runs:
+            in_run |= r.ir_span
+        for inst in insts:  # constants first: re-rolled blocks read them from any position
+            if inst.op == "const":
+                self._thread_inst(inst)
+        for k, inst in enumerate(insts):
+            if inst.op == "const":
+                continue
+            if k in run_at:
+                self._emit_run(run_at[k], groups)
+            if k in in_run:
+                continue
             if k in groups:
                 if groups[k]:
-                    self._dot_group([self.ir.insts[j] for j in groups[k]])
+                    self._dot_group([insts[j] for j in groups[k]])
                 continue
             self._thread_inst(inst)
         return self.lines
+
+    def _emit_run(self, run: Run, groups: dict[int, list[int]]) -> None:
+        """Print a run of identical unrolled blocks as one loop over block 0 (bit-identical: the same
+        operations in the same order).  Loop-carried operands live in mutable variables updated at
+        the end of each iteration; the last iteration's values read after the loop are copied out."""
+        insts = self.ir.insts
+        n = len(self.lines)
+        rv = f"eas_r{n}"
+        fresh = 1 << 40
+        body: dict[int, Inst] = {}
+        carries: dict[str, tuple[str, int]] = {}  # variable -> (C type, q)
+        for j, k in enumerate(run.first):
+            inst = insts[k]
+            args = list(inst.args)
+            for a_i, f in enumerate(run.forms[j]):
+                a = args[a_i]
+                if f[0] == "carry":
+                    _, q, init = f
+                    var = f"eas_c{n}_{q}_{init}"
+                    if var not in carries:
+                        t = ctype(insts[run.first[q]].out.dtype)
+                        carries[var] = (t, q)
+                        self.emit(f"{t} {var} = {self.name(a)};")
+                    fresh += 1
+                    self.alias[fresh] = var
+                    args[a_i] = ValueRef(fresh, a.dtype, a.lanes)
+                elif f[0] == "affine":
+                    _, c0, d = f
+                    fresh += 1
+                    self.alias[fresh] = f"({c0 % (1 << 32)}u + {rv} * {d}u)"
+                    args[a_i] = ValueRef(fresh, a.dtype, a.lanes)
+            body[k] = Inst(inst.op, inst.out, tuple(args))
+        escapes = {}
+        for q in run.escapes:
+            o = insts[run.first[q]].out
+            self.uses[o.id] = max(1, self.uses.get(o.id, 0))
+            escapes[q] = f"eas_e{n}_{q}"
+            self.emit(f"{ctype(o.dtype)} {escapes[q]};")
+        self.emit(f"for (uint32_t {rv} = 0u; {rv} < {run.count}u; ++{rv}) {{")
+        self.depth += 1
+        for k in run.first:
+            if k in groups:
+                if groups[k]:
+                    self._dot_group([body[j] for j in groups[k]])
+                continue
+            self._thread_inst(body[k])
+        for var, (_t, q) in carries.items():
+            self.emit(f"{var} = v{insts[run.first[q]].out.id};")
+        for q, var in escapes.items():
+            self.emit(f"{var} = v{insts[run.first[q]].out.id};")
+        self.depth -= 1
+        self.emit("}")
+        for q, var in escapes.items():
+            o = run.last_out[q]
+            self.emit(f"const {ctype(insts[run.first[q]].out.dtype)} v{o} = {var};")
 
     _PURE = frozenset({"const", "add", "mul", "floordiv", "mod", "lt", "and", "or", "not", "where", "cast", "fma",
                        "program_id", "thread_id", "local_id", "lane_id", "sg_id", "tid"})

@@ -41,10 +41,12 @@ def test_dot_reads_f16_as_float_in_a_k_loop():
     assert "fmaf(" in s
 
 
-def test_tiled_matmul_groups_dots_with_float4_b_loads():
+def test_tiled_matmul_groups_dots_with_float4_b_loads(monkeypatch):
     s = src("matmul_tiled_masked")
     assert "const float4 bv = *reinterpret_cast<const float4*>" in s
-    assert s.count("const float av =") == 4  # one grouped k loop per BK step (K=64, BK=16)
+    assert s.count("const float av =") == 2  # BK steps 1..3 (K=64, BK=16) re-rolled into one loop
+    monkeypatch.setenv("EAS_REROLL", "0")
+    assert src("matmul_tiled_masked").count("const float av =") == 4  # one grouped k loop per BK step
 
 
 def test_mma_uses_tensor_core_mma_sync():

@@ -74,3 +74,22 @@ def test_add_config1_known_answer(cuda_rt):
     out = np.zeros_like(a)
     cuda_rt.run(ck, {"a": a, "b": b, "c": out, "N": 1031}, {"BLOCK": 256})
     np.testing.assert_array_equal(out, a + b)
+
+
+@pytest.mark.parametrize("cid", ["matmul_naive", "matmul_tiled_masked", "t_fma_matmul", "t_matmul"])
+def test_rerolled_and_unrolled_sources_agree(cuda_rt, cid, monkeypatch):
+    """Kernels whose unrolled constexpr loops the emitter prints as loops give the same bits
+    as the straight-line source (EAS_REROLL=0)."""
+    c = goldens.case(cid)
+    ir = goldens.ir_from_json(c["opt"])
+    rolled = compile_ir(ir)
+    monkeypatch.setenv("EAS_REROLL", "0")
+    flat = compile_ir(ir)
+    assert "eas_r" in rolled.src and "eas_r" not in flat.src
+    outs = []
+    for ck in (rolled, flat):
+        inp = goldens.make_inputs(c, 5)
+        cuda_rt.run(ck, inp, c["meta"], sync=True, **goldens.launch_opts(c))
+        outs.append(inp)
+    for name in c["writes"]:
+        np.testing.assert_array_equal(outs[0][name], outs[1][name])
