@@ -368,4 +368,9 @@ def _match_dot_gemm(ir: IRModule, lowered: Any) -> DotGemmPlan | None:
 
 
 def match_native(ir: IRModule, lowered: Any) -> Any:
-    return _match_dot_gemm(ir, lowered)
+    plan = _match_dot_gemm(ir, lowered)
+    if plan is None:
+        from .tiled import match_tiled
+
+        plan = match_tiled(ir, lowered)
+    return plan

@@ -146,6 +146,25 @@ int eas_gemm_f16(const void* a, const void* b, float* c, uint32_t M, uint32_t N,
                  uint64_t lda, uint64_t a_bstride, uint64_t ldb, uint64_t b_bstride, int b_kmajor, uint64_t ldc,
                  uint64_t c_bstride, int block_n, void* stream);
 
+/* Strided batched fp32 GEMM with per-K-tile partial sums, true fp32 FFMA on
+ * the CUDA cores.  Replaces the launch of the generated kernel for the
+ * reference's fp32 tiled matmul (easy_as examples/matmul_tiled.py:134-230,
+ * its dot groups lowered by eas/codegen/msl.py:1201-1359 and launched through
+ * eas._metal.launch_tg, _metal.mm:1013-1222):
+ *   for each K tile t of k_tile elements:
+ *     p = fma(A[m][k], B[k][n], p) for k ascending in the tile, p from 0.0f
+ *     acc = acc + p   (first tile: acc = 0.0f + p if zero_init, else acc = p)
+ *   C[b][m][n] = acc
+ *   A at a + b*a_bstride + m*lda + k, B at b + b*b_bstride + k*ldb + n,
+ *   C at c + b*c_bstride + m*ldc + n   (elements)
+ * The same operations in the same order as the generated kernel, so the
+ * results are bit-identical.  K must be a multiple of k_tile and k_tile a
+ * multiple of 8; operands 16-byte aligned, strides multiples of 4 elements;
+ * otherwise EAS_ERR_VALUE.  Asynchronous on `stream`. */
+int eas_sgemm_f32_tiled(const float* a, const float* b, float* c, uint32_t M, uint32_t N, uint32_t K,
+                        uint32_t k_tile, uint32_t batch, uint64_t lda, uint64_t a_bstride, uint64_t ldb,
+                        uint64_t b_bstride, uint64_t ldc, uint64_t c_bstride, int zero_init, void* stream);
+
 /* Read and clear the status word of native kernels on `dev` (0 = ok,
  * EAS_ERR_TIMEOUT = a bounded wait expired).  Valid after the stream synced. */
 int eas_gemm_status(int dev, int* code);

@@ -91,6 +91,7 @@ def test_c3_rerolled_loop_matches_unrolled_source_full_size(cuda_rt, monkeypatch
 
     c = goldens.case("matmul_tiled_c3_full")
     ir = goldens.ir_from_json(c["opt"])
+    monkeypatch.setenv("EAS_DISABLE_NATIVE", "1")  # compare the two generic sources
     rolled = compile_ir(ir)
     monkeypatch.setenv("EAS_REROLL", "0")
     flat = compile_ir(ir)
@@ -106,3 +107,31 @@ def test_c3_rerolled_loop_matches_unrolled_source_full_size(cuda_rt, monkeypatch
         outs.append(out)
     torch.cuda.synchronize()
     assert torch.equal(outs[0], outs[1])
+
+
+@pytest.mark.parametrize("mn,grid", [((2048, 2048), (64, 64, 1)), ((96, 160), (5, 3, 1)), ((32, 32), (1, 1, 1))])
+def test_c3_native_ffma_kernel_matches_generic_kernel_bit_for_bit(cuda_rt, monkeypatch, mn, grid):
+    """The proven tiled-GEMM launch (eas_sgemm_f32_tiled) against the generated kernel of the same
+    IR: identical bits, at the full 2048^3 size and at sizes that are not multiples of its
+    128 x 128 tile."""
+    import torch
+
+    c = goldens.case("matmul_tiled_c3_full")
+    ir = goldens.ir_from_json(c["opt"])
+    M, N = mn
+    K = 2048
+    g = torch.Generator(device="cuda").manual_seed(7)
+    a = torch.randn(M * K, device="cuda", generator=g)
+    b = torch.randn(K * N, device="cuda", generator=g)
+    ck = compile_ir(ir)
+    assert ck.plan.native is not None and ck.plan.native.kind == "tiled_f32_ffma"
+    before = cuda_rt.native_launches
+    native = torch.full((M * N,), float("nan"), device="cuda")
+    cuda_rt.run(ck, {"a": a, "b": b, "c": native, "M": M, "N": N}, c["meta"], grid=grid)
+    assert cuda_rt.native_launches == before + 1, ck.plan.native.last_reason
+    monkeypatch.setenv("EAS_DISABLE_NATIVE", "1")
+    generic = torch.full((M * N,), float("nan"), device="cuda")
+    cuda_rt.run(ck, {"a": a, "b": b, "c": generic, "M": M, "N": N}, c["meta"], grid=grid)
+    torch.cuda.synchronize()
+    assert cuda_rt.native_launches == before + 1
+    assert torch.equal(native, generic)
