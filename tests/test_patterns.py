@@ -79,12 +79,13 @@ def gemv_like_f32(a, x, y, M, K, BLOCK: eas.constexpr):
 
 
 @pytest.mark.parametrize("cid", ["add_c1", "matmul_tiled_masked", "matmul_simdgroup", "t_gemv_dot", "t_tg_copy"])
-def test_other_kernels_have_no_native_plan(cid):
+def test_other_kernels_have_no_f16_gemm_plan(cid):
+    """Only fp32 dot kernels may carry the tiled-FFMA plan, which proves its case per launch."""
     ck = compile_ir(goldens.ir_from_json(goldens.case(cid)["opt"]))
-    assert ck.plan.native is None
+    assert getattr(ck.plan.native, "kind", None) in (None, "tiled_f32_ffma")
 
 
-def test_f32_dot_is_not_gemm_pattern():
+def test_f32_dot_is_not_f16_gemm_pattern():
     ck = gemv_like_f32.compile(np.zeros(1, np.float32), np.zeros(1, np.float32), np.zeros(1, np.float32), 4, 4,
                                BLOCK=64)
-    assert ck.plan.native is None
+    assert getattr(ck.plan.native, "kind", None) in (None, "tiled_f32_ffma")
