@@ -15,8 +15,10 @@ L2), so no L2 flush is needed between steps.
   copies c back.
 * ``roofline``: the add kernel's achieved bytes / launch time against the
   measured HBM copy peak (MEASURED_PEAKS.json).
-* ``gemm``: the fp16 ``mk.dot`` GEMM (config C4, 8192^3) TFLOP/s when its
-  native tcgen05 path is available.
+* ``gemm``: the fp16 ``mk.dot`` GEMM (configs C4 8192^3 and C5 batched) TFLOP/s
+  on the native tcgen05 path.
+* ``matmul_tiled``: config C3, the reference's fp32 tiled matmul at 2048^3 on
+  the proven-GEMM FFMA path (1 GPU), with cuBLAS fp32 timed beside it.
 * ``cpu_baseline``: numpy on the host cores on a bounded sample.
 
 ``--impl reference`` times the reference's CPU semantics instead (the CPU
@@ -261,6 +263,99 @@ def run_gemm(name: str, args, world: int, rank: int, rt) -> dict:
     }
 
 
+C3_SIZE = 2048
+
+
+def run_tiled(args, rt) -> dict:
+    """Config C3: the reference's unmodified fp32 tiled matmul (its front end's IR, committed as
+    tests/golden/reference_ir_big.json.gz), M = N = K = 2048, 32x32x32 tiles, 256 threads per
+    group, A, B ~ U(-1, 1).  The runtime proves the IR is a tiled GEMM and launches the
+    FFMA kernel (bit-identical to the generated kernel).  Inputs (48 MB) fit in L2, so every
+    timed step follows a 512 MB L2 flush outside its CUDA events."""
+    import gzip
+
+    import torch
+
+    from easy_as_b200.compiler import compile_ir
+    from easy_as_b200.ir import ir_from_json
+
+    with gzip.open(ROOT / "tests" / "golden" / "reference_ir_big.json.gz", "rt") as f:
+        case = next(c for c in json.load(f)["cases"] if c["id"] == "matmul_tiled_c3_full")
+    ck = compile_ir(ir_from_json(case["opt"]))
+    M = N = K = C3_SIZE
+    g = torch.Generator(device="cuda").manual_seed(2)
+    a = torch.rand(M * K, device="cuda", generator=g) * 2 - 1
+    b = torch.rand(K * N, device="cuda", generator=g) * 2 - 1
+    c = torch.empty(M * N, device="cuda")
+    flush = torch.empty(512 << 20, dtype=torch.uint8, device="cuda")
+    grid = (N // 32, M // 32, 1)
+    args_ = {"a": a, "b": b, "c": c, "M": M, "N": N}
+
+    def step():
+        rt.run(ck, args_, case["meta"], grid=grid, sync=False)
+
+    native0 = rt.native_launches
+    step()
+    torch.cuda.synchronize()
+    if rt.native_launches == native0:
+        raise SystemExit("bench: C3 did not take the native FFMA path: " + ck.plan.native.last_reason)
+    ref = a.view(M, K)[:4].double() @ b.view(K, N).double()
+    err = ((c.view(M, N)[:4].double() - ref).abs().max() / ref.abs().max()).item()
+    if err > 1e-4:
+        raise SystemExit(f"bench: C3 result off by {err:.2e}")
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    steps = max(5, args.steps)
+    stream = torch.cuda.current_stream()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    launches0 = rt.launch_count
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        for e0, e1 in evs:
+            flush.zero_()
+            e0.record(stream)
+            step()
+            e1.record(stream)
+        torch.cuda.synchronize()
+    ms = sum(e0.elapsed_time(e1) for e0, e1 in evs) / steps
+    flops = 2.0 * M * N * K
+    tf = flops / (ms * 1e-3) / 1e12
+    cl = clk.summary()
+    mhz = cl.get("sm_mhz") or 1965.0
+    peak = 148 * 128 * 2 * mhz * 1e6 / 1e12
+    # cuBLAS fp32 (TF32 off) on the same operands, for context
+    torch.backends.cuda.matmul.allow_tf32 = False
+    A2, B2 = a.view(M, K), b.view(K, N)
+    for _ in range(3):
+        torch.mm(A2, B2)
+    lib_ms = []
+    for _ in range(steps):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        torch.mm(A2, B2)
+        e1.record(stream)
+        e1.synchronize()
+        lib_ms.append(e0.elapsed_time(e1))
+    lib_tf = flops / (sum(lib_ms) / steps * 1e-3) / 1e12
+    del flush
+    return {
+        "metric": "fp32 tiled matmul TFLOP/s", "value": round(tf, 2), "unit": "TFLOP/s", "ms_per_step": round(ms, 4),
+        "steps": steps, "dtype": "f32",
+        "config": {"workload": "C3 matmul_tiled_full_kernel (reference IR) M=N=K=2048, BM=BN=BK=32, NT=256",
+                   "kernel": "proven tiled GEMM -> FFMA sgemm_ffma 64x64x32 tiles, 8x4 per thread, cp.async "
+                             "2-stage (128x128x32, 8x8 per thread from 4 waves of 128-tiles up)",
+                   "l2": "512 MB flush before each timed step (outside the events)", "spot_check_rel_err": err},
+        "roofline": {"bound": "fp32_fma", "achieved": round(tf, 2), "peak": round(peak, 1), "unit": "TFLOP/s",
+                     "frac": round(tf / peak, 4),
+                     "peak_source": "nominal 148 SM x 128 FP32 lanes x 2 at the median sampled SM clock",
+                     "traffic": profile_traffic("sgemm_c3_n1")},
+        "cublas_fp32_tflops": round(lib_tf, 2),
+        "gpu_launches": rt.launch_count - launches0,
+        "clocks": cl,
+    }
+
+
 def cpu_add_baseline(seconds: float = 10.0) -> dict:
     """numpy add on the host cores over 2**24-element chunks for ~``seconds`` (all threads)."""
     cores = os.cpu_count() or 1
@@ -295,6 +390,9 @@ def run_eas(args) -> None:
     from easy_as_b200.runtime import get_runtime
 
     rt = get_runtime()
+    if args.only == "C3":
+        print(json.dumps(run_tiled(args, rt)), flush=True)
+        return
     if args.only in ("C4", "C5"):
         # profiling mode: one GEMM workload only
         res = run_gemm(args.only, args, world, rank, rt)
@@ -375,6 +473,9 @@ def run_eas(args) -> None:
         torch.cuda.empty_cache()
         for name in ("C4", "C5"):
             gemm[name] = run_gemm(name, args, world, rank, rt)
+    tiled = None
+    if not args.quick and not args.no_gemm and world == 1:
+        tiled = run_tiled(args, rt)
     if rank != 0:
         return
     pk = peaks()
@@ -396,6 +497,8 @@ def run_eas(args) -> None:
     }
     if gemm:
         line["gemm"] = gemm
+    if tiled is not None:
+        line["matmul_tiled"] = tiled
     if world == 1 and not args.no_cpu_baseline and not args.quick:
         line["cpu_baseline"] = cpu_add_baseline(args.cpu_seconds)
     print(json.dumps(line), flush=True)
@@ -458,7 +561,7 @@ def main() -> None:
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--n", type=int, default=N_TOTAL, help="total elements (profiling runs use a smaller case)")
     ap.add_argument("--no-gemm", action="store_true", help="skip the fp16 GEMM configs (C4, C5)")
-    ap.add_argument("--only", choices=["all", "C4", "C5"], default="all",
+    ap.add_argument("--only", choices=["all", "C3", "C4", "C5"], default="all",
                     help="run a single GEMM workload (profiling)")
     ap.add_argument("--gemm-steps", type=int, default=20)
     ap.add_argument("--quick", action="store_true",

@@ -9,141 +9,174 @@
 //
 // in true fp32 (no TF32, no reassociation).  This kernel performs exactly those
 // operations for every output, in the same order, so its results are
-// bit-identical; only the work split differs: a 128 x 128 output tile per CTA,
-// an 8 x 8 register tile per thread (two 4-wide row and column groups, so the
-// shared-memory reads are 128-bit and conflict-free), K staged BKS = 8 or 16
-// deep through double-buffered shared memory with register prefetch, one
-// __syncthreads per stage.  A is stored transposed (k-major) in shared memory.
+// bit-identical; only the work split differs:
+//
+//   * a BM x BN output tile per CTA, a TM x TN register tile per thread (rows
+//     ty + (BM/TM)*i, TN/4 column groups of 4); a warp covers 4 thread rows by
+//     8 thread columns.  128 x 128 tiles with 8 x 8 per thread (256 threads,
+//     1 CTA/SM) for large launches, 64 x 64 with 8 x 4 (128 threads, 4 CTAs/SM)
+//     when there are fewer than four waves of 128 x 128 tiles;
+//   * K staged BKS = 32, 16 or 8 deep (the largest that divides KT) through a
+//     2- or 3-deep cp.async ring (16-byte copies, zero-filled past M, N), one
+//     __syncthreads per stage;
+//   * A kept k-contiguous in shared memory ([BM][BKS+4]) and read as float4
+//     along k; interleaved thread rows put the 4 rows a warp reads at once in
+//     different banks; B as [BKS][BN+4], 8 consecutive float4 per warp read;
+//   * the first k of every K tile starts the partial sums with
+//     fmaf(a, b, 0.0f); the running sum starts at -0.0f (zero_init = 0, and
+//     -0.0f + p == p bit for bit, NaN included) or +0.0f (zero_init = 1), so
+//     the fold is a plain __fadd_rn.
 //
 //   C[b][m][n] at c + b*c_bs + m*ldc + n
 //   A[b][m][k] at a + b*a_bs + m*lda + k
 //   B[b][k][n] at b + b*b_bs + k*ldb + n
 //
 // Rows m >= M and columns n >= N are read as zero and not stored.  No spin
-// waits; the only synchronisation is __syncthreads.
+// waits; the only synchronisation is cp.async.wait_group and __syncthreads.
 #include <cuda_runtime.h>
 #include <stdint.h>
+
+#include <type_traits>
 
 #include "eas_internal.h"
 
 namespace {
 
-constexpr int kBM = 128, kBN = 128, kThreads = 256, kPad = 4;
+__device__ __forceinline__ void cp_async16(float* dst, const float* src, uint32_t bytes) {
+  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(dst));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(d), "l"(src), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
 
-template <int BKS>
-struct SgemmSmem {
-  float a[2][BKS][kBM + kPad];  // k-major A tile
-  float b[2][BKS][kBN + kPad];
+template <int BM, int BN, int BKS, int STAGES, int TM, int TN>
+struct SgemmCfg {
+  static constexpr int kTX = BN / TN, kTY = BM / TM, kThreads = kTX * kTY, kCG = TN / 4;
+  static constexpr int kLdA = BKS + 4, kLdB = BN + 4;
+  static constexpr int kAStage = BM * kLdA, kBStage = BKS * kLdB;
+  static constexpr int kSmemFloats = STAGES * (kAStage + kBStage);
+  static constexpr int kAChunks = BM * BKS / 4 / kThreads, kBChunks = BKS * BN / 4 / kThreads;
+  static_assert(kTX % 8 == 0 && kTY % 4 == 0, "warp layout needs BN % 64 == 0 and BM % 32 == 0");
+  static_assert(kAChunks >= 1 && kBChunks >= 1, "staging does not divide");
+  static_assert(BKS % 4 == 0, "BKS must be a multiple of 4");
 };
 
-template <int BKS>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int BM, int BN, int BKS, int STAGES, int TM, int TN, int MINB>
+__global__ void __launch_bounds__(SgemmCfg<BM, BN, BKS, STAGES, TM, TN>::kThreads, MINB)
 sgemm_ffma_kernel(const float* __restrict__ A, const float* __restrict__ B, float* __restrict__ C, uint32_t M,
                   uint32_t N, uint32_t K, uint32_t stages_per_tile, uint64_t lda, uint64_t ldb, uint64_t ldc,
                   uint64_t a_bs, uint64_t b_bs, uint64_t c_bs, int zero_init) {
-  __shared__ __align__(16) SgemmSmem<BKS> sm;
+  using Cfg = SgemmCfg<BM, BN, BKS, STAGES, TM, TN>;
+  extern __shared__ __align__(16) float smem[];
+  float* sA = smem;
+  float* sB = smem + STAGES * Cfg::kAStage;
   const int tid = threadIdx.x;
-  const int tx = tid & 15, ty = tid >> 4;
-  const uint32_t m0 = blockIdx.y * kBM, n0 = blockIdx.x * kBN;
+  const int warp = tid >> 5, lane = tid & 31;
+  constexpr int kWarpsX = Cfg::kTX / 8;
+  const int ty = (warp / kWarpsX) * 4 + (lane >> 3);
+  const int tx = (warp % kWarpsX) * 8 + (lane & 7);
+  const uint32_t m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
   A += (uint64_t)blockIdx.z * a_bs;
   B += (uint64_t)blockIdx.z * b_bs;
   C += (uint64_t)blockIdx.z * c_bs;
+  const uint32_t nstages = K / BKS;
 
-  // global -> register staging: A rows of BKS floats (BKS/4 float4 each), B rows of 128 floats
-  constexpr int kAPerRow = BKS / 4;                     // float4 per A row
-  constexpr int kARowsPerPass = kThreads / kAPerRow;    // rows covered by one pass of the CTA
-  constexpr int kPasses = BKS / 8;                      // passes for A (128 rows) and for B (BKS rows)
-  const int a_row = tid / kAPerRow, a_kc = (tid % kAPerRow) * 4;
-  const int b_row = tid >> 5, b_nc = (tid & 31) * 4;
-  float4 ra[kPasses], rb[kPasses];
-
-  auto load_stage = [&](uint32_t k0) {
+  auto issue = [&](uint32_t st) {
+    if (st < nstages) {
+      const int buf = st % STAGES;
+      const uint32_t k0 = st * BKS;
 #pragma unroll
-    for (int q = 0; q < kPasses; ++q) {
-      const uint32_t m = m0 + a_row + q * kARowsPerPass;
-      ra[q] = m < M ? __ldg(reinterpret_cast<const float4*>(A + (uint64_t)m * lda + k0 + a_kc))
-                    : make_float4(0.f, 0.f, 0.f, 0.f);
-      const uint32_t k = k0 + b_row + q * 8;
-      const uint32_t n = n0 + b_nc;
-      const float* src = B + (uint64_t)k * ldb + n;
-      if (n + 3 < N) {
-        rb[q] = __ldg(reinterpret_cast<const float4*>(src));
-      } else {
-        rb[q].x = n < N ? src[0] : 0.f;
-        rb[q].y = n + 1 < N ? src[1] : 0.f;
-        rb[q].z = n + 2 < N ? src[2] : 0.f;
-        rb[q].w = 0.f;
+      for (int q = 0; q < Cfg::kAChunks; ++q) {
+        const int idx = tid + q * Cfg::kThreads;
+        const int r = idx / (BKS / 4), kc = (idx % (BKS / 4)) * 4;
+        const uint32_t m = m0 + r;
+        const float* src = A + (uint64_t)(m < M ? m : 0) * lda + k0 + kc;
+        cp_async16(sA + buf * Cfg::kAStage + r * Cfg::kLdA + kc, src, m < M ? 16u : 0u);
+      }
+#pragma unroll
+      for (int q = 0; q < Cfg::kBChunks; ++q) {
+        const int idx = tid + q * Cfg::kThreads;
+        const int r = idx / (BN / 4), nc = (idx % (BN / 4)) * 4;
+        const uint32_t n = n0 + nc;
+        const uint32_t bytes = n + 3 < N ? 16u : (n < N ? 4u * (N - n) : 0u);
+        const float* src = B + (uint64_t)(k0 + r) * ldb + (n < N ? n : 0);
+        cp_async16(sB + buf * Cfg::kBStage + r * Cfg::kLdB + nc, src, bytes);
+      }
+    }
+    cp_async_commit();
+  };
+
+  float acc[TM][TN], p[TM][TN];
+  const float init = zero_init ? 0.0f : -0.0f;
+#pragma unroll
+  for (int i = 0; i < TM; ++i)
+#pragma unroll
+    for (int j = 0; j < TN; ++j) acc[i][j] = init;
+
+#pragma unroll
+  for (int st = 0; st < STAGES - 1; ++st) issue(st);
+
+  auto compute = [&](int buf, auto first_tag) {
+    constexpr bool kFirst = decltype(first_tag)::value;
+    const float* a = sA + buf * Cfg::kAStage + ty * Cfg::kLdA;
+    const float* b = sB + buf * Cfg::kBStage + tx * 4;
+#pragma unroll
+    for (int kb = 0; kb < BKS; kb += 4) {
+      float4 af[TM];
+#pragma unroll
+      for (int i = 0; i < TM; ++i) af[i] = *reinterpret_cast<const float4*>(a + i * Cfg::kTY * Cfg::kLdA + kb);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        float bv[TN];
+#pragma unroll
+        for (int g = 0; g < Cfg::kCG; ++g) {
+          const float4 bq = *reinterpret_cast<const float4*>(b + (kb + kk) * Cfg::kLdB + g * (BN / Cfg::kCG));
+          bv[4 * g + 0] = bq.x;
+          bv[4 * g + 1] = bq.y;
+          bv[4 * g + 2] = bq.z;
+          bv[4 * g + 3] = bq.w;
+        }
+        float av[TM];
+#pragma unroll
+        for (int i = 0; i < TM; ++i) av[i] = kk == 0 ? af[i].x : kk == 1 ? af[i].y : kk == 2 ? af[i].z : af[i].w;
+#pragma unroll
+        for (int i = 0; i < TM; ++i)
+#pragma unroll
+          for (int j = 0; j < TN; ++j)
+            p[i][j] = (kFirst && kb == 0 && kk == 0) ? fmaf(av[i], bv[j], 0.0f) : fmaf(av[i], bv[j], p[i][j]);
       }
     }
   };
-  auto store_stage = [&](int buf) {
-#pragma unroll
-    for (int q = 0; q < kPasses; ++q) {
-      const int r = a_row + q * kARowsPerPass;
-      sm.a[buf][a_kc + 0][r] = ra[q].x;
-      sm.a[buf][a_kc + 1][r] = ra[q].y;
-      sm.a[buf][a_kc + 2][r] = ra[q].z;
-      sm.a[buf][a_kc + 3][r] = ra[q].w;
-      *reinterpret_cast<float4*>(&sm.b[buf][b_row + q * 8][b_nc]) = rb[q];
-    }
-  };
 
-  float acc[8][8], p[8][8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i)
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      acc[i][j] = 0.f;
-      p[i][j] = 0.f;
-    }
-  bool first = true;
-
-  const uint32_t nstages = K / BKS;
-  load_stage(0);
-  store_stage(0);
-  __syncthreads();
   uint32_t in_tile = 0;
   for (uint32_t s = 0; s < nstages; ++s) {
-    const int cur = s & 1;
-    if (s + 1 < nstages) load_stage((s + 1) * BKS);
-#pragma unroll
-    for (int k = 0; k < BKS; ++k) {
-      const float4 a0 = *reinterpret_cast<const float4*>(&sm.a[cur][k][ty * 4]);
-      const float4 a1 = *reinterpret_cast<const float4*>(&sm.a[cur][k][64 + ty * 4]);
-      const float4 b0 = *reinterpret_cast<const float4*>(&sm.b[cur][k][tx * 4]);
-      const float4 b1 = *reinterpret_cast<const float4*>(&sm.b[cur][k][64 + tx * 4]);
-      const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-      const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
-#pragma unroll
-      for (int i = 0; i < 8; ++i)
-#pragma unroll
-        for (int j = 0; j < 8; ++j) p[i][j] = fmaf(av[i], bv[j], p[i][j]);
-    }
+    cp_async_wait<STAGES - 2>();
+    __syncthreads();
+    issue(s + STAGES - 1);
+    const int buf = s % STAGES;
+    if (in_tile == 0)
+      compute(buf, std::true_type{});
+    else
+      compute(buf, std::false_type{});
     if (++in_tile == stages_per_tile) {  // end of a K tile: fold its partial sums, in order
       in_tile = 0;
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
+      for (int i = 0; i < TM; ++i)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          acc[i][j] = first ? (zero_init ? __fadd_rn(0.f, p[i][j]) : p[i][j]) : __fadd_rn(acc[i][j], p[i][j]);
-          p[i][j] = 0.f;
-        }
-      first = false;
-    }
-    if (s + 1 < nstages) {
-      store_stage(cur ^ 1);
-      __syncthreads();
+        for (int j = 0; j < TN; ++j) acc[i][j] = __fadd_rn(acc[i][j], p[i][j]);
     }
   }
+  cp_async_wait<0>();
 
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const uint32_t m = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + (i - 4));
+  for (int i = 0; i < TM; ++i) {
+    const uint32_t m = m0 + ty + Cfg::kTY * i;
     if (m >= M) continue;
     float* row = C + (uint64_t)m * ldc;
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const uint32_t n = n0 + h * 64 + tx * 4;
+    for (int h = 0; h < Cfg::kCG; ++h) {
+      const uint32_t n = n0 + h * (BN / Cfg::kCG) + tx * 4;
       const float* v = &acc[i][h * 4];
       if (n + 3 < N) {
         *reinterpret_cast<float4*>(row + n) = make_float4(v[0], v[1], v[2], v[3]);
@@ -155,6 +188,31 @@ sgemm_ffma_kernel(const float* __restrict__ A, const float* __restrict__ B, floa
   }
 }
 
+template <int BM, int BN, int BKS, int STAGES, int TM, int TN, int MINB>
+int launch_sgemm(const float* a, const float* b, float* c, uint32_t M, uint32_t N, uint32_t K, uint32_t k_tile,
+                  uint32_t batch, uint64_t lda, uint64_t a_bs, uint64_t ldb, uint64_t b_bs, uint64_t ldc,
+                  uint64_t c_bs, int zero_init, cudaStream_t s) {
+  using Cfg = SgemmCfg<BM, BN, BKS, STAGES, TM, TN>;
+  const uint32_t gy = (M + BM - 1) / BM;
+  if (gy > 65535) return eas_fail(EAS_ERR_VALUE, "eas_sgemm_f32_tiled: M too large");
+  const size_t smem = Cfg::kSmemFloats * sizeof(float);
+  auto kern = sgemm_ffma_kernel<BM, BN, BKS, STAGES, TM, TN, MINB>;
+  static int attr_done[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return eas_fail(EAS_ERR_VALUE, "eas_sgemm_f32_tiled: device index out of range");
+  if (!attr_done[dev]) {
+    int rc = eas_cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                            "sgemm_ffma smem attribute", EAS_ERR_LAUNCH);
+    if (rc) return rc;
+    attr_done[dev] = 1;
+  }
+  dim3 grid((N + BN - 1) / BN, gy, batch);
+  kern<<<grid, Cfg::kThreads, smem, s>>>(a, b, c, M, N, K, k_tile / BKS, lda, ldb, ldc, a_bs, b_bs, c_bs,
+                                         zero_init);
+  return eas_cuda_check(cudaGetLastError(), "sgemm_ffma launch", EAS_ERR_LAUNCH);
+}
+
 }  // namespace
 
 extern "C" int eas_sgemm_f32_tiled(const float* a, const float* b, float* c, uint32_t M, uint32_t N, uint32_t K,
@@ -164,23 +222,31 @@ extern "C" int eas_sgemm_f32_tiled(const float* a, const float* b, float* c, uin
   if (!a || !b || !c) return eas_fail(EAS_ERR_VALUE, "eas_sgemm_f32_tiled: null operand");
   if (M == 0 || N == 0 || batch == 0) return EAS_OK;
   if (K == 0 || k_tile == 0 || K % k_tile) return eas_fail(EAS_ERR_VALUE, "eas_sgemm_f32_tiled: K must be a positive multiple of k_tile");
-  int bks = (k_tile % 16 == 0) ? 16 : (k_tile % 8 == 0 ? 8 : 0);
-  if (!bks) return eas_fail(EAS_ERR_VALUE, "eas_sgemm_f32_tiled: k_tile must be a multiple of 8");
+  if (k_tile % 8) return eas_fail(EAS_ERR_VALUE, "eas_sgemm_f32_tiled: k_tile must be a multiple of 8");
   if ((reinterpret_cast<uintptr_t>(a) & 15) || (reinterpret_cast<uintptr_t>(b) & 15) ||
       (reinterpret_cast<uintptr_t>(c) & 15))
     return eas_fail(EAS_ERR_VALUE, "eas_sgemm_f32_tiled: operands must be 16-byte aligned");
   if (lda % 4 || ldb % 4 || ldc % 4 || (batch > 1 && (a_bstride % 4 || b_bstride % 4 || c_bstride % 4)))
     return eas_fail(EAS_ERR_VALUE, "eas_sgemm_f32_tiled: strides must be multiples of 4 elements");
   if (batch > 65535) return eas_fail(EAS_ERR_VALUE, "eas_sgemm_f32_tiled: batch exceeds 65535");
-  const uint32_t gy = (M + kBM - 1) / kBM;
-  if (gy > 65535) return eas_fail(EAS_ERR_VALUE, "eas_sgemm_f32_tiled: M too large");
-  dim3 grid((N + kBN - 1) / kBN, gy, batch);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (bks == 16)
-    sgemm_ffma_kernel<16><<<grid, kThreads, 0, s>>>(a, b, c, M, N, K, k_tile / 16, lda, ldb, ldc, a_bstride,
-                                                    b_bstride, c_bstride, zero_init);
-  else
-    sgemm_ffma_kernel<8><<<grid, kThreads, 0, s>>>(a, b, c, M, N, K, k_tile / 8, lda, ldb, ldc, a_bstride,
-                                                   b_bstride, c_bstride, zero_init);
-  return eas_cuda_check(cudaGetLastError(), "sgemm_ffma launch", EAS_ERR_LAUNCH);
+  // 128 x 128 tiles (8 x 8 per thread, 1 CTA per SM) when the launch has at least four waves of
+  // them; otherwise 64 x 64 tiles (8 x 4 per thread, 4 CTAs per SM), which balance small
+  // problems better over the SMs (2048^3: 1024 tiles instead of 256 on 148 SMs).
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const uint64_t big_tiles = (uint64_t)((M + 127) / 128) * ((N + 127) / 128) * batch;
+  const bool small = big_tiles < 4ull * (uint64_t)sms;
+#define EAS_SG(BM, BN, BKS, ST, TM, TN, MINB) \
+  launch_sgemm<BM, BN, BKS, ST, TM, TN, MINB>(a, b, c, M, N, K, k_tile, batch, lda, a_bstride, ldb, b_bstride, ldc, c_bstride, zero_init, s)
+  if (small) {
+    if (k_tile % 32 == 0) return EAS_SG(64, 64, 32, 2, 8, 4, 4);
+    if (k_tile % 16 == 0) return EAS_SG(64, 64, 16, 2, 8, 4, 4);
+    return EAS_SG(64, 64, 8, 3, 8, 4, 4);
+  }
+  if (k_tile % 32 == 0) return EAS_SG(128, 128, 32, 3, 8, 8, 1);
+  if (k_tile % 16 == 0) return EAS_SG(128, 128, 16, 3, 8, 8, 1);
+  return EAS_SG(128, 128, 8, 3, 8, 8, 1);
+#undef EAS_SG
 }

@@ -364,3 +364,38 @@ _Checker.RULES = {
 def validate_ir(ir: IRModule) -> None:
     """Raise ``ValueError("invalid IR: ...")`` if ``ir`` breaks a typing rule."""
     _Checker(ir).run()
+
+
+# --------------------------------------------------------------------------
+# JSON form (the fixture format of tests/golden: plain lists, value refs as {"v": [id, dtype, lanes]})
+# --------------------------------------------------------------------------
+
+def _arg_from_json(x: Any) -> Any:
+    if isinstance(x, dict) and "v" in x:
+        i, dt, lanes = x["v"]
+        return ValueRef(int(i), DType(dt), int(lanes))
+    if isinstance(x, dict) and "dt" in x:
+        return DType(x["dt"])
+    return x
+
+
+def ir_from_json(d: dict) -> IRModule:
+    args = tuple(Arg(n, DType(dt), kind) for n, dt, kind in d["args"])
+    insts = []
+    for op, out, a in d["insts"]:
+        o = None if out is None else ValueRef(int(out[0]), DType(out[1]), int(out[2]))
+        insts.append(Inst(op, o, tuple(_arg_from_json(x) for x in a)))
+    return IRModule(d["name"], args, tuple(insts))
+
+
+def ir_to_json(ir: IRModule) -> dict:
+    def ser(a: Any) -> Any:
+        if isinstance(a, ValueRef):
+            return {"v": [a.id, a.dtype.value, a.lanes]}
+        if isinstance(a, DType):
+            return {"dt": a.value}
+        return a
+
+    return {"name": ir.name, "args": [[a.name, a.dtype.value, a.kind] for a in ir.args],
+            "insts": [[i.op, None if i.out is None else [i.out.id, i.out.dtype.value, i.out.lanes],
+                       [ser(x) for x in i.args]] for i in ir.insts]}

@@ -10,40 +10,9 @@ from typing import Any
 
 import numpy as np
 
-from easy_as_b200.ir import Arg, DType, IRModule, Inst, ValueRef
+from easy_as_b200.ir import ir_from_json, ir_to_json  # noqa: F401  (re-exported for the tests)
 
 GOLDEN = Path(__file__).resolve().parent / "golden"
-
-
-def _arg(x: Any) -> Any:
-    if isinstance(x, dict) and "v" in x:
-        i, dt, lanes = x["v"]
-        return ValueRef(int(i), DType(dt), int(lanes))
-    if isinstance(x, dict) and "dt" in x:
-        return DType(x["dt"])
-    return x
-
-
-def ir_from_json(d: dict) -> IRModule:
-    args = tuple(Arg(n, DType(dt), kind) for n, dt, kind in d["args"])
-    insts = []
-    for op, out, a in d["insts"]:
-        o = None if out is None else ValueRef(int(out[0]), DType(out[1]), int(out[2]))
-        insts.append(Inst(op, o, tuple(_arg(x) for x in a)))
-    return IRModule(d["name"], args, tuple(insts))
-
-
-def ir_to_json(ir: IRModule) -> dict:
-    def ser(a: Any) -> Any:
-        if isinstance(a, ValueRef):
-            return {"v": [a.id, a.dtype.value, a.lanes]}
-        if isinstance(a, DType):
-            return {"dt": a.value}
-        return a
-
-    return {"name": ir.name, "args": [[a.name, a.dtype.value, a.kind] for a in ir.args],
-            "insts": [[i.op, None if i.out is None else [i.out.id, i.out.dtype.value, i.out.lanes],
-                       [ser(x) for x in i.args]] for i in ir.insts]}
 
 
 @lru_cache(maxsize=None)

@@ -109,11 +109,12 @@ def test_c3_rerolled_loop_matches_unrolled_source_full_size(cuda_rt, monkeypatch
     assert torch.equal(outs[0], outs[1])
 
 
-@pytest.mark.parametrize("mn,grid", [((2048, 2048), (64, 64, 1)), ((96, 160), (5, 3, 1)), ((32, 32), (1, 1, 1))])
+@pytest.mark.parametrize("mn,grid", [((2048, 2048), (64, 64, 1)), ((96, 160), (5, 3, 1)), ((32, 32), (1, 1, 1)),
+                                     ((3200, 3232), (101, 100, 1))])
 def test_c3_native_ffma_kernel_matches_generic_kernel_bit_for_bit(cuda_rt, monkeypatch, mn, grid):
     """The proven tiled-GEMM launch (eas_sgemm_f32_tiled) against the generated kernel of the same
-    IR: identical bits, at the full 2048^3 size and at sizes that are not multiples of its
-    128 x 128 tile."""
+    IR: identical bits, at the full 2048^3 size (64 x 64 native tiles) and at sizes that are not
+    multiples of the native tile, for both tile shapes (3200 x 3232 takes the 128 x 128 tiles)."""
     import torch
 
     c = goldens.case("matmul_tiled_c3_full")
