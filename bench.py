@@ -242,6 +242,24 @@ def run_gemm(name: str, args, world: int, rank: int, rt) -> dict:
     barrier(world)
     ms = e0.elapsed_time(e1) / steps
     ms_max = max_over_ranks(ms, world)
+    lib_tf = None
+    if world == 1:
+        # cuBLAS on the same operands (f16 in, f32 out), timed the same way, for context
+        try:
+            def lib_step():
+                torch.bmm(a, b, out_dtype=torch.float32)
+            for _ in range(3):
+                lib_step()
+            torch.cuda.synchronize()
+            l0, l1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            l0.record(stream)
+            for _ in range(steps):
+                lib_step()
+            l1.record(stream)
+            l1.synchronize()
+            lib_tf = round(2.0 * batch * M * N * K / (l0.elapsed_time(l1) / steps * 1e-3) / 1e12, 1)
+        except (TypeError, RuntimeError):
+            lib_tf = None
     flops_total = 2.0 * tb * TM * TN * TK
     flops_local = 2.0 * batch * M * N * K
     pk = peaks()
@@ -258,6 +276,7 @@ def run_gemm(name: str, args, world: int, rank: int, rt) -> dict:
                                      if pk["source"] == "measured" else "fallback"),
                      "frac_of_nominal_2250": round(local_tf / 2250.0, 4),
                      "traffic": profile_traffic(f"gemm_{name.lower()}_n1")},
+        "cublas_f16_f32out_tflops": lib_tf,
         "gpu_launches": rt.launch_count - launches0,
         "clocks": clk.summary(),
     }

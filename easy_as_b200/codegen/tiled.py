@@ -1,43 +1,45 @@
-"""Prove that a thread-mode kernel is a tiled fp32 GEMM, and launch the native FFMA kernel for it.
+"""Prove that a thread-mode kernel is a (masked, tiled) fp32 GEMM, and launch the native FFMA kernel for it.
 
-Target: the reference's fp32 tiled matmul (easy_as
-``examples/matmul_tiled.py:134-230``): threads copy A and B tiles into
-threadgroup memory, a barrier, then each thread runs ``mk.dot`` over the tiles
-for its outputs and adds the dot to a running sum, tile after tile; finally it
-stores the sums.  The generic lowering reproduces that thread structure, so it
-is bound by shared-memory reads (one row by four columns per thread).
+Targets: the reference's fp32 matmul kernels (easy_as ``examples/matmul_tiled.py:27-230``, the
+masked ``matmul_tiled_kernel`` and the interior ``matmul_tiled_full_kernel``, and the naive
+``examples/matmul.py:23-43``).  The tiled ones copy A and B tiles into threadgroup memory, sync,
+run ``mk.dot`` over the tiles and add each dot to a running sum; the naive one is one ``fma``
+chain per output.  The generic lowering keeps their thread structure, so it is bound by
+shared-memory or L1 reads.
 
-Nothing here matches source text or instruction order.  For a given launch
-(scalar argument values, grid, threads per group) the whole thread group is
-executed symbolically, all threads at once:
+Nothing here matches source text or instruction order.  For a given launch (scalar argument
+values, grid, threads per group) the whole thread group is executed symbolically, all threads at
+once:
 
-* every u32 value is, per thread, a linear form ``c + a0*P0 + a1*P1 + a2*P2``
-  modulo 2^32 in the program ids (numpy arrays over the threads); products,
-  divisions, remainders and comparisons need at least one operand free of the
-  program ids, so the forms stay linear and the divisions exact;
-* a float value is a term: a global load at a linear address, a ``dot`` (an
-  ordered ``fma`` chain from 0.0f), a sum of two terms, or a constant;
-* threadgroup memory holds, per slot, the global address its value was
-  loaded from and the barrier phase that wrote it; a slot read by a ``dot`` must
-  have been written before the last barrier and not in the current phase, and
-  no slot is written twice in a phase or after a read in the same phase (race
-  free, so the threads' interleaving cannot matter);
-* masks must be true for every thread, there are no ghost threads, and the only
-  global stores are the final sums.
+* every u32 value is, per thread, a linear form ``c + a0*P0 + a1*P1 + a2*P2`` modulo 2^32 in the
+  program ids (numpy arrays over the threads); products, divisions and remainders need an operand
+  free of the program ids, so the forms stay linear and the divisions exact;
+* a mask is a per-thread boolean (the comparisons between program-id-free values) and a list of
+  atoms ``lhs < rhs`` whose left side depends on the program ids;
+* a float value is a term: a masked global load (0.0f where the mask is false), a ``dot`` (an
+  ordered ``fma`` chain from 0.0f), an ``fma``, a sum of two terms, or a constant;
+* threadgroup memory holds, per slot, the global address and mask of the load stored into it and
+  the barrier phase that wrote it; a slot read by a ``dot`` must have been written before the last
+  barrier and not in the current phase, and no slot is written twice in a phase or after a read in
+  the same phase (race free, so the interleaving of the threads cannot matter);
+* threads of a partial last group (ghosts) touch no memory: their global accesses carry the
+  bound ``global x < active threads`` as one more mask atom; global stores go to one buffer.
 
-The stored terms must then be, for every thread and store, the left fold
-``((z + d_0) + d_1) + ... + d_{T-1}`` (``z`` = 0.0f, or the fold starts at
-``d_0``) of dots of one length KT whose A addresses advance by 1 and B
-addresses by a constant ``ldb`` along ``k = t*KT + j``, and the (A row, B
-column) pairs of the threads' stores must cover a rectangle exactly once, with
-the output address affine in the row and column indices.  The program ids
-shift that rectangle by whole rows/columns (or select a batch), which gives one
-GEMM for the whole launch.  ``eas_sgemm_f32_tiled`` then performs, for every
-output, the same ``fma`` chains and additions in the same order: bit-identical
+The stored terms must then be, for every thread and store, the left fold ``((z + d_0) + d_1) +
+... + d_{T-1}`` (``z`` = 0.0f, or the fold starts at ``d_0``) of dots of one length KT -- an
+``fma`` chain over loads from 0.0f counts as a dot -- whose A addresses advance by 1 and B
+addresses by one stride ``ldb`` along ``k = t*KT + j``, and the (A row, B column) pairs of the
+stores must cover a rectangle exactly once, with the output address affine in row and column.
+The program ids must shift that rectangle by whole rows/columns (or select a batch): one GEMM per
+launch.  Finally every mask must be a rectangle bound: each atom a bound ``row < R``, ``col < C``
+or ``k < Kb`` on the global GEMM coordinate it guards (its left side equals that coordinate plus
+a constant), and the program-id-free part a prefix ``k < Kb`` of the K range (stores: all true).
+``eas_sgemm_f32_tiled`` then performs, for every stored output, the same ``fma`` chains on the same
+values (masked elements read as 0.0f) and the same additions in the same order: bit-identical
 results.
 
-Every step that does not hold makes the plan decline (``last_reason``), and
-the generic kernel runs.
+Every step that does not hold makes the plan decline (``last_reason``), and the generic kernel
+runs.
 """
 
 from __future__ import annotations
@@ -53,6 +55,7 @@ from ..ir import DType, IRModule, Inst, ValueRef
 
 M32 = np.uint64(0xFFFFFFFF)
 U32_LIMIT = 1 << 32
+INF = 1 << 40
 
 
 class Decline(Exception):
@@ -65,8 +68,14 @@ def _need(cond: bool, why: str) -> None:
 
 
 # ---------------------------------------------------------------------------
-# float terms
+# values
 # ---------------------------------------------------------------------------
+
+@dataclass(frozen=True, eq=False)
+class Mask:
+    conc: np.ndarray                              # (NT,) bool: the program-id-free comparisons
+    atoms: tuple[tuple[np.ndarray, np.ndarray], ...] = ()   # (lhs (4,NT), rhs (4,NT)): lhs < rhs
+
 
 @dataclass(frozen=True, eq=False)
 class FConst:
@@ -76,18 +85,34 @@ class FConst:
 @dataclass(frozen=True, eq=False)
 class FLoad:
     buf: str
-    lin: np.ndarray  # (4, NT) uint64
+    lin: np.ndarray   # (4, NT) uint64
+    mask: Mask
+
+
+@dataclass(frozen=True, eq=False)
+class Side:
+    """One operand of a dot: element k of thread t is ``buf[base[:, t] + k*step]`` where
+    ``conc[t, k]`` and every atom ``lhs0[:, t] + k*lstep < rhs`` hold, else 0.0f."""
+
+    buf: str
+    base: np.ndarray       # (4, NT)
+    step: int
+    conc: np.ndarray       # (NT, K) bool
+    atoms: tuple[tuple[np.ndarray, int, int], ...]
 
 
 @dataclass(frozen=True, eq=False)
 class FDot:
-    a_buf: str
-    a_base: np.ndarray   # (4, NT) global element address of k = 0
-    a_step: int          # address increment per k (same for all threads)
-    b_buf: str
-    b_base: np.ndarray
-    b_step: int
+    a: Side
+    b: Side
     k: int
+
+
+@dataclass(frozen=True, eq=False)
+class FFma:
+    x: Any
+    y: Any
+    z: Any
 
 
 @dataclass(frozen=True, eq=False)
@@ -100,6 +125,9 @@ class _Smem:
     def __init__(self, n: int):
         self.buf = np.full(n, -1, np.int64)           # global buffer code, -1 = never written
         self.lin = np.zeros((4, n), np.uint64)
+        self.conc = np.zeros(n, np.bool_)
+        self.rec = np.full(n, -1, np.int64)           # index of the writing load's atom record
+        self.writer = np.zeros(n, np.int64)           # thread that wrote the slot
         self.wphase = np.full(n, -1, np.int64)
         self.rphase = np.full(n, -1, np.int64)
 
@@ -112,24 +140,57 @@ def _bits(v: float) -> int:
     return struct.unpack("<I", struct.pack("<f", float(np.float32(v))))[0]
 
 
+def _affine_k(arr: np.ndarray, what: str) -> tuple[np.ndarray, int]:
+    """(4, NT, K) forms -> (form at k = 0, per-k increment) when the increment is one constant."""
+    k = arr.shape[2]
+    base = arr[:, :, 0]
+    if k == 1:
+        return base, 0
+    d = (arr[:, :, 1] - base) & M32
+    _need(_pfree(d) and bool((d[0] == d[0][0]).all()), f"{what} not one stride for all threads")
+    step = int(d[0][0])
+    want = np.repeat(base[:, :, None], k, axis=2)
+    want[0] = (want[0] + np.uint64(step) * np.arange(k, dtype=np.uint64)[None, :]) & M32
+    _need(bool((arr == want).all()), f"{what} not affine in k")
+    return base, step
+
+
+def _uniform_rhs(rhs: np.ndarray, what: str) -> int:
+    """rhs (4, ...) forms: program-id free and one value everywhere."""
+    _need(not rhs[1:].any(), f"{what}: bound depends on program_id")
+    _need(bool((rhs[0] == rhs[0].flat[0]).all()), f"{what}: bound differs between elements")
+    return int(rhs[0].flat[0])
+
+
 # ---------------------------------------------------------------------------
 # symbolic execution of one thread group
 # ---------------------------------------------------------------------------
 
 class _Exec:
-    def __init__(self, ir: IRModule, nt: int, scalars: dict[str, int]):
+    def __init__(self, ir: IRModule, nt: int, scalars: dict[str, int], ghost_limit: int | None = None):
         self.ir, self.nt = ir, nt
         self.scalars = scalars
         self.vals: dict[int, Any] = {}
         self.smem: dict[int, _Smem] = {}
-        self.gbuf: dict[int, str] = {}
         self.codes: dict[str, int] = {}
+        self.records: list[tuple[tuple[np.ndarray, np.ndarray], ...]] = []
         self.phase = 0
-        self.stores: list[tuple[str, np.ndarray, Any]] = []
+        self.stores: list[tuple[str, np.ndarray, Any, Mask]] = []
         self.tvec = np.arange(nt, dtype=np.uint64)
+        # threads whose global x index reaches ghost_limit touch no memory: every global access is
+        # guarded by that bound as one more mask atom
+        self.ghost: tuple[tuple[np.ndarray, np.ndarray], ...] = ()
+        if ghost_limit is not None:
+            gx = np.zeros((4, nt), np.uint64)
+            gx[0] = self.tvec
+            gx[1] = np.uint64(nt)
+            self.ghost = ((gx, self.lin_const(ghost_limit)),)
 
     def code(self, name: str) -> int:
         return self.codes.setdefault(name, len(self.codes))
+
+    def name_of(self, code: int) -> str:
+        return next(n for n, c in self.codes.items() if c == code)
 
     def u(self, ref: ValueRef) -> np.ndarray:
         v = self.vals[ref.id]
@@ -146,9 +207,15 @@ class _Exec:
         _need(bool((c == c[0]).all()), f"v{ref.id} differs between threads")
         return int(c[0])
 
-    def mask_true(self, ref: ValueRef) -> None:
+    def mask(self, ref: ValueRef) -> Mask:
         v = self.vals[ref.id]
-        _need(isinstance(v, np.ndarray) and v.dtype == np.bool_ and bool(v.all()), "mask not true for every thread")
+        _need(isinstance(v, Mask), f"v{ref.id} is not a mask")
+        return v
+
+    def plain(self, ref: ValueRef) -> np.ndarray:
+        m = self.mask(ref)
+        _need(not m.atoms, f"v{ref.id}: a program_id-dependent mask used as a value")
+        return m.conc
 
     def lin_const(self, c: np.ndarray | int) -> np.ndarray:
         out = np.zeros((4, self.nt), np.uint64)
@@ -166,7 +233,6 @@ class _Exec:
         name = str(inst.args[0])
         kind = next(a.kind for a in self.ir.args if a.name == name)
         if kind == "buffer":
-            self.gbuf[inst.out.id] = name
             self.vals[inst.out.id] = ("gbuf", name)
         elif inst.out.dtype == DType.U32:
             self.vals[inst.out.id] = self.lin_const(int(self.scalars[name]) % U32_LIMIT)
@@ -178,7 +244,7 @@ class _Exec:
         if dt == DType.U32:
             self.vals[inst.out.id] = self.lin_const(int(v) % U32_LIMIT)
         elif dt == DType.BOOL:
-            self.vals[inst.out.id] = np.full(self.nt, bool(v))
+            self.vals[inst.out.id] = Mask(np.full(self.nt, bool(v)))
         elif dt == DType.F32:
             self.vals[inst.out.id] = FConst(_bits(float(v)))
         else:
@@ -241,6 +307,11 @@ class _Exec:
         else:
             raise Decline("product of two program_id-dependent values")
 
+    def op_fma(self, inst: Inst) -> None:
+        x, y, z = inst.args
+        _need(inst.out.dtype == DType.F32, "fma of a non-f32 type")
+        self.vals[inst.out.id] = FFma(self.vals[x.id], self.vals[y.id], self.vals[z.id])
+
     def op_floordiv(self, inst: Inst) -> None:
         _need(inst.args[0].dtype == DType.U32, "non-u32 division")
         x, y = self.concrete(inst.args[0]), self.concrete(inst.args[1])
@@ -255,27 +326,26 @@ class _Exec:
 
     def op_lt(self, inst: Inst) -> None:
         _need(inst.args[0].dtype == DType.U32, "non-u32 comparison")
-        self.vals[inst.out.id] = self.concrete(inst.args[0]) < self.concrete(inst.args[1])
-
-    def _bool(self, ref: ValueRef) -> np.ndarray:
-        v = self.vals[ref.id]
-        _need(isinstance(v, np.ndarray) and v.dtype == np.bool_, f"v{ref.id} is not a mask")
-        return v
+        a, b = self.u(inst.args[0]), self.u(inst.args[1])
+        if _pfree(a) and _pfree(b):
+            self.vals[inst.out.id] = Mask(a[0] < b[0])
+        else:
+            self.vals[inst.out.id] = Mask(np.ones(self.nt, np.bool_), ((a, b),))
 
     def op_and(self, inst: Inst) -> None:
-        self.vals[inst.out.id] = self._bool(inst.args[0]) & self._bool(inst.args[1])
+        x, y = self.mask(inst.args[0]), self.mask(inst.args[1])
+        self.vals[inst.out.id] = Mask(x.conc & y.conc, x.atoms + y.atoms)
 
     def op_or(self, inst: Inst) -> None:
-        self.vals[inst.out.id] = self._bool(inst.args[0]) | self._bool(inst.args[1])
+        self.vals[inst.out.id] = Mask(self.plain(inst.args[0]) | self.plain(inst.args[1]))
 
     def op_not(self, inst: Inst) -> None:
-        self.vals[inst.out.id] = ~self._bool(inst.args[0])
+        self.vals[inst.out.id] = Mask(~self.plain(inst.args[0]))
 
     def op_where(self, inst: Inst) -> None:
         c, a, b = inst.args
         _need(a.dtype == DType.U32, "where on a non-u32 value")
-        cond = self._bool(c)
-        self.vals[inst.out.id] = np.where(cond[None, :], self.u(a), self.u(b))
+        self.vals[inst.out.id] = np.where(self.plain(c)[None, :], self.u(a), self.u(b))
 
     def op_barrier(self, inst: Inst) -> None:
         self.phase += 1
@@ -287,18 +357,19 @@ class _Exec:
 
     def op_load(self, inst: Inst) -> None:
         buf, off, mask = inst.args
-        self.mask_true(mask)
         kind, ident = self._buffer(buf)
         _need(kind == "gbuf", "load from threadgroup memory")
         _need(inst.out.dtype == DType.F32, "load of a non-f32 value")
-        self.vals[inst.out.id] = FLoad(ident, self.u(off))
+        m = self.mask(mask)
+        self.vals[inst.out.id] = FLoad(ident, self.u(off), Mask(m.conc, m.atoms + self.ghost))
 
     def op_store(self, inst: Inst) -> None:
         buf, off, val, mask = inst.args
-        self.mask_true(mask)
         kind, ident = self._buffer(buf)
         v = self.vals[val.id]
+        m = self.mask(mask)
         if kind == "smem":
+            _need(not m.atoms and not self.ghost and bool(m.conc.all()), "masked threadgroup store")
             sm = self.smem[ident]
             _need(isinstance(v, FLoad), "threadgroup memory holds something other than a global load")
             slots = self.concrete(off)
@@ -309,15 +380,19 @@ class _Exec:
             _need(bool((sm.rphase[s] != self.phase).all()), "threadgroup slot written after a read between barriers")
             sm.buf[s] = self.code(v.buf)
             sm.lin[:, s] = v.lin
+            sm.conc[s] = v.mask.conc
+            self.records.append(v.mask.atoms)
+            sm.rec[s] = len(self.records) - 1
+            sm.writer[s] = np.arange(self.nt)
             sm.wphase[s] = self.phase
         else:
-            self.stores.append((ident, self.u(off), v))
+            self.stores.append((ident, self.u(off), v, Mask(m.conc, m.atoms + self.ghost)))
 
-    def _dot_side(self, buf: ValueRef, base: ValueRef, stride: ValueRef, k: int) -> tuple[str, np.ndarray, int]:
+    def _side(self, buf: ValueRef, base: ValueRef, stride: ValueRef, k: int) -> Side:
         kind, ident = self._buffer(buf)
         step = self.scalar_const(stride)
         if kind == "gbuf":
-            return ident, self.u(base), step
+            return Side(ident, self.u(base), step, np.ones((self.nt, k), np.bool_), ())
         sm = self.smem[ident]
         b0 = self.concrete(base).astype(np.int64)
         slots = b0[:, None] + np.arange(k, dtype=np.int64)[None, :] * step   # (NT, K), exact
@@ -327,49 +402,82 @@ class _Exec:
         codes = sm.buf[slots]
         _need(bool((codes == codes.flat[0]).all()), "dot reads slots loaded from different buffers")
         sm.rphase[slots.ravel()] = self.phase
-        lin = sm.lin[:, slots]                                   # (4, NT, K)
-        base_lin = lin[:, :, 0]
-        if k > 1:
-            d = (lin[:, :, 1] - base_lin) & M32
-            _need(_pfree(d) and bool((d[0] == d[0][0]).all()), "dot addresses not one stride for all threads")
-            dk = int(d[0][0])
-            want = np.repeat(base_lin[:, :, None], k, axis=2)
-            want[0] = (want[0] + np.uint64(dk) * np.arange(k, dtype=np.uint64)[None, :]) & M32
-            _need(bool((lin == want).all()), "dot addresses not affine in k")
-        else:
-            dk = 0
-        name = next(n for n, c in self.codes.items() if c == int(codes.flat[0]))
-        return name, base_lin, dk
+        lin_base, lstep = _affine_k(sm.lin[:, slots], "dot addresses")
+        rec, writer = sm.rec[slots], sm.writer[slots]
+        recs = np.unique(rec)
+        na = len(self.records[int(recs[0])])
+        _need(all(len(self.records[int(r)]) == na for r in recs), "slots loaded under different mask shapes")
+        atoms = []
+        for a in range(na):
+            lhs = np.zeros((4,) + slots.shape, np.uint64)
+            rhs = np.zeros((4,) + slots.shape, np.uint64)
+            for r in recs:
+                pos = rec == r
+                l_r, r_r = self.records[int(r)][a]
+                lhs[:, pos] = l_r[:, writer[pos]]
+                rhs[:, pos] = r_r[:, writer[pos]]
+            l0, ls = _affine_k(lhs, "mask bound")
+            atoms.append((l0, ls, _uniform_rhs(rhs, "mask")))
+        return Side(self.name_of(int(codes.flat[0])), lin_base, lstep, sm.conc[slots], tuple(atoms))
 
     def op_dot(self, inst: Inst) -> None:
         a_buf, a_base, a_stride, b_buf, b_base, b_stride, k_ref = inst.args
         _need(a_buf.dtype == DType.F32 and b_buf.dtype == DType.F32, "dot over non-f32 operands")
         k = self.scalar_const(k_ref)
         _need(k >= 1, "dot of length 0")
-        an, ab, ad = self._dot_side(a_buf, a_base, a_stride, k)
-        bn, bb, bd = self._dot_side(b_buf, b_base, b_stride, k)
-        self.vals[inst.out.id] = FDot(an, ab, ad, bn, bb, bd, k)
+        self.vals[inst.out.id] = FDot(self._side(a_buf, a_base, a_stride, k), self._side(b_buf, b_base, b_stride, k), k)
 
 
 # ---------------------------------------------------------------------------
 # GEMM derivation
 # ---------------------------------------------------------------------------
 
+def _loads_side(loads: list[FLoad]) -> Side:
+    """Global loads l_0 .. l_{K-1} (one per k) as one dot operand."""
+    _need(all(isinstance(x, FLoad) for x in loads), "fma operand is not a global load")
+    _need(len({x.buf for x in loads}) == 1, "fma operands from different buffers along k")
+    base, step = _affine_k(np.stack([x.lin for x in loads], axis=2), "fma operand addresses")
+    na = len(loads[0].mask.atoms)
+    _need(all(len(x.mask.atoms) == na for x in loads), "fma operands under different mask shapes")
+    atoms = []
+    for a in range(na):
+        l0, ls = _affine_k(np.stack([x.mask.atoms[a][0] for x in loads], axis=2), "mask bound")
+        atoms.append((l0, ls, _uniform_rhs(np.stack([x.mask.atoms[a][1] for x in loads], axis=2), "mask")))
+    conc = np.stack([x.mask.conc for x in loads], axis=1)
+    return Side(loads[0].buf, base, step, conc, tuple(atoms))
+
+
+def _as_dot(term: Any) -> FDot | None:
+    """A dot, or an fma chain fma(x_{K-1}, y_{K-1}, ... fma(x_0, y_0, 0.0f)) over global loads."""
+    if isinstance(term, FDot):
+        return term
+    if not isinstance(term, FFma):
+        return None
+    xs, ys = [], []
+    while isinstance(term, FFma):
+        xs.append(term.x)
+        ys.append(term.y)
+        term = term.z
+    _need(isinstance(term, FConst) and term.bits == 0, "fma chain does not start at +0.0f")
+    return FDot(_loads_side(xs[::-1]), _loads_side(ys[::-1]), len(xs))
+
+
 def _fold(term: Any) -> tuple[bool, list[FDot]]:
-    """((z + d0) + d1) + ...  ->  (zero_init, [d0, d1, ...])."""
+    """((z + d0) + d1) + ...  ->  (zero_init, [d0, d1, ...]); IEEE addition commutes exactly."""
     chain: list[FDot] = []
     while isinstance(term, FAdd):
-        x, y = term.x, term.y
-        if isinstance(y, FDot) and not isinstance(x, FDot) or (isinstance(x, FDot) and isinstance(y, FDot)):
-            chain.append(y)
-            term = x
-        elif isinstance(x, FDot):
-            chain.append(x)
-            term = y
+        dx, dy = _as_dot(term.x), _as_dot(term.y)
+        if dy is not None:
+            chain.append(dy)
+            term = term.x
+        elif dx is not None:
+            chain.append(dx)
+            term = term.y
         else:
             raise Decline("sum of two non-dot terms")
-    if isinstance(term, FDot):
-        chain.append(term)
+    d = _as_dot(term)
+    if d is not None:
+        chain.append(d)
         return False, chain[::-1]
     _need(isinstance(term, FConst) and term.bits == 0, "sum does not start at +0.0f or a dot")
     _need(bool(chain), "store of a constant")
@@ -389,62 +497,62 @@ def _ap(values: np.ndarray) -> tuple[int, int, int] | None:
 
 def derive(ex: _Exec) -> dict[str, Any]:
     _need(bool(ex.stores), "no global stores")
-    outs = {b for b, _, _ in ex.stores}
+    outs = {s[0] for s in ex.stores}
     _need(len(outs) == 1, "stores to more than one buffer")
     c_buf = outs.pop()
-    folds = [_fold(v) for _, _, v in ex.stores]
+    folds = [_fold(v) for _, _, v, _ in ex.stores]
     zero_init = folds[0][0]
     _need(all(z == zero_init for z, _ in folds), "sums start differently")
     ntile = len(folds[0][1])
     _need(all(len(ch) == ntile for _, ch in folds), "sums of different lengths")
-    kt = folds[0][1][0].k
+    # operand roles: A is the side contiguous along k (products commute exactly)
+    d0 = folds[0][1][0]
+    swap = d0.a.step != 1 and d0.b.step == 1
+    chains = [[FDot(d.b, d.a, d.k) if swap else d for d in ch] for _, ch in folds]
+    kt = chains[0][0].k
     _need(kt % 8 == 0, "K tile not a multiple of 8")
-    a_buf, b_buf = folds[0][1][0].a_buf, folds[0][1][0].b_buf
+    a_buf, b_buf = chains[0][0].a.buf, chains[0][0].b.buf
     _need(c_buf not in (a_buf, b_buf), "output buffer is also an operand")
-    S = len(ex.stores)
-    base_a = np.stack([ch[0].a_base for _, ch in folds])          # (S, 4, NT)
-    base_b = np.stack([ch[0].b_base for _, ch in folds])
-    out_c = np.stack([off for _, off, _ in ex.stores])
-    for _, ch in folds:
+    base_a = np.stack([ch[0].a.base for ch in chains])          # (S, 4, NT)
+    base_b = np.stack([ch[0].b.base for ch in chains])
+    out_c = np.stack([s[1] for s in ex.stores])
+    b_sk = chains[0][0].b.step
+    for s, ch in enumerate(chains):
         for t, d in enumerate(ch):
-            _need(d.k == kt and d.a_buf == a_buf and d.b_buf == b_buf, "dots differ in length or operands")
-            _need(d.a_step == 1 or kt == 1, "A not contiguous along k")
-    b_sk = folds[0][1][0].b_step
-    kk0 = np.uint64(kt)
-    for s, (_, ch) in enumerate(folds):
-        for t, d in enumerate(ch):
-            _need(d.b_step == b_sk, "B stride along k differs")
-            sh = np.uint64(t) * kk0
-            _need(bool((((base_a[s] + np.array([sh, 0, 0, 0], np.uint64)[:, None]) & M32) == d.a_base).all()),
+            _need(d.k == kt and d.a.buf == a_buf and d.b.buf == b_buf, "dots differ in length or operands")
+            _need(d.a.step == 1, "A not contiguous along k")
+            _need(d.b.step == b_sk, "B stride along k differs")
+            sh = np.uint64(t) * np.uint64(kt)
+            _need(bool((((base_a[s] + np.array([sh, 0, 0, 0], np.uint64)[:, None]) & M32) == d.a.base).all()),
                   "A tiles not consecutive along k")
             _need(bool((((base_b[s] + np.array([sh * np.uint64(b_sk), 0, 0, 0], np.uint64)[:, None]) & M32)
-                        == d.b_base).all()), "B tiles not consecutive along k")
-    # program-id coefficients, common to every output
+                        == d.b.base).all()), "B tiles not consecutive along k")
     coefs = {}
     for name, arr in (("a", base_a), ("b", base_b), ("c", out_c)):
         p = arr[:, 1:, :]
         _need(bool((p == p[:1, :, :1]).all()), f"{name} address depends on program_id differently per thread")
         coefs[name] = [int(x) for x in p[0, :, 0]]
-    ca = base_a[:, 0, :].ravel().astype(np.int64)
-    cb = base_b[:, 0, :].ravel().astype(np.int64)
-    cc = out_c[:, 0, :].ravel().astype(np.int64)
-    ra, rb = _ap(ca), _ap(cb)
+    S, NT = base_a.shape[0], base_a.shape[2]
+    ca = base_a[:, 0, :].astype(np.int64)                       # (S, NT)
+    cb = base_b[:, 0, :].astype(np.int64)
+    cc = out_c[:, 0, :].astype(np.int64)
+    ra, rb = _ap(ca.ravel()), _ap(cb.ravel())
     _need(ra is not None and rb is not None, "rows or columns not evenly spaced")
     a0, a_sm, bm = ra
     b0, b_sn, bn = rb
     _need(b_sn in (0, 1), "B columns not contiguous")
     i = (ca - a0) // a_sm if a_sm else np.zeros_like(ca)
     j = (cb - b0) // b_sn if b_sn else np.zeros_like(cb)
-    _need(len(ca) == bm * bn and len(np.unique(i * bn + j)) == bm * bn, "outputs do not cover the tile once")
+    _need(S * NT == bm * bn and len(np.unique((i * bn + j).ravel())) == bm * bn, "outputs do not cover the tile once")
     c0 = int(cc[(i == 0) & (j == 0)][0])
-    # C = c0 + i*c_sm + j*c_sn
     c_sn = int(cc[(i == 0) & (j == 1)][0]) - c0 if bn > 1 else 1
     c_sm = int(cc[(i == 1) & (j == 0)][0]) - c0 if bm > 1 else 0
     _need(c_sn == 1, "C columns not contiguous")
     _need(bool((cc == c0 + i * c_sm + j * c_sn).all()), "output addresses not affine in row and column")
     return {"a_buf": a_buf, "b_buf": b_buf, "c_buf": c_buf, "zero_init": zero_init, "kt": kt, "ntile": ntile,
             "a0": a0, "a_sm": a_sm, "b0": b0, "b_sk": b_sk, "c0": c0, "c_sm": c_sm, "bm": bm, "bn": bn,
-            "coef_a": coefs["a"], "coef_b": coefs["b"], "coef_c": coefs["c"]}
+            "coef_a": coefs["a"], "coef_b": coefs["b"], "coef_c": coefs["c"],
+            "_chains": chains, "_i": i, "_j": j, "_store_masks": [s[3] for s in ex.stores]}
 
 
 def map_grid(d: dict[str, Any], programs: tuple[int, int, int]) -> dict[str, Any]:
@@ -452,12 +560,16 @@ def map_grid(d: dict[str, Any], programs: tuple[int, int, int]) -> dict[str, Any
     bm, bn = d["bm"], d["bn"]
     M, N, batch = bm, bn, 1
     row = col = bat = None
+    a_sm, c_sm = d["a_sm"], d["c_sm"]
     for ax in range(3):
         if programs[ax] <= 1:
             continue
         ca, cb, cc = d["coef_a"][ax], d["coef_b"][ax], d["coef_c"][ax]
-        if row is None and bm > 1 and cb == 0 and ca == bm * d["a_sm"] and cc == bm * d["c_sm"]:
+        if row is None and cb == 0 and ca != 0 and (
+                (bm > 1 and ca == bm * a_sm and cc == bm * c_sm) or (bm == 1 and (a_sm, c_sm) == (0, 0))):
             row = ax
+            if bm == 1:  # one row per group: the row strides are the program-id coefficients
+                a_sm, c_sm = ca, cc
         elif col is None and ca == 0 and cb == bn and cc == bn:
             col = ax
         elif bat is None:
@@ -472,16 +584,106 @@ def map_grid(d: dict[str, Any], programs: tuple[int, int, int]) -> dict[str, Any
     if bat is not None:
         batch = programs[bat]
         a_bs, b_bs, c_bs = d["coef_a"][bat], d["coef_b"][bat], d["coef_c"][bat]
-    K = d["kt"] * d["ntile"]
-    # outputs written once: rows apart by >= N, batches apart by the whole M x N block
-    _need(M == 1 or d["c_sm"] >= N, "output rows overlap")
-    _need(batch == 1 or c_bs >= (M - 1) * d["c_sm"] + N, "output batches overlap")
-    top_a = d["a0"] + (M - 1) * d["a_sm"] + (K - 1) + (batch - 1) * a_bs
-    top_b = d["b0"] + (K - 1) * d["b_sk"] + (N - 1) + (batch - 1) * b_bs
-    top_c = d["c0"] + (M - 1) * d["c_sm"] + (N - 1) + (batch - 1) * c_bs
+    return {"M": M, "N": N, "K": d["kt"] * d["ntile"], "batch": batch, "a_sm": a_sm, "c_sm": c_sm,
+            "a_bs": a_bs, "b_bs": b_bs, "c_bs": c_bs, "row_ax": row, "col_ax": col, "bat_ax": bat}
+
+
+def _classify(lhs0: np.ndarray, lstep: int, rhs: int, coords: dict[str, tuple[np.ndarray, int, int, int]],
+              active: list[int], allowed: tuple[str, ...], what: str) -> tuple[str, int]:
+    """An atom ``lhs0 + k*lstep < rhs`` over elements (forms broadcast to the coordinate arrays) as
+    ``coord < bound``: its left side must be coordinate + a constant, with the coordinate's
+    program-id coefficient and no other, and coordinate + constant must stay below 2^32 over the
+    whole launch (so the u32 comparison is the integer one).  coords: name -> (per-element offset,
+    program axis or -1, coefficient per program id, largest value of the coordinate in the launch),
+    the coordinate's value being offset + coefficient * P[axis]."""
+    for name in allowed:
+        off, ax, coef, top = coords[name]
+        kstep = 1 if name == "k" else 0
+        if lstep != kstep:
+            continue
+        ok = True
+        for a in active:
+            want = coef if a == ax else 0
+            if not bool((lhs0[1 + a] == np.uint64(want % U32_LIMIT)).all()):
+                ok = False
+                break
+        if not ok:
+            continue
+        delta = (lhs0[0].astype(np.int64) - np.broadcast_to(off, lhs0[0].shape)) % U32_LIMIT
+        if not bool((delta == delta.flat[0]).all()):
+            continue
+        dlt = int(delta.flat[0])
+        if top + dlt >= U32_LIMIT:
+            continue
+        return name, max(0, rhs - dlt)
+    raise Decline(f"{what}: a mask that is not a row, column or k bound")
+
+
+def bounds(d: dict[str, Any], programs: tuple[int, int, int]) -> dict[str, int]:
+    """Zero-fill and store bounds of the launch from the masks (module docstring)."""
+    active = [ax for ax in range(3) if programs[ax] > 1]
+    kt, bm, bn = d["kt"], d["bm"], d["bn"]
+    row_ax = d["row_ax"] if d["row_ax"] is not None else -1
+    col_ax = d["col_ax"] if d["col_ax"] is not None else -1
+    out = {"a_rows": INF, "a_cols": INF, "a_k": INF, "b_rows": INF, "b_cols": INF, "b_k": INF, "s_rows": INF,
+           "s_cols": INF}
+    i, j = d["_i"], d["_j"]                                      # (S, NT)
+    top_row = int(i.max()) + (bm * (programs[row_ax] - 1) if row_ax >= 0 else 0)
+    top_col = int(j.max()) + (bn * (programs[col_ax] - 1) if col_ax >= 0 else 0)
+    top_k = kt * d["ntile"] - 1
+    for s, ch in enumerate(d["_chains"]):
+        for t, dot in enumerate(ch):
+            kglob = t * kt + np.arange(kt, dtype=np.int64)[None, :]   # (1, K)
+            coords = {"row": (i[s][:, None], row_ax, bm, top_row), "col": (j[s][:, None], col_ax, bn, top_col),
+                      "k": (kglob, -1, 0, top_k)}
+            for side, pre, lim_k in ((dot.a, "a_", "a_k"), (dot.b, "b_", "b_k")):
+                for l0, ls, rhs in side.atoms:
+                    lhs = l0[:, :, None] + np.zeros((1, 1, kt), np.uint64)
+                    kind, bound = _classify(lhs, ls, rhs, coords, active, ("row", "col", "k"), "operand mask")
+                    key = lim_k if kind == "k" else pre + ("rows" if kind == "row" else "cols")
+                    out[key] = min(out[key], bound)
+                # the program-id-free part must be a prefix of the K range
+                conc = side.conc
+                kk = np.broadcast_to(kglob, conc.shape)
+                if not bool(conc.all()):
+                    first_false = int(kk[~conc].min())
+                    _need(bool((conc == (kk < first_false)).all()), "operand mask is not a K prefix")
+                    out[lim_k] = min(out[lim_k], first_false)
+    for s, m in enumerate(d["_store_masks"]):
+        _need(bool(m.conc.all()), "store mask with a program_id-free part")
+        coords = {"row": (i[s], row_ax, bm, top_row), "col": (j[s], col_ax, bn, top_col)}
+        for lhs, rhs in m.atoms:
+            kind, bound = _classify(lhs, 0, _uniform_rhs(rhs, "store mask"), coords, active, ("row", "col"),
+                                    "store mask")
+            key = "s_rows" if kind == "row" else "s_cols"
+            out[key] = min(out[key], bound)
+    return out
+
+
+def plan_launch(d: dict[str, Any], g: dict[str, Any], b: dict[str, int]) -> dict[str, Any]:
+    """Extents, zero-fill bounds and address limits of the native launch."""
+    M = min(g["M"], b["s_rows"])
+    N = min(g["N"], b["s_cols"])
+    K, batch = g["K"], g["batch"]
+    # a bound on A by the output column (or on B by the output row) only holds if no stored output
+    # lies beyond it: then it is true wherever the result is kept
+    _need(b["a_cols"] >= N and b["b_rows"] >= M, "operand masked by the other operand's coordinate")
+    a_rows, b_cols = min(M, b["a_rows"]), min(N, b["b_cols"])
+    a_k, b_k = min(K, b["a_k"]), min(K, b["b_k"])
+    a_sm, c_sm = g["a_sm"], g["c_sm"]
+    _need(M <= 1 or c_sm >= N, "output rows overlap")
+    _need(batch == 1 or g["c_bs"] >= (M - 1) * c_sm + N, "output batches overlap")
+    top_a = d["a0"] + max(a_rows - 1, 0) * a_sm + max(a_k - 1, 0) + (batch - 1) * g["a_bs"]
+    top_b = d["b0"] + max(b_k - 1, 0) * d["b_sk"] + max(b_cols - 1, 0) + (batch - 1) * g["b_bs"]
+    top_c = d["c0"] + max(M - 1, 0) * c_sm + max(N - 1, 0) + (batch - 1) * g["c_bs"]
     _need(max(top_a, top_b, top_c) < U32_LIMIT, "an index would wrap at 2^32")
-    return {"M": M, "N": N, "K": K, "batch": batch, "a_bs": a_bs, "b_bs": b_bs, "c_bs": c_bs,
-            "top_a": top_a, "top_b": top_b, "top_c": top_c}
+    out = {k: v for k, v in d.items() if not k.startswith("_")}
+    out.update({"M": M, "N": N, "K": K, "batch": batch, "a_sm": a_sm, "c_sm": c_sm, "a_bs": g["a_bs"],
+                "b_bs": g["b_bs"], "c_bs": g["c_bs"], "a_rows": a_rows, "a_k": a_k, "b_cols": b_cols, "b_k": b_k,
+                "top_a": top_a, "top_b": top_b, "top_c": top_c,
+                "empty": M <= 0 or N <= 0,
+                "reads_a": a_rows > 0 and a_k > 0, "reads_b": b_cols > 0 and b_k > 0})
+    return out
 
 
 # ---------------------------------------------------------------------------
@@ -489,7 +691,7 @@ def map_grid(d: dict[str, Any], programs: tuple[int, int, int]) -> dict[str, Any
 # ---------------------------------------------------------------------------
 
 _OPS = {"arg", "const", "alloc_tg", "program_id", "thread_id", "tid", "local_id", "lane_id", "sg_id", "add", "mul",
-        "floordiv", "mod", "lt", "and", "or", "not", "where", "barrier", "load", "store", "dot"}
+        "floordiv", "mod", "lt", "and", "or", "not", "where", "barrier", "load", "store", "dot", "fma"}
 
 
 class TiledGemmPlan:
@@ -508,12 +710,13 @@ class TiledGemmPlan:
         hit = self.cache.get(key)
         if hit is None:
             try:
-                _need(ntx >= programs[0] * self.block, "partial thread groups (ghost threads)")
-                ex = _Exec(self.ir, self.block, scalars)
+                ghost = ntx if ntx < programs[0] * self.block else None
+                ex = _Exec(self.ir, self.block, scalars, ghost)
                 ex.run()
                 d = derive(ex)
-                d.update(map_grid(d, programs))
-                hit = d
+                g = map_grid(d, programs)
+                d.update({"row_ax": g["row_ax"], "col_ax": g["col_ax"]})
+                hit = plan_launch(d, g, bounds(d, programs))
             except Decline as e:
                 hit = str(e)
             if len(self.cache) > 64:
@@ -534,10 +737,13 @@ class TiledGemmPlan:
         d = self.analyse(scalars, programs, ntx)
         if d is None:
             return False
+        if d["empty"]:
+            return True  # the kernel stores nothing for these values
         from .patterns import _numel
 
-        for n, top in ((d["a_buf"], d["top_a"]), (d["b_buf"], d["top_b"]), (d["c_buf"], d["top_c"])):
-            if top >= _numel(runtime_args[n]):
+        for n, top, used in ((d["a_buf"], d["top_a"], d["reads_a"]), (d["b_buf"], d["top_b"], d["reads_b"]),
+                             (d["c_buf"], d["top_c"], True)):
+            if used and top >= _numel(runtime_args[n]):
                 self.last_reason = f"{n}: the product reaches past the buffer"
                 return False
         pa, pb, pc = args[d["a_buf"]].ptr, args[d["b_buf"]].ptr, args[d["c_buf"]].ptr
@@ -549,7 +755,8 @@ class TiledGemmPlan:
         lib = rt.lib()
         rc = lib.eas_sgemm_f32_tiled(pa + 4 * d["a0"], pb + 4 * d["b0"], pc + 4 * d["c0"], d["M"], d["N"], d["K"],
                                      d["kt"], d["batch"], d["a_sm"], d["a_bs"], d["b_sk"], d["b_bs"], d["c_sm"],
-                                     d["c_bs"], int(d["zero_init"]), stream)
+                                     d["c_bs"], int(d["zero_init"]), d["a_rows"], d["a_k"], d["b_cols"], d["b_k"],
+                                     stream)
         from ..runtime import cuda_ext
 
         if rc == cuda_ext.EAS_ERR_VALUE:
@@ -567,6 +774,8 @@ def match_tiled(ir: IRModule, lowered: Any) -> TiledGemmPlan | None:
         return None
     if any(i.op not in _OPS for i in ir.insts):
         return None
-    if not any(i.op == "dot" for i in ir.insts):
+    if not any(i.op in ("dot", "fma") for i in ir.insts):
+        return None
+    if any(i.op == "fma" and i.out.dtype != DType.F32 for i in ir.insts):
         return None
     return TiledGemmPlan(ir, lowered.block_size)

@@ -31,7 +31,9 @@
 //   A[b][m][k] at a + b*a_bs + m*lda + k
 //   B[b][k][n] at b + b*b_bs + k*ldb + n
 //
-// Rows m >= M and columns n >= N are read as zero and not stored.  No spin
+// A[m][k] reads as zero unless m < a_rows and k < a_k, B[k][n] unless k < b_k
+// and n < b_cols (the DSL kernel's masked loads); outputs m < M, n < N are
+// computed and stored.  No spin
 // waits; the only synchronisation is cp.async.wait_group and __syncthreads.
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -41,6 +43,12 @@
 #include "eas_internal.h"
 
 namespace {
+
+// Zero-fill bounds of the operands: A[m][k] reads as 0 unless m < a_rows and k < a_k, B[k][n]
+// unless k < b_k and n < b_cols (the masked loads of the DSL kernel).  Stores cover m < M, n < N.
+struct SgemmValid {
+  uint32_t a_rows, a_k, b_cols, b_k;
+};
 
 __device__ __forceinline__ void cp_async16(float* dst, const float* src, uint32_t bytes) {
   const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(dst));
@@ -66,7 +74,7 @@ template <int BM, int BN, int BKS, int STAGES, int TM, int TN, int MINB>
 __global__ void __launch_bounds__(SgemmCfg<BM, BN, BKS, STAGES, TM, TN>::kThreads, MINB)
 sgemm_ffma_kernel(const float* __restrict__ A, const float* __restrict__ B, float* __restrict__ C, uint32_t M,
                   uint32_t N, uint32_t K, uint32_t stages_per_tile, uint64_t lda, uint64_t ldb, uint64_t ldc,
-                  uint64_t a_bs, uint64_t b_bs, uint64_t c_bs, int zero_init) {
+                  uint64_t a_bs, uint64_t b_bs, uint64_t c_bs, int zero_init, SgemmValid valid) {
   using Cfg = SgemmCfg<BM, BN, BKS, STAGES, TM, TN>;
   extern __shared__ __align__(16) float smem[];
   float* sA = smem;
@@ -90,17 +98,20 @@ sgemm_ffma_kernel(const float* __restrict__ A, const float* __restrict__ B, floa
       for (int q = 0; q < Cfg::kAChunks; ++q) {
         const int idx = tid + q * Cfg::kThreads;
         const int r = idx / (BKS / 4), kc = (idx % (BKS / 4)) * 4;
-        const uint32_t m = m0 + r;
-        const float* src = A + (uint64_t)(m < M ? m : 0) * lda + k0 + kc;
-        cp_async16(sA + buf * Cfg::kAStage + r * Cfg::kLdA + kc, src, m < M ? 16u : 0u);
+        const uint32_t m = m0 + r, k = k0 + kc;
+        const bool live = m < valid.a_rows && k < valid.a_k;
+        const uint32_t bytes = live ? (k + 4 <= valid.a_k ? 16u : 4u * (valid.a_k - k)) : 0u;
+        const float* src = live ? A + (uint64_t)m * lda + k : A;
+        cp_async16(sA + buf * Cfg::kAStage + r * Cfg::kLdA + kc, src, bytes);
       }
 #pragma unroll
       for (int q = 0; q < Cfg::kBChunks; ++q) {
         const int idx = tid + q * Cfg::kThreads;
         const int r = idx / (BN / 4), nc = (idx % (BN / 4)) * 4;
-        const uint32_t n = n0 + nc;
-        const uint32_t bytes = n + 3 < N ? 16u : (n < N ? 4u * (N - n) : 0u);
-        const float* src = B + (uint64_t)(k0 + r) * ldb + (n < N ? n : 0);
+        const uint32_t n = n0 + nc, k = k0 + r;
+        const bool live = n < valid.b_cols && k < valid.b_k;
+        const uint32_t bytes = live ? (n + 4 <= valid.b_cols ? 16u : 4u * (valid.b_cols - n)) : 0u;
+        const float* src = live ? B + (uint64_t)k * ldb + n : B;
         cp_async16(sB + buf * Cfg::kBStage + r * Cfg::kLdB + nc, src, bytes);
       }
     }
@@ -190,8 +201,8 @@ sgemm_ffma_kernel(const float* __restrict__ A, const float* __restrict__ B, floa
 
 template <int BM, int BN, int BKS, int STAGES, int TM, int TN, int MINB>
 int launch_sgemm(const float* a, const float* b, float* c, uint32_t M, uint32_t N, uint32_t K, uint32_t k_tile,
-                  uint32_t batch, uint64_t lda, uint64_t a_bs, uint64_t ldb, uint64_t b_bs, uint64_t ldc,
-                  uint64_t c_bs, int zero_init, cudaStream_t s) {
+                 uint32_t batch, uint64_t lda, uint64_t a_bs, uint64_t ldb, uint64_t b_bs, uint64_t ldc,
+                 uint64_t c_bs, int zero_init, SgemmValid valid, cudaStream_t s) {
   using Cfg = SgemmCfg<BM, BN, BKS, STAGES, TM, TN>;
   const uint32_t gy = (M + BM - 1) / BM;
   if (gy > 65535) return eas_fail(EAS_ERR_VALUE, "eas_sgemm_f32_tiled: M too large");
@@ -209,7 +220,7 @@ int launch_sgemm(const float* a, const float* b, float* c, uint32_t M, uint32_t 
   }
   dim3 grid((N + BN - 1) / BN, gy, batch);
   kern<<<grid, Cfg::kThreads, smem, s>>>(a, b, c, M, N, K, k_tile / BKS, lda, ldb, ldc, a_bs, b_bs, c_bs,
-                                         zero_init);
+                                         zero_init, valid);
   return eas_cuda_check(cudaGetLastError(), "sgemm_ffma launch", EAS_ERR_LAUNCH);
 }
 
@@ -218,7 +229,7 @@ int launch_sgemm(const float* a, const float* b, float* c, uint32_t M, uint32_t 
 extern "C" int eas_sgemm_f32_tiled(const float* a, const float* b, float* c, uint32_t M, uint32_t N, uint32_t K,
                                    uint32_t k_tile, uint32_t batch, uint64_t lda, uint64_t a_bstride, uint64_t ldb,
                                    uint64_t b_bstride, uint64_t ldc, uint64_t c_bstride, int zero_init,
-                                   void* stream) {
+                                   uint32_t a_rows, uint32_t a_k, uint32_t b_cols, uint32_t b_k, void* stream) {
   if (!a || !b || !c) return eas_fail(EAS_ERR_VALUE, "eas_sgemm_f32_tiled: null operand");
   if (M == 0 || N == 0 || batch == 0) return EAS_OK;
   if (K == 0 || k_tile == 0 || K % k_tile) return eas_fail(EAS_ERR_VALUE, "eas_sgemm_f32_tiled: K must be a positive multiple of k_tile");
@@ -230,6 +241,7 @@ extern "C" int eas_sgemm_f32_tiled(const float* a, const float* b, float* c, uin
     return eas_fail(EAS_ERR_VALUE, "eas_sgemm_f32_tiled: strides must be multiples of 4 elements");
   if (batch > 65535) return eas_fail(EAS_ERR_VALUE, "eas_sgemm_f32_tiled: batch exceeds 65535");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const SgemmValid valid{a_rows < M ? a_rows : M, a_k < K ? a_k : K, b_cols < N ? b_cols : N, b_k < K ? b_k : K};
   // 128 x 128 tiles (8 x 8 per thread, 1 CTA per SM) when the launch has at least four waves of
   // them; otherwise 64 x 64 tiles (8 x 4 per thread, 4 CTAs per SM), which balance small
   // problems better over the SMs (2048^3: 1024 tiles instead of 256 on 148 SMs).
@@ -239,7 +251,7 @@ extern "C" int eas_sgemm_f32_tiled(const float* a, const float* b, float* c, uin
   const uint64_t big_tiles = (uint64_t)((M + 127) / 128) * ((N + 127) / 128) * batch;
   const bool small = big_tiles < 4ull * (uint64_t)sms;
 #define EAS_SG(BM, BN, BKS, ST, TM, TN, MINB) \
-  launch_sgemm<BM, BN, BKS, ST, TM, TN, MINB>(a, b, c, M, N, K, k_tile, batch, lda, a_bstride, ldb, b_bstride, ldc, c_bstride, zero_init, s)
+  launch_sgemm<BM, BN, BKS, ST, TM, TN, MINB>(a, b, c, M, N, K, k_tile, batch, lda, a_bstride, ldb, b_bstride, ldc, c_bstride, zero_init, valid, s)
   if (small) {
     if (k_tile % 32 == 0) return EAS_SG(64, 64, 32, 2, 8, 4, 4);
     if (k_tile % 16 == 0) return EAS_SG(64, 64, 16, 2, 8, 4, 4);

@@ -157,13 +157,17 @@ int eas_gemm_f16(const void* a, const void* b, float* c, uint32_t M, uint32_t N,
  *   C[b][m][n] = acc
  *   A at a + b*a_bstride + m*lda + k, B at b + b*b_bstride + k*ldb + n,
  *   C at c + b*c_bstride + m*ldc + n   (elements)
+ * A[m][k] reads as 0.0f unless m < a_rows and k < a_k, B[k][n] unless
+ * k < b_k and n < b_cols (the DSL kernel's masked loads, which yield 0);
+ * outputs m < M, n < N are stored.
  * The same operations in the same order as the generated kernel, so the
  * results are bit-identical.  K must be a multiple of k_tile and k_tile a
  * multiple of 8; operands 16-byte aligned, strides multiples of 4 elements;
  * otherwise EAS_ERR_VALUE.  Asynchronous on `stream`. */
 int eas_sgemm_f32_tiled(const float* a, const float* b, float* c, uint32_t M, uint32_t N, uint32_t K,
                         uint32_t k_tile, uint32_t batch, uint64_t lda, uint64_t a_bstride, uint64_t ldb,
-                        uint64_t b_bstride, uint64_t ldc, uint64_t c_bstride, int zero_init, void* stream);
+                        uint64_t b_bstride, uint64_t ldc, uint64_t c_bstride, int zero_init,
+                        uint32_t a_rows, uint32_t a_k, uint32_t b_cols, uint32_t b_k, void* stream);
 
 /* Read and clear the status word of native kernels on `dev` (0 = ok,
  * EAS_ERR_TIMEOUT = a bounded wait expired).  Valid after the stream synced. */

@@ -15,7 +15,7 @@ import pytest
 import goldens
 from easy_as_b200.codegen.tiled import TiledGemmPlan, match_tiled
 from easy_as_b200.compiler import compile_ir
-from easy_as_b200.ir import IRModule
+from easy_as_b200.ir import Inst, IRModule
 
 
 def _plan(cid):
@@ -53,20 +53,96 @@ def test_grid_smaller_than_the_matrix_is_a_smaller_gemm():
     assert d is not None and (d["M"], d["N"]) == (64, 96)
 
 
-def test_ghost_threads_decline():
+def test_ghost_threads_of_the_tiled_kernel_decline():
+    """Ghost threads skip their threadgroup stores, so the tile would be incomplete."""
     plan, _ = _plan("matmul_tiled_full")
     assert plan.analyse({"M": 64, "N": 128}, (4, 2, 1), 4 * 256 - 3) is None
-    assert "ghost" in plan.last_reason
+    assert "threadgroup store" in plan.last_reason
     assert plan.analyse({"M": 64, "N": 128}, (4, 2, 1), 0xFFFFFFFF) is not None  # explicit grid: all threads
 
 
-@pytest.mark.parametrize("cid", ["matmul_tiled_masked", "t_matmul_tiled"])
-def test_masked_kernels_decline(cid):
-    c = goldens.case(cid)
-    plan = TiledGemmPlan(goldens.ir_from_json(c["opt"]), c["block_size"])
-    scal = {n: v for n, v in zip(c["arg_names"], c["args"]) if not isinstance(v, dict)}
-    g = c["launch"]["grid"]
-    assert plan.analyse(scal, tuple(g), g[0] * c["block_size"]) is None
+def test_masked_tiled_kernel_is_a_zero_filled_gemm():
+    plan, c = _plan("matmul_tiled_masked")
+    d = plan.analyse({"M": 50, "N": 70, "PID_M_BASE": 0, "PID_N_BASE": 0}, (2, 4, 1), 0xFFFFFFFF)
+    assert d is not None, plan.last_reason
+    assert (d["M"], d["N"], d["K"], d["kt"]) == (50, 70, 64, 16)          # stores clipped to row < M, col < N
+    assert (d["a_rows"], d["a_k"], d["b_cols"], d["b_k"]) == (50, 64, 70, 64)
+
+
+def test_k_tail_mask_becomes_a_zero_filled_k_range():
+    plan, c = _plan("t_matmul_tiled")                                       # K = 31 in tiles of 16
+    d = plan.analyse({"M": 17, "N": 130}, (3, 2, 1), 0xFFFFFFFF)
+    assert d is not None, plan.last_reason
+    assert (d["K"], d["a_k"], d["b_k"], d["ntile"]) == (32, 31, 31, 2)
+
+
+def test_pid_base_offsets_shift_the_bounds():
+    plan, c = _plan("matmul_tiled_masked")
+    # programs start at row group 1 and column group 1: rows 16.., columns 64.. of the matrices
+    d = plan.analyse({"M": 50, "N": 150, "PID_M_BASE": 1, "PID_N_BASE": 1}, (1, 2, 1), 0xFFFFFFFF)
+    assert d is not None, plan.last_reason
+    assert (d["a0"], d["b0"], d["c0"]) == (16 * 64, 64, 16 * 150 + 64)
+    assert (d["M"], d["N"], d["a_rows"], d["b_cols"]) == (32, 64, 32, 64)
+
+
+def test_naive_fma_chain_with_ghost_threads_is_a_gemm():
+    """examples/matmul.py: one fma chain per output, 1-D thread groups of 32 over W = 70 columns;
+    the 26 ghost threads of the last group become the column bound."""
+    plan, _ = _plan("matmul_naive")
+    d = plan.analyse({"H": 40, "W": 70}, (3, 40, 1), 70)
+    assert d is not None, plan.last_reason
+    assert (d["M"], d["N"], d["K"], d["ntile"], d["zero_init"]) == (40, 70, 16, 1, False)
+    assert (d["a_sm"], d["b_sk"], d["c_sm"]) == (16, 70, 70)
+
+
+def test_operand_bound_on_the_other_coordinate():
+    """t_matmul guards A and B with (row < M) & (col < N): harmless, since no output beyond it is kept."""
+    plan, _ = _plan("t_matmul")
+    assert plan.analyse({"M": 32, "N": 100}, (32, 2, 1), 0xFFFFFFFF) is not None
+
+
+def _retarget_a_mask(ir: IRModule, extra: Inst, new_and: Inst) -> IRModule:
+    """Insert ``extra`` and ``new_and`` before the first A load and make every A load use new_and."""
+    a_id = next(i.out.id for i in ir.insts if i.op == "arg" and i.args[0] == "a")
+    first = next(k for k, i in enumerate(ir.insts) if i.op == "load" and i.args[0].id == a_id)
+    insts = list(ir.insts[:first]) + [extra, new_and]
+    for i in ir.insts[first:]:
+        if i.op == "load" and i.args[0].id == a_id:
+            i = dataclasses.replace(i, args=(i.args[0], i.args[1], new_and.out))
+        insts.append(i)
+    return dataclasses.replace(ir, insts=tuple(insts))
+
+
+def test_a_masked_by_column_inside_the_stored_range_declines():
+    from easy_as_b200.ir import DType, ValueRef
+
+    plan, c = _plan("t_matmul")
+    ir = plan.ir
+    col = next(i.args[0] for i in ir.insts if i.op == "lt" and i.args[1].id == 4)       # col < N
+    mask = next(i.out for i in ir.insts if i.op == "and")
+    c50 = ValueRef(9001, DType.U32)
+    lt = ValueRef(9002, DType.BOOL)
+    both = ValueRef(9003, DType.BOOL)
+    ir2 = dataclasses.replace(ir, insts=(Inst("const", c50, (50,)),) + ir.insts)
+    ir2 = _retarget_a_mask(ir2, Inst("lt", lt, (col, c50)), Inst("and", both, (mask, lt)))
+    bad = TiledGemmPlan(ir2, c["block_size"])
+    assert bad.analyse({"M": 32, "N": 100}, (32, 2, 1), 0xFFFFFFFF) is None
+    assert "other operand" in bad.last_reason
+
+
+def test_triangular_mask_declines():
+    from easy_as_b200.ir import DType, ValueRef
+
+    plan, c = _plan("t_matmul")
+    ir = plan.ir
+    row = next(i.args[0] for i in ir.insts if i.op == "lt" and i.args[1].id == 3)       # row < M
+    col = next(i.args[0] for i in ir.insts if i.op == "lt" and i.args[1].id == 4)
+    mask = next(i.out for i in ir.insts if i.op == "and")
+    lt = ValueRef(9002, DType.BOOL)
+    both = ValueRef(9003, DType.BOOL)
+    ir2 = _retarget_a_mask(ir, Inst("lt", lt, (col, row)), Inst("and", both, (mask, lt)))
+    bad = TiledGemmPlan(ir2, c["block_size"])
+    assert bad.analyse({"M": 32, "N": 100}, (32, 2, 1), 0xFFFFFFFF) is None
 
 
 def _without(ir: IRModule, op: str) -> IRModule:
