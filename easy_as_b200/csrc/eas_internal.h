@@ -23,3 +23,7 @@ int eas_driver_init();
 int eas_fail(int code, const char* fmt, ...);
 int eas_cuda_check(cudaError_t e, const char* what, int code);
 int eas_drv_check(CUresult r, const char* what, int code);
+
+// Device address of this device's native-kernel status word (host-mapped, read and cleared by
+// eas_gemm_status); kernels write EAS_ERR_TIMEOUT there when a bounded wait expires.
+int* eas_native_status_dev(int dev);

@@ -735,6 +735,20 @@ std::once_flag g_status_once;
 
 }  // namespace
 
+int* eas_native_status_dev(int dev) {
+  std::call_once(g_status_once, [] {
+    void* h = nullptr;
+    if (cudaHostAlloc(&h, 64 * sizeof(int), cudaHostAllocMapped | cudaHostAllocPortable) == cudaSuccess) {
+      g_status_host = static_cast<int*>(h);
+      for (int i = 0; i < 64; ++i) g_status_host[i] = 0;
+      void* d = nullptr;
+      if (cudaHostGetDevicePointer(&d, h, 0) == cudaSuccess) g_status_dev = static_cast<int*>(d);
+    }
+    cudaGetLastError();
+  });
+  return (g_status_dev && dev >= 0 && dev < 64) ? g_status_dev + dev : nullptr;
+}
+
 extern "C" int eas_gemm_status(int dev, int* code) {
   if (!code) return eas_fail(EAS_ERR_VALUE, "eas_gemm_status: null pointer");
   *code = (g_status_host && dev >= 0 && dev < 64) ? g_status_host[dev] : 0;
@@ -760,17 +774,7 @@ extern "C" int eas_gemm_f16(const void* a, const void* b, float* c, uint32_t M, 
     return eas_fail(EAS_ERR_VALUE, "eas_gemm_f16: A/B strides must be multiples of 8 elements");
   int dev = 0;
   cudaGetDevice(&dev);
-  std::call_once(g_status_once, [] {
-    void* h = nullptr;
-    if (cudaHostAlloc(&h, 64 * sizeof(int), cudaHostAllocMapped | cudaHostAllocPortable) == cudaSuccess) {
-      g_status_host = static_cast<int*>(h);
-      for (int i = 0; i < 64; ++i) g_status_host[i] = 0;
-      void* d = nullptr;
-      if (cudaHostGetDevicePointer(&d, h, 0) == cudaSuccess) g_status_dev = static_cast<int*>(d);
-    }
-    cudaGetLastError();
-  });
-  int* status = (g_status_dev && dev < 64) ? g_status_dev + dev : nullptr;
+  int* status = eas_native_status_dev(dev);
   int num_sms = 148;
   cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev);
 
