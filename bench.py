@@ -277,6 +277,9 @@ def run_gemm(name: str, args, world: int, rank: int, rt) -> dict:
                      "frac_of_nominal_2250": round(local_tf / 2250.0, 4),
                      "traffic": profile_traffic(f"gemm_{name.lower()}_n1")},
         "cublas_f16_f32out_tflops": lib_tf,
+        "cpu_baseline": (cpu_gemm_baseline(min(M, 2048), N, K, 1, 5, f"one {min(M, 2048)}-row slice of one problem "
+                                           f"of the {name} workload (f16 inputs upcast to f32)")
+                         if world == 1 and not args.no_cpu_baseline else None),
         "gpu_launches": rt.launch_count - launches0,
         "clocks": clk.summary(),
     }
@@ -370,9 +373,31 @@ def run_tiled(args, rt) -> dict:
                      "peak_source": "nominal 148 SM x 128 FP32 lanes x 2 at the median sampled SM clock",
                      "traffic": profile_traffic("sgemm_c3_n1")},
         "cublas_fp32_tflops": round(lib_tf, 2),
+        "cpu_baseline": (None if args.no_cpu_baseline else
+                         cpu_gemm_baseline(M, N, K, 1, 6, "the full C3 problem")),
         "gpu_launches": rt.launch_count - launches0,
         "clocks": cl,
     }
+
+
+def cpu_gemm_baseline(m: int, n: int, k: int, batch: int, seed: int, what: str, seconds: float = 3.0) -> dict:
+    """numpy (OpenBLAS, all host threads) float32 A @ B on a bounded sample of the same shape:
+    repeated for about ``seconds``; fp16 operands are upcast to f32 first, as the reference's
+    CPU-side check does."""
+    rng = np.random.default_rng(seed)
+    a = rng.standard_normal((m, k), dtype=np.float32)
+    b = rng.standard_normal((k, n), dtype=np.float32)
+    a @ b
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        a @ b
+        reps += 1
+        dt = time.perf_counter() - t0
+        if dt > seconds:
+            break
+    tf = 2.0 * m * n * k * reps / dt / 1e12
+    return {"value": round(tf, 4), "unit": "TFLOP/s", "cores": os.cpu_count() or 1, "kind": "port",
+            "sample": f"numpy float32 {m}x{k} @ {k}x{n} (OpenBLAS, all threads), {reps} reps in {dt:.1f} s; {what}"}
 
 
 def cpu_add_baseline(seconds: float = 10.0) -> dict:

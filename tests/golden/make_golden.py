@@ -87,6 +87,13 @@ CASES: list[tuple[str, str, str, list, dict, dict]] = [
     ("t_matmul_tiled", "tests/test_matmul_tiled.py", "matmul_tiled_kernel_test",
      [B("f32", 17 * 31), B("f32", 31 * 130), B("f32", 17 * 130), 17, 130],
      {"BM": 16, "BN": 64, "BK": 16, "K": 31, "NT": 256}, {"grid": [cdiv(130, 64), cdiv(17, 16), 1]}),
+    # the other two shapes of the reference test's device check (tests/test_matmul_tiled.py:128-178)
+    ("t_matmul_tiled_33x65x48", "tests/test_matmul_tiled.py", "matmul_tiled_kernel_test",
+     [B("f32", 33 * 48), B("f32", 48 * 65), B("f32", 33 * 65), 33, 65],
+     {"BM": 16, "BN": 64, "BK": 16, "K": 48, "NT": 256}, {"grid": [cdiv(65, 64), cdiv(33, 16), 1]}),
+    ("t_matmul_tiled_64x64x32", "tests/test_matmul_tiled.py", "matmul_tiled_kernel_test",
+     [B("f32", 64 * 32), B("f32", 32 * 64), B("f32", 64 * 64), 64, 64],
+     {"BM": 16, "BN": 64, "BK": 16, "K": 32, "NT": 256}, {"grid": [cdiv(64, 64), cdiv(64, 16), 1]}),
     ("t_grid_hw", "tests/test_grid_infer.py", "add2d_hw_kernel",
      [B("f32", 17 * 103), B("f32", 17 * 103), B("f32", 17 * 103), 17, 103], {"BLOCK": 32}, {}),
     ("t_bool_simplify", "tests/test_bool_simplify.py", "bool_simplify_kernel", [B("f32", 256), 128], {"BLOCK": 256},

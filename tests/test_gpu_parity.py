@@ -93,3 +93,44 @@ def test_rerolled_and_unrolled_sources_agree(cuda_rt, cid, monkeypatch):
         outs.append(inp)
     for name in c["writes"]:
         np.testing.assert_array_equal(outs[0][name], outs[1][name])
+
+
+@pytest.mark.parametrize("cid", ["t_matmul_tiled_33x65x48", "t_matmul_tiled_64x64x32", "t_matmul_tiled"])
+def test_reference_tiled_matmul_device_check(cuda_rt, cid):
+    """The reference test's own device check (tests/test_matmul_tiled.py:128-178): shapes
+    (33,65,48), (64,64,32), (17,130,31), BM=16 BN=64 BK=16 NT=256, against a @ b with rtol=atol=2e-3;
+    here also bit for bit against the oracle."""
+    c = goldens.case(cid)
+    ir = goldens.ir_from_json(c["opt"])
+    M, N = c["args"][3], c["args"][4]
+    K = c["meta"]["K"]
+    rng = np.random.default_rng(5)
+    a = rng.standard_normal(M * K).astype(np.float32)
+    b = rng.standard_normal(K * N).astype(np.float32)
+    gpu = np.zeros(M * N, np.float32)
+    cpu = np.zeros(M * N, np.float32)
+    cuda_rt.run(compile_ir(ir), {"a": a, "b": b, "c": gpu, "M": M, "N": N}, c["meta"], sync=True,
+                **goldens.launch_opts(c))
+    execute(ir, {"a": a, "b": b, "c": cpu, "M": M, "N": N}, **goldens.launch_opts(c))
+    np.testing.assert_array_equal(gpu, cpu)
+    want = a.reshape(M, K).astype(np.float64) @ b.reshape(K, N).astype(np.float64)
+    np.testing.assert_allclose(gpu.reshape(M, N), want, rtol=2e-3, atol=2e-3)
+
+
+@pytest.mark.parametrize("k", [7, 31, 64])
+def test_reference_dot_dynamic_k_device_check(cuda_rt, k):
+    """tests/test_dot_dynamic_k.py:27-50: gemv with a runtime K in {7, 31, 64}, M = 33, BLOCK = 64,
+    rtol=atol=1e-4 against a @ x; here also bit for bit against the oracle."""
+    c = goldens.case("t_gemv_dot")
+    ir = goldens.ir_from_json(c["opt"])
+    m = 33
+    rng = np.random.default_rng(k)
+    a = rng.standard_normal(m * k).astype(np.float32)
+    x = rng.standard_normal(k).astype(np.float32)
+    gpu = np.zeros(m, np.float32)
+    cpu = np.zeros(m, np.float32)
+    args = {"a": a, "x": x, "M": m, "K": k, "N": m}
+    cuda_rt.run(compile_ir(ir), {**args, "y": gpu}, {"BLOCK": 64}, sync=True, nthreads=m)
+    execute(ir, {**args, "y": cpu}, nthreads=m)
+    np.testing.assert_array_equal(gpu, cpu)
+    np.testing.assert_allclose(gpu, a.reshape(m, k).astype(np.float64) @ x.astype(np.float64), rtol=1e-4, atol=1e-4)
