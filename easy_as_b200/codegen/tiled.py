@@ -149,9 +149,9 @@ def _affine_k(arr: np.ndarray, what: str) -> tuple[np.ndarray, int]:
     d = (arr[:, :, 1] - base) & M32
     _need(_pfree(d) and bool((d[0] == d[0][0]).all()), f"{what} not one stride for all threads")
     step = int(d[0][0])
-    want = np.repeat(base[:, :, None], k, axis=2)
-    want[0] = (want[0] + np.uint64(step) * np.arange(k, dtype=np.uint64)[None, :]) & M32
-    _need(bool((arr == want).all()), f"{what} not affine in k")
+    ks = np.uint64(step) * np.arange(k, dtype=np.uint64)
+    _need(bool((arr[1:] == base[1:, :, None]).all()) and bool((arr[0] == ((base[0][:, None] + ks) & M32)).all()),
+          f"{what} not affine in k")
     return base, step
 
 
@@ -694,6 +694,31 @@ _OPS = {"arg", "const", "alloc_tg", "program_id", "thread_id", "tid", "local_id"
         "floordiv", "mod", "lt", "and", "or", "not", "where", "barrier", "load", "store", "dot", "fma"}
 
 
+_SELF_HASH: str | None = None
+
+
+def _disk_path(ir: IRModule, block: int, key: tuple) -> Any:
+    """Cache file of one proof result under EAS_CACHE_DIR/plans (None when caching is off).  The
+    key hashes the IR, the launch values and this module's own source, so a change of the proof
+    logic never reuses an old result."""
+    global _SELF_HASH
+    import hashlib
+    import json
+
+    from ..ir import ir_to_json
+    from ..runtime.cuda import _cache_dir
+
+    cdir = _cache_dir()
+    if cdir is None or os.environ.get("EAS_PLAN_CACHE", "1") == "0":
+        return None
+    if _SELF_HASH is None:
+        _SELF_HASH = hashlib.sha256(open(__file__, "rb").read()).hexdigest()
+    h = hashlib.sha256()
+    h.update(_SELF_HASH.encode())
+    h.update(json.dumps([ir_to_json(ir), block, repr(key)], separators=(",", ":")).encode())
+    return cdir / "plans" / f"{h.hexdigest()}.json"
+
+
 class TiledGemmPlan:
     """Native FFMA launch for kernels proven to be tiled fp32 GEMMs (module docstring)."""
 
@@ -708,6 +733,16 @@ class TiledGemmPlan:
     def analyse(self, scalars: dict[str, int], programs: tuple[int, int, int], ntx: int) -> dict[str, Any] | None:
         key = (tuple(sorted(scalars.items())), programs, ntx)
         hit = self.cache.get(key)
+        disk = None
+        if hit is None:
+            disk = _disk_path(self.ir, self.block, key)
+            if disk is not None and disk.exists():
+                try:
+                    import json
+
+                    hit = json.loads(disk.read_text())["result"]
+                except (OSError, ValueError, KeyError):
+                    hit = None
         if hit is None:
             try:
                 ghost = ntx if ntx < programs[0] * self.block else None
@@ -719,9 +754,19 @@ class TiledGemmPlan:
                 hit = plan_launch(d, g, bounds(d, programs))
             except Decline as e:
                 hit = str(e)
-            if len(self.cache) > 64:
-                self.cache.clear()
-            self.cache[key] = hit
+            if disk is not None:
+                try:
+                    import json
+
+                    disk.parent.mkdir(parents=True, exist_ok=True)
+                    tmp = disk.with_suffix(f".{os.getpid()}.tmp")
+                    tmp.write_text(json.dumps({"result": hit}))
+                    os.replace(tmp, disk)
+                except OSError:
+                    pass
+        if len(self.cache) > 64:
+            self.cache.clear()
+        self.cache[key] = hit
         if isinstance(hit, str):
             self.last_reason = hit
             return None

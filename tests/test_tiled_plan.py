@@ -177,3 +177,23 @@ def test_static_filter_rejects_spmd_and_dotless_kernels():
         c = goldens.case(cid)
         ck = compile_ir(goldens.ir_from_json(c["opt"]))
         assert match_tiled(ck.ir, ck.plan) is None
+
+
+def test_proof_results_are_cached_on_disk(tmp_path, monkeypatch):
+    monkeypatch.setenv("EAS_CACHE_DIR", str(tmp_path))
+    c = goldens.case("matmul_tiled_full")
+    ir = goldens.ir_from_json(c["opt"])
+    first = TiledGemmPlan(ir, c["block_size"]).analyse({"M": 64, "N": 128}, (4, 2, 1), 0xFFFFFFFF)
+    files = list((tmp_path / "plans").glob("*.json"))
+    assert len(files) == 1
+    again = TiledGemmPlan(ir, c["block_size"]).analyse({"M": 64, "N": 128}, (4, 2, 1), 0xFFFFFFFF)
+    assert again == first
+    # declines are cached too, with their reason
+    bad = TiledGemmPlan(ir, c["block_size"])
+    assert bad.analyse({"M": 64, "N": 128}, (4, 2, 1), 4 * 256 - 3) is None
+    reason = bad.last_reason
+    bad2 = TiledGemmPlan(ir, c["block_size"])
+    assert bad2.analyse({"M": 64, "N": 128}, (4, 2, 1), 4 * 256 - 3) is None and bad2.last_reason == reason
+    monkeypatch.setenv("EAS_PLAN_CACHE", "0")
+    TiledGemmPlan(ir, c["block_size"]).analyse({"M": 64, "N": 256}, (8, 2, 1), 0xFFFFFFFF)
+    assert len(list((tmp_path / "plans").glob("*.json"))) == 2
