@@ -17,7 +17,8 @@
 //     1 CTA/SM) for large launches, 64 x 64 with 8 x 4 (128 threads, 4 CTAs/SM)
 //     when there are fewer than four waves of 128 x 128 tiles;
 //   * K staged BKS = 32, 16 or 8 deep (the largest that divides KT) through a
-//     2- or 3-deep cp.async ring (16-byte copies, zero-filled past M, N), one
+//     2- or 3-deep cp.async ring (16-byte copies, zero-filled outside the valid
+//     bounds; 4-byte copies when a row of A, B or C is not 16-byte aligned), one
 //     __syncthreads per stage;
 //   * A kept k-contiguous in shared memory ([BM][BKS+4]) and read as float4
 //     along k; interleaved thread rows put the 4 rows a warp reads at once in
@@ -54,6 +55,10 @@ __device__ __forceinline__ void cp_async16(float* dst, const float* src, uint32_
   const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(dst));
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(d), "l"(src), "r"(bytes) : "memory");
 }
+__device__ __forceinline__ void cp_async4(float* dst, const float* src, uint32_t bytes) {
+  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(dst));
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(d), "l"(src), "r"(bytes) : "memory");
+}
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
@@ -70,7 +75,7 @@ struct SgemmCfg {
   static_assert(BKS % 4 == 0, "BKS must be a multiple of 4");
 };
 
-template <int BM, int BN, int BKS, int STAGES, int TM, int TN, int MINB>
+template <int BM, int BN, int BKS, int STAGES, int TM, int TN, int MINB, bool VEC>
 __global__ void __launch_bounds__(SgemmCfg<BM, BN, BKS, STAGES, TM, TN>::kThreads, MINB)
 sgemm_ffma_kernel(const float* __restrict__ A, const float* __restrict__ B, float* __restrict__ C, uint32_t M,
                   uint32_t N, uint32_t K, uint32_t stages_per_tile, uint64_t lda, uint64_t ldb, uint64_t ldc,
@@ -91,7 +96,26 @@ sgemm_ffma_kernel(const float* __restrict__ A, const float* __restrict__ B, floa
   const uint32_t nstages = K / BKS;
 
   auto issue = [&](uint32_t st) {
-    if (st < nstages) {
+    if (st < nstages && !VEC) {  // rows not 16-byte aligned: element-wise copies
+      const int buf = st % STAGES;
+      const uint32_t k0 = st * BKS;
+#pragma unroll
+      for (int q = 0; q < BM * BKS / Cfg::kThreads; ++q) {
+        const int idx = tid + q * Cfg::kThreads;
+        const int r = idx / BKS, kc = idx % BKS;
+        const uint32_t m = m0 + r, k = k0 + kc;
+        const bool live = m < valid.a_rows && k < valid.a_k;
+        cp_async4(sA + buf * Cfg::kAStage + r * Cfg::kLdA + kc, live ? A + (uint64_t)m * lda + k : A, live ? 4u : 0u);
+      }
+#pragma unroll
+      for (int q = 0; q < BKS * BN / Cfg::kThreads; ++q) {
+        const int idx = tid + q * Cfg::kThreads;
+        const int r = idx / BN, nc = idx % BN;
+        const uint32_t n = n0 + nc, k = k0 + r;
+        const bool live = n < valid.b_cols && k < valid.b_k;
+        cp_async4(sB + buf * Cfg::kBStage + r * Cfg::kLdB + nc, live ? B + (uint64_t)k * ldb + n : B, live ? 4u : 0u);
+      }
+    } else if (st < nstages) {
       const int buf = st % STAGES;
       const uint32_t k0 = st * BKS;
 #pragma unroll
@@ -189,7 +213,7 @@ sgemm_ffma_kernel(const float* __restrict__ A, const float* __restrict__ B, floa
     for (int h = 0; h < Cfg::kCG; ++h) {
       const uint32_t n = n0 + h * (BN / Cfg::kCG) + tx * 4;
       const float* v = &acc[i][h * 4];
-      if (n + 3 < N) {
+      if (VEC && n + 3 < N) {
         *reinterpret_cast<float4*>(row + n) = make_float4(v[0], v[1], v[2], v[3]);
       } else {
         for (int j = 0; j < 4; ++j)
@@ -199,7 +223,7 @@ sgemm_ffma_kernel(const float* __restrict__ A, const float* __restrict__ B, floa
   }
 }
 
-template <int BM, int BN, int BKS, int STAGES, int TM, int TN, int MINB>
+template <int BM, int BN, int BKS, int STAGES, int TM, int TN, int MINB, bool VEC>
 int launch_sgemm(const float* a, const float* b, float* c, uint32_t M, uint32_t N, uint32_t K, uint32_t k_tile,
                  uint32_t batch, uint64_t lda, uint64_t a_bs, uint64_t ldb, uint64_t b_bs, uint64_t ldc,
                  uint64_t c_bs, int zero_init, SgemmValid valid, cudaStream_t s) {
@@ -207,7 +231,7 @@ int launch_sgemm(const float* a, const float* b, float* c, uint32_t M, uint32_t 
   const uint32_t gy = (M + BM - 1) / BM;
   if (gy > 65535) return eas_fail(EAS_ERR_VALUE, "eas_sgemm_f32_tiled: M too large");
   const size_t smem = Cfg::kSmemFloats * sizeof(float);
-  auto kern = sgemm_ffma_kernel<BM, BN, BKS, STAGES, TM, TN, MINB>;
+  auto kern = sgemm_ffma_kernel<BM, BN, BKS, STAGES, TM, TN, MINB, VEC>;
   static int attr_done[64];
   int dev = 0;
   cudaGetDevice(&dev);
@@ -234,11 +258,13 @@ extern "C" int eas_sgemm_f32_tiled(const float* a, const float* b, float* c, uin
   if (M == 0 || N == 0 || batch == 0) return EAS_OK;
   if (K == 0 || k_tile == 0 || K % k_tile) return eas_fail(EAS_ERR_VALUE, "eas_sgemm_f32_tiled: K must be a positive multiple of k_tile");
   if (k_tile % 8) return eas_fail(EAS_ERR_VALUE, "eas_sgemm_f32_tiled: k_tile must be a multiple of 8");
-  if ((reinterpret_cast<uintptr_t>(a) & 15) || (reinterpret_cast<uintptr_t>(b) & 15) ||
-      (reinterpret_cast<uintptr_t>(c) & 15))
-    return eas_fail(EAS_ERR_VALUE, "eas_sgemm_f32_tiled: operands must be 16-byte aligned");
-  if (lda % 4 || ldb % 4 || ldc % 4 || (batch > 1 && (a_bstride % 4 || b_bstride % 4 || c_bstride % 4)))
-    return eas_fail(EAS_ERR_VALUE, "eas_sgemm_f32_tiled: strides must be multiples of 4 elements");
+  if ((reinterpret_cast<uintptr_t>(a) & 3) || (reinterpret_cast<uintptr_t>(b) & 3) ||
+      (reinterpret_cast<uintptr_t>(c) & 3))
+    return eas_fail(EAS_ERR_VALUE, "eas_sgemm_f32_tiled: operands must be 4-byte aligned");
+  // 16-byte copies and stores when every row of A, B and C starts on a 16-byte boundary
+  const bool vec = !((reinterpret_cast<uintptr_t>(a) & 15) || (reinterpret_cast<uintptr_t>(b) & 15) ||
+                     (reinterpret_cast<uintptr_t>(c) & 15) || lda % 4 || ldb % 4 || ldc % 4 ||
+                     (batch > 1 && (a_bstride % 4 || b_bstride % 4 || c_bstride % 4)));
   if (batch > 65535) return eas_fail(EAS_ERR_VALUE, "eas_sgemm_f32_tiled: batch exceeds 65535");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const SgemmValid valid{a_rows < M ? a_rows : M, a_k < K ? a_k : K, b_cols < N ? b_cols : N, b_k < K ? b_k : K};
@@ -250,8 +276,11 @@ extern "C" int eas_sgemm_f32_tiled(const float* a, const float* b, float* c, uin
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const uint64_t big_tiles = (uint64_t)((M + 127) / 128) * ((N + 127) / 128) * batch;
   const bool small = big_tiles < 4ull * (uint64_t)sms;
-#define EAS_SG(BM, BN, BKS, ST, TM, TN, MINB) \
-  launch_sgemm<BM, BN, BKS, ST, TM, TN, MINB>(a, b, c, M, N, K, k_tile, batch, lda, a_bstride, ldb, b_bstride, ldc, c_bstride, zero_init, valid, s)
+#define EAS_SG(BM, BN, BKS, ST, TM, TN, MINB)                                                                    \
+  (vec ? launch_sgemm<BM, BN, BKS, ST, TM, TN, MINB, true>(a, b, c, M, N, K, k_tile, batch, lda, a_bstride, ldb,    \
+                                                           b_bstride, ldc, c_bstride, zero_init, valid, s)        \
+       : launch_sgemm<BM, BN, BKS, ST, TM, TN, MINB, false>(a, b, c, M, N, K, k_tile, batch, lda, a_bstride, ldb,   \
+                                                            b_bstride, ldc, c_bstride, zero_init, valid, s))
   if (small) {
     if (k_tile % 32 == 0) return EAS_SG(64, 64, 32, 2, 8, 4, 4);
     if (k_tile % 16 == 0) return EAS_SG(64, 64, 16, 2, 8, 4, 4);

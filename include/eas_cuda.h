@@ -162,8 +162,8 @@ int eas_gemm_f16(const void* a, const void* b, float* c, uint32_t M, uint32_t N,
  * outputs m < M, n < N are stored.
  * The same operations in the same order as the generated kernel, so the
  * results are bit-identical.  K must be a multiple of k_tile and k_tile a
- * multiple of 8; operands 16-byte aligned, strides multiples of 4 elements;
- * otherwise EAS_ERR_VALUE.  Asynchronous on `stream`. */
+ * multiple of 8, operands 4-byte aligned; otherwise EAS_ERR_VALUE (16-byte
+ * aligned rows take the vector path).  Asynchronous on `stream`. */
 int eas_sgemm_f32_tiled(const float* a, const float* b, float* c, uint32_t M, uint32_t N, uint32_t K,
                         uint32_t k_tile, uint32_t batch, uint64_t lda, uint64_t a_bstride, uint64_t ldb,
                         uint64_t b_bstride, uint64_t ldc, uint64_t c_bstride, int zero_init,

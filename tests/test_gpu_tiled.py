@@ -27,6 +27,14 @@ CASES = [
     ("matmul_tiled_masked", {"M": 300, "N": 260, "PID_M_BASE": 2, "PID_N_BASE": 1}, (2, 5, 1),
      {"a": 300 * 64, "b": 64 * 260, "c": 300 * 260}),
     ("matmul_naive", {"H": 40, "W": 72}, None, {"a": 40 * 16, "b": 16 * 72, "c": 40 * 72}),
+    # rows not 16-byte aligned: element-wise staging
+    ("matmul_tiled_masked", {"M": 50, "N": 70, "PID_M_BASE": 0, "PID_N_BASE": 0}, (_cdiv(70, 64), _cdiv(50, 16), 1),
+     {"a": 50 * 64, "b": 64 * 70, "c": 50 * 70}),
+    ("t_matmul_tiled", {"M": 17, "N": 130}, (_cdiv(130, 64), _cdiv(17, 16), 1), {"a": 17 * 31, "b": 31 * 130,
+                                                                                "c": 17 * 130}),
+    ("t_matmul_tiled_33x65x48", {"M": 33, "N": 65}, (_cdiv(65, 64), _cdiv(33, 16), 1),
+     {"a": 33 * 48, "b": 48 * 65, "c": 33 * 65}),
+    ("matmul_naive", {"H": 40, "W": 70}, None, {"a": 40 * 16, "b": 16 * 70, "c": 40 * 70}),
     ("t_matmul", {"M": 32, "N": 100}, (32, 2, 1), {"a": 32 * 16, "b": 16 * 100, "c": 32 * 100}),
     ("t_fma_matmul", {"M": 32, "N": 64}, (32, 2, 1), {"a": 32 * 8, "b": 8 * 64, "c": 32 * 64}),
 ]
