@@ -111,8 +111,9 @@ class DotGemmPlan:
             out[name] = {"": f.get("", 0), "X": t, "Y": f.get("P1", 0), "Z": f.get("P2", 0)}
         return out
 
-    def map_launch(self, scalars: dict[str, int], programs: tuple[int, int, int], ntx: int
-                   ) -> dict[str, Any] | None:
+    def map_launch(self, scalars: dict[str, int], programs: tuple[int, int, int], ntx: int,
+                   pid_base: tuple[int, int, int] = (0, 0, 0)) -> dict[str, Any] | None:
+        """GEMM of the programs ``pid_base + [0, programs)`` (program ids offset per axis)."""
         polys = {"a": self.a_base, "b": self.b_base, "sa": self.a_stride, "sb": self.b_stride, "k": self.k,
                  "c": self.c_off}
         for i, (lhs, rhs) in enumerate(self.atoms):
@@ -133,18 +134,22 @@ class DotGemmPlan:
             if f[n]["X"] or f[n]["Y"] or f[n]["Z"]:
                 self.last_reason = f"{n} depends on the thread coordinates"
                 return None
+        # program-id offsets: X = X' + base_x, Y = Y' + base_y, Z = Z' + base_z with X', Y', Z' from 0
+        shift = {"X": pid_base[0] * self.block, "Y": pid_base[1], "Z": pid_base[2]}
+        for form in f.values():
+            form[""] += sum(form[c] * shift[c] for c in "XYZ")
         gx, gy, gz = programs
-        ext = {"X": min(gx * self.block, ntx), "Y": gy, "Z": gz}
+        ext = {"X": min(gx * self.block, ntx - shift["X"]), "Y": gy, "Z": gz}
         for i in range(len(self.atoms)):
             lhs, rhs = f[f"l{i}"], f[f"r{i}"]
             if rhs["X"] or rhs["Y"] or rhs["Z"]:
                 self.last_reason = "mask bound depends on the thread coordinates"
                 return None
             coords = [c for c in "XYZ" if lhs[c]]
-            if len(coords) != 1 or lhs[coords[0]] != 1 or lhs[""] != 0:
+            if len(coords) != 1 or lhs[coords[0]] != 1 or lhs[""] != shift[coords[0]]:
                 self.last_reason = "mask is not coordinate < bound"
                 return None
-            ext[coords[0]] = min(ext[coords[0]], max(rhs[""], 0))
+            ext[coords[0]] = min(ext[coords[0]], max(rhs[""] - lhs[""], 0))
         if min(ext.values()) <= 0:
             return {"empty": True}
         roles: dict[str, str] = {}
@@ -195,7 +200,7 @@ class DotGemmPlan:
         top_a = f["a"][""] + lda * (M - 1) + abs_ * (B - 1) + (K - 1)
         top_b = f["b"][""] + (b_n * (N - 1) + bbs * (B - 1) + sb * (K - 1))
         top_c = f["c"][""] + ldc * (M - 1) + cbs * (B - 1) + (N - 1)
-        if max(top_a, top_b, top_c) >= U32_LIMIT or not self._no_wrap(scalars, programs):
+        if max(top_a, top_b, top_c) >= U32_LIMIT or not self._no_wrap(scalars, programs, pid_base):
             self.last_reason = "u32 index arithmetic would wrap"
             return None
         return {"M": M, "N": N, "K": K, "batch": B, "a0": f["a"][""], "b0": f["b"][""], "c0": f["c"][""],
@@ -203,10 +208,11 @@ class DotGemmPlan:
                 "b_kmajor": b_kmajor, "ldc": ldc if M > 1 else N, "c_bs": cbs if B > 1 else 0,
                 "top_a": top_a, "top_b": top_b, "top_c": top_c}
 
-    def _no_wrap(self, scalars: dict[str, int], programs: tuple[int, int, int]) -> bool:
+    def _no_wrap(self, scalars: dict[str, int], programs: tuple[int, int, int],
+                 pid_base: tuple[int, int, int] = (0, 0, 0)) -> bool:
         """Interval upper bounds of every u32 node stay below 2**32 for this launch."""
         hi: dict[int, int] = {}
-        gx, gy, gz = programs
+        gx, gy, gz = (b + n for b, n in zip(pid_base, programs))
         for inst in self.ir.insts:
             o = inst.out
             if o is None or o.dtype != DType.U32:
@@ -238,22 +244,29 @@ class DotGemmPlan:
 
     # -- launch ------------------------------------------------------------------
     def try_launch(self, rt: Any, ck: Any, runtime_args: dict[str, Any], args: dict[str, Any], device: int,
-                   stream: int, programs: tuple[int, int, int], ntx: int) -> bool:
+                   stream: int, programs: tuple[int, int, int], ntx: int, pid_base: tuple[int, int, int] = (0, 0, 0),
+                   elem_base: dict[str, int] | None = None) -> bool:
+        """Launch the native kernel for programs ``pid_base + [0, programs)``; buffers listed in
+        ``elem_base`` hold only the elements from that global index on (their pointers are already
+        moved back by it)."""
         import os
 
         if os.environ.get("EAS_DISABLE_NATIVE", "0") not in ("", "0"):
             self.last_reason = "disabled by EAS_DISABLE_NATIVE"
             return False
         scalars = {f"${a.name}": int(runtime_args[a.name]) for a in self.ir.args if a.kind == "scalar"}
-        m = self.map_launch(scalars, programs, ntx)
+        m = self.map_launch(scalars, programs, ntx, pid_base)
         if m is None:
             return False
         if m.get("empty"):
             return True
-        sizes = {n: _numel(runtime_args[n]) for n in (self.a_arg, self.b_arg, self.c_arg)}
-        if m["top_a"] >= sizes[self.a_arg] or m["top_b"] >= sizes[self.b_arg] or m["top_c"] >= sizes[self.c_arg]:
-            self.last_reason = "operand extents exceed the buffers"
-            return False
+        eb = elem_base or {}
+        for name, lo, top in ((self.a_arg, m["a0"], m["top_a"]), (self.b_arg, m["b0"], m["top_b"]),
+                              (self.c_arg, m["c0"], m["top_c"])):
+            e = int(eb.get(name, 0))
+            if lo < e or top >= e + _numel(runtime_args[name]):
+                self.last_reason = "operand extents exceed the buffers"
+                return False
         a = args[self.a_arg].ptr + 2 * m["a0"]
         b = args[self.b_arg].ptr + 2 * m["b0"]
         c = args[self.c_arg].ptr + 4 * m["c0"]

@@ -167,8 +167,10 @@ def _uniform_rhs(rhs: np.ndarray, what: str) -> int:
 # ---------------------------------------------------------------------------
 
 class _Exec:
-    def __init__(self, ir: IRModule, nt: int, scalars: dict[str, int], ghost_limit: int | None = None):
+    def __init__(self, ir: IRModule, nt: int, scalars: dict[str, int], ghost_limit: int | None = None,
+                 pid_base: tuple[int, int, int] = (0, 0, 0)):
         self.ir, self.nt = ir, nt
+        self.pid_base = pid_base                      # program id = pid_base + P (P from 0)
         self.scalars = scalars
         self.vals: dict[int, Any] = {}
         self.smem: dict[int, _Smem] = {}
@@ -182,7 +184,7 @@ class _Exec:
         self.ghost: tuple[tuple[np.ndarray, np.ndarray], ...] = ()
         if ghost_limit is not None:
             gx = np.zeros((4, nt), np.uint64)
-            gx[0] = self.tvec
+            gx[0] = (self.tvec + np.uint64(pid_base[0] * nt)) & M32
             gx[1] = np.uint64(nt)
             self.ghost = ((gx, self.lin_const(ghost_limit)),)
 
@@ -256,17 +258,20 @@ class _Exec:
         self.vals[inst.out.id] = ("smem", inst.out.id)
 
     def op_program_id(self, inst: Inst) -> None:
+        ax = int(inst.args[0])
         out = np.zeros((4, self.nt), np.uint64)
-        out[1 + int(inst.args[0])] = 1
+        out[0] = np.uint64(self.pid_base[ax] % U32_LIMIT)
+        out[1 + ax] = 1
         self.vals[inst.out.id] = out
 
     def op_thread_id(self, inst: Inst) -> None:
         ax = int(inst.args[0])
         out = np.zeros((4, self.nt), np.uint64)
         if ax == 0:
-            out[0] = self.tvec
+            out[0] = (self.tvec + np.uint64(self.pid_base[0] * self.nt)) & M32
             out[1] = np.uint64(self.nt)
         else:
+            out[0] = np.uint64(self.pid_base[ax] % U32_LIMIT)
             out[1 + ax] = 1
         self.vals[inst.out.id] = out
 
@@ -730,8 +735,10 @@ class TiledGemmPlan:
         self.cache: dict[Any, Any] = {}
         self.last_reason = ""
 
-    def analyse(self, scalars: dict[str, int], programs: tuple[int, int, int], ntx: int) -> dict[str, Any] | None:
-        key = (tuple(sorted(scalars.items())), programs, ntx)
+    def analyse(self, scalars: dict[str, int], programs: tuple[int, int, int], ntx: int,
+                pid_base: tuple[int, int, int] = (0, 0, 0)) -> dict[str, Any] | None:
+        """Proof and launch values for the programs ``pid_base + [0, programs)``."""
+        key = (tuple(sorted(scalars.items())), programs, ntx, tuple(pid_base))
         hit = self.cache.get(key)
         disk = None
         if hit is None:
@@ -745,8 +752,8 @@ class TiledGemmPlan:
                     hit = None
         if hit is None:
             try:
-                ghost = ntx if ntx < programs[0] * self.block else None
-                ex = _Exec(self.ir, self.block, scalars, ghost)
+                ghost = ntx if ntx < (pid_base[0] + programs[0]) * self.block else None
+                ex = _Exec(self.ir, self.block, scalars, ghost, tuple(pid_base))
                 ex.run()
                 d = derive(ex)
                 g = map_grid(d, programs)
@@ -773,23 +780,28 @@ class TiledGemmPlan:
         return hit
 
     def try_launch(self, rt: Any, ck: Any, runtime_args: dict[str, Any], args: dict[str, Any], device: int,
-                   stream: int, programs: tuple[int, int, int], ntx: int) -> bool:
+                   stream: int, programs: tuple[int, int, int], ntx: int, pid_base: tuple[int, int, int] = (0, 0, 0),
+                   elem_base: dict[str, int] | None = None) -> bool:
+        """Launch for programs ``pid_base + [0, programs)``; buffers in ``elem_base`` hold only the
+        elements from that global index on (pointers already moved back by it)."""
         if os.environ.get("EAS_DISABLE_NATIVE", "0") not in ("", "0"):
             self.last_reason = "disabled by EAS_DISABLE_NATIVE"
             return False
         scalars = {a.name: int(runtime_args[a.name]) for a in self.ir.args
                    if a.kind == "scalar" and a.dtype == DType.U32}
-        d = self.analyse(scalars, programs, ntx)
+        d = self.analyse(scalars, programs, ntx, pid_base)
         if d is None:
             return False
         if d["empty"]:
             return True  # the kernel stores nothing for these values
         from .patterns import _numel
 
-        for n, top, used in ((d["a_buf"], d["top_a"], d["reads_a"]), (d["b_buf"], d["top_b"], d["reads_b"]),
-                             (d["c_buf"], d["top_c"], True)):
-            if used and top >= _numel(runtime_args[n]):
-                self.last_reason = f"{n}: the product reaches past the buffer"
+        eb = elem_base or {}
+        for n, lo, top, used in ((d["a_buf"], d["a0"], d["top_a"], d["reads_a"]),
+                                 (d["b_buf"], d["b0"], d["top_b"], d["reads_b"]), (d["c_buf"], d["c0"], d["top_c"], True)):
+            e = int(eb.get(n, 0))
+            if used and (lo < e or top >= e + _numel(runtime_args[n])):
+                self.last_reason = f"{n}: the product reaches outside the buffer"
                 return False
         pa, pb, pc = args[d["a_buf"]].ptr, args[d["b_buf"]].ptr, args[d["c_buf"]].ptr
         c_lo, c_hi = pc + 4 * d["c0"], pc + 4 * (d["top_c"] + 1)

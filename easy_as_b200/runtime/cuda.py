@@ -699,7 +699,8 @@ class CudaRuntime:
         global index ``e`` on: the kernel receives its pointer moved back by
         ``e`` elements, and must only touch indices ``>= e`` in it (true for a
         program-id shard whose programs address disjoint element ranges).
-        Used by :mod:`easy_as_b200.shard` to split a grid across GPUs.
+        Used by :mod:`easy_as_b200.shard` to split a grid across GPUs.  A kernel with a native
+        plan (fp16 dot GEMM, tiled fp32 GEMM) runs it on the sub-range when the plan applies.
         """
         geo = launch_geometry(ck, runtime_args, nthreads=nthreads, grid=grid, tptg=None, shape=shape)
         if geo is None:
@@ -721,9 +722,13 @@ class CudaRuntime:
         host_copies = [(a.dev_buf, a.host) for a in args.values() if a.host is not None]
         if host_copies:
             raise ValueError("run_range needs device buffers (torch CUDA tensors or eas.Tensor on cuda)")
-        self._launch_generic(ck, runtime_args, args, device, stream, tuple(sub), ntx, tuple(base))
+        native = getattr(ck.plan, "native", None)
+        if native is None or not native.try_launch(self, ck, runtime_args, args, device, stream, tuple(sub), ntx,
+                                                   pid_base=tuple(base), elem_base=dict(buffer_base or {})):
+            self._launch_generic(ck, runtime_args, args, device, stream, tuple(sub), ntx, tuple(base))
         if sync:
             cuda_ext.check(self.lib().eas_stream_synchronize(stream), "kernel execution")
+            self._check_native_status(device)
 
     def _check_native_status(self, device: int) -> None:
         if not self.native_launches:

@@ -197,3 +197,12 @@ def test_proof_results_are_cached_on_disk(tmp_path, monkeypatch):
     monkeypatch.setenv("EAS_PLAN_CACHE", "0")
     TiledGemmPlan(ir, c["block_size"]).analyse({"M": 64, "N": 256}, (8, 2, 1), 0xFFFFFFFF)
     assert len(list((tmp_path / "plans").glob("*.json"))) == 2
+
+
+def test_program_id_sub_range_is_the_shifted_gemm():
+    """Programs 32..63 along y of the C3 launch: rows 1024..2047 of the same GEMM."""
+    plan, _ = _plan("matmul_tiled_c3_full")
+    d = plan.analyse({"M": 2048, "N": 2048}, (64, 32, 1), 0xFFFFFFFF, pid_base=(0, 32, 0))
+    assert d is not None, plan.last_reason
+    assert (d["M"], d["N"], d["K"]) == (1024, 2048, 2048)
+    assert (d["a0"], d["b0"], d["c0"]) == (1024 * 2048, 0, 1024 * 2048)
