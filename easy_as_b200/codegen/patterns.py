@@ -386,4 +386,8 @@ def match_native(ir: IRModule, lowered: Any) -> Any:
         from .tiled import match_tiled
 
         plan = match_tiled(ir, lowered)
+    if plan is None:
+        from .mma_gemm import match_mma
+
+        plan = match_mma(ir, lowered)
     return plan

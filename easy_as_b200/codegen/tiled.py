@@ -374,21 +374,22 @@ class _Exec:
         v = self.vals[val.id]
         m = self.mask(mask)
         if kind == "smem":
-            _need(not m.atoms and not self.ghost and bool(m.conc.all()), "masked threadgroup store")
+            # a program-id-free mask selects the writing threads; the others leave their slot alone
+            _need(not m.atoms and not self.ghost, "threadgroup store under a program_id-dependent mask")
             sm = self.smem[ident]
             _need(isinstance(v, FLoad), "threadgroup memory holds something other than a global load")
-            slots = self.concrete(off)
-            _need(bool((slots < len(sm.buf)).all()), "threadgroup store out of range")
-            s = slots.astype(np.int64)
+            who = np.nonzero(m.conc)[0]
+            s = self.concrete(off).astype(np.int64)[who]
+            _need(bool((s < len(sm.buf)).all()), "threadgroup store out of range")
             _need(len(np.unique(s)) == len(s), "two threads store to one threadgroup slot")
             _need(bool((sm.wphase[s] != self.phase).all()), "threadgroup slot written twice between barriers")
             _need(bool((sm.rphase[s] != self.phase).all()), "threadgroup slot written after a read between barriers")
             sm.buf[s] = self.code(v.buf)
-            sm.lin[:, s] = v.lin
-            sm.conc[s] = v.mask.conc
+            sm.lin[:, s] = v.lin[:, who]
+            sm.conc[s] = v.mask.conc[who]
             self.records.append(v.mask.atoms)
             sm.rec[s] = len(self.records) - 1
-            sm.writer[s] = np.arange(self.nt)
+            sm.writer[s] = who
             sm.wphase[s] = self.phase
         else:
             self.stores.append((ident, self.u(off), v, Mask(m.conc, m.atoms + self.ghost)))

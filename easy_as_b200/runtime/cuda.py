@@ -233,6 +233,27 @@ class CudaRuntime:
         self._event_pool: list[int] = []
         self.launch_count = 0  # kernels launched through this runtime (generic + native)
         self.native_launches = 0  # of which pattern-lowered native kernels
+        self._scratch_bufs: dict[tuple[int, int, str], DeviceBuffer] = {}
+
+    def scratch(self, device: int, stream: int, tag: str, nbytes: int) -> int | None:
+        """Device scratch of at least ``nbytes`` for native plans, one per (device, stream, tag), so
+        work on one stream reuses it in order.  Grows by reallocating after the stream drained;
+        None when that would have to happen inside a CUDA-graph capture (the caller then declines)."""
+        key = (int(device), int(stream), tag)
+        buf = self._scratch_bufs.get(key)
+        if buf is not None and buf.nbytes >= nbytes:
+            return buf.ptr
+        capturing = cuda_ext.ctypes.c_int(0)
+        if stream:
+            cuda_ext.check(self.lib().eas_stream_is_capturing(stream, cuda_ext.ctypes.byref(capturing)), "capture state")
+        if capturing.value:
+            return None
+        if buf is not None:
+            cuda_ext.check(self.lib().eas_stream_synchronize(stream), "scratch resize")
+            buf.free()
+        buf = DeviceBuffer(max(int(nbytes), 256), int(device))
+        self._scratch_bufs[key] = buf
+        return buf.ptr
 
     # -- availability ----------------------------------------------------------
     def is_available(self) -> bool:

@@ -169,6 +169,19 @@ int eas_sgemm_f32_tiled(const float* a, const float* b, float* c, uint32_t M, ui
                         uint64_t b_bstride, uint64_t ldc, uint64_t c_bstride, int zero_init,
                         uint32_t a_rows, uint32_t a_k, uint32_t b_cols, uint32_t b_k, void* stream);
 
+/* f32 -> f16 operand staging (round to nearest even, cvt.rn.f16.f32, the cast
+ * of the generated kernels) for the proven simdgroup-MMA GEMM of the
+ * reference's matmul_simdgroup kernel (easy_as examples/matmul_simdgroup.py:
+ * 29-127, whose tiles are cast to f16 in threadgroup memory before
+ * simdgroup_multiply_accumulate, eas/codegen/msl.py:953-1002):
+ *   dst[b][r][c] = (r < rows_valid && c < cols_valid) ? f16(src[b*bs_src + r*ld_src + c]) : 0
+ * for r < rows, c < cols_pad.  cols_pad and ld_dst multiples of 8, dst
+ * 16-byte aligned (bs_dst a multiple of 8 when batch > 1); otherwise
+ * EAS_ERR_VALUE.  Asynchronous on `stream`. */
+int eas_cast_f32_f16_2d(const float* src, void* dst, uint32_t rows, uint32_t cols_pad, uint64_t ld_src,
+                        uint64_t ld_dst, uint32_t rows_valid, uint32_t cols_valid, uint32_t batch, uint64_t bs_src,
+                        uint64_t bs_dst, void* stream);
+
 /* Read and clear the status word of native kernels on `dev` (0 = ok,
  * EAS_ERR_TIMEOUT = a bounded wait expired).  Valid after the stream synced. */
 int eas_gemm_status(int dev, int* code);

@@ -115,6 +115,11 @@ BIG_CASES = [
     ("matmul_tiled_c3_full", "examples/matmul_tiled.py", "matmul_tiled_full_kernel",
      [B("f32", 1), B("f32", 1), B("f32", 1), 2048, 2048],
      {"BM": 32, "BN": 32, "BK": 32, "K": 2048, "NT": 256}, {"grid": [64, 64, 1]}),
+    # the simdgroup-MMA example's own default run (examples/matmul_simdgroup.py:138-160): 512^3,
+    # BM=16 BN=32 BK=8, NT=(BM/8)(BN/8)*32
+    ("matmul_simdgroup_512", "examples/matmul_simdgroup.py", "matmul_simdgroup_mma_kernel",
+     [B("f32", 512 * 512), B("f32", 512 * 512), B("f32", 512 * 512), 512, 512],
+     {"BM": 16, "BN": 32, "BK": 8, "K": 512, "NT": 256}, {"grid": [512 // 32, 512 // 16, 1]}),
 ]
 
 

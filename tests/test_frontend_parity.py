@@ -39,8 +39,8 @@ def test_passes_reproduce_reference(c):
     assert sorted(infer_writes(opt)) == c["writes"]
 
 
-def test_big_case_passes():
-    (c,) = goldens.big_cases()
+@pytest.mark.parametrize("c", goldens.big_cases(), ids=[c["id"] for c in goldens.big_cases()])
+def test_big_case_passes(c):
     opt = optimize_ir(goldens.ir_from_json(c["raw"]))
     assert goldens.ir_to_json(opt) == c["opt"]
 

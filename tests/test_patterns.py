@@ -80,9 +80,10 @@ def gemv_like_f32(a, x, y, M, K, BLOCK: eas.constexpr):
 
 @pytest.mark.parametrize("cid", ["add_c1", "matmul_tiled_masked", "matmul_simdgroup", "t_gemv_dot", "t_tg_copy"])
 def test_other_kernels_have_no_f16_gemm_plan(cid):
-    """Only fp32 dot kernels may carry the tiled-FFMA plan, which proves its case per launch."""
+    """Other kernels may only carry the plans that prove their case per launch (tiled fp32 GEMM,
+    simdgroup-MMA GEMM), never the f16 dot plan."""
     ck = compile_ir(goldens.ir_from_json(goldens.case(cid)["opt"]))
-    assert getattr(ck.plan.native, "kind", None) in (None, "tiled_f32_ffma")
+    assert getattr(ck.plan.native, "kind", None) in (None, "tiled_f32_ffma", "mma_f16_tcgen05")
 
 
 def test_f32_dot_is_not_f16_gemm_pattern():
