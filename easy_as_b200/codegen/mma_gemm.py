@@ -28,15 +28,13 @@ masks, program-id shifts) is the tiled one.  The launch writes A and B once as z
 
 from __future__ import annotations
 
-import os
 from dataclasses import dataclass
 from typing import Any
 
 import numpy as np
 
 from ..ir import DType, IRModule, Inst, ValueRef
-from .tiled import (Decline, FDot, FLoad, Side, _affine_k, _Exec, _need, _Smem, _uniform_rhs, bounds, derive,
-                    map_grid, plan_launch)
+from .tiled import FDot, FLoad, ProvenGemmPlan, Side, _affine_k, _Exec, _need, _Smem, _uniform_rhs
 
 
 @dataclass(frozen=True, eq=False)
@@ -112,7 +110,7 @@ class _MmaExec(_Exec):
         _need(bool((v == v[:, :1]).all()), f"{what} differs between the lanes of a warp")
         return v[:, 0]
 
-    def _operand(self, buf: ValueRef, base: ValueRef, stride: ValueRef, a_side: bool) -> dict:
+    def _operand(self, buf: ValueRef, base: ValueRef, stride: ValueRef) -> dict:
         kind, ident = self._buffer(buf)
         _need(kind == "smem", "mma operand outside threadgroup memory")
         sm = self.smem[ident]
@@ -136,7 +134,7 @@ class _MmaExec(_Exec):
         a_buf, a_base, a_stride, b_buf, b_base, b_stride, acc = inst.args
         prev = self.vals[acc.id]
         _need(isinstance(prev, FFrag), "mma accumulator is not a fragment")
-        step = (self._operand(a_buf, a_base, a_stride, True), self._operand(b_buf, b_base, b_stride, False))
+        step = (self._operand(a_buf, a_base, a_stride), self._operand(b_buf, b_base, b_stride))
         self.vals[inst.out.id] = FFrag(prev.steps + (step,))
 
     def op_mma_store(self, inst: Inst) -> None:
@@ -162,29 +160,19 @@ class _MmaExec(_Exec):
         sm.buf[flat] = -1
         sm.wphase[flat] = self.phase
 
+    def _slot_load(self, v: Any) -> tuple[FLoad, Any]:
+        if isinstance(v, FCast16):
+            return v.x, True
+        return super()._slot_load(v)[0], False
+
+    def _slot_written(self, sm: _Smem, slots: np.ndarray, extra: Any) -> None:
+        sm.cast[slots] = bool(extra)
+        sm.fidx[slots] = -1
+
     def run(self) -> None:
-        for inst in self.ir.insts:
-            if inst.op == "store" and inst.args[0].id in self.smem and isinstance(self.vals.get(inst.args[2].id),
-                                                                                    FCast16):
-                self._store_cast(inst)
-                continue
-            getattr(self, "op_" + inst.op, self.op_unsupported)(inst)
+        super().run()
         self.stores = [(b, off, self._as_dot(v), m) if isinstance(v, FFragElem) else (b, off, v, m)
                        for b, off, v, m in self.stores]
-
-    def _store_cast(self, inst: Inst) -> None:
-        """Threadgroup store of f16(load): the load's slot data plus the cast flag."""
-        buf, off, val, mask = inst.args
-        load = self.vals[val.id].x
-        self.vals[val.id] = load
-        try:
-            super().op_store(inst)
-        finally:
-            self.vals[val.id] = FCast16(load)
-        sm = self.smem[self._buffer(buf)[1]]
-        written = self.concrete(off).astype(np.int64)[np.nonzero(self.plain(mask))[0]]
-        sm.cast[written] = True
-        sm.fidx[written] = -1
 
     def _as_dot(self, e: FFragElem) -> FDot:
         """The products of each thread's fragment element, sorted by A address, as one dot."""
@@ -239,73 +227,24 @@ _OPS = {"arg", "const", "alloc_tg", "program_id", "thread_id", "tid", "local_id"
         "mma_store"}
 
 
-class MmaGemmPlan:
+class MmaGemmPlan(ProvenGemmPlan):
     """tcgen05 launch for simdgroup-MMA kernels proven to be f16 GEMMs (module docstring)."""
 
     kind = "mma_f16_tcgen05"
+    executor = _MmaExec
+    allow_ghosts = False
 
-    def __init__(self, ir: IRModule, block: int):
-        self.ir = ir
-        self.block = block
-        self.cache: dict[Any, Any] = {}
-        self.last_reason = ""
-
-    def analyse(self, scalars: dict[str, int], programs: tuple[int, int, int], ntx: int,
-                pid_base: tuple[int, int, int] = (0, 0, 0)) -> dict[str, Any] | None:
-        key = (tuple(sorted(scalars.items())), programs, ntx, tuple(pid_base))
-        hit = self.cache.get(key)
-        if hit is None:
-            try:
-                _need(ntx >= (pid_base[0] + programs[0]) * self.block, "partial thread groups")
-                ex = _MmaExec(self.ir, self.block, scalars, None, tuple(pid_base))
-                ex.run()
-                d = derive(ex)
-                g = map_grid(d, programs)
-                d.update({"row_ax": g["row_ax"], "col_ax": g["col_ax"]})
-                hit = plan_launch(d, g, bounds(d, programs))
-            except Decline as e:
-                hit = str(e)
-            if len(self.cache) > 64:
-                self.cache.clear()
-            self.cache[key] = hit
-        if isinstance(hit, str):
-            self.last_reason = hit
-            return None
-        return hit
-
-    def try_launch(self, rt: Any, ck: Any, runtime_args: dict[str, Any], args: dict[str, Any], device: int,
-                   stream: int, programs: tuple[int, int, int], ntx: int, pid_base: tuple[int, int, int] = (0, 0, 0),
-                   elem_base: dict[str, int] | None = None) -> bool:
-        if os.environ.get("EAS_DISABLE_NATIVE", "0") not in ("", "0"):
-            self.last_reason = "disabled by EAS_DISABLE_NATIVE"
-            return False
-        scalars = {a.name: int(runtime_args[a.name]) for a in self.ir.args
-                   if a.kind == "scalar" and a.dtype == DType.U32}
-        d = self.analyse(scalars, programs, ntx, pid_base)
-        if d is None:
-            return False
-        if d["empty"]:
-            return True
-        from .patterns import _numel
-
-        eb = elem_base or {}
-        for n, lo, top, used in ((d["a_buf"], d["a0"], d["top_a"], d["reads_a"]),
-                                 (d["b_buf"], d["b0"], d["top_b"], d["reads_b"]), (d["c_buf"], d["c0"], d["top_c"], True)):
-            e = int(eb.get(n, 0))
-            if used and (lo < e or top >= e + _numel(runtime_args[n])):
-                self.last_reason = f"{n}: the product reaches outside the buffer"
-                return False
-        M, N, K, batch = d["M"], d["N"], d["K"], d["batch"]
-        n_pad = -(-N // 8) * 8
-        lib = rt.lib()
+    def _launch(self, rt: Any, d: dict[str, Any], pa: int, pb: int, pc: int, device: int, stream: int) -> bool:
         from ..runtime import cuda_ext
 
+        M, N, K, batch = d["M"], d["N"], d["K"], d["batch"]
+        n_pad = -(-N // 8) * 8
         a16 = rt.scratch(device, stream, "mma_a16", 2 * batch * M * K)
         b16 = rt.scratch(device, stream, "mma_b16", 2 * batch * K * n_pad)
         if a16 is None or b16 is None:
             self.last_reason = "f16 staging buffers cannot be allocated during graph capture"
             return False
-        pa, pb, pc = args[d["a_buf"]].ptr, args[d["b_buf"]].ptr, args[d["c_buf"]].ptr
+        lib = rt.lib()
         cuda_ext.check(lib.eas_cast_f32_f16_2d(pa + 4 * d["a0"], a16, M, K, d["a_sm"], K, d["a_rows"], d["a_k"], batch,
                                                d["a_bs"], M * K, stream), "cast A to f16")
         cuda_ext.check(lib.eas_cast_f32_f16_2d(pb + 4 * d["b0"], b16, K, n_pad, d["b_sk"], n_pad, d["b_k"],
@@ -315,7 +254,7 @@ class MmaGemmPlan:
         if rc == cuda_ext.EAS_ERR_VALUE:
             self.last_reason = cuda_ext.last_error()
             return False
-        cuda_ext.check(rc, "gemm_f16 (tcgen05) for mma kernel")
+        cuda_ext.check(rc, "gemm_f16 (tcgen05) for an mma kernel")
         rt.launch_count += 3
         rt.native_launches += 1
         return True

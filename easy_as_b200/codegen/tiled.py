@@ -377,7 +377,7 @@ class _Exec:
             # a program-id-free mask selects the writing threads; the others leave their slot alone
             _need(not m.atoms and not self.ghost, "threadgroup store under a program_id-dependent mask")
             sm = self.smem[ident]
-            _need(isinstance(v, FLoad), "threadgroup memory holds something other than a global load")
+            v, extra = self._slot_load(v)
             who = np.nonzero(m.conc)[0]
             s = self.concrete(off).astype(np.int64)[who]
             _need(bool((s < len(sm.buf)).all()), "threadgroup store out of range")
@@ -391,8 +391,17 @@ class _Exec:
             sm.rec[s] = len(self.records) - 1
             sm.writer[s] = who
             sm.wphase[s] = self.phase
+            self._slot_written(sm, s, extra)
         else:
             self.stores.append((ident, self.u(off), v, Mask(m.conc, m.atoms + self.ghost)))
+
+    def _slot_load(self, v: Any) -> tuple[FLoad, Any]:
+        """What a threadgroup store may write: a global load (extensions also accept e.g. its cast)."""
+        _need(isinstance(v, FLoad), "threadgroup memory holds something other than a global load")
+        return v, None
+
+    def _slot_written(self, sm: _Smem, slots: np.ndarray, extra: Any) -> None:
+        """Per-slot bookkeeping of extensions after a threadgroup store."""
 
     def _side(self, buf: ValueRef, base: ValueRef, stride: ValueRef, k: int) -> Side:
         kind, ident = self._buffer(buf)
@@ -700,35 +709,24 @@ _OPS = {"arg", "const", "alloc_tg", "program_id", "thread_id", "tid", "local_id"
         "floordiv", "mod", "lt", "and", "or", "not", "where", "barrier", "load", "store", "dot", "fma"}
 
 
-_SELF_HASH: str | None = None
+_SRC_HASHES: dict[str, str] = {}
 
 
-def _disk_path(ir: IRModule, block: int, key: tuple) -> Any:
-    """Cache file of one proof result under EAS_CACHE_DIR/plans (None when caching is off).  The
-    key hashes the IR, the launch values and this module's own source, so a change of the proof
-    logic never reuses an old result."""
-    global _SELF_HASH
+def _src_hash(path: str) -> str:
     import hashlib
-    import json
 
-    from ..ir import ir_to_json
-    from ..runtime.cuda import _cache_dir
-
-    cdir = _cache_dir()
-    if cdir is None or os.environ.get("EAS_PLAN_CACHE", "1") == "0":
-        return None
-    if _SELF_HASH is None:
-        _SELF_HASH = hashlib.sha256(open(__file__, "rb").read()).hexdigest()
-    h = hashlib.sha256()
-    h.update(_SELF_HASH.encode())
-    h.update(json.dumps([ir_to_json(ir), block, repr(key)], separators=(",", ":")).encode())
-    return cdir / "plans" / f"{h.hexdigest()}.json"
+    if path not in _SRC_HASHES:
+        _SRC_HASHES[path] = hashlib.sha256(open(path, "rb").read()).hexdigest()
+    return _SRC_HASHES[path]
 
 
-class TiledGemmPlan:
-    """Native FFMA launch for kernels proven to be tiled fp32 GEMMs (module docstring)."""
+class ProvenGemmPlan:
+    """Per-launch proof (a symbolic execution, cached in memory and on disk) and the checks every
+    native GEMM launch shares; subclasses give the executor and the launch itself."""
 
-    kind = "tiled_f32_ffma"
+    kind = ""
+    executor: type = _Exec
+    allow_ghosts = True
 
     def __init__(self, ir: IRModule, block: int):
         self.ir = ir
@@ -736,25 +734,46 @@ class TiledGemmPlan:
         self.cache: dict[Any, Any] = {}
         self.last_reason = ""
 
+    def _disk_path(self, key: tuple) -> Any:
+        """Cache file of one proof result under EAS_CACHE_DIR/plans (None when caching is off).  The
+        key hashes the IR, the launch values and the proof's own source files, so a change of the
+        proof logic never reuses an old result."""
+        import hashlib
+        import json
+        import sys
+
+        from ..ir import ir_to_json
+        from ..runtime.cuda import _cache_dir
+
+        cdir = _cache_dir()
+        if cdir is None or os.environ.get("EAS_PLAN_CACHE", "1") == "0":
+            return None
+        h = hashlib.sha256()
+        for mod in {__name__, type(self).__module__}:
+            h.update(_src_hash(sys.modules[mod].__file__).encode())
+        h.update(json.dumps([self.kind, ir_to_json(self.ir), self.block, repr(key)], separators=(",", ":")).encode())
+        return cdir / "plans" / f"{h.hexdigest()}.json"
+
     def analyse(self, scalars: dict[str, int], programs: tuple[int, int, int], ntx: int,
                 pid_base: tuple[int, int, int] = (0, 0, 0)) -> dict[str, Any] | None:
         """Proof and launch values for the programs ``pid_base + [0, programs)``."""
+        import json
+
         key = (tuple(sorted(scalars.items())), programs, ntx, tuple(pid_base))
         hit = self.cache.get(key)
         disk = None
         if hit is None:
-            disk = _disk_path(self.ir, self.block, key)
+            disk = self._disk_path(key)
             if disk is not None and disk.exists():
                 try:
-                    import json
-
                     hit = json.loads(disk.read_text())["result"]
                 except (OSError, ValueError, KeyError):
                     hit = None
         if hit is None:
             try:
                 ghost = ntx if ntx < (pid_base[0] + programs[0]) * self.block else None
-                ex = _Exec(self.ir, self.block, scalars, ghost, tuple(pid_base))
+                _need(ghost is None or self.allow_ghosts, "partial thread groups")
+                ex = self.executor(self.ir, self.block, scalars, ghost, tuple(pid_base))
                 ex.run()
                 d = derive(ex)
                 g = map_grid(d, programs)
@@ -764,8 +783,6 @@ class TiledGemmPlan:
                 hit = str(e)
             if disk is not None:
                 try:
-                    import json
-
                     disk.parent.mkdir(parents=True, exist_ok=True)
                     tmp = disk.with_suffix(f".{os.getpid()}.tmp")
                     tmp.write_text(json.dumps({"result": hit}))
@@ -784,7 +801,8 @@ class TiledGemmPlan:
                    stream: int, programs: tuple[int, int, int], ntx: int, pid_base: tuple[int, int, int] = (0, 0, 0),
                    elem_base: dict[str, int] | None = None) -> bool:
         """Launch for programs ``pid_base + [0, programs)``; buffers in ``elem_base`` hold only the
-        elements from that global index on (pointers already moved back by it)."""
+        elements from that global index on (pointers already moved back by it).  False (and
+        ``last_reason``) when the proof or a check fails: the caller runs the generated kernel."""
         if os.environ.get("EAS_DISABLE_NATIVE", "0") not in ("", "0"):
             self.last_reason = "disabled by EAS_DISABLE_NATIVE"
             return False
@@ -810,13 +828,24 @@ class TiledGemmPlan:
             if p < c_hi and c_lo < p + 4 * (top + 1):
                 self.last_reason = "output overlaps an operand"
                 return False
-        lib = rt.lib()
-        rc = lib.eas_sgemm_f32_tiled(pa + 4 * d["a0"], pb + 4 * d["b0"], pc + 4 * d["c0"], d["M"], d["N"], d["K"],
-                                     d["kt"], d["batch"], d["a_sm"], d["a_bs"], d["b_sk"], d["b_bs"], d["c_sm"],
-                                     d["c_bs"], int(d["zero_init"]), d["a_rows"], d["a_k"], d["b_cols"], d["b_k"],
-                                     stream)
+        return self._launch(rt, d, pa, pb, pc, device, stream)
+
+    def _launch(self, rt: Any, d: dict[str, Any], pa: int, pb: int, pc: int, device: int, stream: int) -> bool:
+        raise NotImplementedError
+
+
+class TiledGemmPlan(ProvenGemmPlan):
+    """Native FFMA launch for kernels proven to be tiled fp32 GEMMs (module docstring)."""
+
+    kind = "tiled_f32_ffma"
+
+    def _launch(self, rt: Any, d: dict[str, Any], pa: int, pb: int, pc: int, device: int, stream: int) -> bool:
         from ..runtime import cuda_ext
 
+        rc = rt.lib().eas_sgemm_f32_tiled(pa + 4 * d["a0"], pb + 4 * d["b0"], pc + 4 * d["c0"], d["M"], d["N"], d["K"],
+                                          d["kt"], d["batch"], d["a_sm"], d["a_bs"], d["b_sk"], d["b_bs"], d["c_sm"],
+                                          d["c_bs"], int(d["zero_init"]), d["a_rows"], d["a_k"], d["b_cols"],
+                                          d["b_k"], stream)
         if rc == cuda_ext.EAS_ERR_VALUE:
             self.last_reason = cuda_ext.last_error()
             return False
