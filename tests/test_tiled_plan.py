@@ -206,3 +206,21 @@ def test_program_id_sub_range_is_the_shifted_gemm():
     assert d is not None, plan.last_reason
     assert (d["M"], d["N"], d["K"]) == (1024, 2048, 2048)
     assert (d["a0"], d["b0"], d["c0"]) == (1024 * 2048, 0, 1024 * 2048)
+
+
+def test_own_tiled_variants_are_proven():
+    """Kernels of another shape than the reference's (tests/tiled_variants.py) are proven too."""
+    import numpy as np
+
+    from tiled_variants import VARIANTS, grid, tile_mm
+
+    M, N, K = 70, 150, 48
+    for tm, tn, tk, nt, pad in VARIANTS:
+        kk = -(-K // tk) * tk if K % tk else K
+        ck = tile_mm.compile(np.zeros(M * kk, np.float32), np.zeros(kk * N, np.float32), np.zeros(M * N, np.float32),
+                             M, N, K=K, TM=tm, TN=tn, TK=tk, NT=nt, PAD=pad)
+        plan = ck.plan.native
+        assert plan is not None and plan.kind == "tiled_f32_ffma"
+        d = plan.analyse({"M": M, "N": N}, grid(M, N, tm, tn), 0xFFFFFFFF)
+        assert d is not None, (tm, tn, tk, nt, pad, plan.last_reason)
+        assert (d["M"], d["N"], d["a_k"], d["kt"]) == (M, N, K, tk)
