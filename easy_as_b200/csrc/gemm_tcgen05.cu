@@ -73,17 +73,31 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Bounded wait: false when the budget ran out or another role aborted.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          long long budget = kWaitBudget) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (clock64() - t0 > kWaitBudget) {
+    if (clock64() - t0 > budget) {
       *abort_flag = 1;
       return false;
     }
   }
+}
+
+// Self-test of the expiry path: a barrier that nothing ever completes, waited on with `budget`.
+__global__ void wait_selftest_kernel(long long budget, int* status) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && !mbar_wait(&bar, 0, &abort_flag, budget) && status) *status = EAS_ERR_TIMEOUT;
 }
 
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z) {
@@ -754,6 +768,17 @@ extern "C" int eas_gemm_status(int dev, int* code) {
   *code = (g_status_host && dev >= 0 && dev < 64) ? g_status_host[dev] : 0;
   if (g_status_host && dev >= 0 && dev < 64) g_status_host[dev] = 0;
   return EAS_OK;
+}
+
+extern "C" int eas_wait_selftest(long long budget_cycles, void* stream) {
+  if (budget_cycles <= 0 || budget_cycles > kWaitBudget)
+    return eas_fail(EAS_ERR_VALUE, "eas_wait_selftest: budget must be in (0, %lld] cycles", kWaitBudget);
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int* status = eas_native_status_dev(dev);
+  if (!status) return eas_fail(EAS_ERR_MEMORY, "eas_wait_selftest: no status word");
+  wait_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(budget_cycles, status);
+  return eas_cuda_check(cudaGetLastError(), "wait_selftest launch", EAS_ERR_LAUNCH);
 }
 
 extern "C" int eas_gemm_f16(const void* a, const void* b, float* c, uint32_t M, uint32_t N, uint32_t K,

@@ -182,6 +182,15 @@ int eas_cast_f32_f16_2d(const float* src, void* dst, uint32_t rows, uint32_t col
                         uint64_t ld_dst, uint32_t rows_valid, uint32_t cols_valid, uint32_t batch, uint64_t bs_src,
                         uint64_t bs_dst, void* stream);
 
+/* Self-test of the bounded waits of the native kernels (no counterpart in
+ * the reference): launches one warp that waits, with the same bounded
+ * mbarrier wait the GEMM uses, on a barrier that nothing ever completes.  The
+ * wait gives up after budget_cycles (1 .. the kernels' own budget of 4e9
+ * cycles), the kernel sets EAS_ERR_TIMEOUT in the device's status word and
+ * returns; read it with eas_gemm_status after the stream synchronised.
+ * Nothing faults or hangs; the context stays usable.  Asynchronous. */
+int eas_wait_selftest(long long budget_cycles, void* stream);
+
 /* Read and clear the status word of native kernels on `dev` (0 = ok,
  * EAS_ERR_TIMEOUT = a bounded wait expired).  Valid after the stream synced. */
 int eas_gemm_status(int dev, int* code);
