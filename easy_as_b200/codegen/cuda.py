@@ -374,7 +374,29 @@ class _Emitter:
             mem_after[k] = seen
             if insts[k].op in ("load", "store"):
                 seen = True
+        runs = find_runs(insts) if os.environ.get("EAS_REROLL", "1") != "0" else []
+        run_at = {r.first[0]: r for r in runs}
+        in_run: set[int] = set()
+        for r in runs:
+            in_run |= r.ir_span
+        if runs:  # constants first: re-rolled blocks read them from any position
+            for inst in insts:
+                if inst.op == "const":
+                    self._spmd_inst(inst)
+
+        def block(run: Run, body: dict[int, Inst]) -> None:
+            for k in run.first:
+                self._spmd_inst(body[k])
+                if body[k].op == "store" and mem_after[k]:
+                    self.emit("__syncthreads();")
+
         for k, inst in enumerate(insts):
+            if runs and inst.op == "const":
+                continue
+            if k in run_at:
+                self._emit_run(run_at[k], lambda body, r=run_at[k]: block(r, body))
+            if k in in_run:
+                continue
             self._spmd_inst(inst)
             if inst.op == "store" and mem_after[k]:
                 self.emit("__syncthreads();")
@@ -563,7 +585,7 @@ class _Emitter:
             if inst.op == "const":
                 continue
             if k in run_at:
-                self._emit_run(run_at[k], groups)
+                self._emit_run(run_at[k], lambda body, r=run_at[k]: self._thread_block(r, body, groups))
             if k in in_run:
                 continue
             if k in groups:
@@ -573,16 +595,44 @@ class _Emitter:
             self._thread_inst(inst)
         return self.lines
 
-    def _emit_run(self, run: Run, groups: dict[int, list[int]]) -> None:
+    def _thread_block(self, run: Run, body: dict[int, Inst], groups: dict[int, list[int]]) -> None:
+        for k in run.first:
+            if k in groups:
+                if groups[k]:
+                    self._dot_group([body[j] for j in groups[k]])
+                continue
+            self._thread_inst(body[k])
+
+    def _emit_run(self, run: Run, emit_body: Any) -> None:
         """Print a run of identical unrolled blocks as one loop over block 0 (bit-identical: the same
-        operations in the same order).  Loop-carried operands live in mutable variables updated at
-        the end of each iteration; the last iteration's values read after the loop are copied out."""
+        operations in the same order).  Loop-carried operands live in mutable variables (lane arrays
+        in SPMD mode) updated at the end of each iteration; the last iteration's values read after
+        the loop are copied out.  ``emit_body(body)`` prints block 0 with ``body`` = {IR index:
+        instruction with the carried and affine operands substituted}."""
         insts = self.ir.insts
         n = len(self.lines)
         rv = f"eas_r{n}"
         fresh = 1 << 40
+
+        def declare(var: str, out: ValueRef, init: str | None) -> None:
+            t = ctype(out.dtype)
+            if out.lanes > 1:
+                self.emit(f"{t} {var}[{self.L}];")
+                if init is not None:
+                    for i in range(self.L):
+                        self.emit(f"{var}[{i}] = {init}[{i}];")
+            else:
+                self.emit(f"{t} {var}" + (f" = {init};" if init is not None else ";"))
+
+        def copy(dst: str, src: str, lanes: int) -> None:
+            if lanes > 1:
+                for i in range(self.L):
+                    self.emit(f"{dst}[{i}] = {src}[{i}];")
+            else:
+                self.emit(f"{dst} = {src};")
+
         body: dict[int, Inst] = {}
-        carries: dict[str, tuple[str, int]] = {}  # variable -> (C type, q)
+        carries: dict[str, int] = {}  # variable -> q
         for j, k in enumerate(run.first):
             inst = insts[k]
             args = list(inst.args)
@@ -592,9 +642,8 @@ class _Emitter:
                     _, q, init = f
                     var = f"eas_c{n}_{q}_{init}"
                     if var not in carries:
-                        t = ctype(insts[run.first[q]].out.dtype)
-                        carries[var] = (t, q)
-                        self.emit(f"{t} {var} = {self.name(a)};")
+                        carries[var] = q
+                        declare(var, insts[run.first[q]].out, self.name(a))
                     fresh += 1
                     self.alias[fresh] = var
                     args[a_i] = ValueRef(fresh, a.dtype, a.lanes)
@@ -609,24 +658,25 @@ class _Emitter:
             o = insts[run.first[q]].out
             self.uses[o.id] = max(1, self.uses.get(o.id, 0))
             escapes[q] = f"eas_e{n}_{q}"
-            self.emit(f"{ctype(o.dtype)} {escapes[q]};")
+            declare(escapes[q], o, None)
         self.emit(f"for (uint32_t {rv} = 0u; {rv} < {run.count}u; ++{rv}) {{")
         self.depth += 1
-        for k in run.first:
-            if k in groups:
-                if groups[k]:
-                    self._dot_group([body[j] for j in groups[k]])
-                continue
-            self._thread_inst(body[k])
-        for var, (_t, q) in carries.items():
-            self.emit(f"{var} = v{insts[run.first[q]].out.id};")
+        emit_body(body)
+        for var, q in carries.items():
+            o = insts[run.first[q]].out
+            copy(var, f"v{o.id}", o.lanes)
         for q, var in escapes.items():
-            self.emit(f"{var} = v{insts[run.first[q]].out.id};")
+            o = insts[run.first[q]].out
+            copy(var, f"v{o.id}", o.lanes)
         self.depth -= 1
         self.emit("}")
         for q, var in escapes.items():
-            o = run.last_out[q]
-            self.emit(f"const {ctype(insts[run.first[q]].out.dtype)} v{o} = {var};")
+            o = insts[run.first[q]].out
+            if o.lanes > 1:
+                self.emit(f"{ctype(o.dtype)} v{run.last_out[q]}[{self.L}];")
+                copy(f"v{run.last_out[q]}", var, o.lanes)
+            else:
+                self.emit(f"const {ctype(o.dtype)} v{run.last_out[q]} = {var};")
 
     _PURE = frozenset({"const", "add", "mul", "floordiv", "mod", "lt", "and", "or", "not", "where", "cast", "fma",
                        "program_id", "thread_id", "local_id", "lane_id", "sg_id", "tid"})

@@ -148,3 +148,29 @@ def test_rerolled_sources_compile(cid):
         pytest.skip("NVRTC not loadable here")
     assert rc == 0, cuda_ext.last_error()
     lib.eas_free_host(img)
+
+
+@pytest.mark.parametrize("name", ["colsum", "rows_scale"])
+def test_spmd_loops_are_rerolled_and_compile(name, monkeypatch):
+    import numpy as np
+
+    import spmd_loops
+
+    k = getattr(spmd_loops, name)
+    x = np.zeros(64 * 1000, np.float32)
+    y = np.zeros(64 * 1000, np.float32)
+    src = k.compile(x, y, 1000, W=64, BLOCK=256).src
+    assert "for (uint32_t eas_r" in src and src.count("\n") < 400
+    for run in find_runs(k.compile(x, y, 1000, W=64, BLOCK=256).ir.insts):
+        _check_run(k.compile(x, y, 1000, W=64, BLOCK=256).ir.insts, run)
+    lib = cuda_ext.load()
+    img, size = ctypes.c_void_p(), ctypes.c_size_t()
+    rc = lib.eas_compile(src.encode(), b"k.cu", None, 0, ctypes.byref(img), ctypes.byref(size))
+    if rc == cuda_ext.EAS_ERR_UNAVAILABLE:
+        pytest.skip("NVRTC not loadable here")
+    assert rc == 0, cuda_ext.last_error()
+    lib.eas_free_host(img)
+    from easy_as_b200.compiler import compile_ir
+
+    monkeypatch.setenv("EAS_REROLL", "0")      # the kernel's compile cache is bypassed: lower the IR again
+    assert "eas_r" not in compile_ir(k.compile(x, y, 1000, W=64, BLOCK=256).ir).src
