@@ -239,11 +239,12 @@ class MmaGemmPlan(ProvenGemmPlan):
 
         M, N, K, batch = d["M"], d["N"], d["K"], d["batch"]
         n_pad = -(-N // 8) * 8
-        a16 = rt.scratch(device, stream, "mma_a16", 2 * batch * M * K)
-        b16 = rt.scratch(device, stream, "mma_b16", 2 * batch * K * n_pad)
-        if a16 is None or b16 is None:
+        sa = rt.scratch(device, stream, "mma_a16", 2 * batch * M * K)
+        sb = rt.scratch(device, stream, "mma_b16", 2 * batch * K * n_pad)
+        if sa is None or sb is None:
             self.last_reason = "f16 staging buffers cannot be allocated during graph capture"
             return False
+        (a16, _keep_a), (b16, _keep_b) = sa, sb          # owners stay alive until the launches are enqueued
         lib = rt.lib()
         cuda_ext.check(lib.eas_cast_f32_f16_2d(pa + 4 * d["a0"], a16, M, K, d["a_sm"], K, d["a_rows"], d["a_k"], batch,
                                                d["a_bs"], M * K, stream), "cast A to f16")

@@ -235,14 +235,28 @@ class CudaRuntime:
         self.native_launches = 0  # of which pattern-lowered native kernels
         self._scratch_bufs: dict[tuple[int, int, str], DeviceBuffer] = {}
 
-    def scratch(self, device: int, stream: int, tag: str, nbytes: int) -> int | None:
-        """Device scratch of at least ``nbytes`` for native plans, one per (device, stream, tag), so
-        work on one stream reuses it in order.  Grows by reallocating after the stream drained;
-        None when that would have to happen inside a CUDA-graph capture (the caller then declines)."""
+    def scratch(self, device: int, stream: int, tag: str, nbytes: int) -> tuple[int, Any] | None:
+        """Device scratch of at least ``nbytes`` for a native launch on ``stream``: (pointer, owner);
+        keep ``owner`` until the launch is enqueued.  With torch, the block comes from torch's
+        caching allocator on ``stream`` (stream-ordered reuse; inside a CUDA-graph capture, from the
+        graph's private pool, kept for its replays).  Without torch: one cached buffer per
+        (device, stream, tag), grown after the stream drained; None when that would have to happen
+        inside a capture (the caller then declines)."""
+        try:
+            import torch  # type: ignore
+        except Exception:  # pragma: no cover - torch is part of the image
+            torch = None
+        if torch is not None and torch.cuda.is_available():
+            with torch.cuda.device(int(device)):
+                ctx = (torch.cuda.stream(torch.cuda.ExternalStream(int(stream), device=int(device))) if stream
+                       else torch.cuda.stream(torch.cuda.default_stream(int(device))))
+                with ctx:
+                    t = torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=f"cuda:{int(device)}")
+            return int(t.data_ptr()), t
         key = (int(device), int(stream), tag)
         buf = self._scratch_bufs.get(key)
         if buf is not None and buf.nbytes >= nbytes:
-            return buf.ptr
+            return buf.ptr, buf
         capturing = cuda_ext.ctypes.c_int(0)
         if stream:
             cuda_ext.check(self.lib().eas_stream_is_capturing(stream, cuda_ext.ctypes.byref(capturing)), "capture state")
@@ -253,7 +267,7 @@ class CudaRuntime:
             buf.free()
         buf = DeviceBuffer(max(int(nbytes), 256), int(device))
         self._scratch_bufs[key] = buf
-        return buf.ptr
+        return buf.ptr, buf
 
     # -- availability ----------------------------------------------------------
     def is_available(self) -> bool:
