@@ -30,3 +30,28 @@ def test_variant_native_equals_generated(cuda_rt, monkeypatch, v, M, N, K):
     assert torch.equal(outs[0].view(torch.int32), outs[1].view(torch.int32))
     ref = a.view(M, K).double() @ b.view(K, N).double()
     np.testing.assert_allclose(outs[0].view(M, N).double().cpu().numpy(), ref.cpu().numpy(), rtol=1e-4, atol=1e-4)
+
+
+@pytest.mark.parametrize("batch,M,N,K", [(5, 70, 150, 64), (3, 128, 96, 32)])
+def test_batched_variant_native_equals_generated(cuda_rt, monkeypatch, batch, M, N, K):
+    import torch
+
+    from tiled_variants import tile_mm_batched
+
+    tm, tn, tk, nt = 32, 32, 16, 128
+    g = torch.Generator(device="cuda").manual_seed(batch)
+    a = torch.randn(batch * M * K, device="cuda", generator=g)
+    b = torch.randn(batch * K * N, device="cuda", generator=g)
+    outs = []
+    for disable in ("0", "1"):
+        monkeypatch.setenv("EAS_DISABLE_NATIVE", disable)
+        c = torch.full((batch * M * N,), float("nan"), device="cuda")
+        before = cuda_rt.native_launches
+        tile_mm_batched(a, b, c, M, N, K=K, TM=tm, TN=tn, TK=tk, NT=nt,
+                        _grid=(-(-N // tn), -(-M // tm), batch), _sync=True)
+        assert (cuda_rt.native_launches == before + 1) == (disable == "0")
+        outs.append(c)
+    assert torch.equal(outs[0].view(torch.int32), outs[1].view(torch.int32))
+    ref = torch.bmm(a.view(batch, M, K).double(), b.view(batch, K, N).double())
+    np.testing.assert_allclose(outs[0].view(batch, M, N).double().cpu().numpy(), ref.cpu().numpy(), rtol=1e-4,
+                               atol=1e-4)

@@ -224,3 +224,16 @@ def test_own_tiled_variants_are_proven():
         d = plan.analyse({"M": M, "N": N}, grid(M, N, tm, tn), 0xFFFFFFFF)
         assert d is not None, (tm, tn, tk, nt, pad, plan.last_reason)
         assert (d["M"], d["N"], d["a_k"], d["kt"]) == (M, N, K, tk)
+
+
+def test_batched_variant_maps_the_z_axis_to_the_batch():
+    import numpy as np
+
+    from tiled_variants import tile_mm_batched
+
+    M, N, K = 70, 150, 64
+    ck = tile_mm_batched.compile(np.zeros(1, np.float32), np.zeros(1, np.float32), np.zeros(1, np.float32), M, N,
+                                 K=K, TM=32, TN=32, TK=16, NT=128)
+    d = ck.plan.native.analyse({"M": M, "N": N}, (5, 3, 5), 0xFFFFFFFF)
+    assert d is not None, ck.plan.native.last_reason
+    assert (d["batch"], d["a_bs"], d["b_bs"], d["c_bs"]) == (5, M * K, K * N, M * N)

@@ -51,3 +51,36 @@ VARIANTS = [(16, 64, 16, 256, 1), (32, 32, 32, 256, 1), (64, 64, 16, 256, 0), (8
 
 def grid(M, N, TM, TN):
     return (-(-N // TN), -(-M // TM), 1)
+
+
+@eas.kernel
+def tile_mm_batched(a, b, c, M, N, K: eas.constexpr, TM: eas.constexpr, TN: eas.constexpr,
+                    TK: eas.constexpr, NT: eas.constexpr):
+    """Batch on program_id(2): A[z] at z*M*K, B[z] at z*K*N, C[z] at z*M*N."""
+    t = mk.tid(0, NT)
+    z = mk.program_id(2)
+    row0 = mk.program_id(1) * TM
+    col0 = mk.program_id(0) * TN
+    sa = mk.alloc_tg(TM * TK)
+    sb = mk.alloc_tg(TK * TN)
+    per = TM * TN // NT
+    r = t // (TN // per)
+    cq = (t % (TN // per)) * per
+    acc = [0.0] * per
+    for k0 in range(0, K, TK):
+        for i in range(0, TM * TK, NT):
+            e = t + i
+            ar, ak = e // TK, e % TK
+            ok = (row0 + ar < M) & (k0 + ak < K)
+            mk.store(sa, ar * TK + ak, mk.load(a, z * M * K + (row0 + ar) * K + k0 + ak, ok))
+        for i in range(0, TK * TN, NT):
+            e = t + i
+            bk, bc = e // TN, e % TN
+            ok = (k0 + bk < K) & (col0 + bc < N)
+            mk.store(sb, bk * TN + bc, mk.load(b, z * K * N + (k0 + bk) * N + col0 + bc, ok))
+        mk.barrier()
+        for j in range(per):
+            acc[j] = acc[j] + mk.dot(sa, r * TK, 1, sb, cq + j, TN, TK)
+        mk.barrier()
+    for j in range(per):
+        mk.store(c, z * M * N + (row0 + r) * N + col0 + cq + j, acc[j], (row0 + r < M) & (col0 + cq + j < N))
