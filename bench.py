@@ -516,10 +516,18 @@ def run_eas(args) -> None:
         del a, b, c
         torch.cuda.empty_cache()
         for name in ("C4", "C5"):
-            gemm[name] = run_gemm(name, args, world, rank, rt)
+            try:
+                gemm[name] = run_gemm(name, args, world, rank, rt)
+            except (SystemExit, Exception) as e:
+                if world > 1:   # keep the ranks' collectives aligned: fail the whole run
+                    raise
+                gemm[name] = {"metric": "fp16 mk.dot GEMM TFLOP/s", "error": f"{type(e).__name__}: {e}"}
     tiled = None
     if not args.quick and not args.no_gemm and world == 1:
-        tiled = run_tiled(args, rt)
+        try:
+            tiled = run_tiled(args, rt)
+        except (SystemExit, Exception) as e:  # a secondary leg never suppresses the headline line
+            tiled = {"metric": "fp32 tiled matmul TFLOP/s", "error": f"{type(e).__name__}: {e}"}
     if rank != 0:
         return
     pk = peaks()
