@@ -838,10 +838,13 @@ class TiledGemmPlan(ProvenGemmPlan):
     """Native FFMA launch for kernels proven to be tiled fp32 GEMMs (module docstring)."""
 
     kind = "tiled_f32_ffma"
+    last_mode = ""
 
     def _launch(self, rt: Any, d: dict[str, Any], pa: int, pb: int, pc: int, device: int, stream: int) -> bool:
         from ..runtime import cuda_ext
 
+        if fp32_mode() == "3xtf32" and self._launch_3xtf32(rt, d, pa, pb, pc, device, stream):
+            return True
         rc = rt.lib().eas_sgemm_f32_tiled(pa + 4 * d["a0"], pb + 4 * d["b0"], pc + 4 * d["c0"], d["M"], d["N"], d["K"],
                                           d["kt"], d["batch"], d["a_sm"], d["a_bs"], d["b_sk"], d["b_bs"], d["c_sm"],
                                           d["c_bs"], int(d["zero_init"]), d["a_rows"], d["a_k"], d["b_cols"],
@@ -852,7 +855,52 @@ class TiledGemmPlan(ProvenGemmPlan):
         cuda_ext.check(rc, "sgemm_f32_tiled (FFMA)")
         rt.launch_count += 1
         rt.native_launches += 1
+        self.last_mode = "exact"
         return True
+
+
+    def _launch_3xtf32(self, rt: Any, d: dict[str, Any], pa: int, pb: int, pc: int, device: int,
+                       stream: int) -> bool:
+        """Opt-in 3xTF32 mode: C = A_hi.B_hi + A_hi.B_lo + A_lo.B_hi as ONE tcgen05 kind::tf32 GEMM
+        over K' = 3 kp (kp = K rounded up to 4, so every segment starts on 16 bytes), with
+        A' = [A_hi | A_hi | A_lo] (rows of A) and B'^T = [B_hi | B_lo | B_hi] (columns of B), both
+        written by eas_split3_tf32 with the proof's zero-fill bounds.  Not bit-identical to the
+        kernel's own fma chains: relative error ~1e-6 of |A||B| (the dropped A_lo.B_lo term is
+        2^-22 of a product), inside the fp32 matmul tolerance rtol 1e-4.  False (FFMA runs instead)
+        when the operands cannot be staged or the GEMM declines the shape."""
+        from ..runtime import cuda_ext
+
+        M, N, K, batch = d["M"], d["N"], d["K"], d["batch"]
+        kp = -(-K // 4) * 4
+        sa = rt.scratch(device, stream, "tf32_a3", 4 * batch * M * 3 * kp)
+        sb = rt.scratch(device, stream, "tf32_b3", 4 * batch * N * 3 * kp)
+        if sa is None or sb is None or K == 0:
+            return False
+        (a3, _keep_a), (b3, _keep_b) = sa, sb
+        lib = rt.lib()
+        cuda_ext.check(lib.eas_split3_tf32(pa + 4 * d["a0"], a3, M, kp, d["a_sm"], d["a_rows"], d["a_k"], batch,
+                                           d["a_bs"], 0b100, 0, stream), "split A into tf32 pairs")
+        cuda_ext.check(lib.eas_split3_tf32(pb + 4 * d["b0"], b3, N, kp, d["b_sk"], d["b_cols"], d["b_k"], batch,
+                                           d["b_bs"], 0b010, 1, stream), "split B into tf32 pairs")
+        rc = lib.eas_gemm_tf32(a3, b3, pc + 4 * d["c0"], M, N, 3 * kp, batch, 3 * kp, 3 * M * kp, 3 * kp, 3 * N * kp,
+                               d["c_sm"] if M > 1 else N, d["c_bs"], 256 if M > 128 else 128, stream)
+        if rc == cuda_ext.EAS_ERR_VALUE:
+            self.last_reason = cuda_ext.last_error()
+            return False
+        cuda_ext.check(rc, "gemm_tf32 (tcgen05, 3xTF32)")
+        rt.launch_count += 3
+        rt.native_launches += 1
+        self.last_mode = "3xtf32"
+        return True
+
+
+def fp32_mode() -> str:
+    """EAS_FP32_MATMUL: "exact" (default; the FFMA kernel repeats the kernel's fma chains bit for
+    bit) or "3xtf32" (tensor cores, within rtol 1e-4 of the exact product)."""
+    m = os.environ.get("EAS_FP32_MATMUL", "exact").strip().lower() or "exact"
+    if m not in ("exact", "3xtf32"):
+        raise ValueError(f"EAS_FP32_MATMUL must be 'exact' or '3xtf32', not {m!r}")
+    return m
 
 
 def match_tiled(ir: IRModule, lowered: Any) -> TiledGemmPlan | None:

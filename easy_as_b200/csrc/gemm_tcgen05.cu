@@ -127,14 +127,23 @@ __device__ __forceinline__ void tc_commit(uint64_t* bar) {
                : "memory");
 }
 
+template <bool TF>
 __device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                        uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
+  if constexpr (TF)
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+  else
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
 }
 
 // Shared-memory matrix descriptor (tcgen05), 128-byte swizzle:
@@ -146,10 +155,13 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo_bytes,
          ((uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
 }
 
-// Instruction descriptor, kind::f16: D = f32 (bits 4-5 = 1), A = B = f16 (0),
-// A K-major (bit 15 = 0), B major per b_mn (bit 16), N >> 3 at bits 17-22, M >> 4 at bits 24-28.
-__host__ __device__ constexpr uint32_t instr_desc(int n, bool b_mn_major) {
-  return (1u << 4) | ((b_mn_major ? 1u : 0u) << 16) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+// Instruction descriptor, kind::f16 / kind::tf32: D = f32 (bits 4-5 = 1), A and B formats at bits
+// 7-9 and 10-12 (f16 = 0, tf32 = 2), A K-major (bit 15 = 0), B major per b_mn (bit 16),
+// N >> 3 at bits 17-22, M >> 4 at bits 24-28.
+constexpr uint32_t kFmtTF32 = (2u << 7) | (2u << 10);
+__host__ __device__ constexpr uint32_t instr_desc(int n, bool b_mn_major, bool tf32 = false) {
+  return (1u << 4) | (tf32 ? kFmtTF32 : 0u) | ((b_mn_major ? 1u : 0u) << 16) | ((uint32_t)(n >> 3) << 17) |
+         ((uint32_t)(BM >> 4) << 24);
 }
 
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
@@ -197,11 +209,13 @@ struct Smem {
   static constexpr int kTotal = kBarOffset + (2 * STAGES + 4) * 8 + 16 + 1024;  // + alignment slack
 };
 
-template <int BN, int STAGES, bool B_MN, bool TMA_C>
+template <int BN, int STAGES, bool B_MN, bool TMA_C, bool TF = false>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_f16_tcgen05_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                             const __grid_constant__ CUtensorMap map_c, float* __restrict__ c, int M, int N, int K,
                             int batch, long long ldc, long long c_bstride, int* status) {
+  static_assert(!(TF && B_MN), "tf32 operands are K-major here");
+  constexpr int kBKe = TF ? 32 : BK;  // elements per 128-byte K row of a stage
   using L = Smem<BN, STAGES, B_MN>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -245,7 +259,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   sched.nt = (N + BN - 1) / BN;
   sched.tiles_per_batch = sched.mt * sched.nt;
   sched.total = sched.tiles_per_batch * batch;
-  const int kblocks = (K + BK - 1) / BK;
+  const int kblocks = (K + kBKe - 1) / kBKe;
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
@@ -260,12 +274,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* sa = smem + s * L::kStageBytes;
           uint8_t* sb = sa + L::kABytes;
           mbar_expect_tx(&full[s], L::kStageBytes);
-          tma_load_3d(sa, &map_a, &full[s], kb * BK, tc.m0, tc.b);
+          tma_load_3d(sa, &map_a, &full[s], kb * kBKe, tc.m0, tc.b);
           if (B_MN) {
 #pragma unroll
             for (int j = 0; j < BN / 64; ++j) tma_load_3d(sb + j * (BK * 128), &map_b, &full[s], n0 + 64 * j, kb * BK, tc.b);
           } else {
-            tma_load_3d(sb, &map_b, &full[s], kb * BK, n0, tc.b);
+            tma_load_3d(sb, &map_b, &full[s], kb * kBKe, n0, tc.b);
           }
           if (++s == STAGES) {
             s = 0;
@@ -277,7 +291,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      constexpr uint32_t idesc = instr_desc(BN, B_MN);
+      constexpr uint32_t idesc = instr_desc(BN, B_MN, TF);
       int s = 0;
       uint32_t ph = 0;
       int local = 0;
@@ -301,7 +315,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint64_t adesc = smem_desc(a_addr + kk * 32, 16, 1024);
             const uint64_t bdesc = B_MN ? smem_desc(b_addr + kk * 2048, BK * 128, 1024)
                                         : smem_desc(b_addr + kk * 32, 16, 1024);
-            tc_mma(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
+            tc_mma<TF>(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
           }
           tc_commit(&empty[s]);  // slot s is free once these MMAs have read it
           if (++s == STAGES) {
@@ -458,11 +472,13 @@ struct Smem2 {
   static constexpr int kTotal = kBarOffset + (2 * kStages2 + 4) * 8 + 16 + 1024;
 };
 
-template <int kStages2, bool B_MN, bool TMA_C>
+template <int kStages2, bool B_MN, bool TMA_C, bool TF = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_f16_tcgen05_2sm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                                 const __grid_constant__ CUtensorMap map_c, float* __restrict__ c, int M, int N, int K,
                                 int batch, long long ldc, long long c_bstride, int* status) {
+  static_assert(!(TF && B_MN), "tf32 operands are K-major here");
+  constexpr int kBKe = TF ? 32 : BK;  // elements per 128-byte K row of a stage
   using L = Smem2<kStages2, TMA_C>;
   constexpr int BN = 256;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -510,7 +526,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   sched.nt = (N + BN - 1) / BN;
   sched.tiles_per_batch = sched.mt * sched.nt;
   sched.total = sched.tiles_per_batch * batch;
-  const int kblocks = (K + BK - 1) / BK;
+  const int kblocks = (K + kBKe - 1) / kBKe;
   const int cid = blockIdx.x >> 1;
   const int ncl = gridDim.x >> 1;
 
@@ -528,12 +544,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           uint8_t* sb = sa + L::kABytes;
           const uint32_t fl = mapa_rank(smem_u32(&full[s]), 0);
           if (rank == 0) mbar_expect_tx(&full[s], 2 * L::kStageBytes);
-          tma_load_3d_pair(sa, &map_a, fl, kb * BK, m0, tc.b);
+          tma_load_3d_pair(sa, &map_a, fl, kb * kBKe, m0, tc.b);
           if (B_MN) {
             tma_load_3d_pair(sb, &map_b, fl, n0, kb * BK, tc.b);
             tma_load_3d_pair(sb + BK * 128, &map_b, fl, n0 + 64, kb * BK, tc.b);
           } else {
-            tma_load_3d_pair(sb, &map_b, fl, kb * BK, n0, tc.b);
+            tma_load_3d_pair(sb, &map_b, fl, kb * kBKe, n0, tc.b);
           }
           if (++s == kStages2) {
             s = 0;
@@ -544,7 +560,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     if (lane == 0 && rank == 0) {
-      constexpr uint32_t idesc = (1u << 4) | ((B_MN ? 1u : 0u) << 16) | ((uint32_t)(BN >> 3) << 17) |
+      constexpr uint32_t idesc = (1u << 4) | (TF ? kFmtTF32 : 0u) | ((B_MN ? 1u : 0u) << 16) | ((uint32_t)(BN >> 3) << 17) |
                                  ((uint32_t)(256 >> 4) << 24);
       int s = 0;
       uint32_t ph = 0;
@@ -569,12 +585,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             const uint64_t adesc = smem_desc(a_addr + kk * 32, 16, 1024);
             const uint64_t bdesc = B_MN ? smem_desc(b_addr + kk * 2048, BK * 128, 1024)
                                         : smem_desc(b_addr + kk * 32, 16, 1024);
-            asm volatile(
-                "{\n\t.reg .pred p;\n\t"
-                "setp.ne.b32 p, %4, 0;\n\t"
-                "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-                "l"(adesc), "l"(bdesc), "r"(idesc), "r"((kb | kk) != 0 ? 1u : 0u)
-                : "memory");
+            if constexpr (TF)
+              asm volatile(
+                  "{\n\t.reg .pred p;\n\t"
+                  "setp.ne.b32 p, %4, 0;\n\t"
+                  "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+                  "l"(adesc), "l"(bdesc), "r"(idesc), "r"((kb | kk) != 0 ? 1u : 0u)
+                  : "memory");
+            else
+              asm volatile(
+                  "{\n\t.reg .pred p;\n\t"
+                  "setp.ne.b32 p, %4, 0;\n\t"
+                  "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+                  "l"(adesc), "l"(bdesc), "r"(idesc), "r"((kb | kk) != 0 ? 1u : 0u)
+                  : "memory");
           }
           asm volatile(
               "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
@@ -688,11 +712,11 @@ int encode_map(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uin
   return eas_drv_check(r, "cuTensorMapEncodeTiled", EAS_ERR_VALUE);
 }
 
-template <int BN, int STAGES, bool B_MN, bool TMA_C>
+template <int BN, int STAGES, bool B_MN, bool TMA_C, bool TF = false>
 int launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, float* c, int M, int N, int K,
                    int batch, long long ldc, long long cbs, int* status, cudaStream_t stream, int num_sms) {
   using L = Smem<BN, STAGES, B_MN>;
-  auto kern = gemm_f16_tcgen05_kernel<BN, STAGES, B_MN, TMA_C>;
+  auto kern = gemm_f16_tcgen05_kernel<BN, STAGES, B_MN, TMA_C, TF>;
   int rc = eas_cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal),
                           "gemm: set smem attribute", EAS_ERR_LAUNCH);
   if (rc) return rc;
@@ -702,11 +726,11 @@ int launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorM
   return eas_cuda_check(cudaGetLastError(), "gemm: launch", EAS_ERR_LAUNCH);
 }
 
-template <int STAGES, bool B_MN, bool TMA_C>
+template <int STAGES, bool B_MN, bool TMA_C, bool TF = false>
 int launch_2sm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, float* c, int M, int N, int K,
                int batch, long long ldc, long long cbs, int* status, cudaStream_t stream, int num_sms) {
   using L = Smem2<STAGES, TMA_C>;
-  auto kern = gemm_f16_tcgen05_2sm_kernel<STAGES, B_MN, TMA_C>;
+  auto kern = gemm_f16_tcgen05_2sm_kernel<STAGES, B_MN, TMA_C, TF>;
   int rc = eas_cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal),
                           "gemm(2sm): set smem attribute", EAS_ERR_LAUNCH);
   if (rc) return rc;
@@ -781,39 +805,49 @@ extern "C" int eas_wait_selftest(long long budget_cycles, void* stream) {
   return eas_cuda_check(cudaGetLastError(), "wait_selftest launch", EAS_ERR_LAUNCH);
 }
 
-extern "C" int eas_gemm_f16(const void* a, const void* b, float* c, uint32_t M, uint32_t N, uint32_t K,
-                            uint32_t batch, uint64_t lda, uint64_t a_bstride, uint64_t ldb, uint64_t b_bstride,
-                            int b_kmajor, uint64_t ldc, uint64_t c_bstride, int block_n, void* stream) {
+namespace {
+
+// Host side shared by the f16 and tf32 entries: TMA maps over 2- or 4-byte operands with 128-byte
+// K rows (64 f16 or 32 tf32 elements), then the 1-SM or CTA-pair kernel.
+template <bool TF>
+int gemm_entry(const char* who, const void* a, const void* b, float* c, uint32_t M, uint32_t N, uint32_t K,
+               uint32_t batch, uint64_t lda, uint64_t a_bstride, uint64_t ldb, uint64_t b_bstride, int b_kmajor,
+               uint64_t ldc, uint64_t c_bstride, int block_n, void* stream) {
+  constexpr uint64_t kElem = TF ? 4 : 2;
+  constexpr uint32_t kBoxK = TF ? 32 : BK;
+  const CUtensorMapDataType dt = TF ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   int rc = eas_driver_init();
   if (rc) return rc;
-  if (!a || !b || !c) return eas_fail(EAS_ERR_VALUE, "eas_gemm_f16: null operand");
+  if (!a || !b || !c) return eas_fail(EAS_ERR_VALUE, "%s: null operand", who);
   if (M == 0 || N == 0 || batch == 0) return EAS_OK;
-  if (K == 0) return eas_fail(EAS_ERR_VALUE, "eas_gemm_f16: K == 0 (nothing to accumulate)");
-  if (block_n != 128 && block_n != 256) return eas_fail(EAS_ERR_VALUE, "eas_gemm_f16: block_n must be 128 or 256");
+  if (K == 0) return eas_fail(EAS_ERR_VALUE, "%s: K == 0 (nothing to accumulate)", who);
+  if (block_n != 128 && block_n != 256) return eas_fail(EAS_ERR_VALUE, "%s: block_n must be 128 or 256", who);
   if (M > 0x7fffffffu || N > 0x7fffffffu || K > 0x7fffffffu)
-    return eas_fail(EAS_ERR_VALUE, "eas_gemm_f16: dimension exceeds 2^31-1");
+    return eas_fail(EAS_ERR_VALUE, "%s: dimension exceeds 2^31-1", who);
+  if (TF && !b_kmajor) return eas_fail(EAS_ERR_VALUE, "%s: B must be K-major", who);
   // TMA rules: 16-byte aligned bases, 16-byte multiple strides
   if ((reinterpret_cast<uintptr_t>(a) & 15) || (reinterpret_cast<uintptr_t>(b) & 15))
-    return eas_fail(EAS_ERR_VALUE, "eas_gemm_f16: A/B base must be 16-byte aligned");
-  if ((lda * 2) % 16 || (ldb * 2) % 16 || (batch > 1 && ((a_bstride * 2) % 16 || (b_bstride * 2) % 16)))
-    return eas_fail(EAS_ERR_VALUE, "eas_gemm_f16: A/B strides must be multiples of 8 elements");
+    return eas_fail(EAS_ERR_VALUE, "%s: A/B base must be 16-byte aligned", who);
+  if ((lda * kElem) % 16 || (ldb * kElem) % 16 ||
+      (batch > 1 && ((a_bstride * kElem) % 16 || (b_bstride * kElem) % 16)))
+    return eas_fail(EAS_ERR_VALUE, "%s: A/B strides must be multiples of 16 bytes", who);
   int dev = 0;
   cudaGetDevice(&dev);
   int* status = eas_native_status_dev(dev);
   int num_sms = 148;
   cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev);
 
-  const uint64_t ab = batch > 1 ? a_bstride * 2 : (uint64_t)M * lda * 2;
-  const uint64_t bb = batch > 1 ? b_bstride * 2 : (uint64_t)(b_kmajor ? N : K) * ldb * 2;
+  const uint64_t ab = batch > 1 ? a_bstride * kElem : (uint64_t)M * lda * kElem;
+  const uint64_t bb = batch > 1 ? b_bstride * kElem : (uint64_t)(b_kmajor ? N : K) * ldb * kElem;
   CUtensorMap ma, mb;
-  rc = encode_map(&ma, a, K, M, batch, lda * 2, ab ? ab : 16, BK, BM);
+  rc = encode_map(&ma, a, K, M, batch, lda * kElem, ab ? ab : 16, kBoxK, BM, dt);
   if (rc) return rc;
   const bool b_mn = !b_kmajor;
   const bool pair = use_2sm(block_n, M);
   if (b_mn)
-    rc = encode_map(&mb, b, N, K, batch, ldb * 2, bb ? bb : 16, 64, BK);
+    rc = encode_map(&mb, b, N, K, batch, ldb * kElem, bb ? bb : 16, 64, kBoxK, dt);
   else
-    rc = encode_map(&mb, b, K, N, batch, ldb * 2, bb ? bb : 16, BK, pair ? 128u : (uint32_t)block_n);
+    rc = encode_map(&mb, b, K, N, batch, ldb * kElem, bb ? bb : 16, kBoxK, pair ? 128u : (uint32_t)block_n, dt);
   if (rc) return rc;
   // C through TMA stores when its rows/batches are 16-byte strided and the base is aligned
   CUtensorMap mc;
@@ -836,16 +870,42 @@ extern "C" int eas_gemm_f16(const void* a, const void* b, float* c, uint32_t M, 
                                                          num_sms)                                                \
                  : launch_variant<BN_, ST_, false, false>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s,    \
                                                           num_sms)))
-  if (pair) {
-    if (!tma_c)  // C not TMA-storable: direct stores, and the smem freed by the staging boxes buys a 7th stage
-      return b_mn ? launch_2sm<7, true, false>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s, num_sms)
-                  : launch_2sm<7, false, false>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s, num_sms);
-    return b_mn ? launch_2sm<6, true, true>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s, num_sms)
-                : launch_2sm<6, false, true>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s, num_sms);
+  if constexpr (TF) {  // K-major operands only
+    if (pair)
+      return tma_c ? launch_2sm<6, false, true, true>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s, num_sms)
+                   : launch_2sm<7, false, false, true>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s, num_sms);
+    return tma_c ? launch_variant<128, 6, false, true, true>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s,
+                                                             num_sms)
+                 : launch_variant<128, 6, false, false, true>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s,
+                                                              num_sms);
+  } else {
+    if (pair) {
+      if (!tma_c)  // C not TMA-storable: direct stores, and the smem freed by the staging boxes buys a 7th stage
+        return b_mn ? launch_2sm<7, true, false>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s, num_sms)
+                    : launch_2sm<7, false, false>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s, num_sms);
+      return b_mn ? launch_2sm<6, true, true>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s, num_sms)
+                  : launch_2sm<6, false, true>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s, num_sms);
+    }
+    if (block_n == 256) return EAS_GEMM_VARIANT(256, 4);
+    return EAS_GEMM_VARIANT(128, 6);
   }
-  if (block_n == 256) return EAS_GEMM_VARIANT(256, 4);
-  return EAS_GEMM_VARIANT(128, 6);
 #undef EAS_GEMM_VARIANT
+}
+
+}  // namespace
+
+extern "C" int eas_gemm_f16(const void* a, const void* b, float* c, uint32_t M, uint32_t N, uint32_t K,
+                            uint32_t batch, uint64_t lda, uint64_t a_bstride, uint64_t ldb, uint64_t b_bstride,
+                            int b_kmajor, uint64_t ldc, uint64_t c_bstride, int block_n, void* stream) {
+  return gemm_entry<false>("eas_gemm_f16", a, b, c, M, N, K, batch, lda, a_bstride, ldb, b_bstride, b_kmajor, ldc,
+                           c_bstride, block_n, stream);
+}
+
+extern "C" int eas_gemm_tf32(const float* a, const float* b, float* c, uint32_t M, uint32_t N, uint32_t K,
+                             uint32_t batch, uint64_t lda, uint64_t a_bstride, uint64_t ldb, uint64_t b_bstride,
+                             uint64_t ldc, uint64_t c_bstride, int block_n, void* stream) {
+  return gemm_entry<true>("eas_gemm_tf32", a, b, c, M, N, K, batch, lda, a_bstride, ldb, b_bstride, 1, ldc,
+                          c_bstride, block_n, stream);
 }
 
 // ---------------------------------------------------------------------------

@@ -191,6 +191,28 @@ int eas_cast_f32_f16_2d(const float* src, void* dst, uint32_t rows, uint32_t col
  * Nothing faults or hangs; the context stays usable.  Asynchronous. */
 int eas_wait_selftest(long long budget_cycles, void* stream);
 
+/* Strided batched GEMM on tcgen05 with TF32 operands (kind::tf32, f32
+ * accumulate): C[b][m][n] = sum_k A[b][m][k] * B[b][n][k] with A at
+ * a + b*a_bstride + m*lda + k and B K-major at b + b*b_bstride + n*ldb + k
+ * (f32 storage; the tensor core reads the TF32 part, the 19 high bits).  Used
+ * by the opt-in 3xTF32 mode of proven fp32 matmuls (north_star: 3xTF32 where
+ * it meets rtol 1e-4) over operands from eas_split3_tf32.  Alignment and
+ * status as eas_gemm_f16 (strides multiples of 4 elements). */
+int eas_gemm_tf32(const float* a, const float* b, float* c, uint32_t M, uint32_t N, uint32_t K, uint32_t batch,
+                  uint64_t lda, uint64_t a_bstride, uint64_t ldb, uint64_t b_bstride, uint64_t ldc,
+                  uint64_t c_bstride, int block_n, void* stream);
+
+/* 3xTF32 operand staging: each value x splits into hi = tf32(x) and
+ * lo = tf32(x - hi) (round to nearest, ties away; x - hi is exact).  Row r of
+ * the source (transpose = 0: src[r][k], row pitch ld_src) or column r
+ * (transpose = 1: src[k][r]) becomes dst row r of 3 segments of kp elements;
+ * segment s holds lo if bit s of lo_mask is set, else hi; zero outside
+ * r < rows_valid, k < k_valid.  dst is dense: [batch][rows][3*kp].  With
+ * A' = split(A, mask 0b100) and B'^T = split(B, transpose, mask 0b010),
+ * A' . B' = A_hi.B_hi + A_hi.B_lo + A_lo.B_hi. */
+int eas_split3_tf32(const float* src, float* dst, uint32_t rows, uint32_t kp, uint64_t ld_src, uint32_t rows_valid,
+                    uint32_t k_valid, uint32_t batch, uint64_t bs_src, int lo_mask, int transpose, void* stream);
+
 /* Read and clear the status word of native kernels on `dev` (0 = ok,
  * EAS_ERR_TIMEOUT = a bounded wait expired).  Valid after the stream synced. */
 int eas_gemm_status(int dev, int* code);

@@ -237,3 +237,15 @@ def test_batched_variant_maps_the_z_axis_to_the_batch():
     d = ck.plan.native.analyse({"M": M, "N": N}, (5, 3, 5), 0xFFFFFFFF)
     assert d is not None, ck.plan.native.last_reason
     assert (d["batch"], d["a_bs"], d["b_bs"], d["c_bs"]) == (5, M * K, K * N, M * N)
+
+
+def test_fp32_matmul_mode_knob(monkeypatch):
+    from easy_as_b200.codegen.tiled import fp32_mode
+
+    monkeypatch.delenv("EAS_FP32_MATMUL", raising=False)
+    assert fp32_mode() == "exact"
+    monkeypatch.setenv("EAS_FP32_MATMUL", "3xTF32")
+    assert fp32_mode() == "3xtf32"
+    monkeypatch.setenv("EAS_FP32_MATMUL", "tf32")
+    with pytest.raises(ValueError):
+        fp32_mode()
