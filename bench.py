@@ -323,7 +323,7 @@ def _c3_3xtf32(rt, ck, case, args_, grid, a, b, c, flush, steps, flops) -> dict:
     ms = total / steps
     return {"tflops": round(flops / (ms * 1e-3) / 1e12, 2), "ms_per_step": round(ms, 4),
             "rel_err_vs_f64": err, "tolerance": 1e-4,
-            "kernels": "2x eas_split3_tf32 + tcgen05 kind::tf32 GEMM over K' = 3K (opt-in; default stays exact)"}
+            "kernels": "2x eas_split_tf32 ([hi | lo] rows) + tcgen05 kind::tf32 GEMM over 3 K/32 k-blocks (opt-in; default stays exact)"}
 
 
 def run_tiled(args, rt) -> dict:

@@ -861,33 +861,34 @@ class TiledGemmPlan(ProvenGemmPlan):
 
     def _launch_3xtf32(self, rt: Any, d: dict[str, Any], pa: int, pb: int, pc: int, device: int,
                        stream: int) -> bool:
-        """Opt-in 3xTF32 mode: C = A_hi.B_hi + A_hi.B_lo + A_lo.B_hi as ONE tcgen05 kind::tf32 GEMM
-        over K' = 3 kp (kp = K rounded up to 4, so every segment starts on 16 bytes), with
-        A' = [A_hi | A_hi | A_lo] (rows of A) and B'^T = [B_hi | B_lo | B_hi] (columns of B), both
-        written by eas_split3_tf32 with the proof's zero-fill bounds.  Not bit-identical to the
-        kernel's own fma chains: relative error ~1e-6 of |A||B| (the dropped A_lo.B_lo term is
-        2^-22 of a product), inside the fp32 matmul tolerance rtol 1e-4.  False (FFMA runs instead)
-        when the operands cannot be staged or the GEMM declines the shape."""
+        """Opt-in 3xTF32 mode: C = A_hi.B_hi + A_hi.B_lo + A_lo.B_hi as ONE tcgen05 kind::tf32 GEMM.
+        eas_split_tf32 writes each row of A and each column of B (K-major) as [hi | lo] segments of
+        kp = K rounded up to 32 (zero outside the proof's bounds); the GEMM's producer maps its
+        3 kp/32 k-blocks onto the segment pairs (hi, hi), (hi, lo), (lo, hi).  Not bit-identical to
+        the kernel's own fma chains: the dropped A_lo.B_lo term is 2^-22 of a product and the tensor
+        core rounds its accumulator once per 8-deep MMA, so the error grows with K (~3e-5 normwise
+        at K = 2048), inside the fp32 matmul tolerance rtol 1e-4.  False (FFMA runs instead) when
+        the operands cannot be staged or the GEMM declines the shape."""
         from ..runtime import cuda_ext
 
         M, N, K, batch = d["M"], d["N"], d["K"], d["batch"]
-        kp = -(-K // 4) * 4
-        sa = rt.scratch(device, stream, "tf32_a3", 4 * batch * M * 3 * kp)
-        sb = rt.scratch(device, stream, "tf32_b3", 4 * batch * N * 3 * kp)
+        kp = -(-K // 32) * 32
+        sa = rt.scratch(device, stream, "tf32_a2", 4 * batch * M * 2 * kp)
+        sb = rt.scratch(device, stream, "tf32_b2", 4 * batch * N * 2 * kp)
         if sa is None or sb is None or K == 0:
             return False
-        (a3, _keep_a), (b3, _keep_b) = sa, sb
+        (a2, _keep_a), (b2, _keep_b) = sa, sb
         lib = rt.lib()
-        cuda_ext.check(lib.eas_split3_tf32(pa + 4 * d["a0"], a3, M, kp, d["a_sm"], d["a_rows"], d["a_k"], batch,
-                                           d["a_bs"], 0b100, 0, stream), "split A into tf32 pairs")
-        cuda_ext.check(lib.eas_split3_tf32(pb + 4 * d["b0"], b3, N, kp, d["b_sk"], d["b_cols"], d["b_k"], batch,
-                                           d["b_bs"], 0b010, 1, stream), "split B into tf32 pairs")
-        rc = lib.eas_gemm_tf32(a3, b3, pc + 4 * d["c0"], M, N, 3 * kp, batch, 3 * kp, 3 * M * kp, 3 * kp, 3 * N * kp,
-                               d["c_sm"] if M > 1 else N, d["c_bs"], 256 if M > 128 else 128, stream)
+        cuda_ext.check(lib.eas_split_tf32(pa + 4 * d["a0"], a2, M, kp, d["a_sm"], d["a_rows"], d["a_k"], batch,
+                                          d["a_bs"], 0, stream), "split A into tf32 pairs")
+        cuda_ext.check(lib.eas_split_tf32(pb + 4 * d["b0"], b2, N, kp, d["b_sk"], d["b_cols"], d["b_k"], batch,
+                                          d["b_bs"], 1, stream), "split B into tf32 pairs")
+        rc = lib.eas_gemm_3xtf32(a2, b2, pc + 4 * d["c0"], M, N, kp, batch, 2 * kp, 2 * M * kp, 2 * kp, 2 * N * kp,
+                                 d["c_sm"] if M > 1 else N, d["c_bs"], 256 if M > 128 else 128, stream)
         if rc == cuda_ext.EAS_ERR_VALUE:
             self.last_reason = cuda_ext.last_error()
             return False
-        cuda_ext.check(rc, "gemm_tf32 (tcgen05, 3xTF32)")
+        cuda_ext.check(rc, "gemm_3xtf32 (tcgen05)")
         rt.launch_count += 3
         rt.native_launches += 1
         self.last_mode = "3xtf32"

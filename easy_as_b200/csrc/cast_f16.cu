@@ -56,85 +56,98 @@ __global__ void cast_f32_f16_kernel(const float* __restrict__ src, uint16_t* __r
 
 namespace {
 
-// x = hi + lo + (rest): hi = tf32(x), lo = tf32(x - hi) (x - hi is exact in f32); both have their
-// 13 low mantissa bits clear, so kind::tf32 reads them exactly.
+// x = hi + lo + (rest): hi = tf32(x), lo = tf32(x - hi) (x - hi is exact in f32), both rounded to
+// nearest with ties away from zero; their 13 low mantissa bits are clear, so kind::tf32 reads
+// them exactly.
 __device__ __forceinline__ float tf32_rna(float x) {
   uint32_t r;
   asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
   return __uint_as_float(r);
 }
 
-__device__ __forceinline__ float tf32_part(float x, bool lo) {
-  const float hi = tf32_rna(x);
-  return lo ? tf32_rna(x - hi) : hi;
-}
-
-// Rows of src ([rows][k], row pitch ld_src) into dst rows of 3 segments of kp elements:
-// segment s holds tf32_part(src, bit s of lo_mask), zero outside r < rows_valid, k < k_valid.
-__global__ void split3_rows_kernel(const float* __restrict__ src, float* __restrict__ dst, uint32_t rows,
-                                   uint32_t kp, uint64_t ld_src, uint32_t rows_valid, uint32_t k_valid,
-                                   uint32_t batch, uint64_t bs_src, int lo_mask) {
-  const uint64_t per = (uint64_t)rows * kp;
-  const uint64_t total = (uint64_t)batch * per;
-  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
-    const uint64_t b = i / per;
-    const uint64_t rk = i % per;
-    const uint32_t r = rk / kp, k = rk % kp;
-    const float x = (r < rows_valid && k < k_valid) ? src[b * bs_src + (uint64_t)r * ld_src + k] : 0.0f;
-    float* d = dst + b * 3 * per + (uint64_t)r * 3 * kp + k;
+// Rows of src ([rows][k], row pitch ld_src) into dst rows [hi | lo] of kp elements each (kp a
+// multiple of 4), zero outside r < rows_valid, k < k_valid.  Four k per thread, 16-byte stores.
+__global__ void split_rows_kernel(const float* __restrict__ src, float* __restrict__ dst, uint32_t rows, uint32_t kp,
+                                  uint64_t ld_src, uint32_t rows_valid, uint32_t k_valid, uint32_t batch,
+                                  uint64_t bs_src) {
+  const uint32_t k0 = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
+  if (k0 >= kp) return;
+  for (uint32_t b = blockIdx.z; b < batch; b += gridDim.z) {
+    for (uint32_t r = blockIdx.y; r < rows; r += gridDim.y) {
+      const float* s = src + b * bs_src + (uint64_t)r * ld_src;
+      float x[4];
 #pragma unroll
-    for (int seg = 0; seg < 3; ++seg) d[(uint64_t)seg * kp] = tf32_part(x, (lo_mask >> seg) & 1);
+      for (int j = 0; j < 4; ++j) x[j] = (r < rows_valid && k0 + j < k_valid) ? s[k0 + j] : 0.0f;
+      float4 hi, lo;
+      hi.x = tf32_rna(x[0]); lo.x = tf32_rna(x[0] - hi.x);
+      hi.y = tf32_rna(x[1]); lo.y = tf32_rna(x[1] - hi.y);
+      hi.z = tf32_rna(x[2]); lo.z = tf32_rna(x[2] - hi.z);
+      hi.w = tf32_rna(x[3]); lo.w = tf32_rna(x[3] - hi.w);
+      float* d = dst + ((uint64_t)b * rows + r) * 2 * kp + k0;
+      *reinterpret_cast<float4*>(d) = hi;
+      *reinterpret_cast<float4*>(d + kp) = lo;
+    }
   }
 }
 
-// Columns of src ([k][cols], row pitch ld_src) into dst rows (one per column) of 3 segments of kp
-// elements, through a 32 x 32 shared-memory transpose: dst[n][s*kp + k] = tf32_part(src[k][n], ...).
-__global__ void split3_cols_kernel(const float* __restrict__ src, float* __restrict__ dst, uint32_t cols,
-                                   uint32_t kp, uint64_t ld_src, uint32_t cols_valid, uint32_t k_valid,
-                                   uint64_t bs_src, int lo_mask) {
-  __shared__ float tile[32][33];
-  const uint32_t k0 = blockIdx.x * 32, n0 = blockIdx.y * 32, b = blockIdx.z;
-  const float* s = src + (uint64_t)b * bs_src;
-  float* d = dst + (uint64_t)b * 3 * (uint64_t)cols * kp;
-  for (int j = threadIdx.y; j < 32; j += blockDim.y) {
-    const uint32_t k = k0 + j, n = n0 + threadIdx.x;
-    tile[j][threadIdx.x] = (k < k_valid && n < cols_valid) ? s[(uint64_t)k * ld_src + n] : 0.0f;
-  }
-  __syncthreads();
-  for (int j = threadIdx.y; j < 32; j += blockDim.y) {
-    const uint32_t n = n0 + j, k = k0 + threadIdx.x;
-    if (n < cols && k < kp) {
-      const float x = tile[threadIdx.x][j];
+// Columns of src ([k][cols], row pitch ld_src) into dst rows (one per column) [hi | lo] of kp
+// elements each, through a 64 (k) x 32 (column) shared-memory tile: coalesced 128-byte loads
+// along columns, 8-byte stores along k.
+__global__ void split_cols_kernel(const float* __restrict__ src, float* __restrict__ dst, uint32_t cols, uint32_t kp,
+                                  uint64_t ld_src, uint32_t cols_valid, uint32_t k_valid, uint32_t batch,
+                                  uint64_t bs_src) {
+  __shared__ float tile[64][33];
+  const uint32_t k0 = blockIdx.x * 64;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 8 warps
+  for (uint32_t b = blockIdx.z; b < batch; b += gridDim.z) {
+    for (uint32_t n0 = blockIdx.y * 32; n0 < cols; n0 += gridDim.y * 32) {
+      const float* s = src + b * bs_src;
 #pragma unroll
-      for (int seg = 0; seg < 3; ++seg) d[(uint64_t)n * 3 * kp + (uint64_t)seg * kp + k] = tf32_part(x, (lo_mask >> seg) & 1);
+      for (int j = 0; j < 8; ++j) {
+        const uint32_t k = k0 + ty + 8 * j, n = n0 + tx;
+        tile[ty + 8 * j][tx] = (k < k_valid && n < cols_valid) ? s[(uint64_t)k * ld_src + n] : 0.0f;
+      }
+      __syncthreads();
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t nl = ty + 8 * j, n = n0 + nl, k = k0 + 2 * tx;
+        if (n < cols && k < kp) {  // kp is a multiple of 4: k and k + 1 are both inside
+          const float x0 = tile[2 * tx][nl], x1 = tile[2 * tx + 1][nl];
+          float2 hi, lo;
+          hi.x = tf32_rna(x0); lo.x = tf32_rna(x0 - hi.x);
+          hi.y = tf32_rna(x1); lo.y = tf32_rna(x1 - hi.y);
+          float* d = dst + ((uint64_t)b * cols + n) * 2 * kp + k;
+          *reinterpret_cast<float2*>(d) = hi;
+          *reinterpret_cast<float2*>(d + kp) = lo;
+        }
+      }
+      __syncthreads();
     }
   }
 }
 
 }  // namespace
 
-extern "C" int eas_split3_tf32(const float* src, float* dst, uint32_t rows, uint32_t kp, uint64_t ld_src,
-                               uint32_t rows_valid, uint32_t k_valid, uint32_t batch, uint64_t bs_src, int lo_mask,
-                               int transpose, void* stream) {
-  if (!src || !dst) return eas_fail(EAS_ERR_VALUE, "eas_split3_tf32: null pointer");
+extern "C" int eas_split_tf32(const float* src, float* dst, uint32_t rows, uint32_t kp, uint64_t ld_src,
+                              uint32_t rows_valid, uint32_t k_valid, uint32_t batch, uint64_t bs_src, int transpose,
+                              void* stream) {
+  if (!src || !dst) return eas_fail(EAS_ERR_VALUE, "eas_split_tf32: null pointer");
   if (rows == 0 || kp == 0 || batch == 0) return EAS_OK;
-  if (batch > 65535) return eas_fail(EAS_ERR_VALUE, "eas_split3_tf32: batch exceeds 65535");
+  if (kp % 4 || (reinterpret_cast<uintptr_t>(dst) & 15))
+    return eas_fail(EAS_ERR_VALUE, "eas_split_tf32: kp must be a multiple of 4 and dst 16-byte aligned");
+  if (rows_valid > rows || k_valid > kp) return eas_fail(EAS_ERR_VALUE, "eas_split_tf32: valid extents exceed rows/kp");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const unsigned gz = batch < 65535u ? batch : 65535u;
   if (transpose) {
-    dim3 grid((kp + 31) / 32, (rows + 31) / 32, batch);
-    if (grid.y > 65535) return eas_fail(EAS_ERR_VALUE, "eas_split3_tf32: too many columns");
-    split3_cols_kernel<<<grid, dim3(32, 8, 1), 0, s>>>(src, dst, rows, kp, ld_src, rows_valid, k_valid, bs_src,
-                                                       lo_mask);
+    const unsigned gy = (rows + 31) / 32 < 65535u ? (rows + 31) / 32 : 65535u;
+    split_cols_kernel<<<dim3((kp + 63) / 64, gy, gz), 256, 0, s>>>(src, dst, rows, kp, ld_src, rows_valid, k_valid,
+                                                                   batch, bs_src);
   } else {
-    int dev = 0, sms = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const uint64_t total = (uint64_t)batch * rows * kp;
-    const uint64_t want = (total + 255) / 256;
-    const unsigned grid = (unsigned)(want < (uint64_t)sms * 16 ? want : (uint64_t)sms * 16);
-    split3_rows_kernel<<<grid, 256, 0, s>>>(src, dst, rows, kp, ld_src, rows_valid, k_valid, batch, bs_src, lo_mask);
+    const unsigned gy = rows < 65535u ? rows : 65535u;
+    split_rows_kernel<<<dim3((kp / 4 + 255) / 256, gy, gz), 256, 0, s>>>(src, dst, rows, kp, ld_src, rows_valid,
+                                                                         k_valid, batch, bs_src);
   }
-  return eas_cuda_check(cudaGetLastError(), "split3_tf32 launch", EAS_ERR_LAUNCH);
+  return eas_cuda_check(cudaGetLastError(), "split_tf32 launch", EAS_ERR_LAUNCH);
 }
 
 extern "C" int eas_cast_f32_f16_2d(const float* src, void* dst, uint32_t rows, uint32_t cols_pad, uint64_t ld_src,

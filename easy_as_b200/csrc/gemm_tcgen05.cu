@@ -209,11 +209,19 @@ struct Smem {
   static constexpr int kTotal = kBarOffset + (2 * STAGES + 4) * 8 + 16 + 1024;  // + alignment slack
 };
 
+// 3xTF32 k-block map: A and B rows hold [hi | lo] segments of seg_kb k-blocks each; the GEMM runs
+// over 3 seg_kb k-blocks: (A_hi, B_hi), then (A_hi, B_lo), then (A_lo, B_hi).
+__device__ __forceinline__ void seg_coords(int kb, int seg_kb, int& ka, int& kbk) {
+  const int seg = kb / seg_kb, kin = kb - seg * seg_kb;
+  ka = ((seg == 2 ? seg_kb : 0) + kin) * 32;
+  kbk = ((seg == 1 ? seg_kb : 0) + kin) * 32;
+}
+
 template <int BN, int STAGES, bool B_MN, bool TMA_C, bool TF = false>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_f16_tcgen05_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                             const __grid_constant__ CUtensorMap map_c, float* __restrict__ c, int M, int N, int K,
-                            int batch, long long ldc, long long c_bstride, int* status) {
+                            int batch, long long ldc, long long c_bstride, int* status, int seg_kb) {
   static_assert(!(TF && B_MN), "tf32 operands are K-major here");
   constexpr int kBKe = TF ? 32 : BK;  // elements per 128-byte K row of a stage
   using L = Smem<BN, STAGES, B_MN>;
@@ -274,12 +282,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* sa = smem + s * L::kStageBytes;
           uint8_t* sb = sa + L::kABytes;
           mbar_expect_tx(&full[s], L::kStageBytes);
-          tma_load_3d(sa, &map_a, &full[s], kb * kBKe, tc.m0, tc.b);
+          int ka = kb * kBKe, kbk = ka;
+          if (TF && seg_kb) seg_coords(kb, seg_kb, ka, kbk);
+          tma_load_3d(sa, &map_a, &full[s], ka, tc.m0, tc.b);
           if (B_MN) {
 #pragma unroll
             for (int j = 0; j < BN / 64; ++j) tma_load_3d(sb + j * (BK * 128), &map_b, &full[s], n0 + 64 * j, kb * BK, tc.b);
           } else {
-            tma_load_3d(sb, &map_b, &full[s], kb * kBKe, n0, tc.b);
+            tma_load_3d(sb, &map_b, &full[s], kbk, n0, tc.b);
           }
           if (++s == STAGES) {
             s = 0;
@@ -476,7 +486,7 @@ template <int kStages2, bool B_MN, bool TMA_C, bool TF = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_f16_tcgen05_2sm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                                 const __grid_constant__ CUtensorMap map_c, float* __restrict__ c, int M, int N, int K,
-                                int batch, long long ldc, long long c_bstride, int* status) {
+                                int batch, long long ldc, long long c_bstride, int* status, int seg_kb) {
   static_assert(!(TF && B_MN), "tf32 operands are K-major here");
   constexpr int kBKe = TF ? 32 : BK;  // elements per 128-byte K row of a stage
   using L = Smem2<kStages2, TMA_C>;
@@ -544,12 +554,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           uint8_t* sb = sa + L::kABytes;
           const uint32_t fl = mapa_rank(smem_u32(&full[s]), 0);
           if (rank == 0) mbar_expect_tx(&full[s], 2 * L::kStageBytes);
-          tma_load_3d_pair(sa, &map_a, fl, kb * kBKe, m0, tc.b);
+          int ka = kb * kBKe, kbk = ka;
+          if (TF && seg_kb) seg_coords(kb, seg_kb, ka, kbk);
+          tma_load_3d_pair(sa, &map_a, fl, ka, m0, tc.b);
           if (B_MN) {
             tma_load_3d_pair(sb, &map_b, fl, n0, kb * BK, tc.b);
             tma_load_3d_pair(sb + BK * 128, &map_b, fl, n0 + 64, kb * BK, tc.b);
           } else {
-            tma_load_3d_pair(sb, &map_b, fl, kb * kBKe, n0, tc.b);
+            tma_load_3d_pair(sb, &map_b, fl, kbk, n0, tc.b);
           }
           if (++s == kStages2) {
             s = 0;
@@ -714,7 +726,7 @@ int encode_map(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uin
 
 template <int BN, int STAGES, bool B_MN, bool TMA_C, bool TF = false>
 int launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, float* c, int M, int N, int K,
-                   int batch, long long ldc, long long cbs, int* status, cudaStream_t stream, int num_sms) {
+                   int batch, long long ldc, long long cbs, int* status, cudaStream_t stream, int num_sms, int seg_kb = 0) {
   using L = Smem<BN, STAGES, B_MN>;
   auto kern = gemm_f16_tcgen05_kernel<BN, STAGES, B_MN, TMA_C, TF>;
   int rc = eas_cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal),
@@ -722,13 +734,13 @@ int launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorM
   if (rc) return rc;
   const long long tiles = (long long)((M + BM - 1) / BM) * ((N + BN - 1) / BN) * batch;
   const int grid = (int)(tiles < num_sms ? tiles : num_sms);
-  kern<<<grid, kThreads, L::kTotal, stream>>>(ma, mb, mc, c, M, N, K, batch, ldc, cbs, status);
+  kern<<<grid, kThreads, L::kTotal, stream>>>(ma, mb, mc, c, M, N, K, batch, ldc, cbs, status, seg_kb);
   return eas_cuda_check(cudaGetLastError(), "gemm: launch", EAS_ERR_LAUNCH);
 }
 
 template <int STAGES, bool B_MN, bool TMA_C, bool TF = false>
 int launch_2sm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, float* c, int M, int N, int K,
-               int batch, long long ldc, long long cbs, int* status, cudaStream_t stream, int num_sms) {
+               int batch, long long ldc, long long cbs, int* status, cudaStream_t stream, int num_sms, int seg_kb = 0) {
   using L = Smem2<STAGES, TMA_C>;
   auto kern = gemm_f16_tcgen05_2sm_kernel<STAGES, B_MN, TMA_C, TF>;
   int rc = eas_cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal),
@@ -755,7 +767,7 @@ int launch_2sm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& 
   }
   const long long pairs = resident_pairs[which][dev];
   const int grid = 2 * (int)(tiles < pairs ? tiles : pairs);
-  kern<<<grid, kThreads, L::kTotal, stream>>>(ma, mb, mc, c, M, N, K, batch, ldc, cbs, status);
+  kern<<<grid, kThreads, L::kTotal, stream>>>(ma, mb, mc, c, M, N, K, batch, ldc, cbs, status, seg_kb);
   return eas_cuda_check(cudaGetLastError(), "gemm(2sm): launch", EAS_ERR_LAUNCH);
 }
 
@@ -812,7 +824,7 @@ namespace {
 template <bool TF>
 int gemm_entry(const char* who, const void* a, const void* b, float* c, uint32_t M, uint32_t N, uint32_t K,
                uint32_t batch, uint64_t lda, uint64_t a_bstride, uint64_t ldb, uint64_t b_bstride, int b_kmajor,
-               uint64_t ldc, uint64_t c_bstride, int block_n, void* stream) {
+               uint64_t ldc, uint64_t c_bstride, int block_n, void* stream, bool split = false) {
   constexpr uint64_t kElem = TF ? 4 : 2;
   constexpr uint32_t kBoxK = TF ? 32 : BK;
   const CUtensorMapDataType dt = TF ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -825,6 +837,13 @@ int gemm_entry(const char* who, const void* a, const void* b, float* c, uint32_t
   if (M > 0x7fffffffu || N > 0x7fffffffu || K > 0x7fffffffu)
     return eas_fail(EAS_ERR_VALUE, "%s: dimension exceeds 2^31-1", who);
   if (TF && !b_kmajor) return eas_fail(EAS_ERR_VALUE, "%s: B must be K-major", who);
+  // split (3xTF32): A and B rows are [hi | lo] of K elements each (K a multiple of 32); the kernel
+  // runs 3 K/32 k-blocks over them
+  if (split && (K % 32 || 3ull * K > 0x7fffffffull))
+    return eas_fail(EAS_ERR_VALUE, "%s: segment length must be a multiple of 32 below 2^31/3", who);
+  const uint64_t k_map = split ? 2ull * K : K;
+  const int seg_kb = split ? (int)(K / 32) : 0;
+  const int k_run = split ? (int)(3 * K) : (int)K;
   // TMA rules: 16-byte aligned bases, 16-byte multiple strides
   if ((reinterpret_cast<uintptr_t>(a) & 15) || (reinterpret_cast<uintptr_t>(b) & 15))
     return eas_fail(EAS_ERR_VALUE, "%s: A/B base must be 16-byte aligned", who);
@@ -840,14 +859,14 @@ int gemm_entry(const char* who, const void* a, const void* b, float* c, uint32_t
   const uint64_t ab = batch > 1 ? a_bstride * kElem : (uint64_t)M * lda * kElem;
   const uint64_t bb = batch > 1 ? b_bstride * kElem : (uint64_t)(b_kmajor ? N : K) * ldb * kElem;
   CUtensorMap ma, mb;
-  rc = encode_map(&ma, a, K, M, batch, lda * kElem, ab ? ab : 16, kBoxK, BM, dt);
+  rc = encode_map(&ma, a, k_map, M, batch, lda * kElem, ab ? ab : 16, kBoxK, BM, dt);
   if (rc) return rc;
   const bool b_mn = !b_kmajor;
   const bool pair = use_2sm(block_n, M);
   if (b_mn)
     rc = encode_map(&mb, b, N, K, batch, ldb * kElem, bb ? bb : 16, 64, kBoxK, dt);
   else
-    rc = encode_map(&mb, b, K, N, batch, ldb * kElem, bb ? bb : 16, kBoxK, pair ? 128u : (uint32_t)block_n, dt);
+    rc = encode_map(&mb, b, k_map, N, batch, ldb * kElem, bb ? bb : 16, kBoxK, pair ? 128u : (uint32_t)block_n, dt);
   if (rc) return rc;
   // C through TMA stores when its rows/batches are 16-byte strided and the base is aligned
   CUtensorMap mc;
@@ -872,12 +891,14 @@ int gemm_entry(const char* who, const void* a, const void* b, float* c, uint32_t
                                                           num_sms)))
   if constexpr (TF) {  // K-major operands only
     if (pair)
-      return tma_c ? launch_2sm<6, false, true, true>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s, num_sms)
-                   : launch_2sm<7, false, false, true>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s, num_sms);
-    return tma_c ? launch_variant<128, 6, false, true, true>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s,
-                                                             num_sms)
-                 : launch_variant<128, 6, false, false, true>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s,
-                                                              num_sms);
+      return tma_c ? launch_2sm<6, false, true, true>(ma, mb, mc, c, M, N, k_run, batch, ldc_l, cbs, status, s, num_sms,
+                                                      seg_kb)
+                   : launch_2sm<7, false, false, true>(ma, mb, mc, c, M, N, k_run, batch, ldc_l, cbs, status, s,
+                                                       num_sms, seg_kb);
+    return tma_c ? launch_variant<128, 6, false, true, true>(ma, mb, mc, c, M, N, k_run, batch, ldc_l, cbs, status, s,
+                                                             num_sms, seg_kb)
+                 : launch_variant<128, 6, false, false, true>(ma, mb, mc, c, M, N, k_run, batch, ldc_l, cbs, status, s,
+                                                              num_sms, seg_kb);
   } else {
     if (pair) {
       if (!tma_c)  // C not TMA-storable: direct stores, and the smem freed by the staging boxes buys a 7th stage
@@ -906,6 +927,13 @@ extern "C" int eas_gemm_tf32(const float* a, const float* b, float* c, uint32_t 
                              uint64_t ldc, uint64_t c_bstride, int block_n, void* stream) {
   return gemm_entry<true>("eas_gemm_tf32", a, b, c, M, N, K, batch, lda, a_bstride, ldb, b_bstride, 1, ldc,
                           c_bstride, block_n, stream);
+}
+
+extern "C" int eas_gemm_3xtf32(const float* a2, const float* b2, float* c, uint32_t M, uint32_t N, uint32_t K,
+                               uint32_t batch, uint64_t lda, uint64_t a_bstride, uint64_t ldb, uint64_t b_bstride,
+                               uint64_t ldc, uint64_t c_bstride, int block_n, void* stream) {
+  return gemm_entry<true>("eas_gemm_3xtf32", a2, b2, c, M, N, K, batch, lda, a_bstride, ldb, b_bstride, 1, ldc,
+                          c_bstride, block_n, stream, true);
 }
 
 // ---------------------------------------------------------------------------

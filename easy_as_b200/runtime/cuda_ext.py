@@ -76,8 +76,9 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "eas_gemm_status": (_int, [_int, _PINT]),
     "eas_gemm_tf32": (_int, [_vp, _vp, _vp, _u32, _u32, _u32, _u32, ctypes.c_uint64, ctypes.c_uint64,
                              ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64, _int, _vp]),
-    "eas_split3_tf32": (_int, [_vp, _vp, _u32, _u32, ctypes.c_uint64, _u32, _u32, _u32, ctypes.c_uint64, _int, _int,
-                               _vp]),
+    "eas_gemm_3xtf32": (_int, [_vp, _vp, _vp, _u32, _u32, _u32, _u32, ctypes.c_uint64, ctypes.c_uint64,
+                               ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64, _int, _vp]),
+    "eas_split_tf32": (_int, [_vp, _vp, _u32, _u32, ctypes.c_uint64, _u32, _u32, _u32, ctypes.c_uint64, _int, _vp]),
     "eas_wait_selftest": (_int, [ctypes.c_longlong, _vp]),
     "eas_cast_f32_f16_2d": (_int, [_vp, _vp, _u32, _u32, ctypes.c_uint64, ctypes.c_uint64, _u32, _u32, _u32,
                                    ctypes.c_uint64, ctypes.c_uint64, _vp]),

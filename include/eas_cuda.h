@@ -202,16 +202,22 @@ int eas_gemm_tf32(const float* a, const float* b, float* c, uint32_t M, uint32_t
                   uint64_t lda, uint64_t a_bstride, uint64_t ldb, uint64_t b_bstride, uint64_t ldc,
                   uint64_t c_bstride, int block_n, void* stream);
 
+/* 3xTF32 on tcgen05: the same kernel as eas_gemm_tf32 over operands from
+ * eas_split_tf32, whose rows are [hi | lo] segments of K elements each (K a
+ * multiple of 32; lda, ldb >= 2K).  The kernel runs 3K/32 k-blocks:
+ * C = A_hi.B_hi + A_hi.B_lo + A_lo.B_hi (f32 accumulate). */
+int eas_gemm_3xtf32(const float* a2, const float* b2, float* c, uint32_t M, uint32_t N, uint32_t K, uint32_t batch,
+                    uint64_t lda, uint64_t a_bstride, uint64_t ldb, uint64_t b_bstride, uint64_t ldc,
+                    uint64_t c_bstride, int block_n, void* stream);
+
 /* 3xTF32 operand staging: each value x splits into hi = tf32(x) and
- * lo = tf32(x - hi) (round to nearest, ties away; x - hi is exact).  Row r of
- * the source (transpose = 0: src[r][k], row pitch ld_src) or column r
- * (transpose = 1: src[k][r]) becomes dst row r of 3 segments of kp elements;
- * segment s holds lo if bit s of lo_mask is set, else hi; zero outside
- * r < rows_valid, k < k_valid.  dst is dense: [batch][rows][3*kp].  With
- * A' = split(A, mask 0b100) and B'^T = split(B, transpose, mask 0b010),
- * A' . B' = A_hi.B_hi + A_hi.B_lo + A_lo.B_hi. */
-int eas_split3_tf32(const float* src, float* dst, uint32_t rows, uint32_t kp, uint64_t ld_src, uint32_t rows_valid,
-                    uint32_t k_valid, uint32_t batch, uint64_t bs_src, int lo_mask, int transpose, void* stream);
+ * lo = tf32(x - hi) (round to nearest, ties away from zero; x - hi is exact).
+ * Row r of the source (transpose = 0: src[r][k], row pitch ld_src) or column r
+ * (transpose = 1: src[k][r]) becomes dst row r = [hi | lo], each segment kp
+ * elements (kp a multiple of 4; dst 16-byte aligned, dense
+ * [batch][rows][2*kp]); zero outside r < rows_valid, k < k_valid. */
+int eas_split_tf32(const float* src, float* dst, uint32_t rows, uint32_t kp, uint64_t ld_src, uint32_t rows_valid,
+                   uint32_t k_valid, uint32_t batch, uint64_t bs_src, int transpose, void* stream);
 
 /* Read and clear the status word of native kernels on `dev` (0 = ok,
  * EAS_ERR_TIMEOUT = a bounded wait expired).  Valid after the stream synced. */

@@ -1,6 +1,6 @@
 """GPU: the opt-in 3xTF32 mode of proven fp32 matmuls (EAS_FP32_MATMUL=3xtf32).
 
-* ``eas_split3_tf32`` is bit-exact against a numpy restatement of the TF32 rounding
+* ``eas_split_tf32`` is bit-exact against a numpy restatement of the TF32 rounding
   (round to nearest, ties away from zero, on the 13 low mantissa bits);
 * ``eas_gemm_tf32`` (tcgen05 kind::tf32) on TF32-exact inputs agrees with float64 to f32
   accumulation error;
@@ -25,21 +25,22 @@ def tf32_rna(x: np.ndarray) -> np.ndarray:
     return ((u & np.uint32(0x80000000)) | mag).view(np.float32)
 
 
-def _split3_ref(src: np.ndarray, kp: int, lo_mask: int, transpose: bool) -> np.ndarray:
-    """src [batch][rows][k] (or [batch][k][rows] when transposed) -> [batch][rows][3*kp]."""
+def _split_ref(src: np.ndarray, kp: int, transpose: bool) -> np.ndarray:
+    """src [batch][rows][k] (or [batch][k][rows] when transposed) -> [batch][rows][2*kp] = [hi | lo]."""
     s = np.swapaxes(src, 1, 2) if transpose else src
     batch, rows, k = s.shape
     hi = tf32_rna(s)
     lo = tf32_rna(s - hi)
-    out = np.zeros((batch, rows, 3 * kp), np.float32)
-    for seg in range(3):
-        out[:, :, seg * kp:seg * kp + k] = lo if (lo_mask >> seg) & 1 else hi
+    out = np.zeros((batch, rows, 2 * kp), np.float32)
+    out[:, :, :k] = hi
+    out[:, :, kp:kp + k] = lo
     return out
 
 
 @pytest.mark.parametrize("batch,rows,k,transpose", [(1, 37, 19, False), (2, 64, 64, False), (1, 37, 19, True),
-                                                     (3, 100, 70, True), (1, 1, 1, True)])
-def test_split3_bit_exact(cuda_rt, batch, rows, k, transpose):
+                                                     (3, 100, 70, True), (1, 1, 1, True), (1, 1, 1, False),
+                                                     (2, 33, 1100, False), (1, 70, 130, True)])
+def test_split_bit_exact(cuda_rt, batch, rows, k, transpose):
     import torch
 
     lib = cuda_ext.load()
@@ -48,18 +49,40 @@ def test_split3_bit_exact(cuda_rt, batch, rows, k, transpose):
     src = (rng.standard_normal(shape) * np.exp2(rng.integers(-20, 20, shape))).astype(np.float32)
     if src.size >= 3:
         src.reshape(-1)[:3] = [0.0, -0.0, 1.0 + 2.0 ** -11]      # a tie, rounded away from zero
-    kp = -(-k // 4) * 4
-    mask = 0b010 if transpose else 0b100
+    kp = -(-k // 32) * 32
     d_src = torch.from_numpy(src).cuda()
-    d_dst = torch.full((batch, rows, 3 * kp), float("nan"), device="cuda")
+    d_dst = torch.full((batch, rows, 2 * kp), float("nan"), device="cuda")
     ld = rows if transpose else k
-    bs = rows * k
-    cuda_ext.check(lib.eas_split3_tf32(d_src.data_ptr(), d_dst.data_ptr(), rows, kp, ld, rows, k, batch, bs, mask,
-                                       int(transpose), None), "split3")
+    cuda_ext.check(lib.eas_split_tf32(d_src.data_ptr(), d_dst.data_ptr(), rows, kp, ld, rows, k, batch, rows * k,
+                                      int(transpose), None), "split")
     torch.cuda.synchronize()
     got = d_dst.cpu().numpy()
-    want = _split3_ref(src, kp, mask, transpose)
+    want = _split_ref(src, kp, transpose)
     assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+@pytest.mark.parametrize("batch,M,N,K", [(1, 128, 128, 64), (1, 200, 72, 36), (1, 512, 512, 256), (2, 300, 260, 100)])
+def test_gemm_3xtf32_segments(cuda_rt, batch, M, N, K):
+    """eas_gemm_3xtf32 over [hi | lo] rows equals the three-term product of the parts (float64)."""
+    import torch
+
+    lib = cuda_ext.load()
+    rng = np.random.default_rng(M * 7 + K)
+    a = rng.standard_normal((batch, M, K)).astype(np.float32)
+    bt = rng.standard_normal((batch, N, K)).astype(np.float32)
+    kp = -(-K // 32) * 32
+    a2, b2 = _split_ref(a, kp, False), _split_ref(bt, kp, False)
+    da, db = torch.from_numpy(a2).cuda(), torch.from_numpy(b2).cuda()
+    dc = torch.full((batch, M, N), float("nan"), device="cuda")
+    cuda_ext.check(lib.eas_gemm_3xtf32(da.data_ptr(), db.data_ptr(), dc.data_ptr(), M, N, kp, batch, 2 * kp,
+                                       2 * M * kp, 2 * kp, 2 * N * kp, N, M * N, 256 if M > 128 else 128, None),
+                   "gemm_3xtf32")
+    torch.cuda.synchronize()
+    ah, al = a2[..., :kp].astype(np.float64), a2[..., kp:].astype(np.float64)
+    bh, bl = b2[..., :kp].astype(np.float64), b2[..., kp:].astype(np.float64)
+    ref = sum(np.einsum("bmk,bnk->bmn", x, y) for x, y in ((ah, bh), (ah, bl), (al, bh)))
+    err = np.abs(dc.cpu().numpy() - ref).max() / np.abs(ref).max()
+    assert err <= 1e-5, err
 
 
 @pytest.mark.parametrize("batch,M,N,K", [(1, 128, 128, 64), (1, 200, 72, 36), (1, 512, 512, 256), (2, 300, 260, 100),
