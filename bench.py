@@ -11,14 +11,17 @@ L2), so no L2 flush is needed between steps.
 * ``value``: aggregate GB/s = 12 B/element * N / max-over-ranks device time of
   K steps (CUDA events on the launch stream, barrier + synchronize around).
 * ``e2e``: the same metric through the public API with host buffers (pinned
-  torch CPU tensors): every step copies a, b, c host->device, launches and
-  copies c back.
+  torch CPU tensors): every step copies a and b host->device, launches and
+  copies c back (c is never loaded by the kernel, so it is not copied in).
 * ``roofline``: the add kernel's achieved bytes / launch time against the
   measured HBM copy peak (MEASURED_PEAKS.json).
 * ``gemm``: the fp16 ``mk.dot`` GEMM (configs C4 8192^3 and C5 batched) TFLOP/s
   on the native tcgen05 path.
 * ``matmul_tiled``: config C3, the reference's fp32 tiled matmul at 2048^3 on
-  the proven-GEMM FFMA path (1 GPU), with cuBLAS fp32 timed beside it.
+  the proven-GEMM FFMA path (1 GPU), with cuBLAS fp32 timed beside it and the
+  opt-in 3xTF32 mode (``tf32x3``).
+* ``c1_add_call``: config C1 (N = 1031), launch-bound: the cost of one call
+  through the public API (numpy synced, device async, CUDA-graph replay).
 * ``cpu_baseline``: numpy on the host cores on a bounded sample.
 
 ``--impl reference`` times the reference's CPU semantics instead (the CPU
@@ -326,6 +329,95 @@ def _c3_3xtf32(rt, ck, case, args_, grid, a, b, c, flush, steps, flops) -> dict:
             "kernels": "2x eas_split_tf32 ([hi | lo] rows) + tcgen05 kind::tf32 GEMM over 3 K/32 k-blocks (opt-in; default stays exact)"}
 
 
+def run_c1(args, rt) -> dict:
+    """Config C1: the reference's own test case for add_kernel (N = 1031 = 1024 + 7, BLOCK = 256,
+    a, b ~ N(0, 1) from seed 0, grid ceil(N / BLOCK)); a launch-bound workload, so the metric is
+    the cost of one call:
+
+    * ``numpy_sync_us``: numpy host arrays, as the reference's tests pass them (copies in, the
+      kernel, the copy of c out, synchronised), wall clock per call;
+    * ``device_async_us``: torch CUDA tensors, ``_sync=False``; host cost per launch over a
+      burst (the GPU drains behind it), and ``device_us_per_launch`` from CUDA events;
+    * ``graph_replay_us``: 100 launches captured in one CUDA graph, per launch on replay;
+    * ``cpu_baseline``: the oracle interpreting the same compiled IR (``port``, 1 thread).
+    Every path is checked bit-exact against a + b first."""
+    import numpy as np
+    import torch
+
+    from oracle.interp import execute
+
+    add_kernel = make_add_kernel()
+    n, block = 1031, 256
+    rng = np.random.default_rng(0)
+    a = rng.standard_normal(n, dtype=np.float32)
+    b = rng.standard_normal(n, dtype=np.float32)
+    c = np.zeros_like(a)
+    add_kernel(a, b, c, n, BLOCK=block)
+    if not np.array_equal(c, a + b):
+        raise SystemExit("bench: C1 numpy result differs from a + b")
+    calls = 2000
+    t0 = time.perf_counter()
+    for _ in range(calls):
+        add_kernel(a, b, c, n, BLOCK=block)
+    numpy_us = (time.perf_counter() - t0) / calls * 1e6
+
+    da, db = torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
+    dc = torch.zeros(n, device="cuda")
+    launches0 = rt.launch_count
+    for _ in range(10):
+        add_kernel(da, db, dc, n, BLOCK=block, _sync=False)
+    torch.cuda.synchronize()
+    if not torch.equal(dc.cpu(), torch.from_numpy(a + b)):
+        raise SystemExit("bench: C1 device result differs from a + b")
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
+    e0.record(stream)
+    for _ in range(calls):
+        add_kernel(da, db, dc, n, BLOCK=block, _sync=False)
+    e1.record(stream)
+    host_us = (time.perf_counter() - t0) / calls * 1e6
+    torch.cuda.synchronize()
+    dev_us = e0.elapsed_time(e1) * 1e3 / calls
+
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(100):
+            add_kernel(da, db, dc, n, BLOCK=block, _sync=False)
+    dc.zero_()
+    g.replay()
+    torch.cuda.synchronize()
+    if not torch.equal(dc.cpu(), torch.from_numpy(a + b)):
+        raise SystemExit("bench: C1 graph replay differs from a + b")
+    reps = 20
+    e0.record(stream)
+    for _ in range(reps):
+        g.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    graph_us = e0.elapsed_time(e1) * 1e3 / (reps * 100)
+
+    ck = add_kernel.compile(a, b, c, n, BLOCK=block)
+    want = np.zeros_like(a)
+    execute(ck.ir, {"a": a, "b": b, "c": want, "N": n})
+    t0 = time.perf_counter()
+    cpu_calls = 0
+    while time.perf_counter() - t0 < 2.0:
+        execute(ck.ir, {"a": a, "b": b, "c": want, "N": n})
+        cpu_calls += 1
+    cpu_us = (time.perf_counter() - t0) / cpu_calls * 1e6
+    return {
+        "metric": "add_kernel per-call time", "unit": "us", "higher_is_better": False,
+        "numpy_sync_us": round(numpy_us, 2), "device_async_us": round(host_us, 2),
+        "device_us_per_launch": round(dev_us, 2), "graph_replay_us": round(graph_us, 3),
+        "config": {"workload": "C1 add_kernel N=1031 (1024+7), BLOCK=256, grid 5, a, b ~ N(0,1) seed 0",
+                   "calls": calls},
+        "gpu_launches": rt.launch_count - launches0,
+        "cpu_baseline": {"value": round(cpu_us, 1), "unit": "us", "cores": 1, "kind": "port",
+                         "sample": f"oracle interpreting the same IR, {cpu_calls} calls in 2 s"},
+    }
+
+
 def run_tiled(args, rt) -> dict:
     """Config C3: the reference's unmodified fp32 tiled matmul (its front end's IR, committed as
     tests/golden/reference_ir_big.json.gz), M = N = K = 2048, 32x32x32 tiles, 256 threads per
@@ -477,6 +569,9 @@ def run_eas(args) -> None:
     if args.only == "C3":
         print(json.dumps(run_tiled(args, rt)), flush=True)
         return
+    if args.only == "C1":
+        print(json.dumps(run_c1(args, rt)), flush=True)
+        return
     if args.only in ("C4", "C5"):
         # profiling mode: one GEMM workload only
         res = run_gemm(args.only, args, world, rank, rt)
@@ -568,6 +663,12 @@ def run_eas(args) -> None:
             tiled = run_tiled(args, rt)
         except (SystemExit, Exception) as e:  # a secondary leg never suppresses the headline line
             tiled = {"metric": "fp32 tiled matmul TFLOP/s", "error": f"{type(e).__name__}: {e}"}
+    c1 = None
+    if not args.quick and world == 1:
+        try:
+            c1 = run_c1(args, rt)
+        except (SystemExit, Exception) as e:
+            c1 = {"metric": "add_kernel per-call time", "error": f"{type(e).__name__}: {e}"}
     if rank != 0:
         return
     pk = peaks()
@@ -591,6 +692,8 @@ def run_eas(args) -> None:
         line["gemm"] = gemm
     if tiled is not None:
         line["matmul_tiled"] = tiled
+    if c1 is not None:
+        line["c1_add_call"] = c1
     if world == 1 and not args.no_cpu_baseline and not args.quick:
         line["cpu_baseline"] = cpu_add_baseline(args.cpu_seconds)
     print(json.dumps(line), flush=True)
@@ -653,8 +756,8 @@ def main() -> None:
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--n", type=int, default=N_TOTAL, help="total elements (profiling runs use a smaller case)")
     ap.add_argument("--no-gemm", action="store_true", help="skip the fp16 GEMM configs (C4, C5)")
-    ap.add_argument("--only", choices=["all", "C3", "C4", "C5"], default="all",
-                    help="run a single GEMM workload (profiling)")
+    ap.add_argument("--only", choices=["all", "C1", "C3", "C4", "C5"], default="all",
+                    help="run a single secondary workload (profiling)")
     ap.add_argument("--gemm-steps", type=int, default=20)
     ap.add_argument("--quick", action="store_true",
                     help="profiling mode: no clock warm-up loop, no e2e arm, no CPU baseline")
