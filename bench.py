@@ -197,6 +197,41 @@ def gemm_shard(name: str, world: int, rank: int) -> tuple[int, int, int, int]:
     return b1 - b0, M, N, K
 
 
+def gemm_e2e(name, a, b, c, M, N, K, batch, world, flops_total) -> dict:
+    """The GEMM leg end to end through the public API with pinned host tensors: each step copies
+    A, B and C in (C too: the runtime keeps the unwritten part of a host output intact), runs the
+    kernel, copies C out, synchronised; wall clock, max over ranks."""
+    import torch
+
+    from examples.matmul_dot_f16 import grid, matmul_dot_f16_tuned
+
+    ha, hb = a.cpu().pin_memory(), b.cpu().pin_memory()
+    hc = torch.zeros(c.shape, dtype=torch.float32).pin_memory()
+
+    def step():
+        matmul_dot_f16_tuned(ha.reshape(-1), hb.reshape(-1), hc.reshape(-1), M, N, K, _grid=grid(batch))
+
+    step()
+    ref = ha[0, :4].double() @ hb[0].double()
+    err = ((hc[0, :4].double() - ref).abs().max() / ref.abs().max()).item()
+    if err > 1e-4:
+        raise SystemExit(f"bench: {name} e2e result off by {err:.2e}")
+    steps = 2
+    barrier(world)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        step()
+    dt = max_over_ranks((time.perf_counter() - t0) / steps, world)
+    per_rank_in = ha.numel() * 2 + hb.numel() * 2 + hc.numel() * 4
+    per_rank_out = hc.numel() * 4
+    del ha, hb, hc
+    return {"value": round(flops_total / dt / 1e12, 2), "unit": "TFLOP/s",
+            "h2d_bytes_per_step": per_rank_in * world, "d2h_bytes_per_step": per_rank_out * world,
+            "ms_per_step": round(dt * 1e3, 2),
+            "how": "public API, pinned torch CPU tensors in and out (A, B, C copied in; C copied out), "
+                   "synchronised per step; wall clock, max over ranks; PCIe-bound"}
+
+
 def run_gemm(name: str, args, world: int, rank: int, rt) -> dict:
     """fp16 mk.dot GEMM (examples/matmul_dot_f16.py) on this rank's shard; TFLOP/s aggregated over ranks."""
     import torch
@@ -265,6 +300,7 @@ def run_gemm(name: str, args, world: int, rank: int, rt) -> dict:
             lib_tf = None
     flops_total = 2.0 * tb * TM * TN * TK
     flops_local = 2.0 * batch * M * N * K
+    e2e = None if args.quick else gemm_e2e(name, a, b, c, M, N, K, batch, world, flops_total)
     pk = peaks()
     local_tf = flops_local / (ms * 1e-3) / 1e12
     return {
@@ -280,6 +316,7 @@ def run_gemm(name: str, args, world: int, rank: int, rt) -> dict:
                      "frac_of_nominal_2250": round(local_tf / 2250.0, 4),
                      "traffic": profile_traffic(f"gemm_{name.lower()}_n1")},
         "cublas_f16_f32out_tflops": lib_tf,
+        "e2e": e2e,
         "cpu_baseline": (cpu_gemm_baseline(min(M, 2048), N, K, 1, 5, f"one {min(M, 2048)}-row slice of one problem "
                                            f"of the {name} workload (f16 inputs upcast to f32)")
                          if world == 1 and not args.no_cpu_baseline else None),
