@@ -86,7 +86,11 @@ class DeviceBuffer:
         lib = cuda_ext.load()
         cuda_ext.check(lib.eas_copy_from_host(self.ptr, a.ctypes.data, a.nbytes, stream), "copy_from_host")
 
-    def copy_to_host(self, out: np.ndarray, stream: int = 0) -> None:
+    def copy_to_host(self, out: Any, stream: int = 0) -> None:
+        if not isinstance(out, np.ndarray):  # bytearray, memoryview, ...: any writable buffer
+            out = np.frombuffer(out, dtype=np.uint8)
+            if not out.flags.writeable:
+                raise ValueError("copy_to_host needs a writable destination")
         if not out.flags.c_contiguous:
             raise ValueError("copy_to_host needs a C-contiguous destination")
         if out.nbytes > self.nbytes:

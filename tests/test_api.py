@@ -184,3 +184,21 @@ def test_unsupported_buffer_dtype():
 
     with pytest.raises(TypeError):
         k.compile(np.zeros(4, np.float64), 4, BLOCK=32)
+
+
+@eas.kernel
+def _in_tile_store_kernel(src, dst, LIMIT: eas.constexpr, NT: eas.constexpr):
+    tid = mk.tid(0, NT)
+    for i in range(0, LIMIT, NT):
+        idx = tid + i
+        in_tile = idx < LIMIT
+        mk.store(dst, idx, mk.load(src, idx, True), in_tile)
+
+
+@pytest.mark.parametrize("limit,folded", [(64, True), (70, False)])
+def test_interval_lt_fold(limit, folded):
+    """A `tid + i < LIMIT` bound that holds for every thread (LIMIT a multiple of NT) is folded
+    away; otherwise it stays (reference tests/test_interval_lt_fold.py:23-36)."""
+    src = np.arange(limit, dtype=np.float32)
+    ck = _in_tile_store_kernel.compile(src, np.zeros_like(src), LIMIT=limit, NT=16)
+    assert ("lt" in [i.op for i in ck.ir.insts]) is not folded

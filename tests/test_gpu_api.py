@@ -167,3 +167,24 @@ def test_dlpack_export_orders_consumer_stream_without_host_sync(cuda_rt, monkeyp
     s.synchronize()
     assert torch.equal(d, torch.full((n,), 6.0, device="cuda"))
     cuda_rt.synchronize()
+
+
+@pytest.mark.parametrize("kind", ["numpy", "bytearray"])
+def test_device_buffer_copy_roundtrip(cuda_rt, kind):
+    """Host -> device -> host through a device buffer (reference tests/test_metal_copy.py:21-41)."""
+    from easy_as_b200.runtime.cuda import DeviceBuffer
+
+    if kind == "numpy":
+        src = np.random.default_rng(1).standard_normal(4096 + 7).astype(np.float32)
+        dst = np.empty_like(src)
+    else:
+        src = bytearray((i * 7 + 3) & 0xFF for i in range(8192))
+        dst = bytearray(len(src))
+    buf = DeviceBuffer(len(memoryview(src).cast("B")), 0)
+    buf.copy_from_host(src)
+    buf.copy_to_host(dst)
+    buf.free()
+    if kind == "numpy":
+        assert np.array_equal(dst, src)
+    else:
+        assert dst == src

@@ -1,0 +1,226 @@
+"""CPU: the runtime's host logic against a fake native library (no GPU).
+
+The reference checks its Metal bridge the same way (tests/test_metal_numpy_bridge.py:85-104): a
+fake extension receives the launch and the test inspects what the runtime handed it.  Here the
+fake ``libeas_cuda`` keeps "device" memory in host buffers, records every call, and executes a
+launch by running the CPU oracle on the kernel's IR over views of that memory.  Checked:
+numpy inputs are staged into device buffers, scalars are packed little-endian at their
+parameter offsets, only written buffers are copied back, staging buffers are pooled, and
+launch errors surface as Python exceptions."""
+
+from __future__ import annotations
+
+import ctypes
+import struct
+
+import numpy as np
+import pytest
+
+import eas
+from eas import mk
+from easy_as_b200.ir import DType
+from easy_as_b200.runtime import cuda_ext
+from oracle.interp import execute
+
+
+@eas.kernel
+def add_kernel(a, b, c, N, BLOCK: eas.constexpr):
+    offs = mk.program_id(0) * BLOCK + mk.arange(0, BLOCK)
+    m = offs < N
+    mk.store(c, offs, mk.load(a, offs, m) + mk.load(b, offs, m), m)
+
+
+@eas.kernel
+def scale_kernel(x, y, N, alpha, BLOCK: eas.constexpr):
+    offs = mk.program_id(0) * BLOCK + mk.arange(0, BLOCK)
+    m = offs < N
+    mk.store(y, offs, mk.load(x, offs, m) * alpha, m)
+
+
+class FakeLib:
+    """The subset of the C ABI the launch path calls, with host memory standing in for HBM."""
+
+    def __init__(self):
+        self.mem: dict[int, ctypes.Array] = {}
+        self.calls: list[tuple] = []
+        self.kernels: dict[int, object] = {}
+        self.fail_launch = False
+        self.err = b""
+
+    # memory
+    def _find(self, ptr: int) -> tuple[ctypes.Array, int]:
+        for base, buf in self.mem.items():
+            if base <= ptr < base + len(buf):
+                return buf, ptr - base
+        raise AssertionError(f"pointer {ptr:#x} is not a fake device allocation")
+
+    def eas_alloc_buffer(self, dev, nbytes, out):
+        buf = ctypes.create_string_buffer(max(int(nbytes), 1))
+        addr = ctypes.addressof(buf)
+        self.mem[addr] = buf
+        out._obj.value = addr
+        self.calls.append(("alloc", int(nbytes)))
+        return 0
+
+    def eas_free_buffer(self, ptr):
+        self.mem.pop(int(ptr), None)
+        return 0
+
+    def eas_copy_from_host(self, dst, src, nbytes, stream):
+        self._find(int(dst))
+        ctypes.memmove(int(dst), int(src), int(nbytes))
+        self.calls.append(("h2d", int(nbytes)))
+        return 0
+
+    def eas_copy_to_host(self, dst, src, nbytes, stream):
+        self._find(int(src))
+        ctypes.memmove(int(dst), int(src), int(nbytes))
+        self.calls.append(("d2h", int(nbytes)))
+        return 0
+
+    # compile / load: the "binary" is the source text; the pipeline handle indexes it
+    def eas_versions(self, drv, nvrtc):
+        drv._obj.value, nvrtc._obj.value = 12090, 12090
+        return 0
+
+    def eas_compile(self, src, name, opts, nopts, img, size):
+        self._img = ctypes.create_string_buffer(bytes(src))
+        img._obj.value = ctypes.addressof(self._img)
+        size._obj.value = len(src)
+        return 0
+
+    def eas_free_host(self, p):
+        return 0
+
+    def eas_pipeline_load(self, dev, cubin, n, name, smem, out):
+        h = len(self.kernels) + 1
+        self.kernels[h] = name
+        out._obj.value = h
+        return 0
+
+    # launch: decode the parameter block with the kernel's layout, run the oracle
+    def eas_launch(self, pipe, grid, block, smem, stream, blob, offsets, count):
+        self.calls.append(("launch", tuple(grid), tuple(block)))
+        if self.fail_launch:
+            self.err = b"fake launch failure"
+            return cuda_ext.EAS_ERR_LAUNCH
+        ck = self.current
+        layout = ck.plan.layout
+        assert [offsets[i] for i in range(count)] == [o for _p, o, _f in layout.entries]
+        args, hidden = {}, {}
+        for p, off, fmt in layout.entries:
+            (v,) = struct.unpack_from(fmt, blob, off)
+            if p.kind == "buffer":
+                buf, at = self._find(v)
+                arg = next(a for a in ck.ir.args if a.name == p.arg)
+                dt = np.float32 if arg.dtype == DType.F32 else np.float16
+                args[p.arg] = np.frombuffer(buf, dtype=dt, count=(len(buf) - at) // np.dtype(dt).itemsize,
+                                            offset=at)
+            elif p.kind == "hidden":
+                hidden[p.name] = v
+            else:
+                args[p.arg] = v
+        self.scalars = {k: v for k, v in args.items() if not isinstance(v, np.ndarray)}
+        assert all(hidden.get(k, 0) == 0 for k in ("eas_pid_x", "eas_pid_y", "eas_pid_z"))
+        execute(ck.ir, args, grid=tuple(grid))
+        return 0
+
+    # streams, events, status
+    def eas_stream_synchronize(self, stream):
+        return 0
+
+    def eas_stream_is_capturing(self, stream, out):
+        out._obj.value = 0
+        return 0
+
+    def eas_gemm_status(self, dev, out):
+        out._obj.value = 0
+        return 0
+
+    def eas_host_is_pinned(self, ptr, out):
+        out._obj.value = 0
+        return 0
+
+    def eas_is_available(self):
+        return 1
+
+    def eas_last_error(self):
+        return self.err
+
+
+@pytest.fixture
+def fake(monkeypatch):
+    from easy_as_b200.runtime.cuda import CudaRuntime
+
+    lib = FakeLib()
+    monkeypatch.setattr(cuda_ext, "_lib", lib)
+    monkeypatch.setenv("EAS_CACHE_DIR", "off")
+    rt = CudaRuntime()
+    rt.default_device = lambda: 0  # type: ignore[method-assign]
+    return lib, rt
+
+
+def _run(lib, rt, kernel, args, **meta):
+    ck = kernel.compile(*args, **meta)
+    lib.current = ck
+    names = [a.name for a in ck.ir.args]
+    rt.run(ck, dict(zip(names, args)), meta, sync=True)
+    return ck
+
+
+def test_numpy_inputs_are_staged_and_only_outputs_copied_back(fake):
+    lib, rt = fake
+    n = 1024 + 7
+    rng = np.random.default_rng(0)
+    a = rng.standard_normal(n, dtype=np.float32)
+    b = rng.standard_normal(n, dtype=np.float32)
+    c = np.zeros_like(a)
+    _run(lib, rt, add_kernel, (a, b, c, n), BLOCK=256)
+    assert np.array_equal(c, a + b)
+    kinds = [k[0] for k in lib.calls]
+    assert kinds.count("launch") == 1
+    assert [k for k in lib.calls if k[0] == "launch"][0][1] == (5, 1, 1)   # ceil(1031 / 256) programs
+    assert kinds.count("h2d") == 3 and kinds.count("d2h") == 1           # c is written: copied back alone
+    assert [k[1] for k in lib.calls if k[0] == "d2h"] == [c.nbytes]
+    assert lib.scalars == {"N": n}
+
+
+def test_scalars_are_packed_at_their_offsets(fake):
+    lib, rt = fake
+    n = 300
+    x = np.arange(n, dtype=np.float32)
+    y = np.zeros_like(x)
+    _run(lib, rt, scale_kernel, (x, y, n, 0.5), BLOCK=128)
+    assert lib.scalars == {"N": n, "alpha": 0.5}
+    assert np.array_equal(y, x * np.float32(0.5))
+
+
+def test_staging_buffers_are_pooled(fake):
+    lib, rt = fake
+    n = 513
+    a = np.ones(n, np.float32)
+    b = np.ones(n, np.float32)
+    c = np.zeros(n, np.float32)
+    _run(lib, rt, add_kernel, (a, b, c, n), BLOCK=256)
+    allocs = sum(1 for k in lib.calls if k[0] == "alloc")
+    _run(lib, rt, add_kernel, (a, b, c, n), BLOCK=256)
+    assert sum(1 for k in lib.calls if k[0] == "alloc") == allocs     # second call reuses them
+    assert np.array_equal(c, np.full(n, 2.0, np.float32))
+
+
+def test_same_array_passed_twice_is_staged_once(fake):
+    lib, rt = fake
+    n = 100
+    a = np.arange(n, dtype=np.float32)
+    c = np.zeros_like(a)
+    _run(lib, rt, add_kernel, (a, a, c, n), BLOCK=64)
+    assert sum(1 for k in lib.calls if k[0] == "h2d") == 2
+    assert np.array_equal(c, a + a)
+
+
+def test_launch_error_raises_with_the_library_message(fake):
+    lib, rt = fake
+    lib.fail_launch = True
+    a = np.ones(10, np.float32)
+    with pytest.raises(cuda_ext.CudaError, match="fake launch failure"):
+        _run(lib, rt, add_kernel, (a, a.copy(), np.zeros(10, np.float32), 10), BLOCK=32)
