@@ -33,7 +33,7 @@ f32 rounding (the parity tests use the fp16-GEMM tolerance).
 from __future__ import annotations
 
 import ctypes
-from dataclasses import dataclass
+from dataclasses import dataclass, field
 from typing import Any
 
 from ..ir import DType, IRModule, Inst, ValueRef
@@ -98,6 +98,7 @@ class DotGemmPlan:
     block_n: int
     kind: str = "dot_gemm_f16_tcgen05"
     last_reason: str = ""
+    _memo: dict = field(default_factory=dict, repr=False, compare=False)
 
     # -- launch-time mapping -------------------------------------------------
     def _coord_forms(self, forms: dict[str, dict[str, int]]) -> dict[str, dict[str, int]] | None:
@@ -113,7 +114,21 @@ class DotGemmPlan:
 
     def map_launch(self, scalars: dict[str, int], programs: tuple[int, int, int], ntx: int,
                    pid_base: tuple[int, int, int] = (0, 0, 0)) -> dict[str, Any] | None:
-        """GEMM of the programs ``pid_base + [0, programs)`` (program ids offset per axis)."""
+        """GEMM of the programs ``pid_base + [0, programs)`` (program ids offset per axis); memoised
+        per launch values (the mapping is a pure function of them)."""
+        key = (tuple(sorted(scalars.items())), tuple(programs), ntx, tuple(pid_base))
+        hit = self._memo.get(key)
+        if hit is None:
+            m = self._map_launch(scalars, programs, ntx, pid_base)
+            hit = (m, self.last_reason)
+            if len(self._memo) >= 64:
+                self._memo.clear()
+            self._memo[key] = hit
+        self.last_reason = hit[1]
+        return hit[0]
+
+    def _map_launch(self, scalars: dict[str, int], programs: tuple[int, int, int], ntx: int,
+                    pid_base: tuple[int, int, int] = (0, 0, 0)) -> dict[str, Any] | None:
         polys = {"a": self.a_base, "b": self.b_base, "sa": self.a_stride, "sb": self.b_stride, "k": self.k,
                  "c": self.c_off}
         for i, (lhs, rhs) in enumerate(self.atoms):

@@ -115,6 +115,15 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void*
                : "memory");
 }
 
+// f32 add of a shared-memory box into global memory (split-K partial tiles); same bulk group as
+// the stores, so the same waits cover it
+__device__ __forceinline__ void tma_reduce_add_3d(const CUtensorMap* map, const void* src, int x, int y, int z) {
+  asm volatile("cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
+
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
@@ -486,10 +495,14 @@ template <int kStages2, bool B_MN, bool TMA_C, bool TF = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_f16_tcgen05_2sm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                                 const __grid_constant__ CUtensorMap map_c, float* __restrict__ c, int M, int N, int K,
-                                int batch, long long ldc, long long c_bstride, int* status, int seg_kb) {
+                                int batch, long long ldc, long long c_bstride, int* status, int seg_kb,
+                                int ksplit) {
   static_assert(!(TF && B_MN), "tf32 operands are K-major here");
   constexpr int kBKe = TF ? 32 : BK;  // elements per 128-byte K row of a stage
   using L = Smem2<kStages2, TMA_C>;
+  // split-K: work unit u is K part (u % ks) of tile (u / ks); parts after the first are summed into
+  // C (zeroed by the host) with TMA reduce-adds, so only the TMA-store epilogue splits
+  const int ks = TMA_C && ksplit > 1 ? ksplit : 1;
   constexpr int BN = 256;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -539,16 +552,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const int kblocks = (K + kBKe - 1) / kBKe;
   const int cid = blockIdx.x >> 1;
   const int ncl = gridDim.x >> 1;
+  const int units = sched.total * ks;
+  auto k_range = [&](int u, int& kb0, int& kb1) {
+    const int part = u % ks;
+    kb0 = (int)((long long)part * kblocks / ks);
+    kb1 = (int)((long long)(part + 1) * kblocks / ks);
+  };
 
   if (warp == 0) {
     if (lane == 0) {
       int s = 0;
       uint32_t ph = 0;
-      for (int t = cid; t < sched.total && !*abort_flag; t += ncl) {
-        const TileCoord tc = sched.at(t);  // m0 in units of 128: pair tiles are 256 rows
+      for (int u = cid; u < units && !*abort_flag; u += ncl) {
+        const TileCoord tc = sched.at(u / ks);  // m0 in units of 128: pair tiles are 256 rows
         const int m0 = (tc.m0 / BM) * 256 + 128 * (int)rank;
         const int n0 = tc.n0 * BN + 128 * (int)rank;
-        for (int kb = 0; kb < kblocks; ++kb) {
+        int kb_lo, kb_hi;
+        k_range(u, kb_lo, kb_hi);
+        for (int kb = kb_lo; kb < kb_hi; ++kb) {
           if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) break;
           uint8_t* sa = smem + s * L::kStageBytes;
           uint8_t* sb = sa + L::kABytes;
@@ -577,14 +598,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       int s = 0;
       uint32_t ph = 0;
       int local = 0;
-      for (int t = cid; t < sched.total && !*abort_flag; t += ncl, ++local) {
+      for (int u = cid; u < units && !*abort_flag; u += ncl, ++local) {
         const int buf = local & 1;
         const uint32_t acc_ph = (local >> 1) & 1;
         if (!mbar_wait_cl(&acc_empty[buf], acc_ph ^ 1, abort_flag)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * BN;
         bool ok = true;
-        for (int kb = 0; kb < kblocks; ++kb) {
+        int kb_lo, kb_hi;
+        k_range(u, kb_lo, kb_hi);
+        for (int kb = kb_lo; kb < kb_hi; ++kb) {
           if (!mbar_wait(&full[s], ph, abort_flag)) {
             ok = false;
             break;
@@ -602,14 +625,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                   "{\n\t.reg .pred p;\n\t"
                   "setp.ne.b32 p, %4, 0;\n\t"
                   "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-                  "l"(adesc), "l"(bdesc), "r"(idesc), "r"((kb | kk) != 0 ? 1u : 0u)
+                  "l"(adesc), "l"(bdesc), "r"(idesc), "r"((kb != kb_lo || kk != 0) ? 1u : 0u)
                   : "memory");
             else
               asm volatile(
                   "{\n\t.reg .pred p;\n\t"
                   "setp.ne.b32 p, %4, 0;\n\t"
                   "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-                  "l"(adesc), "l"(bdesc), "r"(idesc), "r"((kb | kk) != 0 ? 1u : 0u)
+                  "l"(adesc), "l"(bdesc), "r"(idesc), "r"((kb != kb_lo || kk != 0) ? 1u : 0u)
                   : "memory");
           }
           asm volatile(
@@ -637,12 +660,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const bool vec_ok = ((ldc & 3) == 0) && ((c_bstride & 3) == 0) && ((reinterpret_cast<uintptr_t>(c) & 15) == 0);
     const uint32_t acc_empty_leader[2] = {mapa_rank(smem_u32(&acc_empty[0]), 0), mapa_rank(smem_u32(&acc_empty[1]), 0)};
     int local = 0;
-    for (int t = cid; t < sched.total && !*abort_flag; t += ncl, ++local) {
+    for (int u = cid; u < units && !*abort_flag; u += ncl, ++local) {
       const int buf = local & 1;
       const uint32_t acc_ph = (local >> 1) & 1;
       if (!mbar_wait(&acc_full[buf], acc_ph, abort_flag)) break;
       tc_fence_after();
-      const TileCoord tc = sched.at(t);
+      const TileCoord tc = sched.at(u / ks);
       const int n0 = tc.n0 * BN;
       const int mrow0 = (tc.m0 / BM) * 256 + 128 * (int)rank + q * 32;
       const int m = mrow0 + lane;
@@ -667,7 +690,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             __syncwarp();
             if (lane == 0) {
-              tma_store_3d(&map_c, box, nb, mrow0, tc.b);
+              if (ks > 1)
+                tma_reduce_add_3d(&map_c, box, nb, mrow0, tc.b);
+              else
+                tma_store_3d(&map_c, box, nb, mrow0, tc.b);
               bulk_commit();
             }
             ++nbox;
@@ -724,13 +750,26 @@ int encode_map(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uin
   return eas_drv_check(r, "cuTensorMapEncodeTiled", EAS_ERR_VALUE);
 }
 
+// The dynamic shared-memory opt-in is a per-function, per-device setting: make it once per kernel
+// instantiation and device instead of on every launch.
+template <auto Kern>
+int set_smem_once(int bytes, const char* what) {
+  static bool done[64] = {false};  // one flag array per kernel instantiation
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && done[dev]) return EAS_OK;
+  int rc = eas_cuda_check(cudaFuncSetAttribute(Kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes), what,
+                          EAS_ERR_LAUNCH);
+  if (!rc && dev >= 0 && dev < 64) done[dev] = true;
+  return rc;
+}
+
 template <int BN, int STAGES, bool B_MN, bool TMA_C, bool TF = false>
 int launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, float* c, int M, int N, int K,
                    int batch, long long ldc, long long cbs, int* status, cudaStream_t stream, int num_sms, int seg_kb = 0) {
   using L = Smem<BN, STAGES, B_MN>;
   auto kern = gemm_f16_tcgen05_kernel<BN, STAGES, B_MN, TMA_C, TF>;
-  int rc = eas_cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal),
-                          "gemm: set smem attribute", EAS_ERR_LAUNCH);
+  int rc = set_smem_once<gemm_f16_tcgen05_kernel<BN, STAGES, B_MN, TMA_C, TF>>(L::kTotal, "gemm: set smem attribute");
   if (rc) return rc;
   const long long tiles = (long long)((M + BM - 1) / BM) * ((N + BN - 1) / BN) * batch;
   const int grid = (int)(tiles < num_sms ? tiles : num_sms);
@@ -738,13 +777,33 @@ int launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorM
   return eas_cuda_check(cudaGetLastError(), "gemm: launch", EAS_ERR_LAUNCH);
 }
 
+// Split-K for launches that leave most CTA pairs idle: with at most half as many 256x256 tiles as
+// resident pairs, each tile's K range is cut into ks <= 4 parts (ks <= pairs / tiles, at least 8
+// k-blocks per part) and the parts are summed into a zeroed C with TMA reduce-adds, so up to 4x
+// the pairs work.  Launches with a tile per pair or more do not split: zeroing C and summing 4
+// partial tiles through L2 cost more than the last wave's idle pairs (measured on the per-GPU
+// shards of C4 at 8 GPUs, 128 tiles on 74 pairs: 1109 TFLOP/s split 4 ways vs 1215 unsplit).
+// The reduce-adds land in any order, so split results may differ from run to run in the last
+// bits; EAS_GEMM_SPLITK=0 turns splitting off.
+int choose_ksplit(long long tiles, long long pairs, int kblocks, int batch) {
+  static const bool enabled = [] {
+    const char* e = getenv("EAS_GEMM_SPLITK");
+    return !(e && e[0] == '0');
+  }();
+  if (!enabled || pairs <= 0 || tiles <= 0 || batch > 64 || 2 * tiles > pairs) return 1;
+  long long ks = pairs / tiles;
+  if (ks > 4) ks = 4;
+  while (ks > 1 && kblocks < 8 * ks) --ks;
+  return (int)ks;
+}
+
 template <int STAGES, bool B_MN, bool TMA_C, bool TF = false>
 int launch_2sm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, float* c, int M, int N, int K,
                int batch, long long ldc, long long cbs, int* status, cudaStream_t stream, int num_sms, int seg_kb = 0) {
   using L = Smem2<STAGES, TMA_C>;
   auto kern = gemm_f16_tcgen05_2sm_kernel<STAGES, B_MN, TMA_C, TF>;
-  int rc = eas_cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal),
-                          "gemm(2sm): set smem attribute", EAS_ERR_LAUNCH);
+  int rc = set_smem_once<gemm_f16_tcgen05_2sm_kernel<STAGES, B_MN, TMA_C, TF>>(L::kTotal,
+                                                                             "gemm(2sm): set smem attribute");
   if (rc) return rc;
   const long long tiles = (long long)((M + 255) / 256) * ((N + 255) / 256) * batch;
   // persistent grid: only as many pairs as can be resident at once (GPC boundaries can leave SMs unpaired)
@@ -766,8 +825,18 @@ int launch_2sm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& 
     resident_pairs[which][dev] = n;
   }
   const long long pairs = resident_pairs[which][dev];
-  const int grid = 2 * (int)(tiles < pairs ? tiles : pairs);
-  kern<<<grid, kThreads, L::kTotal, stream>>>(ma, mb, mc, c, M, N, K, batch, ldc, cbs, status, seg_kb);
+  const int ksplit = TMA_C ? choose_ksplit(tiles, pairs, (K + (TF ? 32 : BK) - 1) / (TF ? 32 : BK), batch) : 1;
+  if (ksplit > 1) {  // the K parts are summed into C by TMA reduce-adds: start from zeros
+    for (int b = 0; b < batch; ++b) {
+      rc = eas_cuda_check(cudaMemset2DAsync(c + (long long)b * cbs, (size_t)ldc * 4, 0, (size_t)N * 4, (size_t)M,
+                                            stream),
+                          "gemm(2sm): zero C for split-K", EAS_ERR_LAUNCH);
+      if (rc) return rc;
+    }
+  }
+  const long long units = tiles * ksplit;
+  const int grid = 2 * (int)(units < pairs ? units : pairs);
+  kern<<<grid, kThreads, L::kTotal, stream>>>(ma, mb, mc, c, M, N, K, batch, ldc, cbs, status, seg_kb, ksplit);
   return eas_cuda_check(cudaGetLastError(), "gemm(2sm): launch", EAS_ERR_LAUNCH);
 }
 

@@ -1,0 +1,51 @@
+"""GPU: split-K in the CTA-pair tcgen05 GEMM.
+
+Launches with at most half as many 256x256 tiles as CTA pairs split each tile's K range into
+2-4 parts, summed into a zeroed C with TMA reduce-adds.  The small and ragged launches here
+split; the per-GPU shards of config C4 at 4 and 8 GPUs (256 and 128 tiles) do not, and stay as
+regression cases for the multi-wave schedule.  Each result is held to the fp16 GEMM bound
+against float64 (rtol 2e-2) through a normwise bound of max(1e-5, 4e-9 K)."""
+
+from __future__ import annotations
+
+import pytest
+
+from examples.matmul_dot_f16 import grid, matmul_dot_f16
+
+pytestmark = pytest.mark.gpu
+
+
+def _gemm(cuda_rt, batch, M, N, K, seed):
+    import torch
+
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    a = (torch.randn(batch, M, K, device="cuda", generator=g) / K ** 0.5).half()
+    b = (torch.randn(batch, K, N, device="cuda", generator=g) / K ** 0.5).half()
+    c = torch.full((batch, M, N), float("nan"), device="cuda")
+    before = cuda_rt.native_launches
+    matmul_dot_f16(a.reshape(-1), b.reshape(-1), c.reshape(-1), M, N, K, BLOCK_M=128, BLOCK_N=256, BLOCK_K=64,
+                   _grid=grid(batch), _sync=True)
+    assert cuda_rt.native_launches == before + 1
+    return a, b, c
+
+
+@pytest.mark.parametrize("batch,M,N,K", [(1, 1024, 8192, 8192), (1, 2048, 8192, 8192), (1, 512, 512, 4096),
+                                         (2, 512, 768, 2048), (1, 700, 1000, 3000)])
+def test_split_k_matches_float64(cuda_rt, batch, M, N, K):
+    import torch
+
+    a, b, c = _gemm(cuda_rt, batch, M, N, K, seed=M + K)
+    ref = torch.bmm(a.double(), b.double())
+    err = ((c.double() - ref).abs().max() / ref.abs().max()).item()
+    # f32 accumulation in the tensor core: the normwise error grows with K (1.07e-5 at K = 8192 unsplit)
+    assert err <= max(1e-5, 4e-9 * K), err
+    assert not torch.isnan(c).any()
+
+
+def test_split_k_runs_agree(cuda_rt):
+    """Two launches of the same split GEMM differ at most in the last bits (reduce-add order)."""
+    import torch
+
+    a, b, c1 = _gemm(cuda_rt, 1, 512, 512, 4096, seed=9)
+    _, _, c2 = _gemm(cuda_rt, 1, 512, 512, 4096, seed=9)
+    assert torch.allclose(c1, c2, rtol=0, atol=1e-6 * c1.abs().max().item())
