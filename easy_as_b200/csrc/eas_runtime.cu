@@ -491,6 +491,20 @@ extern "C" int eas_copy_to_host_async(void* dst, const void* src, size_t nbytes,
                         "copy device->host (async)", EAS_ERR_MEMORY);
 }
 
+extern "C" int eas_alloc_pinned(size_t nbytes, void** out) {
+  if (!out) return eas_fail(EAS_ERR_VALUE, "eas_alloc_pinned: null out pointer");
+  *out = nullptr;
+  int rc = eas_driver_init();
+  if (rc) return rc;
+  return eas_cuda_check(cudaHostAlloc(out, nbytes ? nbytes : 1, cudaHostAllocPortable), "pinned host allocation",
+                        EAS_ERR_MEMORY);
+}
+
+extern "C" int eas_free_pinned(void* p) {
+  if (!p) return EAS_OK;
+  return eas_cuda_check(cudaFreeHost(p), "free pinned host memory", EAS_ERR_MEMORY);
+}
+
 extern "C" int eas_host_is_pinned(const void* ptr, int* pinned) {
   if (!pinned) return eas_fail(EAS_ERR_VALUE, "eas_host_is_pinned: null pointer");
   *pinned = 0;

@@ -214,12 +214,36 @@ def _cache_dir() -> Path | None:
 class _Arg:
     """A buffer argument resolved to a device pointer."""
 
-    __slots__ = ("ptr", "device", "keep", "host", "dev_buf", "torch_stream")
+    __slots__ = ("ptr", "device", "keep", "host", "dev_buf", "torch_stream", "bounce")
 
     def __init__(self, ptr: int, device: int | None, keep: Any = None, host: np.ndarray | None = None,
-                 dev_buf: DeviceBuffer | None = None, torch_stream: bool = False):
+                 dev_buf: DeviceBuffer | None = None, torch_stream: bool = False, bounce: int | None = None):
         self.ptr, self.device, self.keep, self.host = ptr, device, keep, host
-        self.dev_buf, self.torch_stream = dev_buf, torch_stream
+        self.dev_buf, self.torch_stream, self.bounce = dev_buf, torch_stream, bounce
+
+
+class _Bounce:
+    """Page-locked host buffer and its device twin, for launches with small host arrays."""
+
+    __slots__ = ("host_ptr", "view", "dev", "nbytes")
+
+    def __init__(self, nbytes: int, device: int):
+        lib = cuda_ext.load()
+        p = cuda_ext.ctypes.c_void_p()
+        cuda_ext.check(lib.eas_alloc_pinned(nbytes, cuda_ext.ctypes.byref(p)), "pinned bounce buffer")
+        self.host_ptr = int(p.value)
+        self.view = np.ctypeslib.as_array((cuda_ext.ctypes.c_uint8 * nbytes).from_address(self.host_ptr))
+        self.dev = DeviceBuffer(nbytes, device)
+        self.nbytes = nbytes
+
+    def free(self) -> None:
+        if self.host_ptr:
+            lib = cuda_ext.load(require=False)
+            if lib is not None:
+                lib.eas_free_pinned(self.host_ptr)
+            self.host_ptr = 0
+            self.view = None
+        self.dev.free()
 
 
 class CudaRuntime:
@@ -230,6 +254,7 @@ class CudaRuntime:
         self._pending: deque[tuple[int, int, Any]] = deque()
         self._max_in_flight: int | None = None
         self._staging: dict[tuple[int, int], list[DeviceBuffer]] = {}
+        self._bounce: dict[int, _Bounce] = {}
         self._bucket_keep: list[Any] = []
         self._pending_n = 0
         self._bucket_n = 0
@@ -429,6 +454,8 @@ class CudaRuntime:
         if torch_stream and torch is not None:
             raw = getattr(torch._C, "_cuda_getCurrentRawStream", None)
             stream = int(raw(device)) if raw is not None else int(torch.cuda.current_stream(device).cuda_stream)
+        if host_pending and self._bounce_resolve(ck, host_pending, resolved, device, stream):
+            return resolved, device, stream
         # host arrays: one temporary device buffer per distinct array object
         staged: dict[int, DeviceBuffer] = {}
         for name, arr in host_pending:
@@ -440,6 +467,65 @@ class CudaRuntime:
             resolved[name] = _Arg(buf.ptr, device, keep=arr, host=arr if name in ck.writes else None,
                                   dev_buf=buf)
         return resolved, device, stream
+
+    # -- small host arrays: one pinned bounce buffer ----------------------------------
+    BOUNCE_MAX_BYTES = 4 << 20   # host arrays up to this total go through the bounce buffer
+    _BOUNCE_ALIGN = 256
+
+    def _bounce_resolve(self, ck: Any, host_pending: list[tuple[str, np.ndarray]], resolved: dict[str, _Arg],
+                        device: int, stream: int) -> bool:
+        """Pack the distinct host arrays into the device's pinned bounce buffer and copy them in
+        with ONE asynchronous copy (instead of a synchronous copy per array).  False when they
+        are too large: the caller stages them one by one."""
+        distinct: dict[int, np.ndarray] = {}
+        for _name, arr in host_pending:
+            distinct.setdefault(id(arr), arr)
+        al = self._BOUNCE_ALIGN
+        total = sum(-(-max(a.nbytes, 1) // al) * al for a in distinct.values())
+        if total > self.BOUNCE_MAX_BYTES:
+            return False
+        bb = self._bounce.get(device)
+        if bb is None or bb.nbytes < total:
+            if bb is not None:
+                cuda_ext.check(self.lib().eas_stream_synchronize(stream), "bounce resize")
+                bb.free()
+            bb = self._bounce[device] = _Bounce(max(64 << 10, 1 << (total - 1).bit_length()), device)
+        offs: dict[int, int] = {}
+        cur = 0
+        for key, arr in distinct.items():
+            n = arr.nbytes
+            if n:
+                bb.view[cur:cur + n] = arr.reshape(-1).view(np.uint8)
+            offs[key] = cur
+            cur += -(-max(n, 1) // al) * al
+        cuda_ext.check(self.lib().eas_copy_from_host_async(bb.dev.ptr, bb.host_ptr, cur, stream), "copy in")
+        for name, arr in host_pending:
+            o = offs[id(arr)]
+            resolved[name] = _Arg(bb.dev.ptr + o, device, keep=arr, host=arr if name in ck.writes else None,
+                                  bounce=o)
+        return True
+
+    def _finish_host_copies(self, host_args: list[_Arg], device: int, stream: int) -> None:
+        """After the launch: copy written host arrays back (one asynchronous copy per array through
+        the bounce buffer, or a synchronous copy per staged buffer), wait once, unpack."""
+        lib = self.lib()
+        bb = self._bounce.get(device)
+        out: dict[int, _Arg] = {}
+        for a in host_args:
+            if a.host is not None and id(a.host) not in out:
+                out[id(a.host)] = a
+        for a in out.values():
+            if a.bounce is not None and a.host.nbytes:
+                cuda_ext.check(lib.eas_copy_to_host_async(bb.host_ptr + a.bounce, bb.dev.ptr + a.bounce, a.host.nbytes,
+                                                          stream), "copy out")
+        cuda_ext.check(lib.eas_stream_synchronize(stream), "kernel execution")
+        self._check_native_status(device)
+        for a in out.values():
+            if a.bounce is not None:
+                if a.host.nbytes:
+                    a.host.reshape(-1).view(np.uint8)[:] = bb.view[a.bounce:a.bounce + a.host.nbytes]
+            else:
+                a.dev_buf.copy_to_host(a.host, stream)
 
     # -- host staging buffers ----------------------------------------------------------
     def _stage(self, device: int, nbytes: int) -> DeviceBuffer:
@@ -503,7 +589,7 @@ class CudaRuntime:
             self._run_pipelined(ck, runtime_args, geo, hosts)
             return
         args, device, stream = self._resolve(ck, runtime_args)
-        host_copies = [(a.dev_buf, a.host) for a in args.values() if a.host is not None]
+        host_copies = [a for a in args.values() if a.host is not None]
         lib = self.lib()
         capturing = cuda_ext.ctypes.c_int(0)
         if stream:
@@ -516,13 +602,7 @@ class CudaRuntime:
             return
         self._dispatch(ck, runtime_args, args, device, stream, *geo)
         if sync or host_copies:
-            cuda_ext.check(lib.eas_stream_synchronize(stream), "kernel execution")
-            self._check_native_status(device)
-            done: set[int] = set()
-            for buf, arr in host_copies:
-                if id(arr) not in done:
-                    buf.copy_to_host(arr, stream)
-                    done.add(id(arr))
+            self._finish_host_copies(host_copies, device, stream)
             self._unstage(args)
             return
         # asynchronous launch: keep the arguments alive until a completion event covers it.
@@ -758,7 +838,7 @@ class CudaRuntime:
         for name, e in (buffer_base or {}).items():
             item = 4 if next(a for a in ck.ir.args if a.name == name).dtype == DType.F32 else 2
             args[name].ptr -= int(e) * item
-        host_copies = [(a.dev_buf, a.host) for a in args.values() if a.host is not None]
+        host_copies = [a for a in args.values() if a.host is not None or a.bounce is not None]
         if host_copies:
             raise ValueError("run_range needs device buffers (torch CUDA tensors or eas.Tensor on cuda)")
         native = getattr(ck.plan, "native", None)

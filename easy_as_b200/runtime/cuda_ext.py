@@ -58,6 +58,8 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "eas_copy_from_host_async": (_int, [_vp, _vp, _sz, _vp]),
     "eas_copy_to_host_async": (_int, [_vp, _vp, _sz, _vp]),
     "eas_host_is_pinned": (_int, [_vp, _PINT]),
+    "eas_alloc_pinned": (_int, [_sz, ctypes.POINTER(ctypes.c_void_p)]),
+    "eas_free_pinned": (_int, [_vp]),
     "eas_stream_wait_event": (_int, [_vp, _vp]),
     "eas_stream_synchronize": (_int, [_vp]),
     "eas_device_synchronize": (_int, [_int]),

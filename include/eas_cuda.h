@@ -107,6 +107,13 @@ int eas_copy_from_host_async(void* dst, const void* src, size_t nbytes, void* st
 int eas_copy_to_host_async(void* dst, const void* src, size_t nbytes, void* stream);
 /* *pinned = 1 when `ptr` lies in page-locked host memory known to CUDA. */
 int eas_host_is_pinned(const void* ptr, int* pinned);
+/* Page-locked host memory (cudaHostAlloc, portable), for the runtime's bounce
+ * buffer of small host-array launches: one asynchronous copy each way instead
+ * of a synchronous copy per array (the reference passes host arrays to Metal
+ * through temporary shared MTLBuffers, eas/runtime/metal.py:209-232
+ * and :335-345). */
+int eas_alloc_pinned(size_t nbytes, void** out);
+int eas_free_pinned(void* p);
 
 /* ---- synchronisation (replaces synchronize / queue_synchronize,
  *      _metal.mm:1397-1434) ------------------------------------------------ */
