@@ -1,7 +1,7 @@
 """Generate tests/golden/reference_ir.json(.gz) from the reference front end.
 
-Run in a checkout that has the reference at $EAS_REFERENCE (default
-/root/reference):
+Run where the reference checkout is readable (its location in
+$EAS_REFERENCE, else the default below):
 
     python tests/golden/make_golden.py
 
