@@ -168,6 +168,46 @@ def shard(n_total: int, block: int, world: int, rank: int) -> tuple[int, int]:
     return p0 * block, min(p1 * block, n_total)
 
 
+def bench_gather(c, n_total: int, world: int, rank: int) -> dict:
+    """The optional collective of the sharded path, reported beside the kernel numbers: the C2
+    output slices gathered into one tensor on rank 0 (``easy_as_b200.shard.gather``: batched NCCL
+    send/recv over NVLink/NVSwitch), checked against each rank's slice, timed from a barrier to
+    the last rank's completion (max over ranks)."""
+    import torch
+    import torch.distributed as dist
+
+    from easy_as_b200.shard import gather
+
+    counts = [hi - lo for lo, hi in (shard(n_total, BLOCK, world, r) for r in range(world))]
+    full = torch.empty(n_total, device="cuda") if rank == 0 else None
+    gather(c, full, counts, dst=0)                       # warm-up (NCCL connections)
+    torch.cuda.synchronize()
+    reps = 3
+    barrier(world)
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        gather(c, full, counts, dst=0)
+    torch.cuda.synchronize()
+    dt = max_over_ranks((time.perf_counter() - t0) / reps, world)
+    # exact check: every slice's bit pattern summed as int64, against the same ranges of `full`
+    mine = c.view(torch.int32).to(torch.int64).sum().reshape(1)
+    sums = [torch.zeros(1, dtype=torch.int64, device="cuda") for _ in range(world)]
+    dist.all_gather(sums, mine)
+    ok = True
+    if rank == 0:
+        off = 0
+        for r, n in enumerate(counts):
+            got = full[off:off + n].view(torch.int32).to(torch.int64).sum()
+            ok = ok and bool(got == sums[r][0])
+            off += n
+    moved = 4 * (n_total - counts[0])
+    del full
+    return {"bytes_into_rank0": moved, "ms": round(dt * 1e3, 3), "GBs_into_rank0": round(moved / dt / 1e9, 1),
+            "checked_rank0": ok,
+            "how": "easy_as_b200.shard.gather (batched NCCL send/recv) of the C2 output slices to rank 0; "
+                   "wall clock from a barrier, synchronised, max over ranks"}
+
+
 def make_add_kernel():
     import eas
     from eas import mk
@@ -658,6 +698,10 @@ def run_eas(args) -> None:
     gbs = BYTES_PER_ELEM * args.n / (ms_max * 1e-3) / 1e9
     kernel_gbs_local = BYTES_PER_ELEM * n / (ms * 1e-3) / 1e9
 
+    gather_res = None
+    if world > 1 and not args.quick:
+        gather_res = bench_gather(c, args.n, world, rank)
+
     # end to end through the public API with pinned host buffers
     e2e = None
     if not args.quick:
@@ -725,6 +769,8 @@ def run_eas(args) -> None:
         "gpu_launches": launches,
         "clocks": clk.summary(),
     }
+    if gather_res is not None:
+        line["gather"] = gather_res
     if gemm:
         line["gemm"] = gemm
     if tiled is not None:

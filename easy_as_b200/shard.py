@@ -65,7 +65,7 @@ def run_shard(kernel: Any, *args: Any, _rank: int, _world: int, _axis: int = 0,
 def gather(local: Any, out: Any | None, counts: Sequence[int], *, dst: int = 0, group: Any = None) -> Any:
     """Concatenate every rank's 1-D ``local`` slice (rank order) into ``out`` on rank ``dst``.
 
-    ``counts[r]`` is the number of elements rank ``r`` holds.  Uses batched
+    ``counts[r]`` is the number of elements rank ``r`` holds.  Every rank uses batched
     point-to-point send/recv, which NCCL runs over NVLink/NVSwitch.
     """
     import torch.distributed as dist
@@ -77,8 +77,9 @@ def gather(local: Any, out: Any | None, counts: Sequence[int], *, dst: int = 0, 
     if int(local.numel()) != int(counts[rank]):
         raise ValueError(f"rank {rank} holds {local.numel()} elements, counts says {counts[rank]}")
     if rank != dst:
-        if counts[rank]:
-            dist.send(local.contiguous(), dst, group=group)
+        if counts[rank]:  # batched like the receives, so NCCL does not serialise it with other ops
+            for w in dist.batch_isend_irecv([dist.P2POp(dist.isend, local.contiguous(), dst, group=group)]):
+                w.wait()
         return None
     if out is None or int(out.numel()) != int(sum(counts)):
         raise ValueError("out on the destination rank must hold sum(counts) elements")
