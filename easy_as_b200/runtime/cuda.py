@@ -384,8 +384,8 @@ class CudaRuntime:
         return self.pipeline(ck.src, plan.kernel_name, device, plan.dyn_smem)
 
     # -- arguments ---------------------------------------------------------------------
-    def _resolve(self, ck: Any, runtime_args: Mapping[str, Any], *, allow_host: bool = True
-                 ) -> tuple[dict[str, _Arg], int, int]:
+    def _resolve(self, ck: Any, runtime_args: Mapping[str, Any], *, allow_host: bool = True,
+                 allow_bounce: bool = True) -> tuple[dict[str, _Arg], int, int]:
         torch = _torch()
         resolved: dict[str, _Arg] = {}
         device: int | None = None
@@ -454,7 +454,7 @@ class CudaRuntime:
         if torch_stream and torch is not None:
             raw = getattr(torch._C, "_cuda_getCurrentRawStream", None)
             stream = int(raw(device)) if raw is not None else int(torch.cuda.current_stream(device).cuda_stream)
-        if host_pending and self._bounce_resolve(ck, host_pending, resolved, device, stream):
+        if host_pending and allow_bounce and self._bounce_resolve(ck, host_pending, resolved, device, stream):
             return resolved, device, stream
         # host arrays: one temporary device buffer per distinct array object
         staged: dict[int, DeviceBuffer] = {}
@@ -834,11 +834,12 @@ class CudaRuntime:
         sub[axis] = hi - lo
         base = [0, 0, 0]
         base[axis] = lo
-        args, device, stream = self._resolve(ck, runtime_args)
+        # per-array staging: a range launch may stay in flight, so no shared bounce buffer
+        args, device, stream = self._resolve(ck, runtime_args, allow_bounce=False)
         for name, e in (buffer_base or {}).items():
             item = 4 if next(a for a in ck.ir.args if a.name == name).dtype == DType.F32 else 2
             args[name].ptr -= int(e) * item
-        host_copies = [a for a in args.values() if a.host is not None or a.bounce is not None]
+        host_copies = [a for a in args.values() if a.host is not None]
         if host_copies:
             raise ValueError("run_range needs device buffers (torch CUDA tensors or eas.Tensor on cuda)")
         native = getattr(ck.plan, "native", None)
