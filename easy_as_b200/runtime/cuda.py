@@ -588,7 +588,9 @@ class CudaRuntime:
         if hosts is not None:
             self._run_pipelined(ck, runtime_args, geo, hosts)
             return
-        args, device, stream = self._resolve(ck, runtime_args)
+        # the shared bounce buffer only serves calls that wait before returning: an asynchronous call
+        # could still be waiting for its copy when the next call refills the buffer
+        args, device, stream = self._resolve(ck, runtime_args, allow_bounce=sync)
         host_copies = [a for a in args.values() if a.host is not None]
         lib = self.lib()
         capturing = cuda_ext.ctypes.c_int(0)

@@ -263,3 +263,20 @@ def test_launch_error_raises_with_the_library_message(fake):
     a = np.ones(10, np.float32)
     with pytest.raises(cuda_ext.CudaError, match="fake launch failure"):
         _run(lib, rt, add_kernel, (a, a.copy(), np.zeros(10, np.float32), 10), BLOCK=32)
+
+
+def test_async_call_with_host_inputs_does_not_share_the_bounce_buffer(fake):
+    """A read-only host input with _sync=False is staged in its own buffer (kept alive by the
+    launch), never in the bounce buffer the next call refills."""
+    lib, rt = fake
+    n = 64
+    x = np.arange(n, dtype=np.float32)
+    y = np.zeros(n, np.float32)
+    ck = scale_kernel.compile(x, y, n, 2.0, BLOCK=64)
+    lib.current = ck
+    import torch
+
+    out = torch.zeros(n)          # CPU tensor: written, so this call still syncs and copies back
+    rt.run(ck, {"x": x, "y": out.numpy(), "N": n, "alpha": 2.0}, {"BLOCK": 64}, sync=False)
+    assert not any(k[0] == "h2d_async" for k in lib.calls)
+    assert np.array_equal(out.numpy(), x * 2)
