@@ -71,9 +71,9 @@ def fma_f32(a: np.ndarray, b: np.ndarray, c: np.ndarray) -> np.ndarray:
     ``e`` decides.
     """
     a, b, c = (np.asarray(x, dtype=F32) for x in (a, b, c))
-    p = a.astype(F64) * b.astype(F64)
     cc = c.astype(F64)
     with np.errstate(over="ignore", invalid="ignore"):
+        p = a.astype(F64) * b.astype(F64)
         s = p + cc
         bb = s - p
         e = (p - (s - bb)) + (cc - bb)
@@ -105,8 +105,9 @@ def cast(x: np.ndarray, src: str, dst: str) -> np.ndarray:
         return f2u(x)
     if dst == "f32":
         return x.astype(F32)  # u32 -> f32 and f16 -> f32: single rounding / exact
-    if dst == "f16":
-        return x.astype(F64).astype(F16) if src == "u32" else x.astype(F32).astype(F16)
+    if dst == "f16":  # beyond the f16 range the round-to-nearest result is +-inf, as intended
+        with np.errstate(over="ignore"):
+            return x.astype(F64).astype(F16) if src == "u32" else x.astype(F32).astype(F16)
     raise OracleError(f"bad cast {src}->{dst}")
 
 
