@@ -125,3 +125,83 @@ def inputs(seed: int, n: int) -> dict:
     h = rng.standard_normal(n).astype(np.float16)
     return {"x": x, "y": y, "h": h, "out": np.full(n, -7.0, np.float32), "outi": np.full(n, -7.0, np.float32),
             "N": n, "S": int(rng.integers(1, 1 << 31)), "alpha": float(np.float32(rng.standard_normal()))}
+
+
+# ---------------------------------------------------------------------------
+# thread-mode kernels: threadgroup memory, barriers, dot
+# ---------------------------------------------------------------------------
+
+
+def thread_kernel_source(seed: int) -> tuple[str, dict]:
+    """A kernel of NT threads per group: every thread fills distinct slots of two threadgroup
+    arrays (masked global loads and f32 expressions), then after a barrier reads other threads'
+    slots at permuted positions into an fma chain, optionally adds an ``mk.dot`` over the
+    arrays, optionally refills one array in a second phase, and stores one result per thread."""
+    r = random.Random(10_000 + seed)
+    nt = r.choice([32, 64, 128, 256])
+    ts = nt * r.choice([1, 2, 3]) + r.choice([0, 0, 5, 17])
+    reps = r.randint(1, 6)
+    g = _Gen(20_000 + seed)
+    lines = []
+    fill = []
+    for i in range(0, ts, nt):
+        src_idx = r.choice(["(pid * {ts} + t + {i}) % N", "(gi * {p} + {i}) % N"]).format(ts=ts, i=i, p=r.choice([3, 5]))
+        fill.append(f"    mk.store(sa, t + {i}, mk.load(x, {src_idx}, m2 & (t + {i} < {ts})), t + {i} < {ts})")
+        fill.append(f"    mk.store(sb, t + {i}, {r.choice(['a', 'b', 'a * b', 'mk.fma(a, alpha, b)', 'mk.to_f32(t + ' + str(i) + ')'])}, "
+                    f"t + {i} < {ts})")
+    chain = []
+    acc = g.f(1)
+    lines.extend(g.lines)
+    g.lines = []
+    for j in range(reps):
+        p_, q_ = r.choice([1, 3, 5, 7]), r.randint(0, ts - 1)
+        chain.append(f"    acc = mk.fma(mk.load(sa, (t * {p_} + {q_}) % {ts}), mk.load(sb, (t + {j * 13 + 1}) % {ts}), acc)")
+    if r.random() < 0.6:
+        k = r.randint(1, min(16, ts))
+        sa_stride = r.choice([1, 1, 2]) if ts >= 2 * k else 1
+        span_a = (k - 1) * sa_stride + 1
+        chain.append(f"    acc = acc + mk.dot(sa, t % {ts - span_a + 1}, {sa_stride}, sb, (t * 3) % {ts - k + 1}, 1, {k})")
+    second = []
+    if r.random() < 0.5:
+        second = ["    mk.barrier()"] + [f"    mk.store(sa, t + {i}, acc * {r.choice(['0.5', 'alpha', 'a'])}, t + {i} < {ts})"
+                                          for i in range(0, ts, nt)] + \
+                 ["    mk.barrier()", f"    acc = acc + mk.load(sa, (t * 7 + 3) % {ts})"]
+    body = "\n".join(lines)
+    src = f'''
+@eas.kernel
+def tfuzz_{seed}(x, y, out, N, S, alpha, NT: eas.constexpr):
+    t = mk.tid(0, NT)
+    pid = mk.program_id(0)
+    gi = pid * NT + t
+    m = gi < N
+    m2 = gi < N + 0
+    a = mk.load(x, gi, m)
+    b = mk.load(y, gi, m)
+    offs = gi
+    hv = a
+    sa = mk.alloc_tg({ts})
+    sb = mk.alloc_tg({ts})
+{chr(10).join(fill)}
+    mk.barrier()
+{body}
+    acc = {acc}
+{chr(10).join(chain)}
+{chr(10).join(second)}
+    mk.store(out, gi, acc, m)
+'''
+    return src, {"NT": nt}
+
+
+def make_thread(seed: int):
+    """(kernel, source, meta) for one seed."""
+    src, meta = thread_kernel_source(seed)
+    ns: dict = {"eas": eas, "mk": mk}
+    exec(compile(src, f"<tfuzz_{seed}>", "exec"), ns)
+    return ns[f"tfuzz_{seed}"], src, meta
+
+
+def thread_inputs(seed: int, n: int) -> dict:
+    rng = np.random.default_rng(50_000 + seed)
+    return {"x": rng.standard_normal(n).astype(np.float32), "y": rng.standard_normal(n).astype(np.float32),
+            "out": np.full(n, -7.0, np.float32), "N": n, "S": int(rng.integers(1, 1 << 20)),
+            "alpha": float(np.float32(rng.standard_normal()))}

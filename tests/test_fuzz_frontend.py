@@ -27,3 +27,13 @@ def test_fuzz_kernel_traces_lowers_and_runs(seed):
 def test_generator_is_deterministic():
     assert fuzz_kernels.kernel_source(7) == fuzz_kernels.kernel_source(7)
     assert fuzz_kernels.kernel_source(7) != fuzz_kernels.kernel_source(8)
+
+
+@pytest.mark.parametrize("seed", range(30))
+def test_thread_fuzz_kernel_traces_lowers_and_runs(seed):
+    k, src, meta = fuzz_kernels.make_thread(seed)
+    n = 500 + 11 * seed
+    args = fuzz_kernels.thread_inputs(seed, n)
+    ck = k.compile(*(args[a] for a in ("x", "y", "out", "N", "S", "alpha")), **meta)
+    assert ck.launch_mode == "thread", src
+    execute(ck.ir, dict(args), grid=(-(-n // meta["NT"]), 1, 1))

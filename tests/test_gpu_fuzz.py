@@ -37,3 +37,27 @@ def test_fuzz_kernel_bit_exact_vs_oracle(cuda_rt, seed):
         bad = np.nonzero((g != c) & ~both_nan)[0]
         assert bad.size == 0, (f"{buf}: {bad.size} of {n} differ, first at {bad[0]}: gpu {gpu[buf][bad[0]]!r} "
                                f"oracle {cpu[buf][bad[0]]!r}\n{src}")
+
+
+@pytest.mark.parametrize("seed", range(60))
+def test_thread_fuzz_kernel_bit_exact_vs_oracle(cuda_rt, seed):
+    """Thread-mode kernels (threadgroup memory, barriers, fma chains, mk.dot): bit-exact against the
+    oracle.  None of them is a GEMM, so the tiled-GEMM proof, which examines every thread-mode
+    kernel with fma or dot, must decline them all; a wrongly accepted kernel would show as a
+    mismatch here."""
+    k, src, meta = fuzz_kernels.make_thread(seed)
+    n = 700 + 29 * seed
+    gpu = fuzz_kernels.thread_inputs(seed, n)
+    cpu = fuzz_kernels.thread_inputs(seed, n)
+    names = ("x", "y", "out", "N", "S", "alpha")
+    grid = (-(-n // meta["NT"]), 1, 1)
+    before = cuda_rt.native_launches
+    k(*(gpu[a] for a in names), _grid=grid, **meta)
+    assert cuda_rt.native_launches == before, "a random thread kernel was launched as a native GEMM"
+    ck = k.compile(*(cpu[a] for a in names), **meta)
+    execute(ck.ir, dict(cpu), grid=grid)
+    g, c = gpu["out"].view(np.uint32), cpu["out"].view(np.uint32)
+    both_nan = np.isnan(gpu["out"]) & np.isnan(cpu["out"])
+    bad = np.nonzero((g != c) & ~both_nan)[0]
+    assert bad.size == 0, (f"{bad.size} of {n} differ, first at {bad[0]}: gpu {gpu['out'][bad[0]]!r} "
+                           f"oracle {cpu['out'][bad[0]]!r}\n{src}")
