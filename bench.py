@@ -237,6 +237,19 @@ def gemm_shard(name: str, world: int, rank: int) -> tuple[int, int, int, int]:
     return b1 - b0, M, N, K
 
 
+def last_gemm_config() -> str:
+    """The tile configuration the library's last GEMM launch used, as text."""
+    import ctypes
+
+    from easy_as_b200.runtime import cuda_ext
+
+    vals = [ctypes.c_int() for _ in range(5)]
+    cuda_ext.check(cuda_ext.load().eas_gemm_last_config(*(ctypes.byref(x) for x in vals)), "gemm config")
+    tm, tn, st, ks, pair = (x.value for x in vals)
+    kind = "tcgen05 cta_group::2 (CTA pair)" if pair else "tcgen05 cta_group::1"
+    return f"{kind}, tile {tm}x{tn}x64, {st} stages" + (f", split-K x{ks}" if ks > 1 else "")
+
+
 def gemm_e2e(name, a, b, c, M, N, K, batch, world, flops_total) -> dict:
     """The GEMM leg end to end through the public API with pinned host tensors: each step copies
     A, B and C in (C too: the runtime keeps the unwritten part of a host output intact), runs the
@@ -338,6 +351,7 @@ def run_gemm(name: str, args, world: int, rank: int, rt) -> dict:
             lib_tf = round(2.0 * batch * M * N * K / (l0.elapsed_time(l1) / steps * 1e-3) / 1e12, 1)
         except (TypeError, RuntimeError):
             lib_tf = None
+    kernel_desc = last_gemm_config()
     flops_total = 2.0 * tb * TM * TN * TK
     flops_local = 2.0 * batch * M * N * K
     e2e = None if args.quick else gemm_e2e(name, a, b, c, M, N, K, batch, world, flops_total)
@@ -347,8 +361,7 @@ def run_gemm(name: str, args, world: int, rank: int, rt) -> dict:
         "metric": "fp16 mk.dot GEMM TFLOP/s", "value": round(flops_total / (ms_max * 1e-3) / 1e12, 1),
         "unit": "TFLOP/s", "ms_per_step": round(ms_max, 4), "steps": steps,
         "config": {"workload": f"{name} batch={tb} M={TM} N={TN} K={TK} f16 in, f32 acc/out", "split": split,
-                   "kernel": ("tcgen05 cta_group::2 (CTA pair), tile 256x256x64, 6 stages" if tuned.get("BLOCK_N") == 256
-                              else "tcgen05 cta_group::1, tile 128x128x64, 6 stages"), "autotuned": tuned, "spot_check_rel_err": err},
+                   "kernel": kernel_desc, "autotuned": tuned, "spot_check_rel_err": err},
         "roofline": {"bound": "tensor", "achieved": round(local_tf, 1), "peak": pk["bf16_tflops"],
                      "unit": "TFLOP/s", "frac": round(local_tf / pk["bf16_tflops"], 4),
                      "peak_source": ("measured burst cuBLAS bf16 (MEASURED_PEAKS.json bf16_tflops)"

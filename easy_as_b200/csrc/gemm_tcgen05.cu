@@ -480,10 +480,10 @@ __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
-template <int kStages2, bool TMA_C>
+template <int kStages2, bool TMA_C, int NH = 1>
 struct Smem2 {
-  static constexpr int kABytes = 128 * BK * 2;   // this CTA's half of the A tile
-  static constexpr int kBBytes = 128 * BK * 2;   // this CTA's half of the B tile
+  static constexpr int kABytes = 128 * BK * 2;        // this CTA's half of the A tile
+  static constexpr int kBBytes = NH * 128 * BK * 2;   // this CTA's half of each 256-column B half
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kEpiOffset = kStages2 * kStageBytes;
   static constexpr int kEpiBytes = TMA_C ? 4 * 2 * 32 * 32 * 4 : 0;
@@ -491,7 +491,7 @@ struct Smem2 {
   static constexpr int kTotal = kBarOffset + (2 * kStages2 + 4) * 8 + 16 + 1024;
 };
 
-template <int kStages2, bool B_MN, bool TMA_C, bool TF = false>
+template <int kStages2, bool B_MN, bool TMA_C, bool TF = false, int NH = 1>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_f16_tcgen05_2sm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                                 const __grid_constant__ CUtensorMap map_c, float* __restrict__ c, int M, int N, int K,
@@ -499,11 +499,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                                 int ksplit) {
   static_assert(!(TF && B_MN), "tf32 operands are K-major here");
   constexpr int kBKe = TF ? 32 : BK;  // elements per 128-byte K row of a stage
-  using L = Smem2<kStages2, TMA_C>;
+  // NH = 2: 256 x 512 pair tiles (two 256-column halves, one MMA each per k step) in ONE 512-column
+  // accumulator, so the epilogue no longer overlaps the next tile's main loop, but each A tile
+  // feeds twice the columns (25 % fewer operand bytes per FLOP from L2)
+  static_assert(NH == 1 || NH == 2, "one or two 256-column halves per pair tile");
+  static_assert(!(TF && NH == 2), "wide tiles are f16 only");
+  using L = Smem2<kStages2, TMA_C, NH>;
   // split-K: work unit u is K part (u % ks) of tile (u / ks); parts after the first are summed into
   // C (zeroed by the host) with TMA reduce-adds, so only the TMA-store epilogue splits
   const int ks = TMA_C && ksplit > 1 ? ksplit : 1;
-  constexpr int BN = 256;
+  constexpr int BN = 256 * NH;       // columns of a pair tile
+  constexpr int NBUF = NH == 1 ? 2 : 1;  // TMEM accumulators (512 columns in all)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
@@ -517,7 +523,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const int lane = threadIdx.x & 31;
   uint32_t rank;
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
-  constexpr uint32_t kTmemCols = 2 * BN;  // 512: two accumulators of 128 lanes x 256 columns per CTA
+  constexpr uint32_t kTmemCols = 512;  // NBUF accumulators of 128 lanes x BN columns per CTA
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages2; ++s) {
@@ -578,11 +584,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           int ka = kb * kBKe, kbk = ka;
           if (TF && seg_kb) seg_coords(kb, seg_kb, ka, kbk);
           tma_load_3d_pair(sa, &map_a, fl, ka, m0, tc.b);
-          if (B_MN) {
-            tma_load_3d_pair(sb, &map_b, fl, n0, kb * BK, tc.b);
-            tma_load_3d_pair(sb + BK * 128, &map_b, fl, n0 + 64, kb * BK, tc.b);
-          } else {
-            tma_load_3d_pair(sb, &map_b, fl, kbk, n0, tc.b);
+#pragma unroll
+          for (int h = 0; h < NH; ++h) {  // this CTA's 128 columns of each 256-column half
+            uint8_t* sbh = sb + h * (128 * BK * 2);
+            if (B_MN) {
+              tma_load_3d_pair(sbh, &map_b, fl, n0 + 256 * h, kb * BK, tc.b);
+              tma_load_3d_pair(sbh + BK * 128, &map_b, fl, n0 + 256 * h + 64, kb * BK, tc.b);
+            } else {
+              tma_load_3d_pair(sbh, &map_b, fl, kbk, n0 + 256 * h, tc.b);
+            }
           }
           if (++s == kStages2) {
             s = 0;
@@ -593,57 +603,102 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     if (lane == 0 && rank == 0) {
-      constexpr uint32_t idesc = (1u << 4) | (TF ? kFmtTF32 : 0u) | ((B_MN ? 1u : 0u) << 16) | ((uint32_t)(BN >> 3) << 17) |
+      constexpr uint32_t idesc = (1u << 4) | (TF ? kFmtTF32 : 0u) | ((B_MN ? 1u : 0u) << 16) | ((uint32_t)(256 >> 3) << 17) |
                                  ((uint32_t)(256 >> 4) << 24);
       int s = 0;
       uint32_t ph = 0;
       int local = 0;
-      for (int u = cid; u < units && !*abort_flag; u += ncl, ++local) {
-        const int buf = local & 1;
-        const uint32_t acc_ph = (local >> 1) & 1;
-        if (!mbar_wait_cl(&acc_empty[buf], acc_ph ^ 1, abort_flag)) break;
-        tc_fence_after();
-        const uint32_t d_tmem = tmem_base + buf * BN;
-        bool ok = true;
-        int kb_lo, kb_hi;
-        k_range(u, kb_lo, kb_hi);
-        for (int kb = kb_lo; kb < kb_hi; ++kb) {
-          if (!mbar_wait(&full[s], ph, abort_flag)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t a_addr = smem_u32(smem + s * L::kStageBytes);
-          const uint32_t b_addr = a_addr + L::kABytes;
+      // MMAs of halves [h0, h1) of the stage in slot st at k-block kb
+      auto issue = [&](int st, int kb, int kb_lo, uint32_t d_tmem, int h0, int h1) {
+        const uint32_t a_addr = smem_u32(smem + st * L::kStageBytes);
+        const uint32_t b_addr = a_addr + L::kABytes;
 #pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk) {
-            const uint64_t adesc = smem_desc(a_addr + kk * 32, 16, 1024);
-            const uint64_t bdesc = B_MN ? smem_desc(b_addr + kk * 2048, BK * 128, 1024)
-                                        : smem_desc(b_addr + kk * 32, 16, 1024);
+        for (int kk = 0; kk < BK / 16; ++kk) {
+          const uint64_t adesc = smem_desc(a_addr + kk * 32, 16, 1024);
+#pragma unroll
+          for (int h = 0; h < NH; ++h) {  // one N = 256 MMA per half, into its 256 accumulator columns
+            if (h < h0 || h >= h1) continue;
+            const uint32_t bh = b_addr + h * (128 * BK * 2);
+            const uint64_t bdesc = B_MN ? smem_desc(bh + kk * 2048, BK * 128, 1024) : smem_desc(bh + kk * 32, 16, 1024);
+            const uint32_t dh = d_tmem + h * 256;
             if constexpr (TF)
               asm volatile(
                   "{\n\t.reg .pred p;\n\t"
                   "setp.ne.b32 p, %4, 0;\n\t"
-                  "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+                  "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(dh),
                   "l"(adesc), "l"(bdesc), "r"(idesc), "r"((kb != kb_lo || kk != 0) ? 1u : 0u)
                   : "memory");
             else
               asm volatile(
                   "{\n\t.reg .pred p;\n\t"
                   "setp.ne.b32 p, %4, 0;\n\t"
-                  "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+                  "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(dh),
                   "l"(adesc), "l"(bdesc), "r"(idesc), "r"((kb != kb_lo || kk != 0) ? 1u : 0u)
                   : "memory");
           }
-          asm volatile(
-              "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
-                  smem_u32(&empty[s])),
-              "h"((uint16_t)3)
-              : "memory");
-          if (++s == kStages2) {
-            s = 0;
-            ph ^= 1;
+        }
+      };
+      auto release = [&](int st) {
+        asm volatile(
+            "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+                smem_u32(&empty[st])),
+            "h"((uint16_t)3)
+            : "memory");
+      };
+      auto advance = [&]() {
+        if (++s == kStages2) {
+          s = 0;
+          ph ^= 1;
+        }
+      };
+      for (int u = cid; u < units && !*abort_flag; u += ncl, ++local) {
+        const int buf = NBUF == 2 ? (local & 1) : 0;
+        const uint32_t acc_ph = NBUF == 2 ? (local >> 1) & 1 : local & 1;
+        if (!mbar_wait_cl(&acc_empty[buf], acc_ph ^ 1, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * BN;
+        bool ok = true;
+        int kb_lo, kb_hi;
+        k_range(u, kb_lo, kb_hi);
+        int kb = kb_lo;
+        if constexpr (NH == 2) {
+          // the epilogue frees the accumulator by halves (acc_empty[0]: columns 0-255, [1]: 256-511):
+          // run half 0 of the first F k-blocks while the epilogue still drains half 1, holding
+          // those stages (F <= the ring depth, so the producer never waits on a held stage), then
+          // half 1 of the same stages once it is free
+          const int F = kb_hi - kb_lo < kStages2 ? kb_hi - kb_lo : kStages2;
+          const int s0 = s;
+          const uint32_t ph0 = ph;
+          for (int i = 0; i < F && ok; ++i) {
+            if (!mbar_wait(&full[s], ph, abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue(s, kb_lo + i, kb_lo, d_tmem, 0, 1);
+            advance();
           }
+          if (ok && !mbar_wait_cl(&acc_empty[1], acc_ph ^ 1, abort_flag)) ok = false;
+          if (!ok) break;
+          tc_fence_after();
+          s = s0;
+          ph = ph0;
+          for (int i = 0; i < F; ++i) {
+            issue(s, kb_lo + i, kb_lo, d_tmem, 1, 2);
+            release(s);
+            advance();
+          }
+          kb = kb_lo + F;
+        }
+        for (; kb < kb_hi; ++kb) {
+          if (!mbar_wait(&full[s], ph, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue(s, kb, kb_lo, d_tmem, 0, NH);
+          release(s);
+          advance();
         }
         if (!ok) break;
         asm volatile(
@@ -661,8 +716,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const uint32_t acc_empty_leader[2] = {mapa_rank(smem_u32(&acc_empty[0]), 0), mapa_rank(smem_u32(&acc_empty[1]), 0)};
     int local = 0;
     for (int u = cid; u < units && !*abort_flag; u += ncl, ++local) {
-      const int buf = local & 1;
-      const uint32_t acc_ph = (local >> 1) & 1;
+      const int buf = NBUF == 2 ? (local & 1) : 0;
+      const uint32_t acc_ph = NBUF == 2 ? (local >> 1) & 1 : local & 1;
       if (!mbar_wait(&acc_full[buf], acc_ph, abort_flag)) break;
       tc_fence_after();
       const TileCoord tc = sched.at(u / ks);
@@ -674,6 +729,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       for (int cc = 0; cc < BN / 32; ++cc) {
         uint32_t r[32];
         tmem_ld32(tmem_base + buf * BN + cc * 32 + ((uint32_t)(q * 32) << 16), r);
+        if (NH == 2 && cc == 256 / 32 - 1) {  // columns 0-255 are in registers: half 0 is free
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0)
+            asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(acc_empty_leader[0])
+                         : "memory");
+        }
         const int nb = n0 + cc * 32;
         if (TMA_C) {
           if (nb < N && mrow0 < M) {
@@ -714,8 +776,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0)
-        asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(acc_empty_leader[buf])
+      if (lane == 0)  // NH == 2: half 1 (barrier 1); otherwise the whole accumulator `buf`
+        asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(
+                         acc_empty_leader[NH == 2 ? 1 : buf])
                      : "memory");
     }
     if (TMA_C && lane == 0) bulk_wait_all0();
@@ -750,6 +813,12 @@ int encode_map(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uin
   return eas_drv_check(r, "cuTensorMapEncodeTiled", EAS_ERR_VALUE);
 }
 
+// Tile configuration of the most recent GEMM launch in this process (reporting only).
+struct LastConfig {
+  int bm, bn, stages, ksplit, pair;
+};
+LastConfig g_last_config = {0, 0, 0, 0, 0};
+
 // The dynamic shared-memory opt-in is a per-function, per-device setting: make it once per kernel
 // instantiation and device instead of on every launch.
 template <auto Kern>
@@ -773,6 +842,7 @@ int launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorM
   if (rc) return rc;
   const long long tiles = (long long)((M + BM - 1) / BM) * ((N + BN - 1) / BN) * batch;
   const int grid = (int)(tiles < num_sms ? tiles : num_sms);
+  g_last_config = {BM, BN, STAGES, 1, 0};
   kern<<<grid, kThreads, L::kTotal, stream>>>(ma, mb, mc, c, M, N, K, batch, ldc, cbs, status, seg_kb);
   return eas_cuda_check(cudaGetLastError(), "gemm: launch", EAS_ERR_LAUNCH);
 }
@@ -797,15 +867,16 @@ int choose_ksplit(long long tiles, long long pairs, int kblocks, int batch) {
   return (int)ks;
 }
 
-template <int STAGES, bool B_MN, bool TMA_C, bool TF = false>
+template <int STAGES, bool B_MN, bool TMA_C, bool TF = false, int NH = 1>
 int launch_2sm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, float* c, int M, int N, int K,
                int batch, long long ldc, long long cbs, int* status, cudaStream_t stream, int num_sms, int seg_kb = 0) {
-  using L = Smem2<STAGES, TMA_C>;
-  auto kern = gemm_f16_tcgen05_2sm_kernel<STAGES, B_MN, TMA_C, TF>;
-  int rc = set_smem_once<gemm_f16_tcgen05_2sm_kernel<STAGES, B_MN, TMA_C, TF>>(L::kTotal,
+  using L = Smem2<STAGES, TMA_C, NH>;
+  static_assert(L::kTotal <= 232448, "shared memory over the 227 KB per-CTA limit");
+  auto kern = gemm_f16_tcgen05_2sm_kernel<STAGES, B_MN, TMA_C, TF, NH>;
+  int rc = set_smem_once<gemm_f16_tcgen05_2sm_kernel<STAGES, B_MN, TMA_C, TF, NH>>(L::kTotal,
                                                                              "gemm(2sm): set smem attribute");
   if (rc) return rc;
-  const long long tiles = (long long)((M + 255) / 256) * ((N + 255) / 256) * batch;
+  const long long tiles = (long long)((M + 255) / 256) * ((N + 256 * NH - 1) / (256 * NH)) * batch;
   // persistent grid: only as many pairs as can be resident at once (GPC boundaries can leave SMs unpaired)
   static int resident_pairs[2][64] = {{0}};
   const int which = TMA_C ? 1 : 0;
@@ -836,8 +907,26 @@ int launch_2sm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& 
   }
   const long long units = tiles * ksplit;
   const int grid = 2 * (int)(units < pairs ? units : pairs);
+  g_last_config = {256, 256 * NH, STAGES, ksplit, 1};
   kern<<<grid, kThreads, L::kTotal, stream>>>(ma, mb, mc, c, M, N, K, batch, ldc, cbs, status, seg_kb, ksplit);
   return eas_cuda_check(cudaGetLastError(), "gemm(2sm): launch", EAS_ERR_LAUNCH);
+}
+
+// 256 x 512 pair tiles read 25 % fewer operand bytes from L2 per FLOP than 256 x 256 ones but
+// keep one accumulator (no epilogue overlap) and halve the tile count.  Taken when they need no
+// more tile-rounds of work over the CTA pairs: 2 * ceil(wide tiles / pairs) <= ceil(tiles / pairs)
+// (C4 8192^3: 512 wide tiles = 7 rounds vs 1024 = 14; M = N = 768: 6 wide tiles pay a half-empty
+// column of tiles and lose).  EAS_GEMM_WIDE=0 / 1 forces the choice.
+bool use_wide(uint32_t M, uint32_t N, uint32_t batch, int num_sms) {
+  static const int forced = [] {
+    const char* e = getenv("EAS_GEMM_WIDE");
+    return e && (e[0] == '0' || e[0] == '1') ? e[0] - '0' : -1;
+  }();
+  if (forced >= 0) return forced == 1;
+  const long long pairs = num_sms / 2 > 0 ? num_sms / 2 : 1;
+  const long long mt = (M + 255) / 256;
+  const long long t1 = mt * ((N + 255) / 256) * batch, t2 = mt * ((N + 511) / 512) * batch;
+  return 2 * ((t2 + pairs - 1) / pairs) <= (t1 + pairs - 1) / pairs;
 }
 
 bool use_2sm(int block_n, uint32_t M) {
@@ -969,6 +1058,10 @@ int gemm_entry(const char* who, const void* a, const void* b, float* c, uint32_t
                  : launch_variant<128, 6, false, false, true>(ma, mb, mc, c, M, N, k_run, batch, ldc_l, cbs, status, s,
                                                               num_sms, seg_kb);
   } else {
+    if (pair && tma_c && N >= 512 && use_wide(M, N, batch, num_sms)) {  // 256 x 512 pair tiles
+      return b_mn ? launch_2sm<4, true, true, false, 2>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s, num_sms)
+                  : launch_2sm<4, false, true, false, 2>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s, num_sms);
+    }
     if (pair) {
       if (!tma_c)  // C not TMA-storable: direct stores, and the smem freed by the staging boxes buys a 7th stage
         return b_mn ? launch_2sm<7, true, false>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s, num_sms)
@@ -983,6 +1076,16 @@ int gemm_entry(const char* who, const void* a, const void* b, float* c, uint32_t
 }
 
 }  // namespace
+
+extern "C" int eas_gemm_last_config(int* tile_m, int* tile_n, int* stages, int* ksplit, int* pair) {
+  if (!tile_m || !tile_n || !stages || !ksplit || !pair) return eas_fail(EAS_ERR_VALUE, "eas_gemm_last_config: null");
+  *tile_m = g_last_config.bm;
+  *tile_n = g_last_config.bn;
+  *stages = g_last_config.stages;
+  *ksplit = g_last_config.ksplit;
+  *pair = g_last_config.pair;
+  return EAS_OK;
+}
 
 extern "C" int eas_gemm_f16(const void* a, const void* b, float* c, uint32_t M, uint32_t N, uint32_t K,
                             uint32_t batch, uint64_t lda, uint64_t a_bstride, uint64_t ldb, uint64_t b_bstride,

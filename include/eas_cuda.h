@@ -198,6 +198,12 @@ int eas_cast_f32_f16_2d(const float* src, void* dst, uint32_t rows, uint32_t col
  * Nothing faults or hangs; the context stays usable.  Asynchronous. */
 int eas_wait_selftest(long long budget_cycles, void* stream);
 
+/* Tile configuration the most recent eas_gemm_* launch in this process used:
+ * output tile (tile_m x tile_n per CTA, or per CTA pair when *pair is 1),
+ * pipeline stages and split-K parts.  Reporting only (no reference
+ * counterpart). */
+int eas_gemm_last_config(int* tile_m, int* tile_n, int* stages, int* ksplit, int* pair);
+
 /* Strided batched GEMM on tcgen05 with TF32 operands (kind::tf32, f32
  * accumulate): C[b][m][n] = sum_k A[b][m][k] * B[b][n][k] with A at
  * a + b*a_bstride + m*lda + k and B K-major at b + b*b_bstride + n*ldb + k
