@@ -329,6 +329,11 @@ class _Emitter:
             PRELUDE,
             f'extern "C" __global__ void __launch_bounds__({self.cuda_threads}, {self._min_blocks()}) {name}(',
             "    " + self.signature() + ") {",
+            # programmatic dependent launch: the next kernel in the stream may be scheduled from now on,
+            # and this one touches no memory before the previous grid has completed (both are no-ops
+            # for a launch without the attribute)
+            '    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");',
+            '    asm volatile("griddepcontrol.wait;" ::: "memory");',
             *body,
             "}",
             "",

@@ -16,6 +16,7 @@ struct DriverApi {
   decltype(&::cuGetErrorString) getErrorString = nullptr;
   decltype(&::cuTensorMapEncodeTiled) tensorMapEncodeTiled = nullptr;
   decltype(&::cuFuncGetParamInfo) funcGetParamInfo = nullptr;  // optional (driver >= 12.4)
+  decltype(&::cuLaunchKernelEx) launchKernelEx = nullptr;      // optional: programmatic dependent launch
 };
 extern DriverApi g_drv;
 

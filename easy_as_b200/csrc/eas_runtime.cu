@@ -165,6 +165,7 @@ int eas_driver_init() {
       return;
     }
     fetch("cuFuncGetParamInfo", g_drv.funcGetParamInfo);
+    fetch("cuLaunchKernelEx", g_drv.launchKernelEx);
     g_drv_status = EAS_OK;
   });
   if (g_drv_status != EAS_OK) return eas_fail(g_drv_status, "%s", g_drv_error.c_str());
@@ -408,8 +409,9 @@ extern "C" int eas_pipeline_attrs(void* pipeline, int* num_regs, int* static_sme
   return rc ? EAS_ERR_VALUE : EAS_OK;
 }
 
-extern "C" int eas_launch(void* pipeline, const uint32_t grid[3], const uint32_t block[3], uint32_t dyn_smem,
-                          void* stream, const void* params, const uint32_t* offsets, uint32_t nparams) {
+namespace {
+int launch_impl(bool pdl, void* pipeline, const uint32_t grid[3], const uint32_t block[3], uint32_t dyn_smem,
+                void* stream, const void* params, const uint32_t* offsets, uint32_t nparams) {
   if (!pipeline || !grid || !block) return eas_fail(EAS_ERR_VALUE, "eas_launch: null argument");
   if (nparams && (!params || !offsets)) return eas_fail(EAS_ERR_VALUE, "eas_launch: null parameter block");
   if (nparams > 256) return eas_fail(EAS_ERR_VALUE, "eas_launch: %u parameters (max 256)", nparams);
@@ -424,9 +426,40 @@ extern "C" int eas_launch(void* pipeline, const uint32_t grid[3], const uint32_t
   if (grid[0] == 0 || grid[1] == 0 || grid[2] == 0) return EAS_OK;
   void* argv[256];
   for (uint32_t i = 0; i < nparams; ++i) argv[i] = const_cast<char*>(static_cast<const char*>(params) + offsets[i]);
+  if (pdl && g_drv.launchKernelEx) {
+    // programmatic stream serialisation: the grid may be scheduled while the previous kernel in the
+    // stream finishes; the kernel's griddepcontrol.wait holds it until that grid has completed
+    CUlaunchAttribute attr[1];
+    attr[0].id = CU_LAUNCH_ATTRIBUTE_PROGRAMMATIC_STREAM_SERIALIZATION;
+    attr[0].value.programmaticStreamSerializationAllowed = 1;
+    CUlaunchConfig cfg = {};
+    cfg.gridDimX = grid[0];
+    cfg.gridDimY = grid[1];
+    cfg.gridDimZ = grid[2];
+    cfg.blockDimX = block[0];
+    cfg.blockDimY = block[1];
+    cfg.blockDimZ = block[2];
+    cfg.sharedMemBytes = dyn_smem;
+    cfg.hStream = (CUstream)stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    CUresult r = g_drv.launchKernelEx(&cfg, p->fn, nparams ? argv : nullptr, nullptr);
+    return eas_drv_check(r, "cuLaunchKernelEx", EAS_ERR_LAUNCH);
+  }
   CUresult r = g_drv.launchKernel(p->fn, grid[0], grid[1], grid[2], block[0], block[1], block[2], dyn_smem,
                                   (CUstream)stream, nparams ? argv : nullptr, nullptr);
   return eas_drv_check(r, "cuLaunchKernel", EAS_ERR_LAUNCH);
+}
+}  // namespace
+
+extern "C" int eas_launch(void* pipeline, const uint32_t grid[3], const uint32_t block[3], uint32_t dyn_smem,
+                          void* stream, const void* params, const uint32_t* offsets, uint32_t nparams) {
+  return launch_impl(false, pipeline, grid, block, dyn_smem, stream, params, offsets, nparams);
+}
+
+extern "C" int eas_launch_pdl(void* pipeline, const uint32_t grid[3], const uint32_t block[3], uint32_t dyn_smem,
+                              void* stream, const void* params, const uint32_t* offsets, uint32_t nparams) {
+  return launch_impl(true, pipeline, grid, block, dyn_smem, stream, params, offsets, nparams);
 }
 
 // ---------------------------------------------------------------------------

@@ -255,6 +255,7 @@ class CudaRuntime:
         self._max_in_flight: int | None = None
         self._staging: dict[tuple[int, int], list[DeviceBuffer]] = {}
         self._bounce: dict[int, _Bounce] = {}
+        self._pdl_on: bool | None = None
         self._bucket_keep: list[Any] = []
         self._pending_n = 0
         self._bucket_n = 0
@@ -322,6 +323,12 @@ class CudaRuntime:
         if t is not None and t.cuda.is_available() and t.cuda.is_initialized():
             return int(t.cuda.current_device())
         return int(os.environ.get("EAS_DEVICE", "0"))
+
+    def _pdl(self) -> bool:
+        """EAS_PDL: launch generated kernels with programmatic dependent launch (see eas_launch_pdl)."""
+        if self._pdl_on is None:
+            self._pdl_on = os.environ.get("EAS_PDL", "1") not in ("0", "off", "")
+        return self._pdl_on
 
     def _max_flight(self) -> int:
         if self._max_in_flight is None:
@@ -564,7 +571,8 @@ class CudaRuntime:
                           "eas_pid_z": pid_base[2] + z0}
                 blob = layout.pack(runtime_args, ptrs, hidden)
                 g = (cuda_ext.ctypes.c_uint32 * 3)(gx, min(MAX_GRID_YZ, gy - y0), min(MAX_GRID_YZ, gz - z0))
-                cuda_ext.check(lib.eas_launch(pipe, g, block, plan.dyn_smem, stream, blob, layout.offsets, layout.count),
+                launch = lib.eas_launch_pdl if self._pdl() else lib.eas_launch
+                cuda_ext.check(launch(pipe, g, block, plan.dyn_smem, stream, blob, layout.offsets, layout.count),
                                f"launch {plan.kernel_name}")
                 self.launch_count += 1
 

@@ -49,6 +49,8 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "eas_pipeline_attrs": (_int, [_vp, _PINT, _PINT, _PINT]),
     "eas_launch": (_int, [_vp, ctypes.POINTER(_u32), ctypes.POINTER(_u32), _u32, _vp, _vp, ctypes.POINTER(_u32),
                           _u32]),
+    "eas_launch_pdl": (_int, [_vp, ctypes.POINTER(_u32), ctypes.POINTER(_u32), _u32, _vp, _vp, ctypes.POINTER(_u32),
+                          _u32]),
     "eas_alloc_buffer": (_int, [_int, _sz, ctypes.POINTER(_vp)]),
     "eas_free_buffer": (_int, [_vp]),
     "eas_copy_from_host": (_int, [_vp, _vp, _sz, _vp]),

@@ -88,6 +88,13 @@ int eas_pipeline_attrs(void* pipeline, int* num_regs, int* static_smem, int* max
  * eas_stream_synchronize / events. */
 int eas_launch(void* pipeline, const uint32_t grid[3], const uint32_t block[3], uint32_t dyn_smem,
                void* stream, const void* params, const uint32_t* offsets, uint32_t nparams);
+/* eas_launch with programmatic dependent launch: the grid may be scheduled
+ * while the previous kernel in the stream is finishing.  For kernels that begin
+ * with griddepcontrol.wait (every generated kernel does), which holds them until
+ * that grid has completed and its memory is visible; same arguments and errors
+ * as eas_launch (falls back to it when the driver lacks cuLaunchKernelEx). */
+int eas_launch_pdl(void* pipeline, const uint32_t grid[3], const uint32_t block[3], uint32_t dyn_smem,
+               void* stream, const void* params, const uint32_t* offsets, uint32_t nparams);
 
 /* ---- memory (replaces alloc_buffer / copy_from_host / copy_to_host,
  *      _metal.mm:262-455) -------------------------------------------------- */

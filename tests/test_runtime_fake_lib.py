@@ -150,6 +150,10 @@ class FakeLib:
         execute(ck.ir, args, grid=tuple(grid))
         return 0
 
+    def eas_launch_pdl(self, *args):
+        self.pdl_launches = getattr(self, "pdl_launches", 0) + 1
+        return self.eas_launch(*args)
+
     # streams, events, status
     def eas_stream_synchronize(self, stream):
         return 0
@@ -280,3 +284,22 @@ def test_async_call_with_host_inputs_does_not_share_the_bounce_buffer(fake):
     rt.run(ck, {"x": x, "y": out.numpy(), "N": n, "alpha": 2.0}, {"BLOCK": 64}, sync=False)
     assert not any(k[0] == "h2d_async" for k in lib.calls)
     assert np.array_equal(out.numpy(), x * 2)
+
+
+def test_generated_kernels_launch_with_pdl_by_default(fake, monkeypatch):
+    """Generated kernels begin with griddepcontrol.wait, and the runtime launches them with
+    programmatic dependent launch unless EAS_PDL=0."""
+    lib, rt = fake
+    n = 64
+    x = np.arange(n, dtype=np.float32)
+    y = np.zeros(n, np.float32)
+    ck = _run(lib, rt, scale_kernel, (x, y, n, 3.0), BLOCK=64)
+    assert "griddepcontrol.wait" in ck.src
+    assert getattr(lib, "pdl_launches", 0) == 1
+    from easy_as_b200.runtime.cuda import CudaRuntime
+
+    monkeypatch.setenv("EAS_PDL", "0")
+    rt2 = CudaRuntime()
+    rt2.default_device = lambda: 0
+    _run(lib, rt2, scale_kernel, (x, y, n, 3.0), BLOCK=64)
+    assert lib.pdl_launches == 1
