@@ -1,4 +1,4 @@
-// gemm_tcgen05.cu — native sm_100a kernel for the fp16 `mk.dot` GEMM pattern.
+// gemm_tcgen05.cu — native sm_100a tensor-core GEMMs for the `mk.dot` / `mk.mma` GEMM patterns.
 //
 // Computes the strided batched product the DSL expresses as one `mk.dot` per
 // output element (reference dot lowering: easy_as eas/codegen/msl.py:920-952,
@@ -22,6 +22,16 @@
 //               f32 stores to C, then release the accumulator buffer.
 // K, M and N tails are zero-filled by TMA (out-of-range box elements read 0),
 // so they add nothing to the sums; stores are masked to m < M, n < N.
+//
+// CTA-pair kernel (gemm_f16_tcgen05_2sm_kernel, cluster of 2,
+// tcgen05.mma.cta_group::2 with M = 256, N = 256): each CTA loads its half of A
+// and of every 256-column B half; the pair tile is 256 x 256 with two TMEM
+// accumulators (NH = 1), or 256 x 512 with one 512-column accumulator that the
+// epilogue frees by halves (NH = 2, taken when it adds no tile rounds).  Split-K
+// (launches that leave most pairs idle) sums K parts into a zeroed C with TMA
+// reduce-adds.  The same kernels run kind::tf32 on f32 operands (TF = true),
+// including the 3xTF32 mode, whose producer maps k-blocks onto [hi | lo] segments.
+// No TMA load uses cluster multicast: every CTA loads only what it keeps.
 //
 // Every mbarrier wait is bounded (clock64 budget).  On expiry the kernel sets
 // a shared abort flag, every role leaves its loop, TMEM is freed, and the
