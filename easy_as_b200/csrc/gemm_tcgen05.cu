@@ -240,10 +240,12 @@ template <int BN, int STAGES, bool B_MN, bool TMA_C, bool TF = false>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_f16_tcgen05_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                             const __grid_constant__ CUtensorMap map_c, float* __restrict__ c, int M, int N, int K,
-                            int batch, long long ldc, long long c_bstride, int* status, int seg_kb) {
+                            int batch, long long ldc, long long c_bstride, int* status, int seg_kb, int ksplit) {
   static_assert(!(TF && B_MN), "tf32 operands are K-major here");
   constexpr int kBKe = TF ? 32 : BK;  // elements per 128-byte K row of a stage
   using L = Smem<BN, STAGES, B_MN>;
+  // split-K as in the pair kernel: unit u is K part (u % ks) of tile (u / ks), summed into a zeroed C
+  const int ks = TMA_C && ksplit > 1 ? ksplit : 1;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
@@ -287,16 +289,24 @@ __global__ void __launch_bounds__(kThreads, 1)
   sched.tiles_per_batch = sched.mt * sched.nt;
   sched.total = sched.tiles_per_batch * batch;
   const int kblocks = (K + kBKe - 1) / kBKe;
+  const int units = sched.total * ks;
+  auto k_range = [&](int u, int& kb0, int& kb1) {
+    const int part = u % ks;
+    kb0 = (int)((long long)part * kblocks / ks);
+    kb1 = (int)((long long)(part + 1) * kblocks / ks);
+  };
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
       int s = 0;
       uint32_t ph = 0;
-      for (int t = blockIdx.x; t < sched.total && !*abort_flag; t += gridDim.x) {
-        const TileCoord tc = sched.at(t);
+      for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
+        const TileCoord tc = sched.at(u / ks);
         const int n0 = tc.n0 * BN;
-        for (int kb = 0; kb < kblocks; ++kb) {
+        int kb_lo, kb_hi;
+        k_range(u, kb_lo, kb_hi);
+        for (int kb = kb_lo; kb < kb_hi; ++kb) {
           if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) break;
           uint8_t* sa = smem + s * L::kStageBytes;
           uint8_t* sb = sa + L::kABytes;
@@ -324,14 +334,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       int s = 0;
       uint32_t ph = 0;
       int local = 0;
-      for (int t = blockIdx.x; t < sched.total && !*abort_flag; t += gridDim.x, ++local) {
+      for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x, ++local) {
         const int buf = local & 1;
         const uint32_t acc_ph = (local >> 1) & 1;
         if (!mbar_wait(&acc_empty[buf], acc_ph ^ 1, abort_flag)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * BN;
         bool ok = true;
-        for (int kb = 0; kb < kblocks; ++kb) {
+        int kb_lo, kb_hi;
+        k_range(u, kb_lo, kb_hi);
+        for (int kb = kb_lo; kb < kb_hi; ++kb) {
           if (!mbar_wait(&full[s], ph, abort_flag)) {
             ok = false;
             break;
@@ -344,7 +356,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint64_t adesc = smem_desc(a_addr + kk * 32, 16, 1024);
             const uint64_t bdesc = B_MN ? smem_desc(b_addr + kk * 2048, BK * 128, 1024)
                                         : smem_desc(b_addr + kk * 32, 16, 1024);
-            tc_mma<TF>(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
+            tc_mma<TF>(d_tmem, adesc, bdesc, idesc, (kb != kb_lo || kk != 0) ? 1u : 0u);
           }
           tc_commit(&empty[s]);  // slot s is free once these MMAs have read it
           if (++s == STAGES) {
@@ -364,12 +376,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* boxes = smem + L::kEpiOffset + q * (2 * 32 * 32 * 4);
     int nbox = 0;  // boxes issued by this warp so far; box nbox & 1 is the next to fill
     int local = 0;
-    for (int t = blockIdx.x; t < sched.total && !*abort_flag; t += gridDim.x, ++local) {
+    for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x, ++local) {
       const int buf = local & 1;
       const uint32_t acc_ph = (local >> 1) & 1;
       if (!mbar_wait(&acc_full[buf], acc_ph, abort_flag)) break;
       tc_fence_after();
-      const TileCoord tc = sched.at(t);
+      const TileCoord tc = sched.at(u / ks);
       const int n0 = tc.n0 * BN;
       const int m = tc.m0 + q * 32 + lane;
       float* crow = c + (long long)tc.b * c_bstride + (long long)m * ldc;
@@ -393,7 +405,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             __syncwarp();
             if (lane == 0) {
-              tma_store_3d(&map_c, box, nb, tc.m0 + q * 32, tc.b);
+              if (ks > 1)
+                tma_reduce_add_3d(&map_c, box, nb, tc.m0 + q * 32, tc.b);
+              else
+                tma_store_3d(&map_c, box, nb, tc.m0 + q * 32, tc.b);
               bulk_commit();
             }
             ++nbox;
@@ -843,6 +858,37 @@ int set_smem_once(int bytes, const char* what) {
   return rc;
 }
 
+// Split-K for launches that leave most CTAs (1-SM kernel) or CTA pairs idle: with at most half as
+// many tiles as resident CTAs / pairs (`slots`), each tile's K range is cut into ks <= 4 parts (ks <= slots / tiles, at least 8
+// k-blocks per part) and the parts are summed into a zeroed C with TMA reduce-adds, so up to 4x
+// the CTAs work.  Launches with a tile per slot or more do not split: zeroing C and summing 4
+// partial tiles through L2 cost more than the last wave's idle pairs (measured on the per-GPU
+// shards of C4 at 8 GPUs, 128 tiles on 74 pairs: 1109 TFLOP/s split 4 ways vs 1215 unsplit).
+// The reduce-adds land in any order, so split results may differ from run to run in the last
+// bits; EAS_GEMM_SPLITK=0 turns splitting off.
+int choose_ksplit(long long tiles, long long slots, int kblocks, int batch) {
+  static const bool enabled = [] {
+    const char* e = getenv("EAS_GEMM_SPLITK");
+    return !(e && e[0] == '0');
+  }();
+  if (!enabled || slots <= 0 || tiles <= 0 || batch > 64 || 2 * tiles > slots) return 1;
+  long long ks = slots / tiles;
+  if (ks > 4) ks = 4;
+  while (ks > 1 && kblocks < 8 * ks) --ks;
+  return (int)ks;
+}
+
+// Zero C before a split launch: its K parts are summed into it.
+int zero_c_for_split(float* c, int M, int N, int batch, long long ldc, long long cbs, cudaStream_t stream) {
+  for (int b = 0; b < batch; ++b) {
+    int rc = eas_cuda_check(cudaMemset2DAsync(c + (long long)b * cbs, (size_t)ldc * 4, 0, (size_t)N * 4, (size_t)M,
+                                              stream),
+                            "gemm: zero C for split-K", EAS_ERR_LAUNCH);
+    if (rc) return rc;
+  }
+  return EAS_OK;
+}
+
 template <int BN, int STAGES, bool B_MN, bool TMA_C, bool TF = false>
 int launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, float* c, int M, int N, int K,
                    int batch, long long ldc, long long cbs, int* status, cudaStream_t stream, int num_sms, int seg_kb = 0) {
@@ -851,30 +897,16 @@ int launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorM
   int rc = set_smem_once<gemm_f16_tcgen05_kernel<BN, STAGES, B_MN, TMA_C, TF>>(L::kTotal, "gemm: set smem attribute");
   if (rc) return rc;
   const long long tiles = (long long)((M + BM - 1) / BM) * ((N + BN - 1) / BN) * batch;
-  const int grid = (int)(tiles < num_sms ? tiles : num_sms);
-  g_last_config = {BM, BN, STAGES, 1, 0};
-  kern<<<grid, kThreads, L::kTotal, stream>>>(ma, mb, mc, c, M, N, K, batch, ldc, cbs, status, seg_kb);
+  const int ksplit = TMA_C ? choose_ksplit(tiles, num_sms, (K + (TF ? 32 : BK) - 1) / (TF ? 32 : BK), batch) : 1;
+  if (ksplit > 1) {
+    rc = zero_c_for_split(c, M, N, batch, ldc, cbs, stream);
+    if (rc) return rc;
+  }
+  const long long units = tiles * ksplit;
+  const int grid = (int)(units < num_sms ? units : num_sms);
+  g_last_config = {BM, BN, STAGES, ksplit, 0};
+  kern<<<grid, kThreads, L::kTotal, stream>>>(ma, mb, mc, c, M, N, K, batch, ldc, cbs, status, seg_kb, ksplit);
   return eas_cuda_check(cudaGetLastError(), "gemm: launch", EAS_ERR_LAUNCH);
-}
-
-// Split-K for launches that leave most CTA pairs idle: with at most half as many 256x256 tiles as
-// resident pairs, each tile's K range is cut into ks <= 4 parts (ks <= pairs / tiles, at least 8
-// k-blocks per part) and the parts are summed into a zeroed C with TMA reduce-adds, so up to 4x
-// the pairs work.  Launches with a tile per pair or more do not split: zeroing C and summing 4
-// partial tiles through L2 cost more than the last wave's idle pairs (measured on the per-GPU
-// shards of C4 at 8 GPUs, 128 tiles on 74 pairs: 1109 TFLOP/s split 4 ways vs 1215 unsplit).
-// The reduce-adds land in any order, so split results may differ from run to run in the last
-// bits; EAS_GEMM_SPLITK=0 turns splitting off.
-int choose_ksplit(long long tiles, long long pairs, int kblocks, int batch) {
-  static const bool enabled = [] {
-    const char* e = getenv("EAS_GEMM_SPLITK");
-    return !(e && e[0] == '0');
-  }();
-  if (!enabled || pairs <= 0 || tiles <= 0 || batch > 64 || 2 * tiles > pairs) return 1;
-  long long ks = pairs / tiles;
-  if (ks > 4) ks = 4;
-  while (ks > 1 && kblocks < 8 * ks) --ks;
-  return (int)ks;
 }
 
 template <int STAGES, bool B_MN, bool TMA_C, bool TF = false, int NH = 1>
@@ -908,12 +940,8 @@ int launch_2sm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& 
   const long long pairs = resident_pairs[which][dev];
   const int ksplit = TMA_C ? choose_ksplit(tiles, pairs, (K + (TF ? 32 : BK) - 1) / (TF ? 32 : BK), batch) : 1;
   if (ksplit > 1) {  // the K parts are summed into C by TMA reduce-adds: start from zeros
-    for (int b = 0; b < batch; ++b) {
-      rc = eas_cuda_check(cudaMemset2DAsync(c + (long long)b * cbs, (size_t)ldc * 4, 0, (size_t)N * 4, (size_t)M,
-                                            stream),
-                          "gemm(2sm): zero C for split-K", EAS_ERR_LAUNCH);
-      if (rc) return rc;
-    }
+    rc = zero_c_for_split(c, M, N, batch, ldc, cbs, stream);
+    if (rc) return rc;
   }
   const long long units = tiles * ksplit;
   const int grid = 2 * (int)(units < pairs ? units : pairs);

@@ -1,4 +1,4 @@
-"""GPU: split-K in the CTA-pair tcgen05 GEMM.
+"""GPU: split-K in the tcgen05 GEMMs (CTA-pair kernel, and the 1-SM kernel that M <= 128 uses).
 
 Launches with at most half as many 256x256 tiles as CTA pairs split each tile's K range into
 2-4 parts, summed into a zeroed C with TMA reduce-adds.  The small and ragged launches here
@@ -15,7 +15,7 @@ from examples.matmul_dot_f16 import grid, matmul_dot_f16
 pytestmark = pytest.mark.gpu
 
 
-def _gemm(cuda_rt, batch, M, N, K, seed):
+def _gemm(cuda_rt, batch, M, N, K, seed, bn=256):
     import torch
 
     g = torch.Generator(device="cuda").manual_seed(seed)
@@ -23,18 +23,22 @@ def _gemm(cuda_rt, batch, M, N, K, seed):
     b = (torch.randn(batch, K, N, device="cuda", generator=g) / K ** 0.5).half()
     c = torch.full((batch, M, N), float("nan"), device="cuda")
     before = cuda_rt.native_launches
-    matmul_dot_f16(a.reshape(-1), b.reshape(-1), c.reshape(-1), M, N, K, BLOCK_M=128, BLOCK_N=256, BLOCK_K=64,
+    matmul_dot_f16(a.reshape(-1), b.reshape(-1), c.reshape(-1), M, N, K, BLOCK_M=128, BLOCK_N=bn, BLOCK_K=64,
                    _grid=grid(batch), _sync=True)
     assert cuda_rt.native_launches == before + 1
     return a, b, c
 
 
-@pytest.mark.parametrize("batch,M,N,K", [(1, 1024, 8192, 8192), (1, 2048, 8192, 8192), (1, 512, 512, 4096),
-                                         (2, 512, 768, 2048), (1, 700, 1000, 3000)])
-def test_split_k_matches_float64(cuda_rt, batch, M, N, K):
+@pytest.mark.parametrize("batch,M,N,K,bn", [(1, 1024, 8192, 8192, 256), (1, 2048, 8192, 8192, 256),
+                                            (1, 512, 512, 4096, 256), (2, 512, 768, 2048, 256),
+                                            (1, 700, 1000, 3000, 256),
+                                            # M <= 128: the 1-SM kernel, split over the SMs
+                                            (1, 128, 8192, 8192, 256), (1, 64, 4096, 2048, 128),
+                                            (3, 100, 1000, 1024, 128)])
+def test_split_k_matches_float64(cuda_rt, batch, M, N, K, bn):
     import torch
 
-    a, b, c = _gemm(cuda_rt, batch, M, N, K, seed=M + K)
+    a, b, c = _gemm(cuda_rt, batch, M, N, K, seed=M + K, bn=bn)
     ref = torch.bmm(a.double(), b.double())
     err = ((c.double() - ref).abs().max() / ref.abs().max()).item()
     # f32 accumulation in the tensor core: the normwise error grows with K (1.07e-5 at K = 8192 unsplit)
