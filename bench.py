@@ -808,7 +808,12 @@ def run_reference(args) -> None:
     case = goldens.case("add_block1024")
     ir = goldens.ir_from_json(case["opt"])
     cores = os.cpu_count() or 1
-    n = 1 << 22  # bounded sample per step: 2^22 elements per thread-chunk
+    # bounded sample per step: 2^22 elements per thread-chunk (about 0.4 s per step on 16 cores),
+    # halved for every doubling of the step count past 100 so the whole run stays within minutes
+    shrink = 0
+    while (args.steps >> shrink) > 100 and shrink < 6:
+        shrink += 1
+    n = 1 << (22 - shrink)
     rng = np.random.default_rng(1)
     a = rng.standard_normal(n * cores, dtype=np.float32)
     b = rng.standard_normal(n * cores, dtype=np.float32)
@@ -830,7 +835,7 @@ def run_reference(args) -> None:
     dt = (time.perf_counter() - t0) / args.steps
     assert np.array_equal(c, a + b)
     gbs = BYTES_PER_ELEM * n * cores / dt / 1e9
-    sample = f"{cores} x 2^22-element chunks of the C2 add per step (oracle interpreter, {cores} threads)"
+    sample = f"{cores} x 2^{22 - shrink}-element chunks of the C2 add per step (oracle interpreter, {cores} threads)"
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True,
