@@ -291,9 +291,6 @@ class _Emitter:
         d = self.defs.get(ref.id)
         return d is not None and d.op == "const" and d.args[0] is True and ref.dtype == DType.BOOL
 
-    def buf_dtype(self, ref: ValueRef) -> DType:
-        return ref.dtype
-
     def emit(self, line: str, indent: int = 1) -> None:
         self.lines.append("  " * (indent + self.depth) + line)
 

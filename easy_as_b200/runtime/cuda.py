@@ -29,7 +29,6 @@ import hashlib
 import math
 import os
 import struct
-import time
 from collections import deque
 from pathlib import Path
 from typing import Any, Mapping
@@ -904,9 +903,3 @@ class CudaRuntime:
             lib.eas_event_destroy(e1)
         return float(ms.value) * 1e-3 / repeat
 
-    def wall_benchmark(self, fn: Any, repeat: int) -> float:  # pragma: no cover - helper for examples
-        t0 = time.perf_counter()
-        for _ in range(repeat):
-            fn()
-        self.synchronize()
-        return (time.perf_counter() - t0) / repeat
