@@ -32,11 +32,10 @@ f32 rounding (the parity tests use the fp16-GEMM tolerance).
 
 from __future__ import annotations
 
-import ctypes
 from dataclasses import dataclass, field
 from typing import Any
 
-from ..ir import DType, IRModule, Inst, ValueRef
+from ..ir import DType, IRModule
 
 Mono = tuple[str, ...]          # sorted symbol names; () is the constant term
 Poly = dict[Mono, int]          # monomial -> integer coefficient

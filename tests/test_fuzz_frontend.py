@@ -4,7 +4,6 @@ oracle; the oracle's f32 results agree with a float64 evaluation where one is si
 
 from __future__ import annotations
 
-import numpy as np
 import pytest
 
 import fuzz_kernels

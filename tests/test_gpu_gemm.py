@@ -6,8 +6,6 @@ tighter normwise bound against the CPU oracle's strictly ordered f32 fma chain
 (the reference's dot semantics): max|gpu - oracle| <= 1e-5 * max|oracle|.
 """
 
-import os
-
 import numpy as np
 import pytest
 

@@ -2,12 +2,11 @@
 it) reproduces the single launch bit for bit, with full-size buffers and with
 slice-only buffers (pointer rebasing)."""
 
-import numpy as np
 import pytest
 
 import eas
 from eas import mk
-from easy_as_b200.shard import element_range, program_range, run_shard
+from easy_as_b200.shard import element_range, run_shard
 
 pytestmark = pytest.mark.gpu
 

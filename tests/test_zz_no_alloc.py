@@ -9,7 +9,6 @@ a failure here never hides the other tests.
 
 import ctypes
 
-import numpy as np
 import pytest
 
 from easy_as_b200.runtime import cuda_ext
