@@ -367,6 +367,7 @@ def run_gemm(name: str, args, world: int, rank: int, rt) -> dict:
                      "peak_source": ("measured burst cuBLAS bf16 (MEASURED_PEAKS.json bf16_tflops)"
                                      if pk["source"] == "measured" else "fallback"),
                      "frac_of_nominal_2250": round(local_tf / 2250.0, 4),
+                     "frac_of_measured_sustained": round(local_tf / pk["bf16_tflops_sustained"], 4),
                      "traffic": profile_traffic(f"gemm_{name.lower()}_n1")},
         "cublas_f16_f32out_tflops": lib_tf,
         "e2e": e2e,
