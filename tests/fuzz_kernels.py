@@ -2,8 +2,8 @@
 CPU oracle.
 
 Each seed gives one kernel over f32 inputs ``x`` and ``y``, an f16 input ``h``, a u32 scalar
-``S`` and an f32 scalar ``alpha``, storing an f32 expression to ``out`` and an integer
-expression (as f32) to ``outi``.  The expressions mix every elementwise op of the DSL with
+``S`` and an f32 scalar ``alpha``, storing an f32 expression to ``out``, an integer
+expression (as f32) to ``outi`` and the f32 expression rounded to f16 to ``outh``.  The expressions mix every elementwise op of the DSL with
 exactly defined results: f32 add, mul and fma (single rounding), f32 <-> f16 <-> u32 casts,
 u32 add, mul, floordiv and mod by non-zero constants (mod 2^32), u32 comparisons, boolean
 and/or/not, ``where``, and masked loads (zero fill) at shifted or permuted offsets.  Results
@@ -96,7 +96,7 @@ def kernel_source(seed: int) -> str:
     body = "\n".join(g.lines)
     return f'''
 @eas.kernel
-def fuzz_{seed}(x, y, h, out, outi, N, S, alpha, BLOCK: eas.constexpr):
+def fuzz_{seed}(x, y, h, out, outi, outh, N, S, alpha, BLOCK: eas.constexpr):
     offs = mk.program_id(0) * BLOCK + mk.arange(0, BLOCK)
     pid = mk.program_id(0)
     m = offs < N
@@ -106,6 +106,7 @@ def fuzz_{seed}(x, y, h, out, outi, N, S, alpha, BLOCK: eas.constexpr):
 {body}
     mk.store(out, offs, {fexpr}, m)
     mk.store(outi, offs, mk.to_f32({iexpr}), m & {smask})
+    mk.store(outh, offs, mk.to_f16({fexpr}), m)
 '''
 
 
@@ -124,6 +125,7 @@ def inputs(seed: int, n: int) -> dict:
     x[: min(n, 4)] = [0.0, -0.0, 3.0e38, -1.0e-40][: min(n, 4)]   # signed zero, large, subnormal
     h = rng.standard_normal(n).astype(np.float16)
     return {"x": x, "y": y, "h": h, "out": np.full(n, -7.0, np.float32), "outi": np.full(n, -7.0, np.float32),
+            "outh": np.full(n, -3.0, np.float16),
             "N": n, "S": int(rng.integers(1, 1 << 31)), "alpha": float(np.float32(rng.standard_normal()))}
 
 

@@ -17,7 +17,7 @@ def test_fuzz_kernel_traces_lowers_and_runs(seed):
     k, _src = fuzz_kernels.make(seed)
     n = 300 + seed
     args = fuzz_kernels.inputs(seed, n)
-    ck = k.compile(*(args[a] for a in ("x", "y", "h", "out", "outi", "N", "S", "alpha")), BLOCK=64)
+    ck = k.compile(*(args[a] for a in ("x", "y", "h", "out", "outi", "outh", "N", "S", "alpha")), BLOCK=64)
     assert "__global__" in ck.src
     execute(ck.ir, dict(args), grid=(-(-n // 64), 1, 1))
     assert args["out"].shape == (n,)

@@ -27,12 +27,13 @@ def test_fuzz_kernel_bit_exact_vs_oracle(cuda_rt, seed):
     block = (64, 128, 256, 1024)[seed % 4]
     gpu = fuzz_kernels.inputs(seed, n)
     cpu = fuzz_kernels.inputs(seed, n)
-    names = ("x", "y", "h", "out", "outi", "N", "S", "alpha")
+    names = ("x", "y", "h", "out", "outi", "outh", "N", "S", "alpha")
     k(*(gpu[a] for a in names), BLOCK=block)
     ck = k.compile(*(cpu[a] for a in names), BLOCK=block)
     execute(ck.ir, dict(cpu), grid=(-(-n // block), 1, 1))
-    for buf in ("out", "outi"):
-        g, c = gpu[buf].view(np.uint32), cpu[buf].view(np.uint32)
+    for buf in ("out", "outi", "outh"):
+        bits = np.uint16 if gpu[buf].dtype == np.float16 else np.uint32
+        g, c = gpu[buf].view(bits), cpu[buf].view(bits)
         both_nan = np.isnan(gpu[buf]) & np.isnan(cpu[buf])
         bad = np.nonzero((g != c) & ~both_nan)[0]
         assert bad.size == 0, (f"{buf}: {bad.size} of {n} differ, first at {bad[0]}: gpu {gpu[buf][bad[0]]!r} "
