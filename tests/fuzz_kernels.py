@@ -136,29 +136,36 @@ def inputs(seed: int, n: int) -> dict:
 
 def thread_kernel_source(seed: int) -> tuple[str, dict]:
     """A kernel of NT threads per group: every thread fills distinct slots of two threadgroup
-    arrays (masked global loads and f32 expressions), then after a barrier reads other threads'
+    arrays (masked global loads and f32 expressions; the second array is f16 in about half the
+    seeds), then after a barrier reads other threads'
     slots at permuted positions into an fma chain, optionally adds an ``mk.dot`` over the
     arrays, optionally refills one array in a second phase, and stores one result per thread."""
     r = random.Random(10_000 + seed)
     nt = r.choice([32, 64, 128, 256])
     ts = nt * r.choice([1, 2, 3]) + r.choice([0, 0, 5, 17])
     reps = r.randint(1, 6)
+    sb_f16 = r.random() < 0.5          # second threadgroup array in f16 (stores round, loads widen)
     g = _Gen(20_000 + seed)
     lines = []
     fill = []
     for i in range(0, ts, nt):
         src_idx = r.choice(["(pid * {ts} + t + {i}) % N", "(gi * {p} + {i}) % N"]).format(ts=ts, i=i, p=r.choice([3, 5]))
         fill.append(f"    mk.store(sa, t + {i}, mk.load(x, {src_idx}, m2 & (t + {i} < {ts})), t + {i} < {ts})")
-        fill.append(f"    mk.store(sb, t + {i}, {r.choice(['a', 'b', 'a * b', 'mk.fma(a, alpha, b)', 'mk.to_f32(t + ' + str(i) + ')'])}, "
-                    f"t + {i} < {ts})")
+        val = r.choice(['a', 'b', 'a * b', 'mk.fma(a, alpha, b)', 'mk.to_f32(t + ' + str(i) + ')'])
+        if sb_f16:
+            val = f"mk.to_f16({val})"
+        fill.append(f"    mk.store(sb, t + {i}, {val}, t + {i} < {ts})")
     chain = []
     acc = g.f(1)
     lines.extend(g.lines)
     g.lines = []
     for j in range(reps):
         p_, q_ = r.choice([1, 3, 5, 7]), r.randint(0, ts - 1)
-        chain.append(f"    acc = mk.fma(mk.load(sa, (t * {p_} + {q_}) % {ts}), mk.load(sb, (t + {j * 13 + 1}) % {ts}), acc)")
-    if r.random() < 0.6:
+        sb_val = f"mk.load(sb, (t + {j * 13 + 1}) % {ts})"
+        if sb_f16:
+            sb_val = f"mk.to_f32({sb_val})"
+        chain.append(f"    acc = mk.fma(mk.load(sa, (t * {p_} + {q_}) % {ts}), {sb_val}, acc)")
+    if r.random() < 0.6 and not sb_f16:
         k = r.randint(1, min(16, ts))
         sa_stride = r.choice([1, 1, 2]) if ts >= 2 * k else 1
         span_a = (k - 1) * sa_stride + 1
@@ -182,7 +189,7 @@ def tfuzz_{seed}(x, y, out, N, S, alpha, NT: eas.constexpr):
     offs = gi
     hv = a
     sa = mk.alloc_tg({ts})
-    sb = mk.alloc_tg({ts})
+    sb = mk.alloc_tg{'_f16' if sb_f16 else ''}({ts})
 {chr(10).join(fill)}
     mk.barrier()
 {body}
