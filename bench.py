@@ -161,11 +161,11 @@ def max_over_ranks(x: float, world: int) -> float:
 
 
 def shard(n_total: int, block: int, world: int, rank: int) -> tuple[int, int]:
-    """Element range [lo, hi) of this rank: contiguous program-id range, whole programs only."""
-    programs = -(-n_total // block)
-    p0 = programs * rank // world
-    p1 = programs * (rank + 1) // world
-    return p0 * block, min(p1 * block, n_total)
+    """Element range [lo, hi) of this rank: contiguous program-id range, whole programs only (the
+    library's own split, ``easy_as_b200.shard.element_range``)."""
+    from easy_as_b200.shard import element_range
+
+    return element_range(n_total, block, rank, world)
 
 
 def bench_gather(c, n_total: int, world: int, rank: int) -> dict:
