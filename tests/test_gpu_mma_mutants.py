@@ -1,6 +1,7 @@
 """GPU: every near-miss variant of the DSL simdgroup-MMA matmul (tests/mma_mutants.py) computes what
 the mutant says, native (f16 staging + tcgen05) or generated (mma.sync): within 1e-5 normwise of
-the oracle, whose 8x8 mma sums in k order (neither GPU path is bound to that order)."""
+the oracle, which sums each 8x8 mma step in float64 and rounds once (the summation order of the
+matrix units is unspecified, so neither GPU path is bound to the oracle's)."""
 
 from __future__ import annotations
 
