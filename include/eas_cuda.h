@@ -46,6 +46,10 @@ const char* eas_last_error(void);
  * Replaces `eas._metal.is_available` (_metal.mm:168-183). */
 int eas_is_available(void);
 
+/* Device selection has no reference counterpart: the Metal extension uses one
+ * process-wide device and queue (_metal.mm:141-166); here each rank or caller
+ * picks one of the box's B200s. */
+
 /* Number of visible CUDA devices. */
 int eas_device_count(int* count);
 
@@ -67,6 +71,8 @@ int eas_versions(int* driver_version, int* nvrtc_version);
 int eas_compile(const char* src, const char* name, const char* const* opts, int nopts,
                 void** image, size_t* image_size);
 
+/* Frees an image returned by eas_compile (the Metal library object needs no
+ * such call, _metal.mm:185-260). */
 void eas_free_host(void* p);
 
 /* Load a CUBIN on `dev` and resolve kernel `name`.  `max_dyn_smem` > 0 raises
@@ -225,7 +231,10 @@ int eas_gemm_tf32(const float* a, const float* b, float* c, uint32_t M, uint32_t
 /* 3xTF32 on tcgen05: the same kernel as eas_gemm_tf32 over operands from
  * eas_split_tf32, whose rows are [hi | lo] segments of K elements each (K a
  * multiple of 32; lda, ldb >= 2K).  The kernel runs 3K/32 k-blocks:
- * C = A_hi.B_hi + A_hi.B_lo + A_lo.B_hi (f32 accumulate). */
+ * C = A_hi.B_hi + A_hi.B_lo + A_lo.B_hi (f32 accumulate).  With eas_split_tf32
+ * it is the opt-in alternative to eas_sgemm_f32_tiled for a launch of the
+ * reference's fp32 tiled matmul (examples/matmul_tiled.py:134-230, dot groups
+ * msl.py:1201-1359). */
 int eas_gemm_3xtf32(const float* a2, const float* b2, float* c, uint32_t M, uint32_t N, uint32_t K, uint32_t batch,
                     uint64_t lda, uint64_t a_bstride, uint64_t ldb, uint64_t b_bstride, uint64_t ldc,
                     uint64_t c_bstride, int block_n, void* stream);
@@ -240,7 +249,9 @@ int eas_split_tf32(const float* src, float* dst, uint32_t rows, uint32_t kp, uin
                    uint32_t k_valid, uint32_t batch, uint64_t bs_src, int transpose, void* stream);
 
 /* Read and clear the status word of native kernels on `dev` (0 = ok,
- * EAS_ERR_TIMEOUT = a bounded wait expired).  Valid after the stream synced. */
+ * EAS_ERR_TIMEOUT = a bounded wait expired).  Valid after the stream synced.
+ * The nearest reference analogue is the command-buffer status check after a
+ * Metal dispatch (_metal.mm:1206-1217); Metal kernels have no bounded waits. */
 int eas_gemm_status(int dev, int* code);
 
 /* Allocation-free form of eas_gemm_f16, for callers that cannot let a library
@@ -268,7 +279,8 @@ int eas_gemm_f16_noalloc(const void* a, const void* b, float* c, uint32_t M, uin
                          int b_kmajor, uint64_t ldc, uint64_t c_bstride, int block_n, void* stream,
                          int* status_out);
 
-/* ---- host-side fault injection (tests; no device fault is ever made) --- */
+/* ---- host-side fault injection (tests; no device fault is ever made; no
+ *      counterpart in the reference) ---------------------------------------- */
 
 /* Make the `nth` (1-based) next call of kind "compile", "alloc", "launch" or
  * "copy" fail with EAS_ERR_INJECTED.  nth <= 0 clears the injection. */
