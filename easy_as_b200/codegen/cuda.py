@@ -79,6 +79,7 @@ class Lowered:
     elementwise: Any = field(default=None)  # ElementwiseInfo when program p touches only elements [p*B, p*B+B)
     layout: Any = field(default=None)   # runtime parameter layout, built on first launch
     grid_rank: Any = field(default=None)  # 1 + highest program_id/thread_id axis, cached by the runtime
+    reads: frozenset = field(default=frozenset())  # buffer args the kernel may read (analysis.infer_reads)
 
 
 HIDDEN = ("eas_ntx", "eas_pid_x", "eas_pid_y", "eas_pid_z")
@@ -1006,4 +1007,7 @@ def ir_to_cuda(ir: IRModule) -> Lowered:
 
     lowered.native = match_native(ir, lowered)
     lowered.elementwise = elementwise_info(ir, lowered.block_size, lowered.mode)
+    from ..analysis import infer_reads
+
+    lowered.reads = infer_reads(ir)
     return lowered

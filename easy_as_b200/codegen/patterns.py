@@ -256,6 +256,21 @@ class DotGemmPlan:
                 return False
         return True
 
+    def covers(self, runtime_args: dict[str, Any], programs: tuple[int, int, int], ntx: int, name: str,
+               numel: int) -> bool:
+        """True when this launch stores every element of buffer ``name`` (numel elements from index 0):
+        the output rectangle M x N of every batch is one dense block starting at 0.  A property of
+        the kernel's stores, so it holds whichever kernel runs the launch."""
+        if name != self.c_arg:
+            return False
+        scalars = {f"${a.name}": int(runtime_args[a.name]) for a in self.ir.args if a.kind == "scalar"}
+        m = self.map_launch(scalars, programs, ntx)
+        if m is None or m.get("empty"):
+            return False
+        M, N, B = m["M"], m["N"], m["batch"]
+        dense = (M == 1 or m["ldc"] == N) and (B == 1 or m["c_bs"] == M * N)
+        return dense and m["c0"] == 0 and M * N * B == numel
+
     # -- launch ------------------------------------------------------------------
     def try_launch(self, rt: Any, ck: Any, runtime_args: dict[str, Any], args: dict[str, Any], device: int,
                    stream: int, programs: tuple[int, int, int], ntx: int, pid_base: tuple[int, int, int] = (0, 0, 0),

@@ -833,6 +833,19 @@ class ProvenGemmPlan:
     def _launch(self, rt: Any, d: dict[str, Any], pa: int, pb: int, pc: int, device: int, stream: int) -> bool:
         raise NotImplementedError
 
+    def covers(self, runtime_args: dict[str, Any], programs: tuple[int, int, int], ntx: int, name: str,
+               numel: int) -> bool:
+        """True when this launch stores every element of buffer ``name`` (numel elements from index 0):
+        the proven output rectangle M x N of every batch is one dense block starting at 0."""
+        scalars = {a.name: int(runtime_args[a.name]) for a in self.ir.args
+                   if a.kind == "scalar" and a.dtype == DType.U32}
+        d = self.analyse(scalars, programs, ntx)
+        if d is None or d["empty"] or d["c_buf"] != name:
+            return False
+        M, N, B = d["M"], d["N"], d["batch"]
+        dense = (M == 1 or d["c_sm"] == N) and (B == 1 or d["c_bs"] == M * N)
+        return dense and d["c0"] == 0 and M * N * B == numel
+
 
 class TiledGemmPlan(ProvenGemmPlan):
     """Native FFMA launch for kernels proven to be tiled fp32 GEMMs (module docstring)."""

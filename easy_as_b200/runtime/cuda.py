@@ -213,12 +213,13 @@ def _cache_dir() -> Path | None:
 class _Arg:
     """A buffer argument resolved to a device pointer."""
 
-    __slots__ = ("ptr", "device", "keep", "host", "dev_buf", "torch_stream", "bounce")
+    __slots__ = ("ptr", "device", "keep", "host", "dev_buf", "torch_stream", "bounce", "deferred")
 
     def __init__(self, ptr: int, device: int | None, keep: Any = None, host: np.ndarray | None = None,
                  dev_buf: DeviceBuffer | None = None, torch_stream: bool = False, bounce: int | None = None):
         self.ptr, self.device, self.keep, self.host = ptr, device, keep, host
         self.dev_buf, self.torch_stream, self.bounce = dev_buf, torch_stream, bounce
+        self.deferred = False  # copy-in not made yet (a write-only host output; see _settle_deferred)
 
 
 class _Bounce:
@@ -255,6 +256,7 @@ class CudaRuntime:
         self._staging: dict[tuple[int, int], list[DeviceBuffer]] = {}
         self._bounce: dict[int, _Bounce] = {}
         self._pdl_on: bool | None = None
+        self.skipped_copy_bytes = 0  # host->device bytes not copied because a launch stores all of them
         self._bucket_keep: list[Any] = []
         self._pending_n = 0
         self._bucket_n = 0
@@ -462,17 +464,43 @@ class CudaRuntime:
             stream = int(raw(device)) if raw is not None else int(torch.cuda.current_stream(device).cuda_stream)
         if host_pending and allow_bounce and self._bounce_resolve(ck, host_pending, resolved, device, stream):
             return resolved, device, stream
-        # host arrays: one temporary device buffer per distinct array object
+        # host arrays: one temporary device buffer per distinct array object.  An array the kernel
+        # only writes, under a single name, is not copied in yet: the launch may store every element
+        # of it (_settle_deferred decides before the launch)
         staged: dict[int, DeviceBuffer] = {}
+        names_of: dict[int, list[str]] = {}
+        for name, arr in host_pending:
+            names_of.setdefault(id(arr), []).append(name)
+        reads = getattr(ck.plan, "reads", None)
         for name, arr in host_pending:
             buf = staged.get(id(arr))
+            names = names_of[id(arr)]
+            defer = (reads is not None and len(names) == 1 and name in ck.writes and name not in reads)
             if buf is None:
                 buf = self._stage(device, max(arr.nbytes, 1))
-                buf.copy_from_host(arr, stream)
+                if not defer:
+                    buf.copy_from_host(arr, stream)
                 staged[id(arr)] = buf
-            resolved[name] = _Arg(buf.ptr, device, keep=arr, host=arr if name in ck.writes else None,
-                                  dev_buf=buf)
+            a = _Arg(buf.ptr, device, keep=arr, host=arr if name in ck.writes else None, dev_buf=buf)
+            a.deferred = defer
+            resolved[name] = a
         return resolved, device, stream
+
+    def _settle_deferred(self, ck: Any, runtime_args: Mapping[str, Any], args: dict[str, _Arg], stream: int,
+                         programs: tuple[int, int, int], ntx: int) -> None:
+        """Make the copy-in of write-only host outputs unless the launch provably stores every
+        element of them (a native GEMM plan's output rectangle covering the whole buffer; the
+        generated kernel stores the same elements, so this holds whichever kernel runs)."""
+        native = getattr(ck.plan, "native", None)
+        for name, a in args.items():
+            if not a.deferred:
+                continue
+            a.deferred = False
+            covers = getattr(native, "covers", None)
+            if covers is not None and covers(runtime_args, programs, ntx, name, int(a.host.size)):
+                self.skipped_copy_bytes += int(a.host.nbytes)
+                continue
+            a.dev_buf.copy_from_host(a.host, stream)
 
     # -- small host arrays: one pinned bounce buffer ----------------------------------
     BOUNCE_MAX_BYTES = 4 << 20   # host arrays up to this total go through the bounce buffer
@@ -599,6 +627,8 @@ class CudaRuntime:
         # could still be waiting for its copy when the next call refills the buffer
         args, device, stream = self._resolve(ck, runtime_args, allow_bounce=sync)
         host_copies = [a for a in args.values() if a.host is not None]
+        if any(a.deferred for a in host_copies):
+            self._settle_deferred(ck, runtime_args, args, stream, *geo)
         lib = self.lib()
         capturing = cuda_ext.ctypes.c_int(0)
         if stream:
