@@ -154,6 +154,29 @@ class FakeLib:
         self.pdl_launches = getattr(self, "pdl_launches", 0) + 1
         return self.eas_launch(*args)
 
+    def eas_gemm_f16(self, a, b, c, M, N, K, batch, lda, a_bs, ldb, b_bs, b_kmajor, ldc, c_bs, block_n, stream):
+        """numpy stand-in for the tcgen05 GEMM over the fake device memory."""
+        self.calls.append(("gemm", M, N, K, batch))
+
+        def view(ptr, dt, count):
+            buf, at = self._find(int(ptr))
+            return np.frombuffer(buf, dtype=dt, count=count, offset=at)
+
+        for z in range(batch):
+            A = view(a + 2 * z * a_bs, np.float16, (M - 1) * lda + K).astype(np.float64)
+            A = np.lib.stride_tricks.as_strided(A, (M, K), (8 * lda, 8))
+            if b_kmajor:
+                B = view(b + 2 * z * b_bs, np.float16, (N - 1) * ldb + K).astype(np.float64)
+                B = np.lib.stride_tricks.as_strided(B, (N, K), (8 * ldb, 8)).T
+            else:
+                B = view(b + 2 * z * b_bs, np.float16, (K - 1) * ldb + N).astype(np.float64)
+                B = np.lib.stride_tricks.as_strided(B, (K, N), (8 * ldb, 8))
+            C = view(c + 4 * z * c_bs, np.float32, (M - 1) * ldc + N)
+            out = (A @ B).astype(np.float32)
+            for m in range(M):
+                C[m * ldc:m * ldc + N] = out[m]
+        return 0
+
     # streams, events, status
     def eas_stream_synchronize(self, stream):
         return 0
@@ -189,11 +212,11 @@ def fake(monkeypatch):
     return lib, rt
 
 
-def _run(lib, rt, kernel, args, **meta):
+def _run(lib, rt, kernel, args, grid=None, **meta):
     ck = kernel.compile(*args, **meta)
     lib.current = ck
     names = [a.name for a in ck.ir.args]
-    rt.run(ck, dict(zip(names, args)), meta, sync=True)
+    rt.run(ck, dict(zip(names, args)), meta, sync=True, grid=grid)
     return ck
 
 
@@ -303,3 +326,30 @@ def test_generated_kernels_launch_with_pdl_by_default(fake, monkeypatch):
     rt2.default_device = lambda: 0
     _run(lib, rt2, scale_kernel, (x, y, n, 3.0), BLOCK=64)
     assert lib.pdl_launches == 1
+
+
+def test_host_output_stored_in_full_is_not_copied_in(fake):
+    """Per-array staging (bounce off): the GEMM's output array is written in full by the launch, so
+    its copy-in is skipped; a larger output buffer, which the launch does not cover, is copied in
+    and its extra elements come back unchanged."""
+    from examples.matmul_dot_f16 import matmul_dot_f16
+
+    lib, rt = fake
+    rt.BOUNCE_MAX_BYTES = 0
+    M, N, K = 16, 32, 8
+    rng = np.random.default_rng(0)
+    a = rng.standard_normal(M * K).astype(np.float16)
+    b = rng.standard_normal(K * N).astype(np.float16)
+    c = np.full(M * N, np.nan, np.float32)
+    _run(lib, rt, matmul_dot_f16, (a, b, c, M, N, K), grid=(1, M, 1), BLOCK_M=128, BLOCK_N=256, BLOCK_K=64)
+    h2d = [k[1] for k in lib.calls if k[0] == "h2d"]
+    assert sorted(h2d) == sorted([a.nbytes, b.nbytes])          # no copy of c
+    assert rt.skipped_copy_bytes == c.nbytes
+    ref = a.reshape(M, K).astype(np.float64) @ b.reshape(K, N).astype(np.float64)
+    np.testing.assert_allclose(c.reshape(M, N), ref, rtol=1e-5, atol=1e-5)
+
+    lib.calls.clear()
+    c2 = np.full(M * N + 8, 3.0, np.float32)
+    _run(lib, rt, matmul_dot_f16, (a, b, c2, M, N, K), grid=(1, M, 1), BLOCK_M=128, BLOCK_N=256, BLOCK_K=64)
+    assert sorted(k[1] for k in lib.calls if k[0] == "h2d") == sorted([a.nbytes, b.nbytes, c2.nbytes])
+    assert np.all(c2[M * N:] == 3.0)
