@@ -529,7 +529,14 @@ extern "C" int eas_alloc_pinned(size_t nbytes, void** out) {
   *out = nullptr;
   int rc = eas_driver_init();
   if (rc) return rc;
-  return eas_cuda_check(cudaHostAlloc(out, nbytes ? nbytes : 1, cudaHostAllocPortable), "pinned host allocation",
+  return eas_cuda_check(cudaHostAlloc(out, nbytes ? nbytes : 1, cudaHostAllocPortable | cudaHostAllocMapped),
+                        "pinned host allocation", EAS_ERR_MEMORY);
+}
+
+extern "C" int eas_pinned_device_pointer(void* host, void** dev) {
+  if (!host || !dev) return eas_fail(EAS_ERR_VALUE, "eas_pinned_device_pointer: null pointer");
+  *dev = nullptr;
+  return eas_cuda_check(cudaHostGetDevicePointer(dev, host, 0), "device address of pinned host memory",
                         EAS_ERR_MEMORY);
 }
 

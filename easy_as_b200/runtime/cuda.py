@@ -213,19 +213,20 @@ def _cache_dir() -> Path | None:
 class _Arg:
     """A buffer argument resolved to a device pointer."""
 
-    __slots__ = ("ptr", "device", "keep", "host", "dev_buf", "torch_stream", "bounce", "deferred")
+    __slots__ = ("ptr", "device", "keep", "host", "dev_buf", "torch_stream", "bounce", "deferred", "zero_copy")
 
     def __init__(self, ptr: int, device: int | None, keep: Any = None, host: np.ndarray | None = None,
                  dev_buf: DeviceBuffer | None = None, torch_stream: bool = False, bounce: int | None = None):
         self.ptr, self.device, self.keep, self.host = ptr, device, keep, host
         self.dev_buf, self.torch_stream, self.bounce = dev_buf, torch_stream, bounce
         self.deferred = False  # copy-in not made yet (a write-only host output; see _settle_deferred)
+        self.zero_copy = False  # the kernel works on the page-locked bounce buffer in place
 
 
 class _Bounce:
     """Page-locked host buffer and its device twin, for launches with small host arrays."""
 
-    __slots__ = ("host_ptr", "view", "dev", "nbytes")
+    __slots__ = ("host_ptr", "view", "dev", "nbytes", "mapped")
 
     def __init__(self, nbytes: int, device: int):
         lib = cuda_ext.load()
@@ -235,6 +236,9 @@ class _Bounce:
         self.view = np.ctypeslib.as_array((cuda_ext.ctypes.c_uint8 * nbytes).from_address(self.host_ptr))
         self.dev = DeviceBuffer(nbytes, device)
         self.nbytes = nbytes
+        m = cuda_ext.ctypes.c_void_p()   # device address of the pinned buffer (zero-copy launches)
+        cuda_ext.check(lib.eas_pinned_device_pointer(self.host_ptr, cuda_ext.ctypes.byref(m)), "mapped bounce buffer")
+        self.mapped = int(m.value or 0)
 
     def free(self) -> None:
         if self.host_ptr:
@@ -504,6 +508,7 @@ class CudaRuntime:
 
     # -- small host arrays: one pinned bounce buffer ----------------------------------
     BOUNCE_MAX_BYTES = 4 << 20   # host arrays up to this total go through the bounce buffer
+    ZERO_COPY_MAX_BYTES = 256 << 10  # elementwise launches up to this total run on the bounce buffer in place
     _BOUNCE_ALIGN = 256
 
     def _bounce_resolve(self, ck: Any, host_pending: list[tuple[str, np.ndarray]], resolved: dict[str, _Arg],
@@ -532,11 +537,21 @@ class CudaRuntime:
                 bb.view[cur:cur + n] = arr.reshape(-1).view(np.uint8)
             offs[key] = cur
             cur += -(-max(n, 1) // al) * al
-        cuda_ext.check(self.lib().eas_copy_from_host_async(bb.dev.ptr, bb.host_ptr, cur, stream), "copy in")
+        # an elementwise launch touches each element once: it reads and writes the page-locked buffer
+        # in place over PCIe (no copies); other kernels may re-read, so they get the device copy
+        # (small launches only: a kernel reaching host memory over PCIe makes many small requests,
+        # so beyond a few hundred KiB one bulk copy each way is faster)
+        zero_copy = (getattr(ck.plan, "elementwise", None) is not None and bb.mapped
+                     and cur <= self.ZERO_COPY_MAX_BYTES
+                     and os.environ.get("EAS_ZERO_COPY", "1") not in ("0", "off"))
+        base = bb.mapped if zero_copy else bb.dev.ptr
+        if not zero_copy:
+            cuda_ext.check(self.lib().eas_copy_from_host_async(bb.dev.ptr, bb.host_ptr, cur, stream), "copy in")
         for name, arr in host_pending:
             o = offs[id(arr)]
-            resolved[name] = _Arg(bb.dev.ptr + o, device, keep=arr, host=arr if name in ck.writes else None,
-                                  bounce=o)
+            a = _Arg(base + o, device, keep=arr, host=arr if name in ck.writes else None, bounce=o)
+            a.zero_copy = zero_copy
+            resolved[name] = a
         return True
 
     def _finish_host_copies(self, host_args: list[_Arg], device: int, stream: int) -> None:
@@ -549,7 +564,7 @@ class CudaRuntime:
             if a.host is not None and id(a.host) not in out:
                 out[id(a.host)] = a
         for a in out.values():
-            if a.bounce is not None and a.host.nbytes:
+            if a.bounce is not None and a.host.nbytes and not a.zero_copy:
                 cuda_ext.check(lib.eas_copy_to_host_async(bb.host_ptr + a.bounce, bb.dev.ptr + a.bounce, a.host.nbytes,
                                                           stream), "copy out")
         cuda_ext.check(lib.eas_stream_synchronize(stream), "kernel execution")

@@ -62,6 +62,7 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "eas_host_is_pinned": (_int, [_vp, _PINT]),
     "eas_alloc_pinned": (_int, [_sz, ctypes.POINTER(ctypes.c_void_p)]),
     "eas_free_pinned": (_int, [_vp]),
+    "eas_pinned_device_pointer": (_int, [_vp, ctypes.POINTER(ctypes.c_void_p)]),
     "eas_stream_wait_event": (_int, [_vp, _vp]),
     "eas_stream_synchronize": (_int, [_vp]),
     "eas_device_synchronize": (_int, [_int]),

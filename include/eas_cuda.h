@@ -127,6 +127,10 @@ int eas_host_is_pinned(const void* ptr, int* pinned);
  * and :335-345). */
 int eas_alloc_pinned(size_t nbytes, void** out);
 int eas_free_pinned(void* p);
+/* Device address of memory from eas_alloc_pinned (it is mapped): kernels of
+ * elementwise launches read and write the bounce buffer in place over PCIe,
+ * with no copies (each element is touched once). */
+int eas_pinned_device_pointer(void* host, void** dev);
 
 /* ---- synchronisation (replaces synchronize / queue_synchronize,
  *      _metal.mm:1397-1434) ------------------------------------------------ */

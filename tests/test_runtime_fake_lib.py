@@ -50,9 +50,10 @@ class FakeLib:
 
     # memory
     def _find(self, ptr: int) -> tuple[ctypes.Array, int]:
-        for base, buf in self.mem.items():
-            if base <= ptr < base + len(buf):
-                return buf, ptr - base
+        for pool in (self.mem, getattr(self, "pinned", {})):   # pinned memory is mapped: devices reach it
+            for base, buf in pool.items():
+                if base <= ptr < base + len(buf):
+                    return buf, ptr - base
         raise AssertionError(f"pointer {ptr:#x} is not a fake device allocation")
 
     def eas_alloc_buffer(self, dev, nbytes, out):
@@ -97,6 +98,10 @@ class FakeLib:
         self.pinned[ctypes.addressof(buf)] = buf
         out._obj.value = ctypes.addressof(buf)
         self.calls.append(("alloc_pinned", int(nbytes)))
+        return 0
+
+    def eas_pinned_device_pointer(self, host, out):
+        out._obj.value = int(host)
         return 0
 
     def eas_free_pinned(self, p):
@@ -220,7 +225,9 @@ def _run(lib, rt, kernel, args, grid=None, **meta):
     return ck
 
 
-def test_numpy_inputs_are_staged_and_only_outputs_copied_back(fake):
+def test_numpy_inputs_are_staged_and_only_outputs_copied_back(fake, monkeypatch):
+    """With zero-copy off: one packed copy in, one copy out of the written array."""
+    monkeypatch.setenv("EAS_ZERO_COPY", "0")
     lib, rt = fake
     n = 1024 + 7
     rng = np.random.default_rng(0)
@@ -274,7 +281,8 @@ def test_staging_buffers_are_pooled(fake):
     assert np.array_equal(c, np.full(n, 2.0, np.float32))
 
 
-def test_same_array_passed_twice_is_staged_once(fake):
+def test_same_array_passed_twice_is_staged_once(fake, monkeypatch):
+    monkeypatch.setenv("EAS_ZERO_COPY", "0")
     lib, rt = fake
     n = 100
     a = np.arange(n, dtype=np.float32)
@@ -353,3 +361,27 @@ def test_host_output_stored_in_full_is_not_copied_in(fake):
     _run(lib, rt, matmul_dot_f16, (a, b, c2, M, N, K), grid=(1, M, 1), BLOCK_M=128, BLOCK_N=256, BLOCK_K=64)
     assert sorted(k[1] for k in lib.calls if k[0] == "h2d") == sorted([a.nbytes, b.nbytes, c2.nbytes])
     assert np.all(c2[M * N:] == 3.0)
+
+
+def test_elementwise_launch_on_host_arrays_is_zero_copy(fake):
+    """An elementwise kernel on small host arrays works on the page-locked bounce buffer in place:
+    no copies either way; a non-elementwise kernel still copies."""
+    lib, rt = fake
+    n = 1031
+    rng = np.random.default_rng(3)
+    a = rng.standard_normal(n, dtype=np.float32)
+    b = rng.standard_normal(n, dtype=np.float32)
+    c = np.zeros_like(a)
+    _run(lib, rt, add_kernel, (a, b, c, n), BLOCK=256)
+    assert np.array_equal(c, a + b)
+    assert not any(k[0] in ("h2d", "h2d_async", "d2h", "d2h_async") for k in lib.calls)
+
+    from examples.matmul_dot_f16 import matmul_dot_f16
+
+    M, N, K = 8, 16, 8
+    x = rng.standard_normal(M * K).astype(np.float16)
+    y = rng.standard_normal(K * N).astype(np.float16)
+    z = np.zeros(M * N, np.float32)
+    lib.calls.clear()
+    _run(lib, rt, matmul_dot_f16, (x, y, z, M, N, K), grid=(1, M, 1), BLOCK_M=128, BLOCK_N=256, BLOCK_K=64)
+    assert any(k[0] == "h2d_async" for k in lib.calls) and any(k[0] == "d2h_async" for k in lib.calls)
