@@ -1115,6 +1115,35 @@ int gemm_entry(const char* who, const void* a, const void* b, float* c, uint32_t
 
 }  // namespace
 
+extern "C" int eas_gemm_f16_plan(uint32_t M, uint32_t N, uint32_t K, uint32_t batch, int block_n, int c_tma_ok,
+                                 int num_sms, int resident_pairs, int* tile_m, int* tile_n, int* stages, int* ksplit,
+                                 int* pair) {
+  // the same helpers, in the same order, as the launch branch of gemm_entry<false> and its launchers
+  if (!tile_m || !tile_n || !stages || !ksplit || !pair) return eas_fail(EAS_ERR_VALUE, "eas_gemm_f16_plan: null");
+  if (block_n != 128 && block_n != 256) return eas_fail(EAS_ERR_VALUE, "eas_gemm_f16_plan: block_n must be 128 or 256");
+  if (M == 0 || N == 0 || K == 0 || batch == 0 || num_sms <= 0)
+    return eas_fail(EAS_ERR_VALUE, "eas_gemm_f16_plan: empty launch");
+  const int kblocks = (int)((K + BK - 1) / BK);
+  const long long mt2 = (M + 255) / 256, mt1 = (M + BM - 1) / BM;
+  if (use_2sm(block_n, M)) {
+    *pair = 1;
+    *tile_m = 256;
+    const bool wide = c_tma_ok && N >= 512 && use_wide(M, N, batch, num_sms);
+    *tile_n = wide ? 512 : 256;
+    *stages = wide ? 4 : (c_tma_ok ? 6 : 7);
+    const long long tiles = mt2 * ((N + *tile_n - 1) / *tile_n) * batch;
+    *ksplit = c_tma_ok ? choose_ksplit(tiles, resident_pairs, kblocks, (int)batch) : 1;
+  } else {
+    *pair = 0;
+    *tile_m = BM;
+    *tile_n = block_n == 256 ? 256 : 128;
+    *stages = block_n == 256 ? 4 : 6;
+    const long long tiles = mt1 * ((N + *tile_n - 1) / *tile_n) * batch;
+    *ksplit = c_tma_ok ? choose_ksplit(tiles, num_sms, kblocks, (int)batch) : 1;
+  }
+  return EAS_OK;
+}
+
 extern "C" int eas_gemm_last_config(int* tile_m, int* tile_n, int* stages, int* ksplit, int* pair) {
   if (!tile_m || !tile_n || !stages || !ksplit || !pair) return eas_fail(EAS_ERR_VALUE, "eas_gemm_last_config: null");
   *tile_m = g_last_config.bm;

@@ -215,6 +215,15 @@ int eas_cast_f32_f16_2d(const float* src, void* dst, uint32_t rows, uint32_t col
  * Nothing faults or hangs; the context stays usable.  Asynchronous. */
 int eas_wait_selftest(long long budget_cycles, void* stream);
 
+/* What eas_gemm_f16 would launch, without a device: the CTA-pair or 1-SM
+ * kernel (*pair), the output tile (tile_m x tile_n per CTA pair or CTA),
+ * pipeline stages and split-K parts, for a C that TMA can store (c_tma_ok:
+ * 16-byte aligned base and strides) on a GPU with num_sms SMs of which
+ * resident_pairs CTA pairs are co-resident (cudaOccupancyMaxActiveClusters).
+ * Composes the same rules the launcher applies (no reference counterpart). */
+int eas_gemm_f16_plan(uint32_t M, uint32_t N, uint32_t K, uint32_t batch, int block_n, int c_tma_ok, int num_sms,
+                      int resident_pairs, int* tile_m, int* tile_n, int* stages, int* ksplit, int* pair);
+
 /* Tile configuration the most recent eas_gemm_* launch in this process used:
  * output tile (tile_m x tile_n per CTA, or per CTA pair when *pair is 1),
  * pipeline stages and split-K parts.  Reporting only (no reference

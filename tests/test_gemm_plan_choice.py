@@ -1,0 +1,54 @@
+"""CPU: the fp16 GEMM launcher's choices (``eas_gemm_f16_plan``: CTA pair or 1-SM kernel, tile,
+stages, split-K), computed without a device from the same rules the launcher applies, for the
+benchmark shapes and their per-GPU shards on a 148-SM B200 with 74 resident pairs."""
+
+from __future__ import annotations
+
+import ctypes
+
+import pytest
+
+from easy_as_b200.runtime import cuda_ext
+
+
+def plan(M, N, K, batch=1, block_n=256, tma=True, sms=148, pairs=74):
+    lib = cuda_ext.load()
+    vals = [ctypes.c_int() for _ in range(5)]
+    cuda_ext.check(lib.eas_gemm_f16_plan(M, N, K, batch, block_n, int(tma), sms, pairs,
+                                         *(ctypes.byref(v) for v in vals)), "plan")
+    tm, tn, st, ks, pair = (v.value for v in vals)
+    return {"pair": bool(pair), "tile": (tm, tn), "stages": st, "ksplit": ks}
+
+
+@pytest.mark.parametrize("shape,want", [
+    # C4 on 1, 2, 4, 8 GPUs (M split across ranks)
+    ((8192, 8192, 8192), {"pair": True, "tile": (256, 512), "stages": 4, "ksplit": 1}),
+    ((4096, 8192, 8192), {"pair": True, "tile": (256, 256), "stages": 6, "ksplit": 1}),   # wide adds a round
+    ((2048, 8192, 8192), {"pair": True, "tile": (256, 512), "stages": 4, "ksplit": 1}),
+    ((1024, 8192, 8192), {"pair": True, "tile": (256, 512), "stages": 4, "ksplit": 1}),
+    # C5 on 1 GPU (batch 64) and on 8 (batch 8)
+    ((4096, 4096, 2088, 64), {"pair": True, "tile": (256, 512), "stages": 4, "ksplit": 1}),
+    ((4096, 4096, 2088, 8), {"pair": True, "tile": (256, 512), "stages": 4, "ksplit": 1}),
+    # launches that leave most SMs idle split K
+    ((512, 512, 4096), {"pair": True, "tile": (256, 256), "stages": 6, "ksplit": 4}),
+    ((128, 8192, 8192), {"pair": False, "tile": (128, 256), "stages": 4, "ksplit": 4}),
+    ((64, 4096, 2048, 1, 128), {"pair": False, "tile": (128, 128), "stages": 6, "ksplit": 4}),
+    # few k-blocks: no split below 8 k-blocks per part
+    ((512, 512, 1024), {"pair": True, "tile": (256, 256), "stages": 6, "ksplit": 2}),   # 16 k-blocks
+    ((512, 512, 256), {"pair": True, "tile": (256, 256), "stages": 6, "ksplit": 1}),    # 4 k-blocks
+])
+def test_launch_choices(shape, want):
+    M, N, K, *rest = shape
+    batch = rest[0] if rest else 1
+    block_n = rest[1] if len(rest) > 1 else 256
+    assert plan(M, N, K, batch, block_n) == want
+
+
+def test_c_not_storable_by_tma_uses_direct_stores_and_never_splits():
+    assert plan(8192, 8192, 8192, tma=False) == {"pair": True, "tile": (256, 256), "stages": 7, "ksplit": 1}
+    assert plan(128, 8192, 8192, tma=False)["ksplit"] == 1
+
+
+def test_bad_arguments():
+    with pytest.raises(ValueError):
+        plan(256, 256, 256, block_n=64)
