@@ -53,3 +53,25 @@ def test_split_k_runs_agree(cuda_rt):
     a, b, c1 = _gemm(cuda_rt, 1, 512, 512, 4096, seed=9)
     _, _, c2 = _gemm(cuda_rt, 1, 512, 512, 4096, seed=9)
     assert torch.allclose(c1, c2, rtol=0, atol=1e-6 * c1.abs().max().item())
+
+
+@pytest.mark.parametrize("batch,M,N,K,bn", [(1, 8192, 8192, 1024, 256), (1, 512, 512, 4096, 256),
+                                            (1, 128, 8192, 8192, 256), (2, 300, 1000, 520, 128)])
+def test_launch_matches_the_plan_query(cuda_rt, batch, M, N, K, bn):
+    """eas_gemm_f16_plan predicts what eas_gemm_f16 launches (checked against the tile configuration
+    the launch recorded)."""
+    import ctypes
+
+    import torch
+
+    from easy_as_b200.runtime import cuda_ext
+
+    _gemm(cuda_rt, batch, M, N, K, seed=1, bn=bn)
+    lib = cuda_ext.load()
+    got = [ctypes.c_int() for _ in range(5)]
+    lib.eas_gemm_last_config(*(ctypes.byref(v) for v in got))
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    want = [ctypes.c_int() for _ in range(5)]
+    cuda_ext.check(lib.eas_gemm_f16_plan(M, N, K, batch, bn, 1, sms, sms // 2, *(ctypes.byref(v) for v in want)),
+                   "plan")
+    assert [v.value for v in got] == [v.value for v in want]
