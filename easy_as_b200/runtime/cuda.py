@@ -638,6 +638,10 @@ class CudaRuntime:
         if hosts is not None:
             self._run_pipelined(ck, runtime_args, geo, hosts)
             return
+        gp = self._gemm_pipeline_plan(ck, runtime_args, geo)
+        if gp is not None:
+            self._run_gemm_pipelined(ck, runtime_args, geo, gp)
+            return
         # the shared bounce buffer only serves calls that wait before returning: an asynchronous call
         # could still be waiting for its copy when the next call refills the buffer
         args, device, stream = self._resolve(ck, runtime_args, allow_bounce=sync)
@@ -855,6 +859,123 @@ class CudaRuntime:
             for e in evs:
                 lib.eas_event_destroy(e)
             for key, bufs in slots.items():
+                for b in bufs:
+                    free = self._staging.setdefault((b.device, b.nbytes), [])
+                    if len(free) < 4 * R:
+                        free.append(b)
+
+    # -- pipelined host-buffer path for batched GEMMs ------------------------------------
+    GEMM_PIPELINE_SLICE_BYTES = 96 << 20   # input bytes (A + B) per batch slice
+
+    def _gemm_pipeline_plan(self, ck: Any, runtime_args: Mapping[str, Any], geo: Any) -> dict[str, Any] | None:
+        """Batch slices of a batched fp16 dot GEMM on page-locked host arrays, when the pipeline
+        applies: a native dot-GEMM plan whose batch is program_id(2), that stores every element of
+        C (so C is never copied in), on host buffers large enough to split, with at least two
+        slices."""
+        native = getattr(ck.plan, "native", None)
+        if native is None or not hasattr(native, "map_launch") or not hasattr(native, "covers"):
+            return None
+        if os.environ.get("EAS_PIPELINE", "1") in ("0", "off"):
+            return None
+        if os.environ.get("EAS_DISABLE_NATIVE", "0") not in ("", "0"):
+            return None
+        torch = _torch()
+        names = [a.name for a in ck.ir.args if a.kind == "buffer"]
+        if sorted(names) != sorted({native.a_arg, native.b_arg, native.c_arg}):
+            return None
+        hosts: dict[str, np.ndarray] = {}
+        lib = self.lib()
+        for n in names:
+            v = runtime_args[n]
+            if torch is not None and isinstance(v, torch.Tensor):
+                if v.device.type != "cpu" or not v.is_contiguous():
+                    return None
+                v = v.detach().numpy()
+            if not isinstance(v, np.ndarray) or not v.flags.c_contiguous:
+                return None
+            pinned = cuda_ext.ctypes.c_int(0)
+            if v.nbytes == 0 or lib.eas_host_is_pinned(v.ctypes.data, cuda_ext.ctypes.byref(pinned)) or not pinned.value:
+                return None
+            hosts[n] = v
+        if len({id(h) for h in hosts.values()}) != 3:
+            return None
+        (gx, gy, gz), ntx = geo
+        scalars = {f"${a.name}": int(runtime_args[a.name]) for a in ck.ir.args if a.kind == "scalar"}
+        m = native.map_launch(scalars, (gx, gy, gz), ntx)
+        if m is None or m.get("empty") or m["batch"] < 2 or gz != m["batch"]:
+            return None
+        if not native.covers(runtime_args, (gx, gy, gz), ntx, native.c_arg, hosts[native.c_arg].size):
+            return None
+        m1 = native.map_launch(scalars, (gx, gy, 1), ntx, (0, 0, 1))  # batch 1 alone: program_id(2) is the batch
+        if (m1 is None or m1.get("empty") or m1["batch"] != 1 or m1["a0"] != m["a0"] + m["a_bs"]
+                or m1["b0"] != m["b0"] + m["b_bs"] or m1["c0"] != m["c0"] + m["c_bs"]):
+            return None
+        M, N, K = m["M"], m["N"], m["K"]
+        spans = {native.a_arg: (m["a0"], m["a_bs"], (M - 1) * m["lda"] + K),
+                 native.b_arg: (m["b0"], m["b_bs"], ((N - 1) * m["ldb"] + K) if m["b_kmajor"] else ((K - 1) * m["ldb"] + N)),
+                 native.c_arg: (m["c0"], m["c_bs"], (M - 1) * m["ldc"] + N)}
+        per_batch_in = 2 * (m["a_bs"] + m["b_bs"])
+        S = max(1, self.GEMM_PIPELINE_SLICE_BYTES // max(per_batch_in, 1))
+        if -(-m["batch"] // S) < 2:
+            return None
+        return {"hosts": hosts, "spans": spans, "batch": m["batch"], "S": S, "c": native.c_arg,
+                "item": {native.a_arg: 2, native.b_arg: 2, native.c_arg: 4}}
+
+    def _run_gemm_pipelined(self, ck: Any, runtime_args: Mapping[str, Any], geo: Any, gp: dict[str, Any]) -> None:
+        """Copy-in of batch slice i+1, the GEMM of slice i and the copy-out of slice i-1 overlap on
+        three streams.  Each slice runs as a program sub-range (program_id(2) in [z0, z1)) on
+        slot buffers holding only its elements (pointers rebased, as run_range does), natively
+        or, if the native kernel declines, with the generated kernel."""
+        (gx, gy, _gz), ntx = geo
+        device = self.default_device()
+        lib = self.lib()
+        s_in, s_run, s_out = self._streams(device)
+        hosts, spans, item, S, B = gp["hosts"], gp["spans"], gp["item"], gp["S"], gp["batch"]
+        R = self.PIPELINE_SLOTS
+        slot_elems = {n: (S - 1) * bs + span for n, (_x0, bs, span) in spans.items()}
+        slots = {n: [self._stage(device, slot_elems[n] * item[n]) for _ in range(R)] for n in spans}
+        evs = []
+        for _ in range(3 * R):
+            e = cuda_ext.ctypes.c_void_p()
+            cuda_ext.check(lib.eas_event_create(cuda_ext.ctypes.byref(e)), "event_create")
+            evs.append(int(e.value))
+        ev_in, ev_run, ev_free = evs[:R], evs[R:2 * R], evs[2 * R:]
+        native = ck.plan.native
+        try:
+            for i, z0 in enumerate(range(0, B, S)):
+                z1 = min(B, z0 + S)
+                k = i % R
+                if i >= R:
+                    cuda_ext.check(lib.eas_stream_wait_event(s_in, ev_free[k]), "stream_wait_event")
+                lo: dict[str, int] = {}
+                for n, (x0, bs, span) in spans.items():
+                    lo[n] = x0 + z0 * bs
+                    if n != gp["c"]:
+                        cnt = (z1 - 1 - z0) * bs + span
+                        cuda_ext.check(lib.eas_copy_from_host_async(slots[n][k].ptr, hosts[n].ctypes.data + lo[n] * item[n],
+                                                                    cnt * item[n], s_in), "pipelined GEMM copy in")
+                cuda_ext.check(lib.eas_event_record(ev_in[k], s_in), "event_record")
+                cuda_ext.check(lib.eas_stream_wait_event(s_run, ev_in[k]), "stream_wait_event")
+                args = {n: _Arg(slots[n][k].ptr - lo[n] * item[n], device) for n in spans}
+                if not native.try_launch(self, ck, runtime_args, args, device, s_run, (gx, gy, z1 - z0), ntx,
+                                         pid_base=(0, 0, z0), elem_base=dict(lo)):
+                    self._launch_generic(ck, runtime_args, args, device, s_run, (gx, gy, z1 - z0), ntx, (0, 0, z0))
+                cuda_ext.check(lib.eas_event_record(ev_run[k], s_run), "event_record")
+                cuda_ext.check(lib.eas_stream_wait_event(s_out, ev_run[k]), "stream_wait_event")
+                c = gp["c"]
+                _x0, bs, span = spans[c]
+                cnt = (z1 - 1 - z0) * bs + span
+                cuda_ext.check(lib.eas_copy_to_host_async(hosts[c].ctypes.data + lo[c] * item[c], slots[c][k].ptr,
+                                                          cnt * item[c], s_out), "pipelined GEMM copy out")
+                cuda_ext.check(lib.eas_event_record(ev_free[k], s_out), "event_record")
+            cuda_ext.check(lib.eas_stream_synchronize(s_out), "kernel execution")
+            cuda_ext.check(lib.eas_stream_synchronize(s_run), "kernel execution")
+            self._check_native_status(device)
+            self.skipped_copy_bytes += int(hosts[gp["c"]].nbytes)   # C is stored in full, never copied in
+        finally:
+            for e in evs:
+                lib.eas_event_destroy(e)
+            for bufs in slots.values():
                 for b in bufs:
                     free = self._staging.setdefault((b.device, b.nbytes), [])
                     if len(free) < 4 * R:
