@@ -195,7 +195,25 @@ class FakeLib:
         return 0
 
     def eas_host_is_pinned(self, ptr, out):
-        out._obj.value = 0
+        out._obj.value = int(any(lo <= int(ptr) < hi for lo, hi in getattr(self, "pinned_ranges", [])))
+        return 0
+
+    # streams and events: the fake executes every call at once, in order
+    def eas_stream_create(self, dev, out):
+        self._handles = getattr(self, "_handles", 1000) + 1
+        out._obj.value = self._handles
+        return 0
+
+    def eas_event_create(self, out):
+        return self.eas_stream_create(0, out)
+
+    def eas_event_record(self, ev, stream):
+        return 0
+
+    def eas_event_destroy(self, ev):
+        return 0
+
+    def eas_stream_wait_event(self, stream, ev):
         return 0
 
     def eas_is_available(self):
@@ -385,3 +403,27 @@ def test_elementwise_launch_on_host_arrays_is_zero_copy(fake):
     lib.calls.clear()
     _run(lib, rt, matmul_dot_f16, (x, y, z, M, N, K), grid=(1, M, 1), BLOCK_M=128, BLOCK_N=256, BLOCK_K=64)
     assert any(k[0] == "h2d_async" for k in lib.calls) and any(k[0] == "d2h_async" for k in lib.calls)
+
+
+def test_batched_gemm_on_pinned_host_arrays_is_pipelined(fake, monkeypatch):
+    """Page-locked host arrays of a batched GEMM: batch slices are copied in, multiplied (one native
+    launch per slice) and copied out; C is never copied in and the result is the GEMM's."""
+    from easy_as_b200.runtime.cuda import CudaRuntime
+    from examples.matmul_dot_f16 import matmul_dot_f16
+
+    lib, rt = fake
+    monkeypatch.setattr(CudaRuntime, "GEMM_PIPELINE_SLICE_BYTES", 2 * 2 * (16 * 8 + 8 * 32))   # two batches of A + B per slice
+    batch, M, N, K = 5, 16, 32, 8
+    rng = np.random.default_rng(1)
+    a = rng.standard_normal(batch * M * K).astype(np.float16)
+    b = rng.standard_normal(batch * K * N).astype(np.float16)
+    c = np.full(batch * M * N, np.nan, np.float32)
+    lib.pinned_ranges = [(x.ctypes.data, x.ctypes.data + x.nbytes) for x in (a, b, c)]
+    _run(lib, rt, matmul_dot_f16, (a, b, c, M, N, K), grid=(1, M, batch), BLOCK_M=128, BLOCK_N=256, BLOCK_K=64)
+    gemms = [k for k in lib.calls if k[0] == "gemm"]
+    assert [g[4] for g in gemms] == [2, 2, 1]                       # slices of 2, 2 and 1 batches
+    copies_in = [k[1] for k in lib.calls if k[0] == "h2d_async"]
+    assert sum(copies_in) == a.nbytes + b.nbytes                    # C never copied in
+    assert sum(k[1] for k in lib.calls if k[0] == "d2h_async") == c.nbytes
+    ref = np.matmul(a.reshape(batch, M, K).astype(np.float64), b.reshape(batch, K, N).astype(np.float64))
+    np.testing.assert_allclose(c.reshape(batch, M, N), ref, rtol=1e-5, atol=1e-5)
