@@ -31,6 +31,7 @@ import numpy as np
 from . import mk
 from .analysis import infer_writes
 from .ir import Arg, ArgKind, DType, IRModule, Inst, SIDE_EFFECT_OPS, ValueRef, validate_ir
+from .tensor import Tensor as _Tensor
 
 # ---------------------------------------------------------------------------
 # argument classification
@@ -127,11 +128,16 @@ _SCALAR_SIGS = {bool: ("scalar", DType.BOOL, None), int: ("scalar", DType.U32, N
                 float: ("scalar", DType.F32, None)}
 
 
+_TENSOR_DTYPES = {np.dtype(np.float32): DType.F32, np.dtype(np.float16): DType.F16}
+
+
 def fast_arg_sig(v: Any) -> tuple[Any, ...]:
     """(kind, dtype, device) of one runtime argument; the launch-path form of ``_arg_sig``."""
     s = _SCALAR_SIGS.get(type(v))
     if s is not None:
         return s
+    if type(v) is _Tensor:   # eas.Tensor: dtype and device are fixed at construction
+        return ("buffer", _TENSOR_DTYPES[v._dtype], v._device)
     t = _torch()
     if t is not None and isinstance(v, t.Tensor):
         if v.dtype == t.float32:

@@ -36,6 +36,7 @@ from typing import Any, Mapping
 import numpy as np
 
 from ..ir import DType
+from ..tensor import Tensor
 from . import cuda_ext
 from .grid import grid_rank, infer_1d_grid, infer_grid, infer_nthreads
 
@@ -408,6 +409,13 @@ class CudaRuntime:
                 continue
             v = runtime_args[a.name]
             want = np.float32 if a.dtype == DType.F32 else np.float16
+            if type(v) is Tensor and v._device == "cuda" and v._dtype == want:
+                dev = v._cuda_device()
+                if device is not None and dev != device:
+                    raise ValueError(f"buffers on different devices: {device} and {dev}")
+                device = dev
+                resolved[a.name] = _Arg(v._cuda_ptr(), dev, keep=v)
+                continue
             if torch is not None and type(v) is torch.Tensor and v.is_cuda and not v.requires_grad:
                 # common case first: a contiguous CUDA tensor of the right dtype
                 if v.dtype == (torch.float32 if a.dtype == DType.F32 else torch.float16) and v.is_contiguous():
@@ -723,6 +731,16 @@ class CudaRuntime:
     PIPELINE_CHUNK_ELEMS = 1 << 23      # elements per operand per chunk (32 MiB of f32)
     PIPELINE_SLOTS = 3
 
+    @staticmethod
+    def _first_buffer_on_device(ck: Any, runtime_args: Mapping[str, Any]) -> bool:
+        """The first buffer argument is device memory (a CUDA torch tensor or a CUDA eas.Tensor):
+        the host-pipelined paths, which need every buffer on the host, cannot apply."""
+        first = next((runtime_args[a.name] for a in ck.ir.args if a.kind == "buffer"), None)
+        if type(first) is Tensor:
+            return first._device == "cuda"
+        torch = _torch()
+        return torch is not None and type(first) is torch.Tensor and first.is_cuda
+
     def _pipeline_candidates(self, ck: Any, runtime_args: Mapping[str, Any], geo: Any) -> dict[str, np.ndarray] | None:
         """Host arrays of an elementwise kernel, when the pipelined copy path applies.
 
@@ -734,10 +752,9 @@ class CudaRuntime:
         ew = getattr(ck.plan, "elementwise", None)
         if ew is None:
             return None
-        torch = _torch()
-        first = next((runtime_args[a.name] for a in ck.ir.args if a.kind == "buffer"), None)
-        if torch is not None and type(first) is torch.Tensor and first.is_cuda:
+        if self._first_buffer_on_device(ck, runtime_args):
             return None  # device tensors: nothing to copy
+        torch = _torch()
         if os.environ.get("EAS_PIPELINE", "1") in ("0", "off"):
             return None
         (gx, gy, gz), _ntx = geo
@@ -874,6 +891,8 @@ class CudaRuntime:
         slices."""
         native = getattr(ck.plan, "native", None)
         if native is None or not hasattr(native, "map_launch") or not hasattr(native, "covers"):
+            return None
+        if self._first_buffer_on_device(ck, runtime_args):
             return None
         if os.environ.get("EAS_PIPELINE", "1") in ("0", "off"):
             return None

@@ -427,3 +427,28 @@ def test_batched_gemm_on_pinned_host_arrays_is_pipelined(fake, monkeypatch):
     assert sum(k[1] for k in lib.calls if k[0] == "d2h_async") == c.nbytes
     ref = np.matmul(a.reshape(batch, M, K).astype(np.float64), b.reshape(batch, K, N).astype(np.float64))
     np.testing.assert_allclose(c.reshape(batch, M, N), ref, rtol=1e-5, atol=1e-5)
+
+
+def test_device_eas_tensors_launch_without_host_copies(fake, monkeypatch):
+    """eas.Tensor(device="cuda") arguments are passed by device pointer: no staging, no copies,
+    one launch, and the specialisation cache is hit on the second call."""
+    import easy_as_b200.runtime as R
+
+    lib, rt = fake
+    rt._available = True
+    monkeypatch.setattr(R, "_cuda", rt)
+    n = 3000
+    x = np.arange(n, dtype=np.float32)
+    a, b, c = (eas.empty(n, device="cuda", dtype=np.float32) for _ in range(3))
+    for t, v in ((a, x), (b, 2 * x)):
+        buf, at = lib._find(t._cuda_ptr())
+        np.frombuffer(buf, np.float32, n, at)[:] = v
+    lib.current = add_kernel.compile(a, b, c, n, BLOCK=1024)
+    lib.calls.clear()
+    add_kernel(a, b, c, n, BLOCK=1024)
+    cached = len(add_kernel._cache)
+    add_kernel(a, b, c, n, BLOCK=1024)
+    assert [k[0] for k in lib.calls] == ["launch", "launch"]
+    buf, at = lib._find(c._cuda_ptr())
+    np.testing.assert_array_equal(np.frombuffer(buf, np.float32, n, at), 3 * x)
+    assert len(add_kernel._cache) == cached
