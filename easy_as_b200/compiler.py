@@ -138,6 +138,10 @@ def fast_arg_sig(v: Any) -> tuple[Any, ...]:
         return s
     if type(v) is _Tensor:   # eas.Tensor: dtype and device are fixed at construction
         return ("buffer", _TENSOR_DTYPES[v._dtype], v._device)
+    if type(v) is np.ndarray:
+        dt = _TENSOR_DTYPES.get(v.dtype)
+        if dt is not None:
+            return ("buffer", dt, "cpu")
     t = _torch()
     if t is not None and isinstance(v, t.Tensor):
         if v.dtype == t.float32:

@@ -754,6 +754,9 @@ class CudaRuntime:
             return None
         if self._first_buffer_on_device(ck, runtime_args):
             return None  # device tensors: nothing to copy
+        min_bytes = int(os.environ.get("EAS_PIPELINE_MIN_BYTES", str(64 << 20)))
+        if sum(getattr(runtime_args[a.name], "nbytes", 0) for a in ck.ir.args if a.kind == "buffer") < min_bytes:
+            return None  # small calls: the bounce buffer or per-array staging serves them
         torch = _torch()
         if os.environ.get("EAS_PIPELINE", "1") in ("0", "off"):
             return None
@@ -762,7 +765,6 @@ class CudaRuntime:
             return None
         hosts: dict[str, np.ndarray] = {}
         total = 0
-        lib = self.lib()
         for a in ck.ir.args:
             if a.kind != "buffer":
                 continue
@@ -780,14 +782,16 @@ class CudaRuntime:
             want = np.float32 if a.dtype == DType.F32 else np.float16
             if v.dtype != want:
                 return None
-            pinned = cuda_ext.ctypes.c_int(0)
+            hosts[a.name] = v
+            total += v.nbytes
+        if not hosts or total < min_bytes:
+            return None
+        lib = self.lib()   # only large calls pay for the page-lock queries
+        pinned = cuda_ext.ctypes.c_int(0)
+        for v in hosts.values():
             lib.eas_host_is_pinned(v.ctypes.data, cuda_ext.ctypes.byref(pinned))
             if not pinned.value:
                 return None
-            hosts[a.name] = v
-            total += v.nbytes
-        if not hosts or total < int(os.environ.get("EAS_PIPELINE_MIN_BYTES", str(64 << 20))):
-            return None
         return hosts
 
     def _streams(self, device: int) -> tuple[int, int, int]:
