@@ -39,6 +39,18 @@ Operations
 Hidden parameters follow the IR arguments: ``eas_ntx`` (active threads along
 x, thread mode) and ``eas_pid_{x,y,z}`` (program-id offsets, used to split a
 grid into several launches or across GPUs).
+
+Bounds-checked mode (``EAS_BOUNDS_CHECK=1``, read when a specialisation is
+compiled): every buffer gets two more hidden parameters, ``eas_lo_<name>`` and
+``eas_n_<name>`` (u64: the buffer holds global elements [lo, lo + n)), and the
+kernel takes ``eas_err``, a pointer to four u32 words.  Every global and
+threadgroup access whose mask holds is first tested against its buffer; an
+access outside is skipped (a load yields 0) and the first one is recorded as
+(1, 2 * slot + is_store, index, 0), slot being the buffer's position in the
+argument list or ``CHECK_TG_SLOT`` + the threadgroup allocation's order.  The
+runtime clears the record before the launch and raises after it.  Vector
+accesses and grouped dot loops are off in this mode, so each element is
+tested on its own.
 """
 
 from __future__ import annotations
@@ -80,9 +92,16 @@ class Lowered:
     layout: Any = field(default=None)   # runtime parameter layout, built on first launch
     grid_rank: Any = field(default=None)  # 1 + highest program_id/thread_id axis, cached by the runtime
     reads: frozenset = field(default=frozenset())  # buffer args the kernel may read (analysis.infer_reads)
+    checked: bool = False  # bounds-checked lowering (extra "check" params; see the module docstring)
 
 
 HIDDEN = ("eas_ntx", "eas_pid_x", "eas_pid_y", "eas_pid_z")
+CHECK_TG_SLOT = 1000   # error-record slot of the first threadgroup allocation (bounds-checked mode)
+
+
+def bounds_check_enabled() -> bool:
+    """EAS_BOUNDS_CHECK=1: lower kernels with per-access bounds checks (read at compile time)."""
+    return os.environ.get("EAS_BOUNDS_CHECK", "0") not in ("", "0", "off", "false")
 
 _CXX_RESERVED = {
     "auto", "bool", "break", "case", "char", "class", "const", "continue", "default", "delete", "do",
@@ -149,6 +168,16 @@ static __device__ __forceinline__ float2 eas_mma_f16(uint32_t a01, uint32_t b01,
                : "=f"(d0), "=f"(d1), "=f"(d2), "=f"(d3)
                : "r"(a01), "r"(0u), "r"(b01), "f"(c.x), "f"(c.y), "f"(0.0f), "f"(0.0f));
   return make_float2(d0, d1);
+}
+"""
+
+CHECK_PRELUDE = r"""
+// bounds-checked mode: true when global element i of a buffer holding [lo, lo + n) exists;
+// otherwise the first failing access in the launch is recorded in err[0..2]
+static __device__ __noinline__ bool eas_inb(uint32_t i, uint64_t lo, uint64_t n, uint32_t* err, uint32_t what) {
+  if ((uint64_t)i - lo < n) return true;
+  if (atomicCAS(err, 0u, 1u) == 0u) { err[1] = what; err[2] = i; }
+  return false;
 }
 """
 
@@ -221,8 +250,9 @@ def _as_float(dt: DType, x: str) -> str:
 
 
 class _Emitter:
-    def __init__(self, ir: IRModule):
+    def __init__(self, ir: IRModule, checked: bool = False):
         self.ir = ir
+        self.checked = checked
         self.block, self.mode = infer_block_and_mode(ir)
         self.defs: dict[int, Inst] = {i.out.id: i for i in ir.insts if i.out is not None}
         self.arg_c: dict[int, str] = {}       # value id of an arg -> C identifier
@@ -272,6 +302,14 @@ class _Emitter:
                 self.tg[inst.out.id] = (smem, int(inst.args[0]))
                 smem += -(-nbytes // 16) * 16
         self.smem = smem
+        # error-record slot of each buffer (bounds-checked mode)
+        arg_pos = {a.name: n for n, a in enumerate(ir.args)}
+        self.slot: dict[int, int] = {}
+        for inst in ir.insts:
+            if inst.op == "arg" and str(inst.args[0]) in arg_pos:
+                self.slot[inst.out.id] = arg_pos[str(inst.args[0])]
+        for n, vid in enumerate(self.tg):
+            self.slot[vid] = CHECK_TG_SLOT + n
 
     # -- naming ---------------------------------------------------------------
     def name(self, ref: ValueRef) -> str:
@@ -292,6 +330,31 @@ class _Emitter:
         d = self.defs.get(ref.id)
         return d is not None and d.op == "const" and d.args[0] is True and ref.dtype == DType.BOOL
 
+    def inb(self, buf: ValueRef, idx: str, store: bool = False) -> str:
+        """Bounds test of one access (checked mode), or "true"."""
+        if not self.checked:
+            return "true"
+        what = 2 * self.slot[buf.id] + int(store)
+        if buf.id in self.tg:
+            return f"eas_inb({idx}, 0ull, {self.tg[buf.id][1]}ull, eas_err, {what}u)"
+        c = self.arg_c[buf.id]
+        return f"eas_inb({idx}, eas_lo_{c}, eas_n_{c}, eas_err, {what}u)"
+
+    def ld(self, buf: ValueRef, idx: str) -> str:
+        """Read of one element inside a dot or mma: unguarded, or 0 when out of bounds (checked mode)."""
+        rhs = f"{self.name(buf)}[{idx}]"
+        if not self.checked:
+            return rhs
+        return f"({self.inb(buf, idx)} ? {rhs} : {_zero(buf.dtype)})"
+
+    @staticmethod
+    def both(a: str, b: str) -> str:
+        if a == "true":
+            return b
+        if b == "true":
+            return a
+        return f"({a} && {b})"
+
     def emit(self, line: str, indent: int = 1) -> None:
         self.lines.append("  " * (indent + self.depth) + line)
 
@@ -301,6 +364,12 @@ class _Emitter:
         for a in self.ir.args:
             ps.append(Param(c_ident(a.name), a.kind, a.dtype, a.name))
         ps += [Param(h, "hidden", DType.U32, None) for h in HIDDEN]
+        if self.checked:
+            for a in self.ir.args:
+                if a.kind == "buffer":
+                    c = c_ident(a.name)
+                    ps += [Param(f"eas_lo_{c}", "check", None, a.name), Param(f"eas_n_{c}", "check", None, a.name)]
+            ps.append(Param("eas_err", "check", None, None))
         return ps
 
     def signature(self) -> str:
@@ -316,6 +385,12 @@ class _Emitter:
             else:
                 parts.append(f"const {ctype(a.dtype)} {cn}")
         parts += [f"const uint32_t {h}" for h in HIDDEN]
+        if self.checked:
+            for a in self.ir.args:
+                if a.kind == "buffer":
+                    c = c_ident(a.name)
+                    parts += [f"const uint64_t eas_lo_{c}", f"const uint64_t eas_n_{c}"]
+            parts.append("uint32_t* const eas_err")
         return ",\n    ".join(parts)
 
     # -- main -------------------------------------------------------------------
@@ -324,7 +399,7 @@ class _Emitter:
         name = c_ident(self.ir.name) if self.ir.name else "eas_kernel"
         src = "\n".join([
             f"// generated by easy_as_b200.codegen.cuda for sm_100a ({self.mode} mode, BLOCK={self.block})",
-            PRELUDE,
+            PRELUDE + (CHECK_PRELUDE if self.checked else ""),
             f'extern "C" __global__ void __launch_bounds__({self.cuda_threads}, {self._min_blocks()}) {name}(',
             "    " + self.signature() + ") {",
             # programmatic dependent launch: the next kernel in the stream may be scheduled from now on,
@@ -337,7 +412,8 @@ class _Emitter:
             "",
         ])
         return Lowered(src=src, kernel_name=name, block_size=self.block, mode=self.mode,
-                       cuda_threads=self.cuda_threads, params=self.params(), dyn_smem=self.smem)
+                       cuda_threads=self.cuda_threads, params=self.params(), dyn_smem=self.smem,
+                       checked=self.checked)
 
     def _min_blocks(self) -> int:
         """CTAs per SM to plan registers for: enough for 2048 resident threads (<= 64 registers each),
@@ -482,7 +558,8 @@ class _Emitter:
         return m
 
     def _vector_ok(self, buf: ValueRef, off: ValueRef) -> bool:
-        return self.V == 4 and off.lanes > 1 and off.id in self.unit and buf.id in self.arg_c
+        return (self.V == 4 and off.lanes > 1 and off.id in self.unit and buf.id in self.arg_c
+                and not self.checked)
 
     def _spmd_load(self, inst: Inst) -> None:
         buf, off, mask = inst.args
@@ -491,6 +568,7 @@ class _Emitter:
         z = _zero(out.dtype)
         if out.lanes == 1:
             m = "true" if self.is_const_true(mask) else self.name(mask)
+            m = self.both(m, self.inb(buf, self.name(off)))
             self.emit(f"const {ctype(out.dtype)} v{out.id} = {m} ? {bn}[{self.name(off)}] : {z};")
             return
         self.emit(self._vec_decl(out))
@@ -516,13 +594,16 @@ class _Emitter:
             self.emit("}")
             return
         for i in range(self.L):
-            self.emit(f"v{out.id}[{i}] = {self._lane_mask(mask, i)} ? {bn}[{self.lane(off, str(i))}] : {z};")
+            o = self.lane(off, str(i))
+            m = self.both(self._lane_mask(mask, i), self.inb(buf, o))
+            self.emit(f"v{out.id}[{i}] = {m} ? {bn}[{o}] : {z};")
 
     def _spmd_store(self, inst: Inst) -> None:
         buf, off, val, mask = inst.args
         bn = self.name(buf)
         if off.lanes == 1:
             m = "true" if self.is_const_true(mask) else self.name(mask)
+            m = self.both(m, self.inb(buf, self.name(off), store=True))
             self.emit(f"if (threadIdx.x == 0 && {m}) {bn}[{self.name(off)}] = {self.name(val)};")
             return
         if self._vector_ok(buf, off):
@@ -545,7 +626,9 @@ class _Emitter:
             self.emit("}")
             return
         for i in range(self.L):
-            self.emit(f"if ({self._lane_mask(mask, i)}) {bn}[{self.lane(off, str(i))}] = {self.lane(val, str(i))};")
+            o = self.lane(off, str(i))
+            m = self.both(self._lane_mask(mask, i), self.inb(buf, o, store=True))
+            self.emit(f"if ({m}) {bn}[{o}] = {self.lane(val, str(i))};")
 
     @staticmethod
     def _const(dt: DType, v: Any) -> str:
@@ -690,6 +773,8 @@ class _Emitter:
         insts = self.ir.insts
         out: dict[int, list[int]] = {}
         taken: set[int] = set()
+        if self.checked:
+            return out
 
         def sig(i: Inst) -> tuple[int, ...]:
             a_buf, a_base, a_stride, b_buf, _b_base, b_stride, k = i.args
@@ -831,6 +916,7 @@ class _Emitter:
         elif op == "load":
             buf, off, mask = args
             m = self._guard("true" if self.is_const_true(mask) else self.name(mask))
+            m = self.both(m, self.inb(buf, self.name(off)))
             rhs = f"{self.name(buf)}[{self.name(off)}]"
             if m == "true":
                 self.emit(f"const {ctype(out.dtype)} v{out.id} = {rhs};")
@@ -839,6 +925,7 @@ class _Emitter:
         elif op == "store":
             buf, off, val, mask = args
             m = self._guard("true" if self.is_const_true(mask) else self.name(mask))
+            m = self.both(m, self.inb(buf, self.name(off), store=True))
             st = f"{self.name(buf)}[{self.name(off)}] = {self.name(val)};"
             self.emit(st if m == "true" else f"if ({m}) {st}")
         elif op == "barrier":
@@ -855,8 +942,12 @@ class _Emitter:
             b, s, f = self.name(base), self.name(stride), self.name(frag)
             self.emit("{")
             self.emit(f"const uint32_t eas_o = {b} + (eas_lane >> 2) * {s} + (eas_lane & 3u) * 2u;", 2)
-            pre = "" if g == "true" else f"if ({g}) "
-            self.emit(f"{pre}{{ {self.name(buf)}[eas_o] = {f}.x; {self.name(buf)}[eas_o + 1u] = {f}.y; }}", 2)
+            if self.checked:
+                for e, comp in ((("eas_o"), "x"), (("eas_o + 1u"), "y")):
+                    self.emit(f"if ({self.both(g, self.inb(buf, e, store=True))}) {self.name(buf)}[{e}] = {f}.{comp};", 2)
+            else:
+                pre = "" if g == "true" else f"if ({g}) "
+                self.emit(f"{pre}{{ {self.name(buf)}[eas_o] = {f}.x; {self.name(buf)}[eas_o + 1u] = {f}.y; }}", 2)
             self.emit("}")
         else:
             raise ValueError(f"unsupported op: {op}")
@@ -873,8 +964,8 @@ class _Emitter:
         if unroll:
             self.emit(unroll, 2)
         self.emit(f"for (uint32_t k = 0; k < {self.name(k_ref)}; ++k) {{", 2)
-        av = _as_float(a_buf.dtype, f"{self.name(a_buf)}[ai]")
-        bv = _as_float(b_buf.dtype, f"{self.name(b_buf)}[bi]")
+        av = _as_float(a_buf.dtype, self.ld(a_buf, "ai"))
+        bv = _as_float(b_buf.dtype, self.ld(b_buf, "bi"))
         self.emit(f"v{o} = fmaf({av}, {bv}, v{o});", 3)
         self.emit(f"ai += {self.name(a_stride)}; bi += {self.name(b_stride)};", 3)
         self.emit("}", 2)
@@ -892,12 +983,14 @@ class _Emitter:
         if a_buf.dtype == DType.F16 and b_buf.dtype == DType.F16:
             ai = f"{ab} + eas_g * {as_} + eas_t * 2u"
             bi0 = f"{bb} + (eas_t * 2u) * {bs} + eas_g"
+            a0, a1 = self.ld(a_buf, f"({ai})"), self.ld(a_buf, f"({ai} + 1u)")
+            b0, b1 = self.ld(b_buf, f"({bi0})"), self.ld(b_buf, f"({bi0} + {bs})")
             if on == "true":
-                self.emit(f"const uint32_t eas_a = eas_pack2({A}[{ai}], {A}[{ai} + 1u]);", 2)
-                self.emit(f"const uint32_t eas_b = eas_pack2({B}[{bi0}], {B}[{bi0} + {bs}]);", 2)
+                self.emit(f"const uint32_t eas_a = eas_pack2({a0}, {a1});", 2)
+                self.emit(f"const uint32_t eas_b = eas_pack2({b0}, {b1});", 2)
             else:
-                self.emit(f"const uint32_t eas_a = {on} ? eas_pack2({A}[{ai}], {A}[{ai} + 1u]) : 0u;", 2)
-                self.emit(f"const uint32_t eas_b = {on} ? eas_pack2({B}[{bi0}], {B}[{bi0} + {bs}]) : 0u;", 2)
+                self.emit(f"const uint32_t eas_a = {on} ? eas_pack2({a0}, {a1}) : 0u;", 2)
+                self.emit(f"const uint32_t eas_b = {on} ? eas_pack2({b0}, {b1}) : 0u;", 2)
             self.emit(f"v{o} = eas_mma_f16(eas_a, eas_b, {self.name(acc)});", 2)
         else:
             self.emit(f"float d0 = {self.name(acc)}.x, d1 = {self.name(acc)}.y;", 2)
@@ -905,9 +998,9 @@ class _Emitter:
             self.emit(f"{pre}{{", 2)
             self.emit("#pragma unroll", 3)
             self.emit("for (uint32_t k = 0; k < 8u; ++k) {", 3)
-            av = _as_float(a_buf.dtype, f"{A}[{ab} + eas_g * {as_} + k]")
-            b0 = _as_float(b_buf.dtype, f"{B}[{bb} + k * {bs} + eas_t * 2u]")
-            b1 = _as_float(b_buf.dtype, f"{B}[{bb} + k * {bs} + eas_t * 2u + 1u]")
+            av = _as_float(a_buf.dtype, self.ld(a_buf, f"({ab} + eas_g * {as_} + k)"))
+            b0 = _as_float(b_buf.dtype, self.ld(b_buf, f"({bb} + k * {bs} + eas_t * 2u)"))
+            b1 = _as_float(b_buf.dtype, self.ld(b_buf, f"({bb} + k * {bs} + eas_t * 2u + 1u)"))
             self.emit(f"const float a = {av};", 4)
             self.emit(f"d0 = fmaf(a, {b0}, d0); d1 = fmaf(a, {b1}, d1);", 4)
             self.emit("}", 3)
@@ -1000,9 +1093,19 @@ def elementwise_info(ir: IRModule, block: int, mode: str) -> ElementwiseInfo | N
     return ElementwiseInfo(block, frozenset(reads), frozenset(writes), tuple(bounds))
 
 
-def ir_to_cuda(ir: IRModule) -> Lowered:
-    """Lower validated, optimised IR to one CUDA kernel (plus an optional native plan)."""
-    lowered = _Emitter(ir).run()
+def ir_to_cuda(ir: IRModule, checked: bool | None = None) -> Lowered:
+    """Lower validated, optimised IR to one CUDA kernel (plus an optional native plan).
+
+    ``checked`` (default: ``EAS_BOUNDS_CHECK``) lowers with per-access bounds checks; such a kernel
+    always runs as generated (no native plan) and is not split by the host pipelines."""
+    if checked is None:
+        checked = bounds_check_enabled()
+    lowered = _Emitter(ir, checked).run()
+    if checked:
+        from ..analysis import infer_reads
+
+        lowered.reads = infer_reads(ir)
+        return lowered
     from .patterns import match_native
 
     lowered.native = match_native(ir, lowered)

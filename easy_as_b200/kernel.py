@@ -17,6 +17,7 @@ Behaviour follows easy_as ``eas/kernel.py``:
 from __future__ import annotations
 
 import inspect
+import os as _os
 from typing import Any, Callable, Mapping
 
 from .autotune import AutotuneSpec, Config
@@ -181,7 +182,8 @@ class Kernel:
         # kinds/dtypes/devices of the runtime args, never scalar values (same distinctions as
         # runtime_arg_signature, computed without sorting on the launch path)
         key = (tuple(sorted(meta.items())) if len(meta) > 1 else tuple(meta.items()),
-               tuple((n, fast_arg_sig(v)) for n, v in runtime_args.items()))
+               tuple((n, fast_arg_sig(v)) for n, v in runtime_args.items()),
+               _os.environ.get("EAS_BOUNDS_CHECK"))   # checked and unchecked lowerings are distinct
         ck = self._cache.get(key)
         if ck is None:
             ck = _compile(self.fn, runtime_args, meta)

@@ -113,7 +113,7 @@ class ParamLayout:
         self.entries: list[tuple[Any, int, str]] = []
         off = 0
         for p in params:
-            if p.kind == "buffer":
+            if p.kind in ("buffer", "check"):   # pointers; the u64 bounds of the checked mode
                 fmt, size = "<Q", 8
             else:
                 fmt, size = _SCALAR_FMT[p.dtype]
@@ -137,7 +137,7 @@ class ParamLayout:
         for p, _off, _fmt in self.entries:
             if p.kind == "buffer":
                 vals.append(pointers[p.arg])
-            elif p.kind == "hidden":
+            elif p.kind in ("hidden", "check"):
                 vals.append(hidden[p.name])
             else:
                 vals.append(_scalar_bits(p.dtype, values[p.arg], p.arg))
@@ -155,6 +155,32 @@ def _scalar_bits(dt: DType, v: Any, name: str) -> Any:
     if dt == DType.F16:
         return int(np.array(v, dtype=np.float16).view(np.uint16))
     return bool(v)
+
+
+def _elem_count(v: Any) -> int:
+    """Elements of a buffer argument (numpy array, torch tensor or eas.Tensor)."""
+    if isinstance(v, np.ndarray):
+        return int(v.size)
+    numel = getattr(v, "numel", None)
+    if callable(numel):
+        return int(numel())
+    return int(v.nbytes) // np.dtype(v.dtype).itemsize
+
+
+def _describe_violation(ck: Any, what: int, index: int, bounds: Mapping[str, tuple[int, int]]) -> str:
+    """Message for the error record (2 * slot + is_store, index) of a bounds-checked kernel."""
+    from ..codegen.cuda import CHECK_TG_SLOT
+
+    slot, store = divmod(what, 2)
+    verb = "store to" if store else "load from"
+    kernel = ck.plan.kernel_name
+    if slot >= CHECK_TG_SLOT:
+        n = [int(i.args[0]) for i in ck.ir.insts if i.op == "alloc_tg"][slot - CHECK_TG_SLOT]
+        return (f"{kernel}: out-of-bounds {verb} threadgroup allocation #{slot - CHECK_TG_SLOT} at element "
+                f"{index} (it holds {n} elements)")
+    name = ck.ir.args[slot].name
+    lo, n = bounds.get(name, (0, 0))
+    return f"{kernel}: out-of-bounds {verb} {name!r} at element {index} (valid elements: [{lo}, {lo + n}))"
 
 
 # ---------------------------------------------------------------------------
@@ -260,6 +286,7 @@ class CudaRuntime:
         self._max_in_flight: int | None = None
         self._staging: dict[tuple[int, int], list[DeviceBuffer]] = {}
         self._bounce: dict[int, _Bounce] = {}
+        self._check_records: dict[int, DeviceBuffer] = {}   # per device: error record of checked kernels
         self._pdl_on: bool | None = None
         self.skipped_copy_bytes = 0  # host->device bytes not copied because a launch stores all of them
         self._bucket_keep: list[Any] = []
@@ -604,7 +631,17 @@ class CudaRuntime:
     # -- launch -------------------------------------------------------------------------
     def _launch_generic(self, ck: Any, runtime_args: Mapping[str, Any], args: dict[str, _Arg], device: int,
                         stream: int, programs: tuple[int, int, int], ntx: int,
-                        pid_base: tuple[int, int, int] = (0, 0, 0)) -> None:
+                        pid_base: tuple[int, int, int] = (0, 0, 0),
+                        elem_base: Mapping[str, int] | None = None) -> None:
+        plan = ck.plan
+        if plan.checked:
+            self._launch_checked(ck, runtime_args, args, device, stream, programs, ntx, pid_base, elem_base or {})
+            return
+        self._launch_generic_raw(ck, runtime_args, args, device, stream, programs, ntx, pid_base, None)
+
+    def _launch_generic_raw(self, ck: Any, runtime_args: Mapping[str, Any], args: dict[str, _Arg], device: int,
+                            stream: int, programs: tuple[int, int, int], ntx: int, pid_base: tuple[int, int, int],
+                            extra: Mapping[str, int] | None) -> None:
         plan = ck.plan
         pipe = self._pipeline_for(ck, device)
         layout = plan.layout
@@ -619,12 +656,47 @@ class CudaRuntime:
             for y0 in range(0, gy, MAX_GRID_YZ):
                 hidden = {"eas_ntx": ntx, "eas_pid_x": pid_base[0], "eas_pid_y": pid_base[1] + y0,
                           "eas_pid_z": pid_base[2] + z0}
+                if extra:
+                    hidden.update(extra)
                 blob = layout.pack(runtime_args, ptrs, hidden)
                 g = (cuda_ext.ctypes.c_uint32 * 3)(gx, min(MAX_GRID_YZ, gy - y0), min(MAX_GRID_YZ, gz - z0))
                 launch = lib.eas_launch_pdl if self._pdl() else lib.eas_launch
                 cuda_ext.check(launch(pipe, g, block, plan.dyn_smem, stream, blob, layout.offsets, layout.count),
                                f"launch {plan.kernel_name}")
                 self.launch_count += 1
+
+    # -- bounds-checked kernels (EAS_BOUNDS_CHECK) ---------------------------------------
+    def _launch_checked(self, ck: Any, runtime_args: Mapping[str, Any], args: dict[str, _Arg], device: int,
+                        stream: int, programs: tuple[int, int, int], ntx: int, pid_base: tuple[int, int, int],
+                        elem_base: Mapping[str, int]) -> None:
+        """Launch a bounds-checked kernel: pass each buffer's element range, clear the error record
+        before and read it after the launch (the stream is synchronised), and raise IndexError
+        for the first access outside its buffer.  The access itself was skipped on the device."""
+        capturing = cuda_ext.ctypes.c_int(0)
+        self.lib().eas_stream_is_capturing(stream, cuda_ext.ctypes.byref(capturing))
+        if capturing.value:
+            raise ValueError("bounds-checked kernels (EAS_BOUNDS_CHECK=1) cannot be captured in a CUDA graph")
+        rec = self._check_records.get(device)
+        if rec is None:
+            rec = self._check_records[device] = DeviceBuffer(16, device)
+        zero = np.zeros(4, np.uint32)
+        rec.copy_from_host(zero, stream)
+        extra: dict[str, int] = {"eas_err": rec.ptr}
+        bounds: dict[str, tuple[int, int]] = {}
+        for p in ck.plan.params:
+            if p.kind == "check" and p.arg is not None and p.arg not in bounds:
+                lo = int(elem_base.get(p.arg, 0))
+                bounds[p.arg] = (lo, _elem_count(runtime_args[p.arg]))
+        for p in ck.plan.params:
+            if p.kind == "check" and p.arg is not None:
+                lo, n = bounds[p.arg]
+                extra[p.name] = lo if p.name.startswith("eas_lo_") else n
+        self._launch_generic_raw(ck, runtime_args, args, device, stream, programs, ntx, pid_base, extra)
+        cuda_ext.check(self.lib().eas_stream_synchronize(stream), "kernel execution")
+        out = np.zeros(4, np.uint32)
+        rec.copy_to_host(out, stream)
+        if out[0]:
+            raise IndexError(_describe_violation(ck, int(out[1]), int(out[2]), bounds))
 
     def _dispatch(self, ck: Any, runtime_args: Mapping[str, Any], args: dict[str, _Arg], device: int, stream: int,
                   programs: tuple[int, int, int], ntx: int) -> None:
@@ -1043,7 +1115,8 @@ class CudaRuntime:
         native = getattr(ck.plan, "native", None)
         if native is None or not native.try_launch(self, ck, runtime_args, args, device, stream, tuple(sub), ntx,
                                                    pid_base=tuple(base), elem_base=dict(buffer_base or {})):
-            self._launch_generic(ck, runtime_args, args, device, stream, tuple(sub), ntx, tuple(base))
+            self._launch_generic(ck, runtime_args, args, device, stream, tuple(sub), ntx, tuple(base),
+                                 dict(buffer_base or {}))
         if sync:
             cuda_ext.check(self.lib().eas_stream_synchronize(stream), "kernel execution")
             self._check_native_status(device)

@@ -146,11 +146,16 @@ class FakeLib:
                 dt = np.float32 if arg.dtype == DType.F32 else np.float16
                 args[p.arg] = np.frombuffer(buf, dtype=dt, count=(len(buf) - at) // np.dtype(dt).itemsize,
                                             offset=at)
-            elif p.kind == "hidden":
+            elif p.kind in ("hidden", "check"):
                 hidden[p.name] = v
             else:
                 args[p.arg] = v
         self.scalars = {k: v for k, v in args.items() if not isinstance(v, np.ndarray)}
+        self.hidden = hidden
+        if getattr(self, "violation", None) is not None:   # a checked kernel's device-side record
+            buf, at = self._find(hidden["eas_err"])
+            np.frombuffer(buf, np.uint32, 4, at)[:3] = (1, *self.violation)
+            return 0
         assert all(hidden.get(k, 0) == 0 for k in ("eas_pid_x", "eas_pid_y", "eas_pid_z"))
         execute(ck.ir, args, grid=tuple(grid))
         return 0
@@ -187,7 +192,7 @@ class FakeLib:
         return 0
 
     def eas_stream_is_capturing(self, stream, out):
-        out._obj.value = 0
+        out._obj.value = int(getattr(self, "capturing", 0))
         return 0
 
     def eas_gemm_status(self, dev, out):
@@ -452,3 +457,100 @@ def test_device_eas_tensors_launch_without_host_copies(fake, monkeypatch):
     buf, at = lib._find(c._cuda_ptr())
     np.testing.assert_array_equal(np.frombuffer(buf, np.float32, n, at), 3 * x)
     assert len(add_kernel._cache) == cached
+
+
+@pytest.fixture
+def checked(monkeypatch):
+    monkeypatch.setenv("EAS_BOUNDS_CHECK", "1")
+
+
+def test_checked_kernel_gets_each_buffers_bounds_and_a_clear_record(fake, checked):
+    """EAS_BOUNDS_CHECK=1: the launch carries (lo, n) of every buffer and the error-record pointer;
+    the record is cleared before the launch and a clean record raises nothing."""
+    lib, rt = fake
+    a = np.arange(1031, dtype=np.float32)
+    b = np.ones(1031, np.float32)
+    c = np.zeros(1031, np.float32)
+    ck = _run(lib, rt, add_kernel, (a, b, c, 1031), BLOCK=256)
+    assert ck.plan.checked
+    h = lib.hidden
+    assert (h["eas_lo_a"], h["eas_n_a"], h["eas_lo_b"], h["eas_n_b"], h["eas_lo_c"], h["eas_n_c"]) == \
+        (0, 1031, 0, 1031, 0, 1031)
+    buf, at = lib._find(h["eas_err"])
+    assert not np.frombuffer(buf, np.uint32, 4, at).any()
+    np.testing.assert_array_equal(c, a + b)
+
+
+def test_checked_kernel_raises_on_a_recorded_violation(fake, checked):
+    """A record (1, 2 * slot + is_store, index) written by the device raises IndexError naming the
+    buffer, the access and its valid range."""
+    lib, rt = fake
+    a, b, c = np.ones(100, np.float32), np.ones(100, np.float32), np.zeros(100, np.float32)
+    lib.violation = (2 * 2 + 1, 130)   # store to argument 2 ("c") at element 130
+    with pytest.raises(IndexError, match=r"out-of-bounds store to 'c' at element 130 \(valid elements: \[0, 100\)\)"):
+        _run(lib, rt, add_kernel, (a, b, c, 100), BLOCK=256)
+    lib.violation = (2 * 1, 7)
+    with pytest.raises(IndexError, match=r"load from 'b' at element 7"):
+        _run(lib, rt, add_kernel, (a, b, c, 100), BLOCK=256)
+
+
+def test_checked_kernel_reports_threadgroup_violations(fake, checked):
+    """Slots from CHECK_TG_SLOT on name a threadgroup allocation and its size."""
+    from easy_as_b200.codegen.cuda import CHECK_TG_SLOT
+
+    @eas.kernel
+    def tg_copy(x, y, N, BLOCK: eas.constexpr):
+        t = mk.tid(0, BLOCK)
+        s = mk.alloc_tg(BLOCK)
+        g = mk.program_id(0) * BLOCK + t
+        mk.store(s, t, mk.load(x, g, g < N), True)
+        mk.barrier()
+        mk.store(y, g, mk.load(s, t, True), g < N)
+
+    lib, rt = fake
+    x, y = np.arange(64, dtype=np.float32), np.zeros(64, np.float32)
+    lib.violation = (2 * CHECK_TG_SLOT + 1, 99)
+    with pytest.raises(IndexError, match=r"store to threadgroup allocation #0 at element 99 \(it holds 32 elements\)"):
+        _run(lib, rt, tg_copy, (x, y, 64), BLOCK=32)
+
+
+def test_checked_kernels_run_as_generated(fake, checked):
+    """A checked fp16 dot GEMM has no native plan (the generated kernel, with its checks, runs) and
+    an elementwise kernel is not offered to the host pipelines."""
+    from examples.matmul_dot_f16 import matmul_dot_f16
+
+    lib, rt = fake
+    M, N, K = 16, 32, 8
+    a = np.ones(M * K, np.float16)
+    b = np.ones(K * N, np.float16)
+    c = np.zeros(M * N, np.float32)
+    ck = matmul_dot_f16.compile(a, b, c, M, N, K, BLOCK_M=128, BLOCK_N=256, BLOCK_K=64)
+    assert ck.plan.checked and ck.plan.native is None
+    ck2 = add_kernel.compile(c, c, c, M * N, BLOCK=256)
+    assert ck2.plan.checked and ck2.plan.elementwise is None
+
+
+def test_checked_range_launch_passes_the_element_base(fake, checked, monkeypatch):
+    """run_range with buffer_base={name: e}: the buffer holds global elements [e, e + n)."""
+    lib, rt = fake
+    n = 512
+    a, b, c = (eas.empty(n, device="cuda", dtype=np.float32) for _ in range(3))
+    ck = add_kernel.compile(a, b, c, 4 * n, BLOCK=256)
+    lib.current = ck
+    monkeypatch.setattr(lib, "eas_launch", lambda *args: (setattr(lib, "blob", args[5]), 0)[1])
+    monkeypatch.setattr(lib, "eas_launch_pdl", lib.eas_launch)
+    rt.run_range(ck, {"a": a, "b": b, "c": c, "N": 4 * n}, {"BLOCK": 256}, axis=0, lo=4, hi=6,
+                 buffer_base={"a": 1024, "b": 1024, "c": 1024})
+    vals = {p.name: struct.unpack_from(f, lib.blob, o)[0] for p, o, f in ck.plan.layout.entries}
+    assert (vals["eas_lo_c"], vals["eas_n_c"], vals["eas_pid_x"]) == (1024, n, 4)
+
+
+def test_checked_kernel_refuses_graph_capture(fake, checked):
+    lib, rt = fake
+    n = 256
+    a, b, c = (eas.empty(n, device="cuda", dtype=np.float32) for _ in range(3))
+    ck = add_kernel.compile(a, b, c, n, BLOCK=256)
+    lib.current = ck
+    lib.capturing = 1
+    with pytest.raises(ValueError, match="cannot be captured"):
+        rt.run(ck, {"a": a, "b": b, "c": c, "N": n}, {"BLOCK": 256}, sync=False, grid=None)
