@@ -12,6 +12,7 @@ launch errors surface as Python exceptions."""
 from __future__ import annotations
 
 import ctypes
+import re
 import struct
 
 import numpy as np
@@ -19,9 +20,10 @@ import pytest
 
 import eas
 from eas import mk
+from easy_as_b200.codegen.cuda import CHECK_TG_SLOT
 from easy_as_b200.ir import DType
 from easy_as_b200.runtime import cuda_ext
-from oracle.interp import execute
+from oracle.interp import OracleError, execute
 
 
 @eas.kernel
@@ -152,12 +154,26 @@ class FakeLib:
                 args[p.arg] = v
         self.scalars = {k: v for k, v in args.items() if not isinstance(v, np.ndarray)}
         self.hidden = hidden
+        for p, _off, _fmt in layout.entries:   # a checked kernel's buffers are exactly eas_n_<name> long
+            if p.kind == "check" and p.name.startswith("eas_n_"):
+                args[p.arg] = args[p.arg][:hidden[p.name]]
         if getattr(self, "violation", None) is not None:   # a checked kernel's device-side record
             buf, at = self._find(hidden["eas_err"])
             np.frombuffer(buf, np.uint32, 4, at)[:3] = (1, *self.violation)
             return 0
         assert all(hidden.get(k, 0) == 0 for k in ("eas_pid_x", "eas_pid_y", "eas_pid_z"))
-        execute(ck.ir, args, grid=tuple(grid))
+        if "eas_err" not in hidden:
+            execute(ck.ir, args, grid=tuple(grid))
+            return 0
+        try:   # a checked kernel: an access the oracle refuses becomes the device's error record
+            execute(ck.ir, args, grid=tuple(grid))
+        except OracleError as e:
+            m = re.match(r"out-of-bounds (load from|store to) '?(\w+)'?: index (\d+)", str(e))
+            assert m, str(e)
+            names = [a.name for a in ck.ir.args]
+            slot = names.index(m.group(2)) if m.group(2) in names else CHECK_TG_SLOT
+            buf, at = self._find(hidden["eas_err"])
+            np.frombuffer(buf, np.uint32, 4, at)[:3] = (1, 2 * slot + (m.group(1) == "store to"), int(m.group(3)))
         return 0
 
     def eas_launch_pdl(self, *args):
@@ -554,3 +570,16 @@ def test_checked_kernel_refuses_graph_capture(fake, checked):
     lib.capturing = 1
     with pytest.raises(ValueError, match="cannot be captured"):
         rt.run(ck, {"a": a, "b": b, "c": c, "N": n}, {"BLOCK": 256}, sync=False, grid=None)
+
+
+def test_out_of_bounds_corpus_raises_index_error_when_checked(fake, checked):
+    """Each kernel of tests/oob_kernels.py, launched checked: the (simulated) device record reaches
+    the caller as IndexError naming the buffer and the access."""
+    from oob_kernels import OOB_CASES
+
+    lib, rt = fake
+    for _cid, kernel, make, meta, grid, buf, kind in OOB_CASES:
+        verb = "load from" if kind == "load" else "store to"
+        where = f"{buf!r}" if buf else "threadgroup allocation #0"
+        with pytest.raises(IndexError, match=f"out-of-bounds {verb} {where}"):
+            _run(lib, rt, kernel, make(), grid=grid, **meta)
