@@ -98,3 +98,27 @@ def _compile(src: str, name: str) -> int:
 def test_checked_reference_kernels_compile_for_sm100a(cid):
     lo = lower(cid)
     assert _compile(lo.src, lo.kernel_name) == 0, cuda_ext.last_error()
+
+
+def test_checked_fuzz_kernels_compile_and_stay_in_bounds():
+    """The differential fuzzer's spmd and thread-mode kernels (tests/fuzz_kernels.py) lower
+    checked and compile; the oracle finds no out-of-bounds access in them, so on a GPU their
+    checked runs must report none."""
+    import fuzz_kernels
+    from oracle.interp import execute
+
+    for seed in range(0, 40, 8):
+        k, _src = fuzz_kernels.make(seed)
+        n = 300 + seed
+        args = fuzz_kernels.inputs(seed, n)
+        ck = k.compile(*(args[a] for a in ("x", "y", "h", "out", "outi", "outh", "N", "S", "alpha")), BLOCK=64)
+        execute(ck.ir, dict(args), grid=(-(-n // 64), 1, 1))
+        lo = ir_to_cuda(ck.ir, checked=True)
+        assert _compile(lo.src, lo.kernel_name) == 0, cuda_ext.last_error()
+    for seed in range(0, 30, 6):
+        k, _src, meta = fuzz_kernels.make_thread(seed)
+        n = 500 + 11 * seed
+        args = fuzz_kernels.thread_inputs(seed, n)
+        ck = k.compile(*(args[a] for a in ("x", "y", "out", "N", "S", "alpha")), **meta)
+        lo = ir_to_cuda(ck.ir, checked=True)
+        assert _compile(lo.src, lo.kernel_name) == 0, cuda_ext.last_error()
