@@ -144,10 +144,11 @@ def fast_arg_sig(v: Any) -> tuple[Any, ...]:
             return ("buffer", dt, "cpu")
     t = _torch()
     if t is not None and isinstance(v, t.Tensor):
+        dev = "cuda" if v.is_cuda else v.device.type
         if v.dtype == t.float32:
-            return ("buffer", DType.F32, v.device.type)
+            return ("buffer", DType.F32, dev)
         if v.dtype == t.float16:
-            return ("buffer", DType.F16, v.device.type)
+            return ("buffer", DType.F16, dev)
     sig = _arg_sig(v)
     return (sig.kind, sig.dtype, sig.device)
 
