@@ -181,19 +181,22 @@ class _Machine:
     """Executes one launch for all programs/threads in lockstep."""
 
     def __init__(self, ir: Any, buffers: dict[str, np.ndarray], scalars: dict[str, Any], block: int, mode: str,
-                 programs: tuple[int, int, int], n_threads_1d: int | None):
+                 programs: tuple[int, int, int], n_threads_1d: int | None,
+                 pid_base: tuple[int, int, int] = (0, 0, 0)):
         self.ir, self.buffers, self.scalars = ir, buffers, scalars
         self.block, self.mode = block, mode
         gx, gy, gz = programs
+        bx, by, bz = (int(b) for b in pid_base)
         self.P = gx * gy * gz
         pid = np.arange(self.P, dtype=np.int64)
-        self.pid = ((pid % gx).astype(U32), ((pid // gx) % gy).astype(U32), (pid // (gx * gy)).astype(U32))
+        self.pid = ((pid % gx + bx).astype(U32), ((pid // gx) % gy + by).astype(U32),
+                    (pid // (gx * gy) + bz).astype(U32))
         if mode == "thread":
             # threads: (program, local) pairs; a 1D launch of exactly n threads drops the tail of the last group
             loc = np.tile(np.arange(block, dtype=np.int64), self.P)
             grp = np.repeat(np.arange(self.P, dtype=np.int64), block)
             if n_threads_1d is not None:
-                keep = grp * block + loc < n_threads_1d
+                keep = (grp + bx) * block + loc < n_threads_1d   # global thread index, as on the device
                 loc, grp = loc[keep], grp[keep]
             self.loc, self.grp = loc, grp
             self.shape = (len(loc),)
@@ -401,9 +404,16 @@ class _Machine:
 
 
 def execute(ir: Any, runtime_args: Mapping[str, Any], *, nthreads: int | None = None,
-            grid: tuple[int, ...] | None = None, shape: tuple[int, ...] | None = None) -> None:
-    """Run ``ir`` once on the CPU.  Buffers are numpy arrays, updated in place."""
+            grid: tuple[int, ...] | None = None, shape: tuple[int, ...] | None = None,
+            pid_base: tuple[int, int, int] = (0, 0, 0), ntx: int | None = None) -> None:
+    """Run ``ir`` once on the CPU.  Buffers are numpy arrays, updated in place.
+
+    ``pid_base`` and ``ntx`` describe one launch of a split grid, as the generated kernel's hidden
+    parameters do: program ids start at ``pid_base``, and in thread mode only global threads below
+    ``ntx`` run."""
     block, mode, programs, n1d = geometry(ir, runtime_args, nthreads=nthreads, grid=grid, shape=shape)
+    if ntx is not None and mode == "thread":
+        n1d = int(ntx)
     if min(programs) == 0 or (n1d is not None and n1d == 0):
         return
     buffers: dict[str, np.ndarray] = {}
@@ -416,4 +426,4 @@ def execute(ir: Any, runtime_args: Mapping[str, Any], *, nthreads: int | None = 
             buffers[arg.name] = v
         else:
             scalars[arg.name] = v
-    _Machine(ir, buffers, scalars, block, mode, programs, n1d).run()
+    _Machine(ir, buffers, scalars, block, mode, programs, n1d, pid_base).run()

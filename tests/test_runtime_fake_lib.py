@@ -41,7 +41,13 @@ def scale_kernel(x, y, N, alpha, BLOCK: eas.constexpr):
 
 
 class FakeLib:
-    """The subset of the C ABI the launch path calls, with host memory standing in for HBM."""
+    """The subset of the C ABI the launch path calls, with host memory standing in for HBM.
+
+    Every device allocation has GUARD bytes in front of it: a launch over program sub-range
+    [p0, p1) may pass a pointer moved back by p0 * BLOCK elements (slot buffers holding only that
+    range), which then still points into the same allocation."""
+
+    GUARD = 1 << 18
 
     def __init__(self):
         self.mem: dict[int, ctypes.Array] = {}
@@ -59,15 +65,15 @@ class FakeLib:
         raise AssertionError(f"pointer {ptr:#x} is not a fake device allocation")
 
     def eas_alloc_buffer(self, dev, nbytes, out):
-        buf = ctypes.create_string_buffer(max(int(nbytes), 1))
+        buf = ctypes.create_string_buffer(self.GUARD + max(int(nbytes), 1))
         addr = ctypes.addressof(buf)
         self.mem[addr] = buf
-        out._obj.value = addr
+        out._obj.value = addr + self.GUARD
         self.calls.append(("alloc", int(nbytes)))
         return 0
 
     def eas_free_buffer(self, ptr):
-        self.mem.pop(int(ptr), None)
+        self.mem.pop(int(ptr) - self.GUARD, None)
         return 0
 
     def eas_copy_from_host(self, dst, src, nbytes, stream):
@@ -161,12 +167,14 @@ class FakeLib:
             buf, at = self._find(hidden["eas_err"])
             np.frombuffer(buf, np.uint32, 4, at)[:3] = (1, *self.violation)
             return 0
-        assert all(hidden.get(k, 0) == 0 for k in ("eas_pid_x", "eas_pid_y", "eas_pid_z"))
+        run = dict(grid=tuple(grid), pid_base=(hidden["eas_pid_x"], hidden["eas_pid_y"], hidden["eas_pid_z"]),
+                   ntx=hidden["eas_ntx"])
+        self.pid_bases = getattr(self, "pid_bases", []) + [run["pid_base"]]
         if "eas_err" not in hidden:
-            execute(ck.ir, args, grid=tuple(grid))
+            execute(ck.ir, args, **run)
             return 0
         try:   # a checked kernel: an access the oracle refuses becomes the device's error record
-            execute(ck.ir, args, grid=tuple(grid))
+            execute(ck.ir, args, **run)
         except OracleError as e:
             m = re.match(r"out-of-bounds (load from|store to) '?(\w+)'?: index (\d+)", str(e))
             assert m, str(e)
@@ -583,3 +591,52 @@ def test_out_of_bounds_corpus_raises_index_error_when_checked(fake, checked):
         where = f"{buf!r}" if buf else "threadgroup allocation #0"
         with pytest.raises(IndexError, match=f"out-of-bounds {verb} {where}"):
             _run(lib, rt, kernel, make(), grid=grid, **meta)
+
+
+def test_elementwise_launch_on_pinned_host_arrays_is_pipelined(fake, monkeypatch):
+    """Large page-locked host arrays of an elementwise kernel: program ranges of one chunk each are
+    copied in, run on slot buffers (pointers moved back by the chunk start, program ids offset by
+    it) and copied out.  c is only written, so it is never copied in, and only its elements below
+    the store bound N come back: host elements past N keep their values."""
+    from easy_as_b200.runtime.cuda import CudaRuntime
+
+    lib, rt = fake
+    monkeypatch.setenv("EAS_PIPELINE_MIN_BYTES", "4096")
+    monkeypatch.setattr(CudaRuntime, "PIPELINE_CHUNK_ELEMS", 1024)
+    n, extra = 10_000, 37
+    rng = np.random.default_rng(3)
+    a = rng.standard_normal(n + extra).astype(np.float32)
+    b = rng.standard_normal(n + extra).astype(np.float32)
+    c = np.full(n + extra, -7.0, np.float32)
+    lib.pinned_ranges = [(x.ctypes.data, x.ctypes.data + x.nbytes) for x in (a, b, c)]
+    lib.pid_bases = []
+    _run(lib, rt, add_kernel, (a, b, c, n), BLOCK=256)
+    gx = -(-n // 256)
+    assert lib.pid_bases == [(p0, 0, 0) for p0 in range(0, gx, 4)]
+    assert sum(k[1] for k in lib.calls if k[0] == "h2d_async") == 2 * 4 * (n + extra)   # a and b, not c
+    assert sum(k[1] for k in lib.calls if k[0] == "d2h_async") == 4 * n
+    np.testing.assert_array_equal(c[:n], a[:n] + b[:n])
+    assert (c[n:] == -7.0).all()
+
+
+def test_thread_mode_program_offsets_reach_the_oracle(fake):
+    """run_range on a thread-mode kernel: the launch's program-id offset and exact thread count
+    decide which global threads run, as in the generated kernel."""
+
+    @eas.kernel
+    def tfill(y, N, BLOCK: eas.constexpr):
+        t = mk.program_id(0) * BLOCK + mk.tid(0, BLOCK)
+        mk.store(y, t, mk.to_f32(t) + 0.5, t < N)
+
+    lib, rt = fake
+    n = 1000
+    y = eas.empty(n, device="cuda", dtype=np.float32)
+    buf, at = lib._find(y._cuda_ptr())
+    view = np.frombuffer(buf, np.float32, n, at)
+    view[:] = -1.0
+    ck = tfill.compile(y, n, BLOCK=128)
+    lib.current = ck
+    rt.run_range(ck, {"y": y, "N": n}, {"BLOCK": 128}, axis=0, lo=3, hi=8)
+    want = np.full(n, -1.0, np.float32)
+    want[3 * 128:n] = np.arange(3 * 128, n, dtype=np.float32) + 0.5
+    np.testing.assert_array_equal(view, want)
