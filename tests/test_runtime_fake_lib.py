@@ -640,3 +640,36 @@ def test_thread_mode_program_offsets_reach_the_oracle(fake):
     want = np.full(n, -1.0, np.float32)
     want[3 * 128:n] = np.arange(3 * 128, n, dtype=np.float32) + 0.5
     np.testing.assert_array_equal(view, want)
+
+
+def test_program_id_shards_on_slice_buffers(fake, monkeypatch):
+    """shard.run_shard for each of three ranks, each holding only its element slice of a, b and c
+    (buffer_base = the slice start): the slices put together equal a + b.  The ranks run one
+    after another in this process; no collective is involved."""
+    import easy_as_b200.runtime as R
+    from easy_as_b200.shard import element_range, run_shard
+
+    lib, rt = fake
+    rt._available = True
+    monkeypatch.setattr(R, "_cuda", rt)
+    n, world, block = 30_001, 3, 256
+    rng = np.random.default_rng(5)
+    a = rng.standard_normal(n).astype(np.float32)
+    b = rng.standard_normal(n).astype(np.float32)
+    out = np.zeros(n, np.float32)
+    for rank in range(world):
+        e0, e1 = element_range(n, block, rank, world)
+        sl = {}
+        for name, src in (("a", a), ("b", b), ("c", None)):
+            t = eas.empty(e1 - e0, device="cuda", dtype=np.float32)
+            if src is not None:
+                buf, at = lib._find(t._cuda_ptr())
+                np.frombuffer(buf, np.float32, e1 - e0, at)[:] = src[e0:e1]
+            sl[name] = t
+        lib.current = add_kernel.compile(sl["a"], sl["b"], sl["c"], n, BLOCK=block)
+        lo, hi = run_shard(add_kernel, sl["a"], sl["b"], sl["c"], n, BLOCK=block, _rank=rank, _world=world,
+                           _buffer_base={"a": e0, "b": e0, "c": e0})
+        assert (lo * block, min(hi * block, n)) == (e0, e1)
+        buf, at = lib._find(sl["c"]._cuda_ptr())
+        out[e0:e1] = np.frombuffer(buf, np.float32, e1 - e0, at)
+    np.testing.assert_array_equal(out, a + b)
