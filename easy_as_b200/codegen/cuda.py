@@ -489,7 +489,7 @@ class _Emitter:
             self.emit(f"const {ctype(out.dtype)} v{out.id} = {expr_of_i('0')};")
             return
         self.emit(self._vec_decl(out))
-        self.emit(f"#pragma unroll\nfor (int i = 0; i < {self.L}; ++i) v{out.id}[i] = {expr_of_i('i')};")
+        self.emit(f"#pragma unroll\nfor (int eas_i = 0; eas_i < {self.L}; ++eas_i) v{out.id}[eas_i] = {expr_of_i('eas_i')};")
 
     def _spmd_inst(self, inst: Inst) -> None:
         op, out, args = inst.op, inst.out, inst.args
@@ -583,9 +583,9 @@ class _Emitter:
                 allm = " && ".join(ms)
                 i0 = j * 4
                 self.emit(f"if (eas_al && {allm}) {{", 2)
-                self.emit(f"const {vt} t = *reinterpret_cast<const {vt}*>({bn} + {self.lane(off, str(i0))});", 3)
+                self.emit(f"const {vt} eas_v = *reinterpret_cast<const {vt}*>({bn} + {self.lane(off, str(i0))});", 3)
                 for e, comp in enumerate("xyzw"):
-                    self.emit(f"v{out.id}[{i0 + e}] = t.{comp};", 3)
+                    self.emit(f"v{out.id}[{i0 + e}] = eas_v.{comp};", 3)
                 self.emit("} else {", 2)
                 for e in range(4):
                     i = i0 + e
@@ -831,25 +831,25 @@ class _Emitter:
                 vec = bases[0][2]
         guard = self._guard("true")
         self.emit("{" if guard == "true" else f"if ({guard}) {{")
-        self.emit(f"uint32_t ai = {self.name(a_base)};", 2)
+        self.emit(f"uint32_t eas_ai = {self.name(a_base)};", 2)
         for n, d in enumerate(dots):
-            self.emit(f"uint32_t bi{n} = {self.name(d.args[4])};", 2)
+            self.emit(f"uint32_t eas_bi{n} = {self.name(d.args[4])};", 2)
         kd = self.defs.get(k_ref.id)
         if kd is not None and kd.op == "const" and 1 <= int(kd.args[0]) <= 32:
             self.emit("#pragma unroll 4", 2)
-        self.emit(f"for (uint32_t k = 0; k < {self.name(k_ref)}; ++k) {{", 2)
+        self.emit(f"for (uint32_t eas_k = 0; eas_k < {self.name(k_ref)}; ++eas_k) {{", 2)
         A, B = self.name(a_buf), self.name(b_buf)
-        self.emit(f"const float av = {_as_float(a_buf.dtype, f'{A}[ai]')};", 3)
+        self.emit(f"const float eas_av = {_as_float(a_buf.dtype, f'{A}[eas_ai]')};", 3)
 
         def scalar(n: int, o: int) -> str:
-            return f"v{o} = fmaf(av, {_as_float(b_buf.dtype, f'{B}[bi{n}]')}, v{o});"
+            return f"v{o} = fmaf(eas_av, {_as_float(b_buf.dtype, f'{B}[eas_bi{n}]')}, v{o});"
 
         if vec is not None:
             vt, comps = ("float4", "xyzw") if b_buf.dtype == DType.F32 else ("eas_h4", "xyzw")
-            self.emit("if ((bi0 & 3u) == 0u) {", 3)
-            self.emit(f"const {vt} bv = *reinterpret_cast<const {vt}*>({B} + bi0);", 4)
+            self.emit("if ((eas_bi0 & 3u) == 0u) {", 3)
+            self.emit(f"const {vt} eas_bv = *reinterpret_cast<const {vt}*>({B} + eas_bi0);", 4)
             for n in range(4):
-                self.emit(f"v{outs[n]} = fmaf(av, {_as_float(b_buf.dtype, f'bv.{comps[n]}')}, v{outs[n]});", 4)
+                self.emit(f"v{outs[n]} = fmaf(eas_av, {_as_float(b_buf.dtype, f'eas_bv.{comps[n]}')}, v{outs[n]});", 4)
             self.emit("} else {", 3)
             for n in range(4):
                 self.emit(scalar(n, outs[n]), 4)
@@ -859,7 +859,7 @@ class _Emitter:
         else:
             for n, o in enumerate(outs):
                 self.emit(scalar(n, o), 3)
-        self.emit(f"ai += {self.name(a_stride)};" + "".join(f" bi{n} += {self.name(b_stride)};"
+        self.emit(f"eas_ai += {self.name(a_stride)};" + "".join(f" eas_bi{n} += {self.name(b_stride)};"
                                                              for n in range(len(dots))), 3)
         self.emit("}", 2)
         self.emit("}")
@@ -960,14 +960,14 @@ class _Emitter:
         self.emit(f"float v{o} = 0.0f;")
         body_guard = self._guard("true")
         self.emit("{" if body_guard == "true" else f"if ({body_guard}) {{")
-        self.emit(f"uint32_t ai = {self.name(a_base)}, bi = {self.name(b_base)};", 2)
+        self.emit(f"uint32_t eas_ai = {self.name(a_base)}, eas_bi = {self.name(b_base)};", 2)
         if unroll:
             self.emit(unroll, 2)
-        self.emit(f"for (uint32_t k = 0; k < {self.name(k_ref)}; ++k) {{", 2)
-        av = _as_float(a_buf.dtype, self.ld(a_buf, "ai"))
-        bv = _as_float(b_buf.dtype, self.ld(b_buf, "bi"))
+        self.emit(f"for (uint32_t eas_k = 0; eas_k < {self.name(k_ref)}; ++eas_k) {{", 2)
+        av = _as_float(a_buf.dtype, self.ld(a_buf, "eas_ai"))
+        bv = _as_float(b_buf.dtype, self.ld(b_buf, "eas_bi"))
         self.emit(f"v{o} = fmaf({av}, {bv}, v{o});", 3)
-        self.emit(f"ai += {self.name(a_stride)}; bi += {self.name(b_stride)};", 3)
+        self.emit(f"eas_ai += {self.name(a_stride)}; eas_bi += {self.name(b_stride)};", 3)
         self.emit("}", 2)
         self.emit("}")
 
@@ -993,19 +993,19 @@ class _Emitter:
                 self.emit(f"const uint32_t eas_b = {on} ? eas_pack2({b0}, {b1}) : 0u;", 2)
             self.emit(f"v{o} = eas_mma_f16(eas_a, eas_b, {self.name(acc)});", 2)
         else:
-            self.emit(f"float d0 = {self.name(acc)}.x, d1 = {self.name(acc)}.y;", 2)
+            self.emit(f"float eas_d0 = {self.name(acc)}.x, eas_d1 = {self.name(acc)}.y;", 2)
             pre = "" if on == "true" else f"if ({on}) "
             self.emit(f"{pre}{{", 2)
             self.emit("#pragma unroll", 3)
-            self.emit("for (uint32_t k = 0; k < 8u; ++k) {", 3)
-            av = _as_float(a_buf.dtype, self.ld(a_buf, f"({ab} + eas_g * {as_} + k)"))
-            b0 = _as_float(b_buf.dtype, self.ld(b_buf, f"({bb} + k * {bs} + eas_t * 2u)"))
-            b1 = _as_float(b_buf.dtype, self.ld(b_buf, f"({bb} + k * {bs} + eas_t * 2u + 1u)"))
-            self.emit(f"const float a = {av};", 4)
-            self.emit(f"d0 = fmaf(a, {b0}, d0); d1 = fmaf(a, {b1}, d1);", 4)
+            self.emit("for (uint32_t eas_k = 0; eas_k < 8u; ++eas_k) {", 3)
+            av = _as_float(a_buf.dtype, self.ld(a_buf, f"({ab} + eas_g * {as_} + eas_k)"))
+            b0 = _as_float(b_buf.dtype, self.ld(b_buf, f"({bb} + eas_k * {bs} + eas_t * 2u)"))
+            b1 = _as_float(b_buf.dtype, self.ld(b_buf, f"({bb} + eas_k * {bs} + eas_t * 2u + 1u)"))
+            self.emit(f"const float eas_av = {av};", 4)
+            self.emit(f"eas_d0 = fmaf(eas_av, {b0}, eas_d0); eas_d1 = fmaf(eas_av, {b1}, eas_d1);", 4)
             self.emit("}", 3)
             self.emit("}", 2)
-            self.emit(f"v{o} = make_float2(d0, d1);", 2)
+            self.emit(f"v{o} = make_float2(eas_d0, eas_d1);", 2)
         self.emit("}")
 
 

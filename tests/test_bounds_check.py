@@ -78,8 +78,8 @@ def test_dot_and_mma_operand_reads_are_checked():
     """dot loops are emitted one per dot (no grouped or vector B loads); each operand read inside
     a dot or mma is guarded."""
     dot = lower("t_many_dot")
-    loop = dot.src[dot.src.index("for (uint32_t k = 0;"):]
-    assert "eas_inb(ai" in loop and "eas_inb(bi" in loop and "bv" not in loop
+    loop = dot.src[dot.src.index("for (uint32_t eas_k = 0;"):]
+    assert "eas_inb(eas_ai" in loop and "eas_inb(eas_bi" in loop and "eas_bv" not in loop
     mma = lower("matmul_simdgroup")
     n_mma = sum(i.op == "mma" for i in goldens.ir_from_json(goldens.case("matmul_simdgroup")["opt"]).insts)
     assert n_mma and mma.src.count("eas_pack2((eas_inb(") == 2 * n_mma   # the A and the B pair of each

@@ -7,6 +7,7 @@ test_dot_codegen_unique_vars.py, test_specialize_scalars.py) for the CUDA emitte
 import re
 
 import numpy as np
+import pytest
 
 import eas
 import goldens
@@ -37,16 +38,16 @@ def test_f16_buffers_are_half_bit_patterns():
 
 def test_dot_reads_f16_as_float_in_a_k_loop():
     s = src("t_gemv_dot")
-    assert "for (uint32_t k = 0; k < K; ++k)" in s
+    assert "for (uint32_t eas_k = 0; eas_k < K; ++eas_k)" in s
     assert "fmaf(" in s
 
 
 def test_tiled_matmul_groups_dots_with_float4_b_loads(monkeypatch):
     s = src("matmul_tiled_masked")
-    assert "const float4 bv = *reinterpret_cast<const float4*>" in s
-    assert s.count("const float av =") == 2  # BK steps 1..3 (K=64, BK=16) re-rolled into one loop
+    assert "const float4 eas_bv = *reinterpret_cast<const float4*>" in s
+    assert s.count("const float eas_av =") == 2  # BK steps 1..3 (K=64, BK=16) re-rolled into one loop
     monkeypatch.setenv("EAS_REROLL", "0")
-    assert src("matmul_tiled_masked").count("const float av =") == 4  # one grouped k loop per BK step
+    assert src("matmul_tiled_masked").count("const float eas_av =") == 4  # one grouped k loop per BK step
 
 
 def test_mma_uses_tensor_core_mma_sync():
@@ -92,3 +93,52 @@ def test_many_dots_share_one_loop_without_redeclaration():
 def test_written_buffers_are_not_const():
     s = src("add_c1")
     assert "const float* __restrict__ a" in s and "float* c" in s and "const float* __restrict__ c" not in s
+
+
+@eas.kernel
+def names_mma_f32(a, b, c, K: eas.constexpr):
+    """f32 mk.mma on buffers named a, b and c."""
+    _t = mk.tid(0, 32)
+    acc = mk.mma_zero()
+    for k0 in range(0, K, 8):
+        acc = mk.mma(a, k0, K, b, k0 * 8, 8, acc)
+    mk.mma_store(c, 0, 8, acc)
+
+
+@eas.kernel
+def names_dot(ai, bi, av, k, t, BLOCK: eas.constexpr):
+    """dot on buffers named like the emitter's loop variables, with a scalar named k."""
+    r = mk.program_id(0) * BLOCK + mk.tid(0, BLOCK)
+    mk.store(av, r, mk.dot(ai, r * k, 1, bi, 0, 1, k), r < t)
+
+
+@eas.kernel
+def names_spmd(d0, d1, i, BLOCK: eas.constexpr):
+    """spmd lane loops with a scalar named i."""
+    offs = mk.program_id(0) * BLOCK + mk.arange(0, BLOCK)
+    mk.store(d1, offs, mk.load(d0, offs, offs < i) * 2.0, offs < i)
+
+
+@pytest.mark.parametrize("checked", [False, True])
+def test_user_names_do_not_collide_with_generated_locals(checked):
+    """Buffers and scalars may be named like the generated kernel's own locals (a, i, k, ai, bi,
+    av, t, d0, d1): those locals carry the reserved eas_ prefix, so every kernel compiles."""
+    import ctypes
+
+    from easy_as_b200.codegen.cuda import ir_to_cuda
+    from easy_as_b200.runtime import cuda_ext
+
+    f32 = np.float32
+    cases = [
+        names_mma_f32.compile(np.ones(128, f32), np.ones(128, f32), np.zeros(64, f32), K=16),
+        names_dot.compile(np.ones(64, f32), np.ones(8, f32), np.zeros(8, f32), 8, 8, BLOCK=32),
+        names_spmd.compile(np.ones(100, f32), np.zeros(100, f32), 100, BLOCK=64),
+    ]
+    lib = cuda_ext.load()
+    for ck in cases:
+        lo = ir_to_cuda(ck.ir, checked=checked)
+        img, size = ctypes.c_void_p(), ctypes.c_size_t()
+        rc = lib.eas_compile(lo.src.encode(), (lo.kernel_name + ".cu").encode(), None, 0, ctypes.byref(img),
+                             ctypes.byref(size))
+        assert rc == 0, cuda_ext.last_error()
+        lib.eas_free_host(img)
