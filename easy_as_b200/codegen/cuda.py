@@ -110,6 +110,14 @@ _CXX_RESERVED = {
     "static", "struct", "switch", "template", "this", "throw", "try", "typedef", "union", "unsigned",
     "virtual", "void", "volatile", "while", "half", "dim3", "uint", "asm", "namespace", "using",
     "threadIdx", "blockIdx", "blockDim", "gridDim", "warpSize", "true", "false", "nullptr",
+    # the remaining C++ keywords a Python identifier can spell
+    "alignas", "alignof", "char16_t", "char32_t", "char8_t", "compl", "bitand", "bitor", "const_cast",
+    "constexpr", "consteval", "constinit", "decltype", "dynamic_cast", "explicit", "export", "friend",
+    "mutable", "noexcept", "not_eq", "and_eq", "or_eq", "xor", "xor_eq", "reinterpret_cast", "static_assert",
+    "static_cast", "thread_local", "typeid", "typename", "wchar_t", "concept", "requires", "co_await",
+    "co_return", "co_yield",
+    # types and functions the generated code names
+    "uint32_t", "uint64_t", "float2", "float4", "make_float2", "fmaf", "atomicCAS",
 }
 
 

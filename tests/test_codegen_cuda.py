@@ -119,10 +119,19 @@ def names_spmd(d0, d1, i, BLOCK: eas.constexpr):
     mk.store(d1, offs, mk.load(d0, offs, offs < i) * 2.0, offs < i)
 
 
+@eas.kernel
+def names_keywords(float4, reinterpret_cast, uint32_t, fmaf, BLOCK: eas.constexpr):
+    """Names of C++ keywords, types and functions the generated code uses."""
+    offs = mk.program_id(0) * BLOCK + mk.arange(0, BLOCK)
+    m = offs < uint32_t
+    mk.store(reinterpret_cast, offs, mk.fma(mk.load(float4, offs, m), fmaf, 1.0), m)
+
+
 @pytest.mark.parametrize("checked", [False, True])
 def test_user_names_do_not_collide_with_generated_locals(checked):
     """Buffers and scalars may be named like the generated kernel's own locals (a, i, k, ai, bi,
-    av, t, d0, d1): those locals carry the reserved eas_ prefix, so every kernel compiles."""
+    av, t, d0, d1), which carry the reserved eas_ prefix, or like C++ keywords and the types and
+    functions the generated code calls, which are renamed: every kernel compiles."""
     import ctypes
 
     from easy_as_b200.codegen.cuda import ir_to_cuda
@@ -130,6 +139,7 @@ def test_user_names_do_not_collide_with_generated_locals(checked):
 
     f32 = np.float32
     cases = [
+        names_keywords.compile(np.ones(100, f32), np.zeros(100, f32), 100, 2.0, BLOCK=64),
         names_mma_f32.compile(np.ones(128, f32), np.ones(128, f32), np.zeros(64, f32), K=16),
         names_dot.compile(np.ones(64, f32), np.ones(8, f32), np.zeros(8, f32), 8, 8, BLOCK=32),
         names_spmd.compile(np.ones(100, f32), np.zeros(100, f32), 100, BLOCK=64),
