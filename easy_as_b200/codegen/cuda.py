@@ -261,6 +261,14 @@ class _Emitter:
     def __init__(self, ir: IRModule, checked: bool = False):
         self.ir = ir
         self.checked = checked
+        # C identifier of each argument: c_ident, made unique ("x" renamed to "x_p" must not meet an
+        # argument that is itself called "x_p")
+        self.cname: dict[str, str] = {}
+        for a in ir.args:
+            c = c_ident(a.name)
+            while c in self.cname.values():
+                c += "_p"
+            self.cname[a.name] = c
         self.block, self.mode = infer_block_and_mode(ir)
         self.defs: dict[int, Inst] = {i.out.id: i for i in ir.insts if i.out is not None}
         self.arg_c: dict[int, str] = {}       # value id of an arg -> C identifier
@@ -277,7 +285,7 @@ class _Emitter:
                     self.uses[a.id] = self.uses.get(a.id, 0) + 1
         for inst in ir.insts:
             if inst.op == "arg":
-                self.arg_c[inst.out.id] = c_ident(str(inst.args[0]))
+                self.arg_c[inst.out.id] = self.cname[str(inst.args[0])]
                 self.arg_dtype[inst.out.id] = inst.out.dtype
             elif inst.op in ("store", "mma_store"):
                 buf = inst.args[0]
@@ -370,12 +378,12 @@ class _Emitter:
     def params(self) -> list[Param]:
         ps = []
         for a in self.ir.args:
-            ps.append(Param(c_ident(a.name), a.kind, a.dtype, a.name))
+            ps.append(Param(self.cname[a.name], a.kind, a.dtype, a.name))
         ps += [Param(h, "hidden", DType.U32, None) for h in HIDDEN]
         if self.checked:
             for a in self.ir.args:
                 if a.kind == "buffer":
-                    c = c_ident(a.name)
+                    c = self.cname[a.name]
                     ps += [Param(f"eas_lo_{c}", "check", None, a.name), Param(f"eas_n_{c}", "check", None, a.name)]
             ps.append(Param("eas_err", "check", None, None))
         return ps
@@ -383,7 +391,7 @@ class _Emitter:
     def signature(self) -> str:
         parts = []
         for a in self.ir.args:
-            cn = c_ident(a.name)
+            cn = self.cname[a.name]
             if a.kind == "buffer":
                 t = ctype(a.dtype)
                 if cn in self.writes:
@@ -396,7 +404,7 @@ class _Emitter:
         if self.checked:
             for a in self.ir.args:
                 if a.kind == "buffer":
-                    c = c_ident(a.name)
+                    c = self.cname[a.name]
                     parts += [f"const uint64_t eas_lo_{c}", f"const uint64_t eas_n_{c}"]
             parts.append("uint32_t* const eas_err")
         return ",\n    ".join(parts)

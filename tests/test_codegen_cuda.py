@@ -120,11 +120,12 @@ def names_spmd(d0, d1, i, BLOCK: eas.constexpr):
 
 
 @eas.kernel
-def names_keywords(float4, reinterpret_cast, uint32_t, fmaf, BLOCK: eas.constexpr):
-    """Names of C++ keywords, types and functions the generated code uses."""
+def names_keywords(float4, reinterpret_cast, uint32_t, fmaf, float4_p, BLOCK: eas.constexpr):
+    """Names of C++ keywords, types and functions the generated code uses, and one that equals the
+    renamed form of another."""
     offs = mk.program_id(0) * BLOCK + mk.arange(0, BLOCK)
     m = offs < uint32_t
-    mk.store(reinterpret_cast, offs, mk.fma(mk.load(float4, offs, m), fmaf, 1.0), m)
+    mk.store(reinterpret_cast, offs, mk.fma(mk.load(float4, offs, m), fmaf, mk.load(float4_p, offs, m)), m)
 
 
 @pytest.mark.parametrize("checked", [False, True])
@@ -139,7 +140,7 @@ def test_user_names_do_not_collide_with_generated_locals(checked):
 
     f32 = np.float32
     cases = [
-        names_keywords.compile(np.ones(100, f32), np.zeros(100, f32), 100, 2.0, BLOCK=64),
+        names_keywords.compile(np.ones(100, f32), np.zeros(100, f32), 100, 2.0, np.ones(100, f32), BLOCK=64),
         names_mma_f32.compile(np.ones(128, f32), np.ones(128, f32), np.zeros(64, f32), K=16),
         names_dot.compile(np.ones(64, f32), np.ones(8, f32), np.zeros(8, f32), 8, 8, BLOCK=32),
         names_spmd.compile(np.ones(100, f32), np.zeros(100, f32), 100, BLOCK=64),
