@@ -35,6 +35,8 @@ from __future__ import annotations
 from dataclasses import dataclass, field
 from typing import Any
 
+import numpy as np
+
 from ..ir import DType, IRModule
 
 Mono = tuple[str, ...]          # sorted symbol names; () is the constant term
@@ -316,6 +318,10 @@ class DotGemmPlan:
 
 
 def _numel(v: Any) -> int:
+    if type(v) is np.ndarray:
+        return int(v.size)
+    if getattr(v, "__eas_tensor__", False):
+        return int(v.nbytes) // v.dtype.itemsize
     if hasattr(v, "numel") and callable(v.numel):
         return int(v.numel())
     if hasattr(v, "size") and isinstance(v.size, int):
