@@ -1,32 +1,19 @@
 """Benchmark of the easy_as hot path on B200 (one JSON line on rank 0).
 
-Workload: the SPMD ``add_kernel`` (c = a + b with masked
-tail), N = 2**28 float32 elements (1 GiB per operand), BLOCK = 1024, a and b ~
-N(0,1) from a seed.  The grid is split by contiguous program-id ranges across
-the ranks (one process per GPU); each GPU holds only its slice and launches the
-unmodified kernel on it, so there is no data-path collective ("strong"
-scaling: the total N is fixed).  Inputs are 3 GiB per step in total (> 126 MB
-L2), so no L2 flush is needed between steps.
+Headline: the SPMD ``add_kernel`` (c = a + b with masked
+tail), N = 2**28 float32 elements (1 GiB per operand), BLOCK = 1024.  Every
+rank runs its contiguous program-id range of the one launch through the
+library's shard path (``easy_as_b200.shard.run_shard`` with ``_buffer_base``:
+each GPU allocates only its slice), so there is no data-path collective and
+the total N is fixed ("strong" scaling).  Inputs are 3 GiB per step (> 126 MB
+L2), so no L2 flush is needed.
 
-* ``value``: aggregate GB/s = 12 B/element * N / max-over-ranks device time of
-  K steps (CUDA events on the launch stream, barrier + synchronize around).
-* ``e2e``: the same metric through the public API with host buffers (pinned
-  torch CPU tensors): every step copies a and b host->device, launches and
-  copies c back (c is never loaded by the kernel, so it is not copied in).
-* ``roofline``: the add kernel's achieved bytes / launch time against the
-  measured HBM copy peak (MEASURED_PEAKS.json).
-* ``gemm``: the fp16 ``mk.dot`` GEMM (configs C4 8192^3 and C5 batched) TFLOP/s
-  on the native tcgen05 path.
-* ``matmul_tiled``: config C3, the reference's fp32 tiled matmul at 2048^3 on
-  the proven-GEMM FFMA path (1 GPU), with cuBLAS fp32 timed beside it and the
-  opt-in 3xTF32 mode (``tf32x3``).
-* ``c1_add_call``: config C1 (N = 1031), launch-bound: the cost of one call
-  through the public API (numpy synced, device async, CUDA-graph replay).
-* ``cpu_baseline``: numpy on the host cores on a bounded sample.
-
-``--impl reference`` times the reference's CPU semantics instead (the CPU
-oracle interpreting the reference front end's IR of the same kernel, on all
-host threads) and prints the same metric.
+The GEMM configs go through the same shard path: C4 (8192^3, autotuned over
+BLOCK_M x BLOCK_N x BLOCK_K) split by rows (program_id(1)), C5 (64 x 4096^2 x
+2088) by batch (program_id(2)); C3 and C1 run on one GPU.  Their compact
+summaries sit in ``configs`` of the same line.  ``--impl reference`` times the
+reference's CPU semantics (the oracle interpreting the reference front end's
+IR of the same kernel, all host threads) on the full C2 problem.
 """
 
 import argparse
@@ -121,9 +108,11 @@ class ClockSampler:
         if self._thread is not None:
             self._thread.join(timeout=5)
 
-    def summary(self) -> dict:
+    def summary(self, short: bool = False) -> dict:
         out = {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.max_mhz,
                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+        if short:
+            out = {"sm_mhz": out["sm_mhz"], "reasons": out["reasons"]}
         if self.error:
             out["error"] = self.error
         return out
@@ -203,9 +192,7 @@ def bench_gather(c, n_total: int, world: int, rank: int) -> dict:
     moved = 4 * (n_total - counts[0])
     del full
     return {"bytes_into_rank0": moved, "ms": round(dt * 1e3, 3), "GBs_into_rank0": round(moved / dt / 1e9, 1),
-            "checked_rank0": ok,
-            "how": "easy_as_b200.shard.gather (batched NCCL send/recv) of the C2 output slices to rank 0; "
-                   "wall clock from a barrier, synchronised, max over ranks"}
+            "checked_rank0": ok}
 
 
 def make_add_kernel():
@@ -222,100 +209,64 @@ def make_add_kernel():
 
 
 GEMM_CONFIGS = {
-    # name: (batch, M, N, K, how the work is split across ranks)
-    "C4": (1, 8192, 8192, 8192, "rows of A/C split across ranks, B replicated"),
-    "C5": (64, 4096, 4096, 2088, "batch split across ranks"),
+    # name: (batch, M, N, K, shard axis: 1 = rows of A and C (program_id(1)), 2 = batch (program_id(2)))
+    "C4": (1, 8192, 8192, 8192, 1),
+    "C5": (64, 4096, 4096, 2088, 2),
 }
 
 
-def gemm_shard(name: str, world: int, rank: int) -> tuple[int, int, int, int]:
-    batch, M, N, K, _ = GEMM_CONFIGS[name]
-    if name == "C4":
-        r0, r1 = M * rank // world, M * (rank + 1) // world
-        return batch, r1 - r0, N, K
-    b0, b1 = batch * rank // world, batch * (rank + 1) // world
-    return b1 - b0, M, N, K
-
-
 def last_gemm_config() -> str:
-    """The tile configuration the library's last GEMM launch used, as text."""
+    """The tile configuration of the library's last GEMM launch, as short text."""
     import ctypes
 
     from easy_as_b200.runtime import cuda_ext
 
-    vals = [ctypes.c_int() for _ in range(5)]
+    vals = [ctypes.c_int() for _ in range(6)]
     cuda_ext.check(cuda_ext.load().eas_gemm_last_config(*(ctypes.byref(x) for x in vals)), "gemm config")
-    tm, tn, st, ks, pair = (x.value for x in vals)
-    kind = "tcgen05 cta_group::2 (CTA pair)" if pair else "tcgen05 cta_group::1"
-    return f"{kind}, tile {tm}x{tn}x64, {st} stages" + (f", split-K x{ks}" if ks > 1 else "")
+    tm, tn, st, ks, pair, bk = (x.value for x in vals)
+    return (f"{'pair' if pair else '1sm'} {tm}x{tn}x{bk} s{st}" + (f" splitk{ks}" if ks > 1 else ""))
 
 
-def gemm_e2e(name, a, b, c, M, N, K, batch, world, flops_total) -> dict:
-    """The GEMM leg end to end through the public API with pinned host tensors: each step copies
-    A and B in, runs the kernel and copies C out, synchronised; wall clock, max over ranks.  C is
-    copied in too unless the launch provably stores every element of it (the runtime keeps any
-    unwritten part of a host output intact)."""
+def _events():
     import torch
 
-    from examples.matmul_dot_f16 import grid, matmul_dot_f16_tuned
-
-    ha, hb = a.cpu().pin_memory(), b.cpu().pin_memory()
-    hc = torch.zeros(c.shape, dtype=torch.float32).pin_memory()
-
-    def step():
-        matmul_dot_f16_tuned(ha.reshape(-1), hb.reshape(-1), hc.reshape(-1), M, N, K, _grid=grid(batch))
-
-    step()
-    ref = ha[0, :4].double() @ hb[0].double()
-    err = ((hc[0, :4].double() - ref).abs().max() / ref.abs().max()).item()
-    if err > 1e-4:
-        raise SystemExit(f"bench: {name} e2e result off by {err:.2e}")
-    steps = 2
-    from easy_as_b200.runtime import get_runtime
-
-    rt = get_runtime()
-    skipped0 = rt.skipped_copy_bytes
-    barrier(world)
-    t0 = time.perf_counter()
-    for _ in range(steps):
-        step()
-    dt = max_over_ranks((time.perf_counter() - t0) / steps, world)
-    skipped = (rt.skipped_copy_bytes - skipped0) // steps   # C's copy-in when the GEMM stores all of C
-    per_rank_in = ha.numel() * 2 + hb.numel() * 2 + hc.numel() * 4 - skipped
-    per_rank_out = hc.numel() * 4
-    del ha, hb, hc
-    return {"value": round(flops_total / dt / 1e12, 2), "unit": "TFLOP/s",
-            "h2d_bytes_per_step": per_rank_in * world, "d2h_bytes_per_step": per_rank_out * world,
-            "ms_per_step": round(dt * 1e3, 2),
-            "how": "public API, pinned torch CPU tensors in and out (A and B copied in; C copied in only when "
-                   "the launch does not store all of it; C copied out), synchronised per step; wall clock, "
-                   "max over ranks; PCIe-bound"}
+    return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 
 
 def run_gemm(name: str, args, world: int, rank: int, rt) -> dict:
-    """fp16 mk.dot GEMM (examples/matmul_dot_f16.py) on this rank's shard; TFLOP/s aggregated over ranks."""
+    """fp16 mk.dot GEMM (examples/matmul_dot_f16.py, autotuned) through ``shard.run_shard``: this
+    rank's program-id range of the one launch, on buffers that hold only its slice (B whole for C4);
+    TFLOP/s aggregated over ranks from the max-over-ranks device time."""
     import torch
 
-    from examples.matmul_dot_f16 import grid, matmul_dot_f16_tuned
+    from easy_as_b200.shard import program_range, run_shard
+    from examples.matmul_dot_f16 import grid, matmul_dot_f16_tuned as kern
 
-    batch, M, N, K = gemm_shard(name, world, rank)
-    tb, TM, TN, TK, split = GEMM_CONFIGS[name]
+    batch, M, N, K, axis = GEMM_CONFIGS[name]
+    p0, p1 = program_range(M if axis == 1 else batch, rank, world)
+    if axis == 1:   # rows p0..p1 of A and C; B whole
+        lb, lm, base = 1, p1 - p0, {"a": p0 * K, "c": p0 * N}
+        bshape = (1, K, N)
+    else:           # batches p0..p1 of A, B and C
+        lb, lm, base = p1 - p0, M, {"a": p0 * M * K, "b": p0 * K * N, "c": p0 * M * N}
+        bshape = (lb, K, N)
     g = torch.Generator(device="cuda").manual_seed(3 + rank)
-    a = (torch.randn(batch, M, K, device="cuda", generator=g) / K ** 0.5).half()
-    b = (torch.randn(batch, K, N, device="cuda", generator=g) / K ** 0.5).half()
-    c = torch.empty(batch, M, N, device="cuda")
+    a = (torch.randn(lb, lm, K, device="cuda", generator=g) / K ** 0.5).half()
+    b = (torch.randn(*bshape, device="cuda", generator=g) / K ** 0.5).half()
+    c = torch.empty(lb, lm, N, device="cuda")
 
     def step(sync=False):
-        # autotuned over BLOCK_M/N in {128, 256} x BLOCK_K in {64, 128} (first call per shape tunes)
-        matmul_dot_f16_tuned(a.reshape(-1), b.reshape(-1), c.reshape(-1), M, N, K, _grid=grid(batch), _sync=sync)
+        run_shard(kern, a, b, c, M, N, K, _grid=grid(batch), _rank=rank, _world=world, _axis=axis,
+                  _buffer_base=base, _sync=sync)
 
     native0 = rt.native_launches
-    step(sync=True)
-    cfg = matmul_dot_f16_tuned._tuned_cache.get((M, N, K))
-    tuned = dict(cfg.meta) if cfg is not None else {}
+    keys0 = set(kern._tuned_times)
+    step(sync=True)                      # first call tunes (8 configs timed on this rank's range)
     if rt.native_launches == native0:
         raise SystemExit(f"bench: {name} did not take the tcgen05 path")
-    # parity spot check: rows 0..3 of the first batch against float64
+    new = [k for k in kern._tuned_times if k not in keys0]
+    times = kern._tuned_times[new[0]] if new else []
+    best = min(times, key=lambda t: t[1])[0] if times else {}
     ref = a[0, :4].double() @ b[0].double()
     err = ((c[0, :4].double() - ref).abs().max() / ref.abs().max()).item()
     if err > 1e-4:
@@ -329,61 +280,100 @@ def run_gemm(name: str, args, world: int, rank: int, rt) -> dict:
     torch.cuda.synchronize()
     launches0 = rt.launch_count
     stream = torch.cuda.current_stream()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0, e1 = _events()
     with ClockSampler(torch.cuda.current_device()) as clk:
         e0.record(stream)
         for _ in range(steps):
             step()
         e1.record(stream)
         e1.synchronize()
-        rt.synchronize()
+    launches = rt.launch_count - launches0
+    rt.synchronize()
     barrier(world)
     ms = e0.elapsed_time(e1) / steps
     ms_max = max_over_ranks(ms, world)
+    tile = last_gemm_config()
     lib_tf = None
     if world == 1:
         # cuBLAS on the same operands (f16 in, f32 out), timed the same way, for context
         try:
-            def lib_step():
-                torch.bmm(a, b, out_dtype=torch.float32)
             for _ in range(3):
-                lib_step()
+                torch.bmm(a, b, out_dtype=torch.float32)
             torch.cuda.synchronize()
-            l0, l1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            l0, l1 = _events()
             l0.record(stream)
             for _ in range(steps):
-                lib_step()
+                torch.bmm(a, b, out_dtype=torch.float32)
             l1.record(stream)
             l1.synchronize()
-            lib_tf = round(2.0 * batch * M * N * K / (l0.elapsed_time(l1) / steps * 1e-3) / 1e12, 1)
+            lib_tf = round(2.0 * lb * lm * N * K / (l0.elapsed_time(l1) / steps * 1e-3) / 1e12, 1)
         except (TypeError, RuntimeError):
             lib_tf = None
-    kernel_desc = last_gemm_config()
-    flops_total = 2.0 * tb * TM * TN * TK
-    flops_local = 2.0 * batch * M * N * K
-    e2e = None if args.quick else gemm_e2e(name, a, b, c, M, N, K, batch, world, flops_total)
+    flops_total = 2.0 * batch * M * N * K
+    local_tf = 2.0 * lb * lm * N * K / (ms * 1e-3) / 1e12
+    e2e = None if args.quick else gemm_e2e(name, a, b, c, step, world, flops_total)
     pk = peaks()
-    local_tf = flops_local / (ms * 1e-3) / 1e12
-    return {
-        "metric": "fp16 mk.dot GEMM TFLOP/s", "value": round(flops_total / (ms_max * 1e-3) / 1e12, 1),
-        "unit": "TFLOP/s", "ms_per_step": round(ms_max, 4), "steps": steps,
-        "config": {"workload": f"{name} batch={tb} M={TM} N={TN} K={TK} f16 in, f32 acc/out", "split": split,
-                   "kernel": kernel_desc, "autotuned": tuned, "spot_check_rel_err": err},
+    out = {
+        "value": round(flops_total / (ms_max * 1e-3) / 1e12, 1), "unit": "TFLOP/s", "ms_per_step": round(ms_max, 4),
+        "steps": steps,
         "roofline": {"bound": "tensor", "achieved": round(local_tf, 1), "peak": pk["bf16_tflops"],
-                     "unit": "TFLOP/s", "frac": round(local_tf / pk["bf16_tflops"], 4),
-                     "peak_source": ("measured burst cuBLAS bf16 (MEASURED_PEAKS.json bf16_tflops)"
-                                     if pk["source"] == "measured" else "fallback"),
-                     "frac_of_nominal_2250": round(local_tf / 2250.0, 4),
-                     "frac_of_measured_sustained": round(local_tf / pk["bf16_tflops_sustained"], 4),
-                     "traffic": profile_traffic(f"gemm_{name.lower()}_n1")},
-        "cublas_f16_f32out_tflops": lib_tf,
-        "e2e": e2e,
-        "cpu_baseline": (cpu_gemm_baseline(min(M, 2048), N, K, 1, 5, f"one {min(M, 2048)}-row slice of one problem "
-                                           f"of the {name} workload (f16 inputs upcast to f32)")
-                         if world == 1 and not args.no_cpu_baseline else None),
-        "gpu_launches": rt.launch_count - launches0,
-        "clocks": clk.summary(),
+                     "frac": round(local_tf / pk["bf16_tflops"], 4),
+                     "frac_sustained": round(local_tf / pk["bf16_tflops_sustained"], 4),
+                     "frac_nominal": round(local_tf / 2250.0, 4),
+                     "traffic": profile_traffic(f"gemm_{name.lower()}_n1") if world == 1 else None},
+        "clocks": clk.summary(short=True), "tile": tile,
+        "tuned": "/".join(str(best.get(k)) for k in ("BLOCK_M", "BLOCK_N", "BLOCK_K")) if best else None,
+        "tune_ms": [round(t * 1e3, 3) for _, t in times] if world == 1 else None,
+        "cublas": lib_tf, "e2e": e2e, "gpu_launches": launches, "rel_err": float(f"{err:.2e}"),
     }
+    if world == 1 and not args.no_cpu_baseline and not args.quick:
+        out["cpu_tflops"] = cpu_gemm_baseline(min(M, 2048), N, K, 5)["value"]
+    return out
+
+
+def gemm_e2e(name, a, b, c, step, world, flops_total) -> dict:
+    """The GEMM end to end with pinned host tensors, synchronised per step, wall clock, max over ranks.
+    One GPU: the public call with host tensors (the runtime pipelines the copies with the kernel).
+    N GPUs: every rank copies its slices in, runs its range (``run_shard``) and copies its C out."""
+    import torch
+
+    from examples.matmul_dot_f16 import grid, matmul_dot_f16_tuned
+
+    batch, M, N, K, _ = GEMM_CONFIGS[name]
+    ha, hb = a.cpu().pin_memory(), b.cpu().pin_memory()
+    hc = torch.zeros(c.shape, dtype=torch.float32).pin_memory()
+    from easy_as_b200.runtime import get_runtime
+
+    rt = get_runtime()
+    if world == 1:
+        def e2e_step():
+            matmul_dot_f16_tuned(ha.reshape(-1), hb.reshape(-1), hc.reshape(-1), M, N, K, _grid=grid(batch))
+    else:
+        def e2e_step():
+            a.copy_(ha, non_blocking=True)
+            b.copy_(hb, non_blocking=True)
+            step()
+            hc.copy_(c, non_blocking=True)
+            torch.cuda.synchronize()
+    e2e_step()
+    ref = ha[0, :4].double() @ hb[0].double()
+    err = ((hc[0, :4].double() - ref).abs().max() / ref.abs().max()).item()
+    if err > 1e-4:
+        raise SystemExit(f"bench: {name} e2e result off by {err:.2e}")
+    steps = 2
+    skipped0 = rt.skipped_copy_bytes
+    barrier(world)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        e2e_step()
+    dt = max_over_ranks((time.perf_counter() - t0) / steps, world)
+    skipped = (rt.skipped_copy_bytes - skipped0) // steps   # C's copy-in when the GEMM stores all of C
+    per_rank_in = ha.numel() * 2 + hb.numel() * 2 + (hc.numel() * 4 - skipped if world == 1 else 0)
+    per_rank_out = hc.numel() * 4
+    del ha, hb, hc
+    return {"value": round(flops_total / dt / 1e12, 2), "unit": "TFLOP/s",
+            "h2d_bytes_per_step": int(sum_over_ranks(per_rank_in, world)),
+            "d2h_bytes_per_step": int(sum_over_ranks(per_rank_out, world))}
 
 
 C3_SIZE = 2048
@@ -604,14 +594,14 @@ def run_tiled(args, rt) -> dict:
         "cublas_fp32_tflops": round(lib_tf, 2),
         "tf32x3": tf32x3,
         "cpu_baseline": (None if args.no_cpu_baseline else
-                         cpu_gemm_baseline(M, N, K, 1, 6, "the full C3 problem")),
+                         cpu_gemm_baseline(M, N, K, 6)),
         "gpu_launches": rt.launch_count - launches0,
         "clocks": cl,
     }
 
 
-def cpu_gemm_baseline(m: int, n: int, k: int, batch: int, seed: int, what: str, seconds: float = 3.0) -> dict:
-    """numpy (OpenBLAS, all host threads) float32 A @ B on a bounded sample of the same shape:
+def cpu_gemm_baseline(m: int, n: int, k: int, seed: int, seconds: float = 3.0) -> dict:
+    """numpy (OpenBLAS, all host threads) float32 A @ B on a bounded sample of the same shape,
     repeated for about ``seconds``; fp16 operands are upcast to f32 first, as the reference's
     CPU-side check does."""
     rng = np.random.default_rng(seed)
@@ -627,7 +617,7 @@ def cpu_gemm_baseline(m: int, n: int, k: int, batch: int, seed: int, what: str, 
             break
     tf = 2.0 * m * n * k * reps / dt / 1e12
     return {"value": round(tf, 4), "unit": "TFLOP/s", "cores": os.cpu_count() or 1, "kind": "port",
-            "sample": f"numpy float32 {m}x{k} @ {k}x{n} (OpenBLAS, all threads), {reps} reps in {dt:.1f} s; {what}"}
+            "sample": f"numpy f32 {m}x{k}@{k}x{n}, {reps} reps"}
 
 
 def cpu_add_baseline(seconds: float = 10.0) -> dict:
@@ -652,7 +642,133 @@ def cpu_add_baseline(seconds: float = 10.0) -> dict:
     dt = time.perf_counter() - t0
     gbs = sum(done) * n * BYTES_PER_ELEM / dt / 1e9
     return {"value": round(gbs, 2), "unit": "GB/s", "cores": cores, "kind": "port",
-            "sample": f"np.add on 2^24 float32 elements, repeated on {cores} threads for {dt:.1f} s"}
+            "sample": f"np.add 2^24 f32, {cores} threads, {dt:.0f} s"}
+
+
+def run_add(args, world: int, rank: int, local: int, rt) -> dict:
+    """Config C2 through ``shard.run_shard``: this rank's program-id range of the one N-element
+    launch, on slice-only buffers (``_buffer_base``)."""
+    import torch
+
+    from easy_as_b200.shard import run_shard
+
+    add_kernel = make_add_kernel()
+    lo, hi = shard(args.n, BLOCK, world, rank)
+    n = hi - lo
+    base = {"a": lo, "b": lo, "c": lo}
+    gen = torch.Generator(device="cuda").manual_seed(1234 + rank)
+    a = torch.randn(n, device="cuda", dtype=torch.float32, generator=gen)
+    b = torch.randn(n, device="cuda", dtype=torch.float32, generator=gen)
+    c = torch.empty_like(a)
+
+    def step(sync=False):
+        run_shard(add_kernel, a, b, c, args.n, BLOCK=BLOCK, _rank=rank, _world=world, _buffer_base=base, _sync=sync)
+
+    step(sync=True)
+    if not torch.equal(c, a + b):            # bit-exact vs torch's own a + b
+        raise SystemExit("bench: add result differs from a + b")
+    stream = torch.cuda.current_stream()
+    t_warm = time.perf_counter()
+    w = 0
+    while w < max(args.warmup, 3) or (not args.quick and time.perf_counter() - t_warm < 0.5):
+        step()
+        w += 1
+        if w % 64 == 0:
+            torch.cuda.synchronize()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    launches0 = rt.launch_count
+    e0, e1 = _events()
+    with ClockSampler(local) as clk:
+        e0.record(stream)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            step()
+        host_us = (time.perf_counter() - t0) / args.steps * 1e6
+        e1.record(stream)
+        e1.synchronize()
+    torch.cuda.synchronize()
+    barrier(world)
+    launches = rt.launch_count - launches0
+    ms = e0.elapsed_time(e1) / args.steps
+    ms_max = max_over_ranks(ms, world)
+    res = {"gbs": BYTES_PER_ELEM * args.n / (ms_max * 1e-3) / 1e9, "ms": ms_max, "n": n,
+           "kernel_gbs": BYTES_PER_ELEM * n / (ms * 1e-3) / 1e9, "launches": launches, "clocks": clk.summary(),
+           "host_us": host_us}
+    if world > 1 and not args.quick:
+        res["gather"] = bench_gather(c, args.n, world, rank)
+    if not args.quick:
+        res["e2e"] = add_e2e(args, add_kernel, a, b, c, step, world, n)
+    return res
+
+
+def add_e2e(args, add_kernel, a, b, c, step, world: int, n: int) -> dict:
+    """C2 end to end with pinned host buffers, wall clock, max over ranks.  One GPU: the public call
+    with host tensors (a and b copied in, c copied out, chunked so both PCIe directions overlap the
+    kernel; c is never loaded, so it is not copied in).  N GPUs: each rank copies its slices in,
+    runs its range and copies its c out."""
+    import torch
+
+    ha, hb = a.cpu().pin_memory(), b.cpu().pin_memory()
+    hc = torch.empty(n, dtype=torch.float32).pin_memory()
+    if world == 1:
+        def e2e_step():
+            add_kernel(ha, hb, hc, n, BLOCK=BLOCK)   # synchronous call: copies in, kernel, copy of c out
+    else:
+        def e2e_step():
+            a.copy_(ha, non_blocking=True)
+            b.copy_(hb, non_blocking=True)
+            step()
+            hc.copy_(c, non_blocking=True)
+            torch.cuda.synchronize()
+    e2e_step()
+    barrier(world)
+    t0 = time.perf_counter()
+    steps = max(1, min(args.steps, 5))
+    for _ in range(steps):
+        e2e_step()
+    dt = max_over_ranks((time.perf_counter() - t0) / steps, world)
+    if not torch.equal(hc, ha + hb):
+        raise SystemExit("bench: e2e add result differs from a + b")
+    return {"value": round(BYTES_PER_ELEM * args.n / dt / 1e9, 2), "unit": "GB/s",
+            "h2d_bytes_per_step": 8 * args.n, "d2h_bytes_per_step": 4 * args.n}
+
+
+def sum_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([float(x)], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+def compact_c3(r: dict) -> dict:
+    if "error" in r:
+        return r
+    out = {"value": r["value"], "unit": "TFLOP/s", "ms_per_step": r["ms_per_step"], "steps": r["steps"],
+           "roofline": {"bound": "fp32_fma", "achieved": r["value"], "peak": r["roofline"]["peak"],
+                        "frac": r["roofline"]["frac"], "traffic": r["roofline"]["traffic"]},
+           "clocks": {k: r["clocks"].get(k) for k in ("sm_mhz", "reasons")}, "cublas": r["cublas_fp32_tflops"],
+           "gpu_launches": r["gpu_launches"], "rel_err": float(f"{r['config']['spot_check_rel_err']:.2e}")}
+    t = r.get("tf32x3") or {}
+    if "tflops" in t:
+        out["tf32x3"] = {"value": t["tflops"], "rel_err": float(f"{t['rel_err_vs_f64']:.2e}")}
+    if r.get("cpu_baseline"):
+        out["cpu_tflops"] = r["cpu_baseline"]["value"]
+    return out
+
+
+def compact_c1(r: dict) -> dict:
+    if "error" in r:
+        return r
+    return {"unit": "us", "higher_is_better": False, "numpy_sync_us": r["numpy_sync_us"],
+            "device_async_us": r["device_async_us"], "device_us_per_launch": r["device_us_per_launch"],
+            "graph_replay_us": r["graph_replay_us"], "gpu_launches": r["gpu_launches"],
+            "cpu_us": r["cpu_baseline"]["value"]}
 
 
 def run_eas(args) -> None:
@@ -660,7 +776,7 @@ def run_eas(args) -> None:
 
     world, rank, local = dist_setup()
     torch.cuda.set_device(local)
-    import eas
+    import eas  # noqa: F401
     from easy_as_b200.runtime import get_runtime
 
     rt = get_runtime()
@@ -676,135 +792,57 @@ def run_eas(args) -> None:
         if rank == 0:
             print(json.dumps(res), flush=True)
         return
-    add_kernel = make_add_kernel()
-    lo, hi = shard(args.n, BLOCK, world, rank)
-    n = hi - lo
-    gen = torch.Generator(device="cuda").manual_seed(1234 + rank)
-    a = torch.randn(n, device="cuda", dtype=torch.float32, generator=gen)
-    b = torch.randn(n, device="cuda", dtype=torch.float32, generator=gen)
-    c = torch.empty_like(a)
-
-    # correctness of the slice (bit-exact vs torch's own a + b)
-    add_kernel(a, b, c, n, BLOCK=BLOCK)
-    torch.cuda.synchronize()
-    if not torch.equal(c, a + b):
-        raise SystemExit("bench: add result differs from a + b")
-
-    stream = torch.cuda.current_stream()
-    t_warm = time.perf_counter()
-    w = 0
-    while w < max(args.warmup, 3) or (not args.quick and time.perf_counter() - t_warm < 0.5):
-        add_kernel(a, b, c, n, BLOCK=BLOCK, _sync=False)
-        w += 1
-        if w % 64 == 0:
-            rt.synchronize()
-    rt.synchronize()
-    torch.cuda.synchronize()
-    barrier(world)
-    torch.cuda.synchronize()
-    launches0 = rt.launch_count
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
-        e0.record(stream)
-        for _ in range(args.steps):
-            add_kernel(a, b, c, n, BLOCK=BLOCK, _sync=False)
-        e1.record(stream)
-        e1.synchronize()
-        rt.synchronize()
-    torch.cuda.synchronize()
-    barrier(world)
-    launches = rt.launch_count - launches0
-    ms = e0.elapsed_time(e1) / args.steps
-    ms_max = max_over_ranks(ms, world)
-    gbs = BYTES_PER_ELEM * args.n / (ms_max * 1e-3) / 1e9
-    kernel_gbs_local = BYTES_PER_ELEM * n / (ms * 1e-3) / 1e9
-
-    gather_res = None
-    if world > 1 and not args.quick:
-        gather_res = bench_gather(c, args.n, world, rank)
-
-    # end to end through the public API with pinned host buffers
-    e2e = None
-    if not args.quick:
-        ha = a.cpu().pin_memory()
-        hb = b.cpu().pin_memory()
-        hc = torch.empty(n, dtype=torch.float32).pin_memory()
-        add_kernel(ha, hb, hc, n, BLOCK=BLOCK)
-        barrier(world)
-        t0 = time.perf_counter()
-        e2e_steps = max(1, min(args.steps, 5))
-        for _ in range(e2e_steps):
-            add_kernel(ha, hb, hc, n, BLOCK=BLOCK)  # sync launch: H2D copies, kernel, D2H copy of c
-        t_e2e = (time.perf_counter() - t0) / e2e_steps
-        t_e2e = max_over_ranks(t_e2e, world)
-        if not torch.equal(hc, ha + hb):
-            raise SystemExit("bench: e2e add result differs from a + b")
-        ck = add_kernel.compile(ha, hb, hc, n, BLOCK=BLOCK)
-        ew = ck.plan.elementwise
-        read_only_in = sorted(ew.reads) if ew is not None else ["a", "b", "c"]
-        e2e = {"value": round(BYTES_PER_ELEM * args.n / t_e2e / 1e9, 2), "unit": "GB/s",
-               "h2d_bytes_per_step": len(read_only_in) * 4 * args.n, "d2h_bytes_per_step": 4 * args.n,
-               "how": f"public API with pinned torch CPU tensors; {', '.join(read_only_in)} copied in, c copied "
-                      "out, chunked so both PCIe directions overlap the kernel (c is never loaded by the kernel, "
-                      "so it is not copied in); wall clock, max over ranks"}
-
-    gemm = {}
+    add = run_add(args, world, rank, local, rt)
+    configs: dict = {}
     if not args.quick and not args.no_gemm:
-        del a, b, c
         torch.cuda.empty_cache()
         for name in ("C4", "C5"):
             try:
-                gemm[name] = run_gemm(name, args, world, rank, rt)
+                configs[name] = run_gemm(name, args, world, rank, rt)
             except (SystemExit, Exception) as e:
                 if world > 1:   # keep the ranks' collectives aligned: fail the whole run
                     raise
-                gemm[name] = {"metric": "fp16 mk.dot GEMM TFLOP/s", "error": f"{type(e).__name__}: {e}"}
-    tiled = None
+                configs[name] = {"error": f"{type(e).__name__}: {e}"[:200]}
+            torch.cuda.empty_cache()
     if not args.quick and not args.no_gemm and world == 1:
         try:
-            tiled = run_tiled(args, rt)
+            configs["C3"] = compact_c3(run_tiled(args, rt))
         except (SystemExit, Exception) as e:  # a secondary leg never suppresses the headline line
-            tiled = {"metric": "fp32 tiled matmul TFLOP/s", "error": f"{type(e).__name__}: {e}"}
-    c1 = None
+            configs["C3"] = {"error": f"{type(e).__name__}: {e}"[:200]}
     if not args.quick and world == 1:
         try:
-            c1 = run_c1(args, rt)
+            configs["C1"] = compact_c1(run_c1(args, rt))
         except (SystemExit, Exception) as e:
-            c1 = {"metric": "add_kernel per-call time", "error": f"{type(e).__name__}: {e}"}
+            configs["C1"] = {"error": f"{type(e).__name__}: {e}"[:200]}
     if rank != 0:
         return
     pk = peaks()
-    traffic = profile_traffic("add_c2_n1")
     line = {
-        "metric": METRIC, "value": round(gbs, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
-        "warmup": max(args.warmup, 3), "ms_per_step": round(ms_max, 4), "higher_is_better": True,
+        "metric": METRIC, "value": round(add["gbs"], 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": round(add["ms"], 4), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (torch.randn, seeded)",
-        "config": {"workload": "C2 add_kernel N=2^28 f32, BLOCK=1024, program-id ranges split across GPUs",
-                   "N": args.n, "BLOCK": BLOCK, "per_gpu_elements": n, "parallelism": f"pid-shard x{world}",
-                   "l2": "inputs 3 GiB/step > 126 MB L2 (no flush needed)"},
-        "e2e": e2e,
-        "roofline": {"bound": "hbm", "achieved": round(kernel_gbs_local, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
-                     "frac": round(kernel_gbs_local / pk["hbm_gbs"], 4),
-                     "traffic": traffic, "peak_source": pk["source"] + " (MEASURED_PEAKS.json hbm_gbs)"
-                     if pk["source"] == "measured" else "fallback"},
-        "gpu_launches": launches,
-        "clocks": clk.summary(),
+        "config": {"workload": "C2 add_kernel N=2^28 f32 BLOCK=1024 via shard.run_shard", "N": args.n,
+                   "BLOCK": BLOCK, "per_gpu_elements": add["n"], "parallelism": f"pid-range x{world}",
+                   "l2": "3 GiB/step inputs > L2, no flush"},
+        "e2e": add.get("e2e"),
+        "roofline": {"bound": "hbm", "achieved": round(add["kernel_gbs"], 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(add["kernel_gbs"] / pk["hbm_gbs"], 4),
+                     "traffic": profile_traffic("add_c2_n1") if world == 1 else None, "peak_source": pk["source"]},
+        "gpu_launches": add["launches"], "host_us_per_launch": round(add["host_us"], 1),
+        "clocks": add["clocks"],
     }
-    if gather_res is not None:
-        line["gather"] = gather_res
-    if gemm:
-        line["gemm"] = gemm
-    if tiled is not None:
-        line["matmul_tiled"] = tiled
-    if c1 is not None:
-        line["c1_add_call"] = c1
     if world == 1 and not args.no_cpu_baseline and not args.quick:
         line["cpu_baseline"] = cpu_add_baseline(args.cpu_seconds)
-    print(json.dumps(line), flush=True)
+    if "gather" in add:
+        line["gather"] = add["gather"]
+    if configs:
+        line["configs"] = configs
+    print(json.dumps(line, separators=(",", ":")), flush=True)
 
 
 def run_reference(args) -> None:
-    """CPU semantics of the reference (oracle interpreting the reference front end's add IR)."""
+    """CPU semantics of the reference: the oracle interpreting the reference front end's IR of the
+    same add kernel, on all host threads, over the whole C2 problem (N = 2**28) per step."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -816,24 +854,25 @@ def run_reference(args) -> None:
     case = goldens.case("add_block1024")
     ir = goldens.ir_from_json(case["opt"])
     cores = os.cpu_count() or 1
-    # bounded sample per step: 2^22 elements per thread-chunk (about 0.4 s per step on 16 cores),
-    # halved for every doubling of the step count past 100 so the whole run stays within minutes
-    shrink = 0
-    while (args.steps >> shrink) > 100 and shrink < 6:
-        shrink += 1
-    n = 1 << (22 - shrink)
+    n_total = args.n
+    # sampled (not the full N) only when the full problem at this step count would take many minutes
+    budget_steps = args.steps + max(args.warmup, 1)
+    while n_total > (1 << 22) and budget_steps * n_total * BYTES_PER_ELEM / 2.0e9 > 240:
+        n_total //= 2
+    chunk = 1 << 22
+    nchunks = -(-n_total // chunk)
     rng = np.random.default_rng(1)
-    a = rng.standard_normal(n * cores, dtype=np.float32)
-    b = rng.standard_normal(n * cores, dtype=np.float32)
+    a = rng.standard_normal(n_total, dtype=np.float32)
+    b = rng.standard_normal(n_total, dtype=np.float32)
     c = np.zeros_like(a)
 
-    def chunk(i):
-        sl = slice(i * n, (i + 1) * n)
-        execute(ir, {"a": a[sl], "b": b[sl], "c": c[sl], "N": n})
+    def run_chunk(i):
+        sl = slice(i * chunk, min((i + 1) * chunk, n_total))
+        execute(ir, {"a": a[sl], "b": b[sl], "c": c[sl], "N": sl.stop - sl.start})
 
     def step():
         with ThreadPoolExecutor(cores) as ex:
-            list(ex.map(chunk, range(cores)))
+            list(ex.map(run_chunk, range(nchunks)))
 
     for _ in range(max(args.warmup, 1)):
         step()
@@ -842,14 +881,16 @@ def run_reference(args) -> None:
         step()
     dt = (time.perf_counter() - t0) / args.steps
     assert np.array_equal(c, a + b)
-    gbs = BYTES_PER_ELEM * n * cores / dt / 1e9
-    sample = f"{cores} x 2^{22 - shrink}-element chunks of the C2 add per step (oracle interpreter, {cores} threads)"
+    gbs = BYTES_PER_ELEM * n_total / dt / 1e9
+    full = n_total == args.n
+    sample = (f"{'the full' if full else 'a sampled'} C2 add, {n_total} elements per step in 2^22-element chunks "
+              f"(oracle interpreter, {cores} threads)")
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (numpy default_rng(1))",
-        "config": {"workload": "C2 add_kernel N=2^28 f32, BLOCK=1024 (bounded CPU sample)", "N": N_TOTAL,
-                   "BLOCK": BLOCK},
+        "config": {"workload": "C2 add_kernel N=2^28 f32 BLOCK=1024 via shard.run_shard", "N": args.n,
+                   "BLOCK": BLOCK, "sampled_N": None if full else n_total},
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
@@ -864,7 +905,7 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--n", type=int, default=N_TOTAL, help="total elements (profiling runs use a smaller case)")
-    ap.add_argument("--no-gemm", action="store_true", help="skip the fp16 GEMM configs (C4, C5)")
+    ap.add_argument("--no-gemm", action="store_true", help="skip the GEMM configs (C3, C4, C5)")
     ap.add_argument("--only", choices=["all", "C1", "C3", "C4", "C5"], default="all",
                     help="run a single secondary workload (profiling)")
     ap.add_argument("--gemm-steps", type=int, default=20)

@@ -33,7 +33,7 @@ f32 rounding (the parity tests use the fp16-GEMM tolerance).
 from __future__ import annotations
 
 from dataclasses import dataclass, field
-from typing import Any
+from typing import Any, Mapping
 
 import numpy as np
 
@@ -99,7 +99,18 @@ class DotGemmPlan:
     block_n: int
     kind: str = "dot_gemm_f16_tcgen05"
     last_reason: str = ""
+    tile_m: int = 0      # 0: the library picks the M tile; 128: 1-SM kernel; 256: CTA pair
+    block_k: int = 0     # 0 / 64: one 64-deep k-block per pipeline stage; 128: two
     _memo: dict = field(default_factory=dict, repr=False, compare=False)
+
+    def apply_tile_hints(self, meta: Mapping[str, Any]) -> None:
+        """Take the kernel's ``BLOCK_M`` / ``BLOCK_K`` constexprs, when it has them, as the native
+        tile request (``eas_gemm_f16_tile``): the autotune space of a dot GEMM, in which the
+        reference's Metal kernel uses the same names as threadgroup tile sizes.  Values other than
+        128/256 (``BLOCK_M``) and 64/128 (``BLOCK_K``), 0 included, leave the choice to the library."""
+        bm, bk = meta.get("BLOCK_M"), meta.get("BLOCK_K")
+        self.tile_m = int(bm) if isinstance(bm, int) and bm in (128, 256) else 0
+        self.block_k = int(bk) if isinstance(bk, int) and bk in (64, 128) else 0
 
     # -- launch-time mapping -------------------------------------------------
     def _coord_forms(self, forms: dict[str, dict[str, int]]) -> dict[str, dict[str, int]] | None:
@@ -302,8 +313,9 @@ class DotGemmPlan:
         b = args[self.b_arg].ptr + 2 * m["b0"]
         c = args[self.c_arg].ptr + 4 * m["c0"]
         lib = rt.lib()
-        rc = lib.eas_gemm_f16(a, b, c, m["M"], m["N"], m["K"], m["batch"], m["lda"], m["a_bs"], m["ldb"], m["b_bs"],
-                              m["b_kmajor"], m["ldc"], m["c_bs"], self.block_n, stream)
+        rc = lib.eas_gemm_f16_tile(a, b, c, m["M"], m["N"], m["K"], m["batch"], m["lda"], m["a_bs"], m["ldb"],
+                                   m["b_bs"], m["b_kmajor"], m["ldc"], m["c_bs"], self.tile_m, self.block_n,
+                                   self.block_k, stream)
         if rc == 4:  # EAS_ERR_VALUE: layout the native kernel does not take (alignment, sizes)
             from ..runtime import cuda_ext
 

@@ -494,6 +494,9 @@ def compile(fn: Callable[..., Any], runtime_args: Mapping[str, Any], meta: Mappi
     from .codegen.cuda import ir_to_cuda
 
     lowered = ir_to_cuda(ir)
+    hints = getattr(getattr(lowered, "native", None), "apply_tile_hints", None)
+    if hints is not None:
+        hints(meta)
     return CompiledKernel(ir=ir, src=lowered.src, block_size=lowered.block_size,
                           launch_mode=lowered.mode, writes=infer_writes(ir), plan=lowered)
 

@@ -217,10 +217,13 @@ struct Sched {
   }
 };
 
-template <int BN, int STAGES, bool B_MN>
+// KS k-blocks of 64 per pipeline stage (BLOCK_K = 64 KS): stage = KS A boxes then KS B boxes.
+template <int BN, int STAGES, bool B_MN, int KS = 1>
 struct Smem {
-  static constexpr int kABytes = BM * BK * 2;
-  static constexpr int kBBytes = BN * BK * 2;
+  static constexpr int kA1 = BM * BK * 2;  // one k-block of A
+  static constexpr int kB1 = BN * BK * 2;  // one k-block of B
+  static constexpr int kABytes = KS * kA1;
+  static constexpr int kBBytes = KS * kB1;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kEpiOffset = STAGES * kStageBytes;       // 4 warps x 2 x 32x32 f32 staging boxes
   static constexpr int kEpiBytes = 4 * 2 * 32 * 32 * 4;
@@ -236,14 +239,15 @@ __device__ __forceinline__ void seg_coords(int kb, int seg_kb, int& ka, int& kbk
   kbk = ((seg == 1 ? seg_kb : 0) + kin) * 32;
 }
 
-template <int BN, int STAGES, bool B_MN, bool TMA_C, bool TF = false>
+template <int BN, int STAGES, bool B_MN, bool TMA_C, bool TF = false, int KS = 1>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_f16_tcgen05_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                             const __grid_constant__ CUtensorMap map_c, float* __restrict__ c, int M, int N, int K,
                             int batch, long long ldc, long long c_bstride, int* status, int seg_kb, int ksplit) {
   static_assert(!(TF && B_MN), "tf32 operands are K-major here");
-  constexpr int kBKe = TF ? 32 : BK;  // elements per 128-byte K row of a stage
-  using L = Smem<BN, STAGES, B_MN>;
+  static_assert(KS == 1 || (KS == 2 && !TF), "two k-blocks per stage are f16 only");
+  constexpr int kBKe = TF ? 32 : BK;  // elements per 128-byte K row of a k-block
+  using L = Smem<BN, STAGES, B_MN, KS>;
   // split-K as in the pair kernel: unit u is K part (u % ks) of tile (u / ks), summed into a zeroed C
   const int ks = TMA_C && ksplit > 1 ? ksplit : 1;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -289,11 +293,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   sched.tiles_per_batch = sched.mt * sched.nt;
   sched.total = sched.tiles_per_batch * batch;
   const int kblocks = (K + kBKe - 1) / kBKe;
+  const int kstages = (kblocks + KS - 1) / KS;  // pipeline stages per tile (the last may overhang K: zeros)
   const int units = sched.total * ks;
-  auto k_range = [&](int u, int& kb0, int& kb1) {
+  auto k_range = [&](int u, int& kb0, int& kb1) {  // stage range of work unit u
     const int part = u % ks;
-    kb0 = (int)((long long)part * kblocks / ks);
-    kb1 = (int)((long long)(part + 1) * kblocks / ks);
+    kb0 = (int)((long long)part * kstages / ks);
+    kb1 = (int)((long long)(part + 1) * kstages / ks);
   };
 
   if (warp == 0) {
@@ -308,17 +313,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         k_range(u, kb_lo, kb_hi);
         for (int kb = kb_lo; kb < kb_hi; ++kb) {
           if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) break;
-          uint8_t* sa = smem + s * L::kStageBytes;
-          uint8_t* sb = sa + L::kABytes;
           mbar_expect_tx(&full[s], L::kStageBytes);
-          int ka = kb * kBKe, kbk = ka;
-          if (TF && seg_kb) seg_coords(kb, seg_kb, ka, kbk);
-          tma_load_3d(sa, &map_a, &full[s], ka, tc.m0, tc.b);
-          if (B_MN) {
 #pragma unroll
-            for (int j = 0; j < BN / 64; ++j) tma_load_3d(sb + j * (BK * 128), &map_b, &full[s], n0 + 64 * j, kb * BK, tc.b);
-          } else {
-            tma_load_3d(sb, &map_b, &full[s], kbk, n0, tc.b);
+          for (int sub = 0; sub < KS; ++sub) {
+            uint8_t* sa = smem + s * L::kStageBytes + sub * L::kA1;
+            uint8_t* sb = smem + s * L::kStageBytes + L::kABytes + sub * L::kB1;
+            const int kbs = kb * KS + sub;  // k-block (of 64 f16 / 32 tf32 elements)
+            int ka = kbs * kBKe, kbk = ka;
+            if (TF && seg_kb) seg_coords(kbs, seg_kb, ka, kbk);
+            tma_load_3d(sa, &map_a, &full[s], ka, tc.m0, tc.b);
+            if (B_MN) {
+#pragma unroll
+              for (int j = 0; j < BN / 64; ++j)
+                tma_load_3d(sb + j * (BK * 128), &map_b, &full[s], n0 + 64 * j, kbs * BK, tc.b);
+            } else {
+              tma_load_3d(sb, &map_b, &full[s], kbk, n0, tc.b);
+            }
           }
           if (++s == STAGES) {
             s = 0;
@@ -349,14 +359,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(smem + s * L::kStageBytes);
-          const uint32_t b_addr = a_addr + L::kABytes;
 #pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk) {
-            const uint64_t adesc = smem_desc(a_addr + kk * 32, 16, 1024);
-            const uint64_t bdesc = B_MN ? smem_desc(b_addr + kk * 2048, BK * 128, 1024)
-                                        : smem_desc(b_addr + kk * 32, 16, 1024);
-            tc_mma<TF>(d_tmem, adesc, bdesc, idesc, (kb != kb_lo || kk != 0) ? 1u : 0u);
+          for (int sub = 0; sub < KS; ++sub) {
+            const uint32_t a_addr = smem_u32(smem + s * L::kStageBytes + sub * L::kA1);
+            const uint32_t b_addr = smem_u32(smem + s * L::kStageBytes + L::kABytes + sub * L::kB1);
+#pragma unroll
+            for (int kk = 0; kk < BK / 16; ++kk) {
+              const uint64_t adesc = smem_desc(a_addr + kk * 32, 16, 1024);
+              const uint64_t bdesc = B_MN ? smem_desc(b_addr + kk * 2048, BK * 128, 1024)
+                                          : smem_desc(b_addr + kk * 32, 16, 1024);
+              tc_mma<TF>(d_tmem, adesc, bdesc, idesc, (kb != kb_lo || sub != 0 || kk != 0) ? 1u : 0u);
+            }
           }
           tc_commit(&empty[s]);  // slot s is free once these MMAs have read it
           if (++s == STAGES) {
@@ -505,10 +518,12 @@ __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
-template <int kStages2, bool TMA_C, int NH = 1>
+template <int kStages2, bool TMA_C, int NH = 1, int KS = 1>
 struct Smem2 {
-  static constexpr int kABytes = 128 * BK * 2;        // this CTA's half of the A tile
-  static constexpr int kBBytes = NH * 128 * BK * 2;   // this CTA's half of each 256-column B half
+  static constexpr int kA1 = 128 * BK * 2;            // one k-block of this CTA's half of the A tile
+  static constexpr int kB1 = NH * 128 * BK * 2;       // one k-block of its half of each 256-column B half
+  static constexpr int kABytes = KS * kA1;
+  static constexpr int kBBytes = KS * kB1;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kEpiOffset = kStages2 * kStageBytes;
   static constexpr int kEpiBytes = TMA_C ? 4 * 2 * 32 * 32 * 4 : 0;
@@ -516,7 +531,7 @@ struct Smem2 {
   static constexpr int kTotal = kBarOffset + (2 * kStages2 + 4) * 8 + 16 + 1024;
 };
 
-template <int kStages2, bool B_MN, bool TMA_C, bool TF = false, int NH = 1>
+template <int kStages2, bool B_MN, bool TMA_C, bool TF = false, int NH = 1, int KS = 1>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_f16_tcgen05_2sm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                                 const __grid_constant__ CUtensorMap map_c, float* __restrict__ c, int M, int N, int K,
@@ -529,7 +544,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   // feeds twice the columns (25 % fewer operand bytes per FLOP from L2)
   static_assert(NH == 1 || NH == 2, "one or two 256-column halves per pair tile");
   static_assert(!(TF && NH == 2), "wide tiles are f16 only");
-  using L = Smem2<kStages2, TMA_C, NH>;
+  static_assert(KS == 1 || (KS == 2 && !TF), "two k-blocks per stage are f16 only");
+  using L = Smem2<kStages2, TMA_C, NH, KS>;
   // split-K: work unit u is K part (u % ks) of tile (u / ks); parts after the first are summed into
   // C (zeroed by the host) with TMA reduce-adds, so only the TMA-store epilogue splits
   const int ks = TMA_C && ksplit > 1 ? ksplit : 1;
@@ -581,13 +597,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   sched.tiles_per_batch = sched.mt * sched.nt;
   sched.total = sched.tiles_per_batch * batch;
   const int kblocks = (K + kBKe - 1) / kBKe;
+  const int kstages = (kblocks + KS - 1) / KS;  // pipeline stages per tile (the last may overhang K: zeros)
   const int cid = blockIdx.x >> 1;
   const int ncl = gridDim.x >> 1;
   const int units = sched.total * ks;
-  auto k_range = [&](int u, int& kb0, int& kb1) {
+  auto k_range = [&](int u, int& kb0, int& kb1) {  // stage range of work unit u
     const int part = u % ks;
-    kb0 = (int)((long long)part * kblocks / ks);
-    kb1 = (int)((long long)(part + 1) * kblocks / ks);
+    kb0 = (int)((long long)part * kstages / ks);
+    kb1 = (int)((long long)(part + 1) * kstages / ks);
   };
 
   if (warp == 0) {
@@ -602,21 +619,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         k_range(u, kb_lo, kb_hi);
         for (int kb = kb_lo; kb < kb_hi; ++kb) {
           if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) break;
-          uint8_t* sa = smem + s * L::kStageBytes;
-          uint8_t* sb = sa + L::kABytes;
           const uint32_t fl = mapa_rank(smem_u32(&full[s]), 0);
           if (rank == 0) mbar_expect_tx(&full[s], 2 * L::kStageBytes);
-          int ka = kb * kBKe, kbk = ka;
-          if (TF && seg_kb) seg_coords(kb, seg_kb, ka, kbk);
-          tma_load_3d_pair(sa, &map_a, fl, ka, m0, tc.b);
 #pragma unroll
-          for (int h = 0; h < NH; ++h) {  // this CTA's 128 columns of each 256-column half
-            uint8_t* sbh = sb + h * (128 * BK * 2);
-            if (B_MN) {
-              tma_load_3d_pair(sbh, &map_b, fl, n0 + 256 * h, kb * BK, tc.b);
-              tma_load_3d_pair(sbh + BK * 128, &map_b, fl, n0 + 256 * h + 64, kb * BK, tc.b);
-            } else {
-              tma_load_3d_pair(sbh, &map_b, fl, kbk, n0 + 256 * h, tc.b);
+          for (int sub = 0; sub < KS; ++sub) {
+            uint8_t* sa = smem + s * L::kStageBytes + sub * L::kA1;
+            uint8_t* sb = smem + s * L::kStageBytes + L::kABytes + sub * L::kB1;
+            const int kbs = kb * KS + sub;  // k-block (of 64 f16 / 32 tf32 elements)
+            int ka = kbs * kBKe, kbk = ka;
+            if (TF && seg_kb) seg_coords(kbs, seg_kb, ka, kbk);
+            tma_load_3d_pair(sa, &map_a, fl, ka, m0, tc.b);
+#pragma unroll
+            for (int h = 0; h < NH; ++h) {  // this CTA's 128 columns of each 256-column half
+              uint8_t* sbh = sb + h * (128 * BK * 2);
+              if (B_MN) {
+                tma_load_3d_pair(sbh, &map_b, fl, n0 + 256 * h, kbs * BK, tc.b);
+                tma_load_3d_pair(sbh + BK * 128, &map_b, fl, n0 + 256 * h + 64, kbs * BK, tc.b);
+              } else {
+                tma_load_3d_pair(sbh, &map_b, fl, kbk, n0 + 256 * h, tc.b);
+              }
             }
           }
           if (++s == kStages2) {
@@ -635,11 +656,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       int local = 0;
       // MMAs of halves [h0, h1) of the stage in slot st at k-block kb
       auto issue = [&](int st, int kb, int kb_lo, uint32_t d_tmem, int h0, int h1) {
-        const uint32_t a_addr = smem_u32(smem + st * L::kStageBytes);
-        const uint32_t b_addr = a_addr + L::kABytes;
+#pragma unroll
+        for (int sub = 0; sub < KS; ++sub) {
+        const uint32_t a_addr = smem_u32(smem + st * L::kStageBytes + sub * L::kA1);
+        const uint32_t b_addr = smem_u32(smem + st * L::kStageBytes + L::kABytes + sub * L::kB1);
 #pragma unroll
         for (int kk = 0; kk < BK / 16; ++kk) {
           const uint64_t adesc = smem_desc(a_addr + kk * 32, 16, 1024);
+          const uint32_t acc = (kb != kb_lo || sub != 0 || kk != 0) ? 1u : 0u;
 #pragma unroll
           for (int h = 0; h < NH; ++h) {  // one N = 256 MMA per half, into its 256 accumulator columns
             if (h < h0 || h >= h1) continue;
@@ -651,16 +675,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                   "{\n\t.reg .pred p;\n\t"
                   "setp.ne.b32 p, %4, 0;\n\t"
                   "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(dh),
-                  "l"(adesc), "l"(bdesc), "r"(idesc), "r"((kb != kb_lo || kk != 0) ? 1u : 0u)
+                  "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
                   : "memory");
             else
               asm volatile(
                   "{\n\t.reg .pred p;\n\t"
                   "setp.ne.b32 p, %4, 0;\n\t"
                   "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(dh),
-                  "l"(adesc), "l"(bdesc), "r"(idesc), "r"((kb != kb_lo || kk != 0) ? 1u : 0u)
+                  "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
                   : "memory");
           }
+        }
         }
       };
       auto release = [&](int st) {
@@ -840,9 +865,9 @@ int encode_map(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uin
 
 // Tile configuration of the most recent GEMM launch in this process (reporting only).
 struct LastConfig {
-  int bm, bn, stages, ksplit, pair;
+  int bm, bn, stages, ksplit, pair, block_k;
 };
-LastConfig g_last_config = {0, 0, 0, 0, 0};
+LastConfig g_last_config = {0, 0, 0, 0, 0, 0};
 
 // The dynamic shared-memory opt-in is a per-function, per-device setting: make it once per kernel
 // instantiation and device instead of on every launch.
@@ -859,21 +884,33 @@ int set_smem_once(int bytes, const char* what) {
 }
 
 // Split-K for launches that leave most CTAs (1-SM kernel) or CTA pairs idle: with at most half as
-// many tiles as resident CTAs / pairs (`slots`), each tile's K range is cut into ks <= 4 parts (ks <= slots / tiles, at least 8
-// k-blocks per part) and the parts are summed into a zeroed C with TMA reduce-adds, so up to 4x
-// the CTAs work.  Launches with a tile per slot or more do not split: zeroing C and summing 4
+// many tiles as resident CTAs / pairs (`slots`), each tile's K range is cut into ks parts
+// (ks <= slots / tiles, at least 8 k-blocks per part) and the parts are summed into a zeroed C with
+// TMA reduce-adds.  Launches with a tile per slot or more do not split: zeroing C and summing
 // partial tiles through L2 cost more than the last wave's idle pairs (measured on the per-GPU
 // shards of C4 at 8 GPUs, 128 tiles on 74 pairs: 1109 TFLOP/s split 4 ways vs 1215 unsplit).
-// The reduce-adds land in any order, so split results may differ from run to run in the last
-// bits; EAS_GEMM_SPLITK=0 turns splitting off.
-int choose_ksplit(long long tiles, long long slots, int kblocks, int batch) {
-  static const bool enabled = [] {
+//
+// Reproducibility: the reduce-adds of one tile land in any order.  With two parts every element
+// is (0 + p) + q or (0 + q) + p, and both are exactly p + q (0 + x is x for every x, the sign of
+// zero included, and f32 addition is commutative), so ks <= 2 gives the same bits on every run.
+// Three or more parts would not (f32 addition is not associative), so the default cap is 2.
+// EAS_GEMM_SPLITK=0 turns splitting off; EAS_GEMM_SPLITK=4 allows up to 4 parts, which is faster
+// on very small grids but may differ from run to run in the last bits.
+int splitk_cap() {
+  static const int cap = [] {
     const char* e = getenv("EAS_GEMM_SPLITK");
-    return !(e && e[0] == '0');
+    if (!e || !e[0]) return 2;
+    const int v = atoi(e);
+    return v <= 1 ? 1 : (v >= 4 ? 4 : v);
   }();
-  if (!enabled || slots <= 0 || tiles <= 0 || batch > 64 || 2 * tiles > slots) return 1;
+  return cap;
+}
+
+int choose_ksplit(long long tiles, long long slots, int kblocks, int batch) {
+  const int cap = splitk_cap();
+  if (cap <= 1 || slots <= 0 || tiles <= 0 || batch > 64 || 2 * tiles > slots) return 1;
   long long ks = slots / tiles;
-  if (ks > 4) ks = 4;
+  if (ks > cap) ks = cap;
   while (ks > 1 && kblocks < 8 * ks) --ks;
   return (int)ks;
 }
@@ -889,12 +926,14 @@ int zero_c_for_split(float* c, int M, int N, int batch, long long ldc, long long
   return EAS_OK;
 }
 
-template <int BN, int STAGES, bool B_MN, bool TMA_C, bool TF = false>
+template <int BN, int STAGES, bool B_MN, bool TMA_C, bool TF = false, int KS = 1>
 int launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, float* c, int M, int N, int K,
                    int batch, long long ldc, long long cbs, int* status, cudaStream_t stream, int num_sms, int seg_kb = 0) {
-  using L = Smem<BN, STAGES, B_MN>;
-  auto kern = gemm_f16_tcgen05_kernel<BN, STAGES, B_MN, TMA_C, TF>;
-  int rc = set_smem_once<gemm_f16_tcgen05_kernel<BN, STAGES, B_MN, TMA_C, TF>>(L::kTotal, "gemm: set smem attribute");
+  using L = Smem<BN, STAGES, B_MN, KS>;
+  static_assert(L::kTotal <= 232448, "shared memory over the 227 KB per-CTA limit");
+  auto kern = gemm_f16_tcgen05_kernel<BN, STAGES, B_MN, TMA_C, TF, KS>;
+  int rc = set_smem_once<gemm_f16_tcgen05_kernel<BN, STAGES, B_MN, TMA_C, TF, KS>>(L::kTotal,
+                                                                               "gemm: set smem attribute");
   if (rc) return rc;
   const long long tiles = (long long)((M + BM - 1) / BM) * ((N + BN - 1) / BN) * batch;
   const int ksplit = TMA_C ? choose_ksplit(tiles, num_sms, (K + (TF ? 32 : BK) - 1) / (TF ? 32 : BK), batch) : 1;
@@ -904,28 +943,27 @@ int launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorM
   }
   const long long units = tiles * ksplit;
   const int grid = (int)(units < num_sms ? units : num_sms);
-  g_last_config = {BM, BN, STAGES, ksplit, 0};
+  g_last_config = {BM, BN, STAGES, ksplit, 0, KS * BK};
   kern<<<grid, kThreads, L::kTotal, stream>>>(ma, mb, mc, c, M, N, K, batch, ldc, cbs, status, seg_kb, ksplit);
   return eas_cuda_check(cudaGetLastError(), "gemm: launch", EAS_ERR_LAUNCH);
 }
 
-template <int STAGES, bool B_MN, bool TMA_C, bool TF = false, int NH = 1>
+template <int STAGES, bool B_MN, bool TMA_C, bool TF = false, int NH = 1, int KS = 1>
 int launch_2sm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, float* c, int M, int N, int K,
                int batch, long long ldc, long long cbs, int* status, cudaStream_t stream, int num_sms, int seg_kb = 0) {
-  using L = Smem2<STAGES, TMA_C, NH>;
+  using L = Smem2<STAGES, TMA_C, NH, KS>;
   static_assert(L::kTotal <= 232448, "shared memory over the 227 KB per-CTA limit");
-  auto kern = gemm_f16_tcgen05_2sm_kernel<STAGES, B_MN, TMA_C, TF, NH>;
-  int rc = set_smem_once<gemm_f16_tcgen05_2sm_kernel<STAGES, B_MN, TMA_C, TF, NH>>(L::kTotal,
-                                                                             "gemm(2sm): set smem attribute");
+  auto kern = gemm_f16_tcgen05_2sm_kernel<STAGES, B_MN, TMA_C, TF, NH, KS>;
+  int rc = set_smem_once<gemm_f16_tcgen05_2sm_kernel<STAGES, B_MN, TMA_C, TF, NH, KS>>(L::kTotal,
+                                                                                 "gemm(2sm): set smem attribute");
   if (rc) return rc;
   const long long tiles = (long long)((M + 255) / 256) * ((N + 256 * NH - 1) / (256 * NH)) * batch;
   // persistent grid: only as many pairs as can be resident at once (GPC boundaries can leave SMs unpaired)
-  static int resident_pairs[2][64] = {{0}};
-  const int which = TMA_C ? 1 : 0;
+  static int resident_pairs[64] = {0};  // one table per kernel instantiation
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) dev = 0;
-  if (resident_pairs[which][dev] == 0) {
+  if (resident_pairs[dev] == 0) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * (num_sms / 2), 1, 1);
     cfg.blockDim = dim3(kThreads, 1, 1);
@@ -935,9 +973,9 @@ int launch_2sm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& 
       cudaGetLastError();
       n = num_sms / 2;
     }
-    resident_pairs[which][dev] = n;
+    resident_pairs[dev] = n;
   }
-  const long long pairs = resident_pairs[which][dev];
+  const long long pairs = resident_pairs[dev];
   const int ksplit = TMA_C ? choose_ksplit(tiles, pairs, (K + (TF ? 32 : BK) - 1) / (TF ? 32 : BK), batch) : 1;
   if (ksplit > 1) {  // the K parts are summed into C by TMA reduce-adds: start from zeros
     rc = zero_c_for_split(c, M, N, batch, ldc, cbs, stream);
@@ -945,7 +983,7 @@ int launch_2sm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& 
   }
   const long long units = tiles * ksplit;
   const int grid = 2 * (int)(units < pairs ? units : pairs);
-  g_last_config = {256, 256 * NH, STAGES, ksplit, 1};
+  g_last_config = {256, 256 * NH, STAGES, ksplit, 1, KS * BK};
   kern<<<grid, kThreads, L::kTotal, stream>>>(ma, mb, mc, c, M, N, K, batch, ldc, cbs, status, seg_kb, ksplit);
   return eas_cuda_check(cudaGetLastError(), "gemm(2sm): launch", EAS_ERR_LAUNCH);
 }
@@ -973,6 +1011,71 @@ bool use_2sm(int block_n, uint32_t M) {
     return !(e && e[0] == '0');
   }();
   return enabled && block_n == 256 && M > 128;
+}
+
+// The f16 kernel a launch runs.  tile_m = 0 lets the library choose (CTA pair for block_n = 256
+// and M > 128, wide pair tiles by use_wide, one k-block per stage); an explicit request is the
+// autotune space of the DSL's BLOCK_M / BLOCK_N / BLOCK_K:
+//   tile_m  128: the 1-SM kernel, tile 128 x block_n;
+//           256: the CTA pair (M = 256 per MMA), each CTA staging block_n columns of B per
+//                k-block, so the pair tile is 256 x 2 block_n (256 x 512 needs a TMA-storable C;
+//                without one the pair tile stays 256 x 256);
+//   block_k 64 or 128: K depth of one pipeline stage (one or two 64-wide k-blocks), with half as
+//                many stages at 128 (same shared memory).
+struct F16Choice {
+  bool pair;
+  int tile_n;  // columns of the (pair) tile
+  int nh;      // pair only: 256-column halves per pair tile
+  int ks;      // k-blocks per stage
+  int stages;
+};
+
+F16Choice choose_f16(uint32_t M, uint32_t N, uint32_t batch, int block_n, int tile_m, int block_k, bool tma_c,
+                     int num_sms) {
+  F16Choice ch{};
+  ch.ks = block_k == 128 ? 2 : 1;
+  ch.pair = tile_m == 0 ? use_2sm(block_n, M) : tile_m == 256;
+  if (ch.pair) {
+    const bool wide = tma_c && (tile_m == 0 ? (N >= 512 && use_wide(M, N, batch, num_sms)) : block_n == 256);
+    ch.nh = wide ? 2 : 1;
+    ch.tile_n = 256 * ch.nh;
+    ch.stages = wide ? 4 / ch.ks : (tma_c ? 6 / ch.ks : (ch.ks == 1 ? 7 : 3));
+  } else {
+    ch.nh = 0;
+    ch.tile_n = block_n;
+    ch.stages = (block_n == 256 ? 4 : 6) / ch.ks;
+  }
+  return ch;
+}
+
+// Launch the kernel of `ch` (f16 operands).  Stage counts here and in choose_f16 agree.
+template <int KS>
+int launch_f16_choice(const F16Choice& ch, bool b_mn, bool tma_c, const CUtensorMap& ma, const CUtensorMap& mb,
+                      const CUtensorMap& mc, float* c, int M, int N, int K, int batch, long long ldc, long long cbs,
+                      int* status, cudaStream_t s, int num_sms) {
+  constexpr int kS1w = 4 / KS, kS1 = 6 / KS, kS1d = KS == 1 ? 7 : 3;  // pair: wide, 256-wide, direct-store C
+  constexpr int kSs256 = 4 / KS, kSs128 = 6 / KS;                    // 1-SM: BN = 256, 128
+#define EAS_ARGS ma, mb, mc, c, M, N, K, batch, ldc, cbs, status, s, num_sms
+  if (ch.pair) {
+    if (ch.nh == 2)  // TMA-storable C only
+      return b_mn ? launch_2sm<kS1w, true, true, false, 2, KS>(EAS_ARGS)
+                  : launch_2sm<kS1w, false, true, false, 2, KS>(EAS_ARGS);
+    if (!tma_c)
+      return b_mn ? launch_2sm<kS1d, true, false, false, 1, KS>(EAS_ARGS)
+                  : launch_2sm<kS1d, false, false, false, 1, KS>(EAS_ARGS);
+    return b_mn ? launch_2sm<kS1, true, true, false, 1, KS>(EAS_ARGS)
+                : launch_2sm<kS1, false, true, false, 1, KS>(EAS_ARGS);
+  }
+  if (ch.tile_n == 256)
+    return b_mn ? (tma_c ? launch_variant<256, kSs256, true, true, false, KS>(EAS_ARGS)
+                         : launch_variant<256, kSs256, true, false, false, KS>(EAS_ARGS))
+                : (tma_c ? launch_variant<256, kSs256, false, true, false, KS>(EAS_ARGS)
+                         : launch_variant<256, kSs256, false, false, false, KS>(EAS_ARGS));
+  return b_mn ? (tma_c ? launch_variant<128, kSs128, true, true, false, KS>(EAS_ARGS)
+                       : launch_variant<128, kSs128, true, false, false, KS>(EAS_ARGS))
+              : (tma_c ? launch_variant<128, kSs128, false, true, false, KS>(EAS_ARGS)
+                       : launch_variant<128, kSs128, false, false, false, KS>(EAS_ARGS));
+#undef EAS_ARGS
 }
 
 int* g_status_host = nullptr;  // host-mapped status words, one per device
@@ -1020,7 +1123,8 @@ namespace {
 template <bool TF>
 int gemm_entry(const char* who, const void* a, const void* b, float* c, uint32_t M, uint32_t N, uint32_t K,
                uint32_t batch, uint64_t lda, uint64_t a_bstride, uint64_t ldb, uint64_t b_bstride, int b_kmajor,
-               uint64_t ldc, uint64_t c_bstride, int block_n, void* stream, bool split = false) {
+               uint64_t ldc, uint64_t c_bstride, int block_n, void* stream, bool split = false, int tile_m = 0,
+               int block_k = 0) {
   constexpr uint64_t kElem = TF ? 4 : 2;
   constexpr uint32_t kBoxK = TF ? 32 : BK;
   const CUtensorMapDataType dt = TF ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -1030,6 +1134,10 @@ int gemm_entry(const char* who, const void* a, const void* b, float* c, uint32_t
   if (M == 0 || N == 0 || batch == 0) return EAS_OK;
   if (K == 0) return eas_fail(EAS_ERR_VALUE, "%s: K == 0 (nothing to accumulate)", who);
   if (block_n != 128 && block_n != 256) return eas_fail(EAS_ERR_VALUE, "%s: block_n must be 128 or 256", who);
+  if (tile_m != 0 && tile_m != 128 && tile_m != 256)
+    return eas_fail(EAS_ERR_VALUE, "%s: tile_m must be 0 (library's choice), 128 or 256", who);
+  if (block_k != 0 && block_k != 64 && block_k != 128)
+    return eas_fail(EAS_ERR_VALUE, "%s: block_k must be 0 (library's choice), 64 or 128", who);
   if (M > 0x7fffffffu || N > 0x7fffffffu || K > 0x7fffffffu)
     return eas_fail(EAS_ERR_VALUE, "%s: dimension exceeds 2^31-1", who);
   if (TF && !b_kmajor) return eas_fail(EAS_ERR_VALUE, "%s: B must be K-major", who);
@@ -1058,16 +1166,17 @@ int gemm_entry(const char* who, const void* a, const void* b, float* c, uint32_t
   rc = encode_map(&ma, a, k_map, M, batch, lda * kElem, ab ? ab : 16, kBoxK, BM, dt);
   if (rc) return rc;
   const bool b_mn = !b_kmajor;
-  const bool pair = use_2sm(block_n, M);
+  // C through TMA stores when its rows/batches are 16-byte strided and the base is aligned
+  const bool tma_c = (reinterpret_cast<uintptr_t>(c) & 15) == 0 && (ldc * 4) % 16 == 0 &&
+                     (batch == 1 || (c_bstride * 4) % 16 == 0) && ldc >= N;
+  const F16Choice ch = choose_f16(M, N, batch, block_n, TF ? 0 : tile_m, TF ? 0 : block_k, tma_c, num_sms);
+  const bool pair = ch.pair;
   if (b_mn)
     rc = encode_map(&mb, b, N, K, batch, ldb * kElem, bb ? bb : 16, 64, kBoxK, dt);
   else
     rc = encode_map(&mb, b, k_map, N, batch, ldb * kElem, bb ? bb : 16, kBoxK, pair ? 128u : (uint32_t)block_n, dt);
   if (rc) return rc;
-  // C through TMA stores when its rows/batches are 16-byte strided and the base is aligned
   CUtensorMap mc;
-  const bool tma_c = (reinterpret_cast<uintptr_t>(c) & 15) == 0 && (ldc * 4) % 16 == 0 &&
-                     (batch == 1 || (c_bstride * 4) % 16 == 0) && ldc >= N;
   if (tma_c) {
     const uint64_t cb = batch > 1 ? c_bstride * 4 : (uint64_t)M * ldc * 4;
     rc = encode_map(&mc, c, N, M, batch, ldc * 4, cb ? cb : 16, 32, 32, CU_TENSOR_MAP_DATA_TYPE_FLOAT32);
@@ -1077,14 +1186,6 @@ int gemm_entry(const char* who, const void* a, const void* b, float* c, uint32_t
   }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const long long ldc_l = (long long)ldc, cbs = (long long)c_bstride;
-#define EAS_GEMM_VARIANT(BN_, ST_)                                                                              \
-  (b_mn ? (tma_c ? launch_variant<BN_, ST_, true, true>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s, num_sms) \
-                 : launch_variant<BN_, ST_, true, false>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s,      \
-                                                         num_sms))                                               \
-        : (tma_c ? launch_variant<BN_, ST_, false, true>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s,     \
-                                                         num_sms)                                                \
-                 : launch_variant<BN_, ST_, false, false>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s,    \
-                                                          num_sms)))
   if constexpr (TF) {  // K-major operands only
     if (pair)
       return tma_c ? launch_2sm<6, false, true, true>(ma, mb, mc, c, M, N, k_run, batch, ldc_l, cbs, status, s, num_sms,
@@ -1096,61 +1197,48 @@ int gemm_entry(const char* who, const void* a, const void* b, float* c, uint32_t
                  : launch_variant<128, 6, false, false, true>(ma, mb, mc, c, M, N, k_run, batch, ldc_l, cbs, status, s,
                                                               num_sms, seg_kb);
   } else {
-    if (pair && tma_c && N >= 512 && use_wide(M, N, batch, num_sms)) {  // 256 x 512 pair tiles
-      return b_mn ? launch_2sm<4, true, true, false, 2>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s, num_sms)
-                  : launch_2sm<4, false, true, false, 2>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s, num_sms);
-    }
-    if (pair) {
-      if (!tma_c)  // C not TMA-storable: direct stores, and the smem freed by the staging boxes buys a 7th stage
-        return b_mn ? launch_2sm<7, true, false>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s, num_sms)
-                    : launch_2sm<7, false, false>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s, num_sms);
-      return b_mn ? launch_2sm<6, true, true>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s, num_sms)
-                  : launch_2sm<6, false, true>(ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s, num_sms);
-    }
-    if (block_n == 256) return EAS_GEMM_VARIANT(256, 4);
-    return EAS_GEMM_VARIANT(128, 6);
+    if (ch.ks == 2)
+      return launch_f16_choice<2>(ch, b_mn, tma_c, ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s, num_sms);
+    return launch_f16_choice<1>(ch, b_mn, tma_c, ma, mb, mc, c, M, N, K, batch, ldc_l, cbs, status, s, num_sms);
   }
-#undef EAS_GEMM_VARIANT
 }
 
 }  // namespace
 
-extern "C" int eas_gemm_f16_plan(uint32_t M, uint32_t N, uint32_t K, uint32_t batch, int block_n, int c_tma_ok,
-                                 int num_sms, int resident_pairs, int* tile_m, int* tile_n, int* stages, int* ksplit,
-                                 int* pair) {
+extern "C" int eas_gemm_f16_plan(uint32_t M, uint32_t N, uint32_t K, uint32_t batch, int block_n, int tile_m,
+                                 int block_k, int c_tma_ok, int num_sms, int resident_pairs, int* out_tile_m,
+                                 int* out_tile_n, int* stages, int* ksplit, int* pair, int* out_block_k) {
   // the same helpers, in the same order, as the launch branch of gemm_entry<false> and its launchers
-  if (!tile_m || !tile_n || !stages || !ksplit || !pair) return eas_fail(EAS_ERR_VALUE, "eas_gemm_f16_plan: null");
+  if (!out_tile_m || !out_tile_n || !stages || !ksplit || !pair || !out_block_k)
+    return eas_fail(EAS_ERR_VALUE, "eas_gemm_f16_plan: null");
   if (block_n != 128 && block_n != 256) return eas_fail(EAS_ERR_VALUE, "eas_gemm_f16_plan: block_n must be 128 or 256");
+  if (tile_m != 0 && tile_m != 128 && tile_m != 256)
+    return eas_fail(EAS_ERR_VALUE, "eas_gemm_f16_plan: tile_m must be 0, 128 or 256");
+  if (block_k != 0 && block_k != 64 && block_k != 128)
+    return eas_fail(EAS_ERR_VALUE, "eas_gemm_f16_plan: block_k must be 0, 64 or 128");
   if (M == 0 || N == 0 || K == 0 || batch == 0 || num_sms <= 0)
     return eas_fail(EAS_ERR_VALUE, "eas_gemm_f16_plan: empty launch");
   const int kblocks = (int)((K + BK - 1) / BK);
-  const long long mt2 = (M + 255) / 256, mt1 = (M + BM - 1) / BM;
-  if (use_2sm(block_n, M)) {
-    *pair = 1;
-    *tile_m = 256;
-    const bool wide = c_tma_ok && N >= 512 && use_wide(M, N, batch, num_sms);
-    *tile_n = wide ? 512 : 256;
-    *stages = wide ? 4 : (c_tma_ok ? 6 : 7);
-    const long long tiles = mt2 * ((N + *tile_n - 1) / *tile_n) * batch;
-    *ksplit = c_tma_ok ? choose_ksplit(tiles, resident_pairs, kblocks, (int)batch) : 1;
-  } else {
-    *pair = 0;
-    *tile_m = BM;
-    *tile_n = block_n == 256 ? 256 : 128;
-    *stages = block_n == 256 ? 4 : 6;
-    const long long tiles = mt1 * ((N + *tile_n - 1) / *tile_n) * batch;
-    *ksplit = c_tma_ok ? choose_ksplit(tiles, num_sms, kblocks, (int)batch) : 1;
-  }
+  const F16Choice ch = choose_f16(M, N, batch, block_n, tile_m, block_k, c_tma_ok != 0, num_sms);
+  *pair = ch.pair ? 1 : 0;
+  *out_tile_m = ch.pair ? 256 : BM;
+  *out_tile_n = ch.tile_n;
+  *stages = ch.stages;
+  *out_block_k = BK * ch.ks;
+  const long long tiles = (long long)((M + *out_tile_m - 1) / *out_tile_m) * ((N + ch.tile_n - 1) / ch.tile_n) * batch;
+  *ksplit = c_tma_ok ? choose_ksplit(tiles, ch.pair ? resident_pairs : num_sms, kblocks, (int)batch) : 1;
   return EAS_OK;
 }
 
-extern "C" int eas_gemm_last_config(int* tile_m, int* tile_n, int* stages, int* ksplit, int* pair) {
-  if (!tile_m || !tile_n || !stages || !ksplit || !pair) return eas_fail(EAS_ERR_VALUE, "eas_gemm_last_config: null");
+extern "C" int eas_gemm_last_config(int* tile_m, int* tile_n, int* stages, int* ksplit, int* pair, int* block_k) {
+  if (!tile_m || !tile_n || !stages || !ksplit || !pair || !block_k)
+    return eas_fail(EAS_ERR_VALUE, "eas_gemm_last_config: null");
   *tile_m = g_last_config.bm;
   *tile_n = g_last_config.bn;
   *stages = g_last_config.stages;
   *ksplit = g_last_config.ksplit;
   *pair = g_last_config.pair;
+  *block_k = g_last_config.block_k;
   return EAS_OK;
 }
 
@@ -1159,6 +1247,14 @@ extern "C" int eas_gemm_f16(const void* a, const void* b, float* c, uint32_t M, 
                             int b_kmajor, uint64_t ldc, uint64_t c_bstride, int block_n, void* stream) {
   return gemm_entry<false>("eas_gemm_f16", a, b, c, M, N, K, batch, lda, a_bstride, ldb, b_bstride, b_kmajor, ldc,
                            c_bstride, block_n, stream);
+}
+
+extern "C" int eas_gemm_f16_tile(const void* a, const void* b, float* c, uint32_t M, uint32_t N, uint32_t K,
+                                 uint32_t batch, uint64_t lda, uint64_t a_bstride, uint64_t ldb, uint64_t b_bstride,
+                                 int b_kmajor, uint64_t ldc, uint64_t c_bstride, int tile_m, int block_n, int block_k,
+                                 void* stream) {
+  return gemm_entry<false>("eas_gemm_f16_tile", a, b, c, M, N, K, batch, lda, a_bstride, ldb, b_bstride, b_kmajor,
+                           ldc, c_bstride, block_n, stream, false, tile_m, block_k);
 }
 
 extern "C" int eas_gemm_tf32(const float* a, const float* b, float* c, uint32_t M, uint32_t N, uint32_t K,

@@ -61,6 +61,7 @@ class Kernel:
         self._defaults = {n: p.default for n, p in self.sig.parameters.items() if p.default is not p.empty}
         self._autotune_spec: AutotuneSpec | None = None
         self._tuned_cache: dict[tuple[Any, ...], Config] = {}
+        self._tuned_times: dict[tuple[Any, ...], list[tuple[dict[str, Any], float]]] = {}
 
     def _set_autotune_spec(self, spec: AutotuneSpec) -> None:
         self._autotune_spec = spec
@@ -145,8 +146,13 @@ class Kernel:
         return tuple(key)
 
     def _autotune_select(self, spec: AutotuneSpec, meta: dict[str, Any], runtime_args: dict[str, Any],
-                         raw_opts: dict[str, Any]) -> tuple[dict[str, Any], dict[str, Any]]:
-        key = self._autotune_key(spec, meta, runtime_args)
+                         raw_opts: dict[str, Any], timer: Callable[..., float] | None = None,
+                         key_extra: tuple[Any, ...] = ()) -> tuple[dict[str, Any], dict[str, Any]]:
+        """Fastest config for this key (easy_as ``eas/kernel.py:73-127``): each config is timed
+        with the runtime's ``benchmark`` (or ``timer(ck, meta, opts)`` when a caller times a
+        different launch, such as one rank's program-id range, whose identity goes in
+        ``key_extra``).  The seconds per config of a search are kept in ``_tuned_times``."""
+        key = self._autotune_key(spec, meta, runtime_args) + tuple(key_extra)
         best = self._tuned_cache.get(key)
         disk_key = None
         if best is None:
@@ -157,22 +163,29 @@ class Kernel:
                 if best is not None:
                     self._tuned_cache[key] = best
         if best is None:
-            bench = getattr(get_runtime(), "benchmark", None)
-            if not callable(bench):
-                raise RuntimeError("autotune requires a runtime with benchmark(); use the CUDA runtime")
+            if timer is None:
+                bench = getattr(get_runtime(), "benchmark", None)
+                if not callable(bench):
+                    raise RuntimeError("autotune requires a runtime with benchmark(); use the CUDA runtime")
+
+                def timer(ck: CompiledKernel, m: dict[str, Any], opts: dict[str, Any]) -> float:
+                    return float(bench(ck, runtime_args, m, repeat=spec.repeat, warmup=spec.warmup,
+                                       nthreads=opts["nthreads"], grid=opts["grid"], tptg=opts["tptg"],
+                                       shape=opts["shape"]))
             best_t = None
+            times = []
             for cfg in spec.configs:
                 m = {**meta, **dict(cfg.meta)}
                 opts = self._normalize_runtime_options(raw_opts, m, runtime_args)
                 ck = self._compile_from_split(m, runtime_args)
-                t = float(bench(ck, runtime_args, m, repeat=spec.repeat, warmup=spec.warmup,
-                                nthreads=opts["nthreads"], grid=opts["grid"], tptg=opts["tptg"],
-                                shape=opts["shape"]))
+                t = float(timer(ck, m, opts))
+                times.append((dict(cfg.meta), t))
                 if best_t is None or t < best_t:
                     best, best_t = cfg, t
             if best is None:  # pragma: no cover
                 raise RuntimeError("autotune failed to select a config")
             self._tuned_cache[key] = best
+            self._tuned_times[key] = times
             _disk_store(disk_key, dict(best.meta))
         m = {**meta, **dict(best.meta)}
         return m, self._normalize_runtime_options(raw_opts, m, runtime_args)

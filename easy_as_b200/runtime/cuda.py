@@ -1131,6 +1131,37 @@ class CudaRuntime:
                                "(a bounded pipeline wait expired; results are incomplete)")
 
     # -- timing ---------------------------------------------------------------------------
+    def benchmark_range(self, ck: Any, runtime_args: Mapping[str, Any], meta: Mapping[str, Any], *, axis: int,
+                        lo: int, hi: int, repeat: int, warmup: int = 0, grid: tuple[int, int, int] | None = None,
+                        nthreads: int | None = None, shape: tuple[int, ...] | None = None,
+                        buffer_base: Mapping[str, int] | None = None) -> float:
+        """Mean seconds per :meth:`run_range` launch of programs ``[lo, hi)`` on ``axis`` (CUDA
+        events on the launch stream, after ``warmup`` launches)."""
+        if repeat <= 0:
+            raise ValueError("repeat must be > 0")
+        kw = dict(axis=axis, lo=lo, hi=hi, grid=grid, nthreads=nthreads, shape=shape, buffer_base=buffer_base)
+        for _ in range(max(warmup, 0)):
+            self.run_range(ck, runtime_args, meta, sync=False, **kw)
+        self.synchronize()
+        _, device, stream = self._resolve(ck, runtime_args, allow_bounce=False)
+        lib = self.lib()
+        e0, e1 = cuda_ext.ctypes.c_void_p(), cuda_ext.ctypes.c_void_p()
+        cuda_ext.check(lib.eas_event_create(cuda_ext.ctypes.byref(e0)), "event_create")
+        cuda_ext.check(lib.eas_event_create(cuda_ext.ctypes.byref(e1)), "event_create")
+        try:
+            cuda_ext.check(lib.eas_event_record(e0, stream), "event_record")
+            for _ in range(repeat):
+                self.run_range(ck, runtime_args, meta, sync=False, **kw)
+            cuda_ext.check(lib.eas_event_record(e1, stream), "event_record")
+            cuda_ext.check(lib.eas_event_synchronize(e1), "kernel execution")
+            ms = cuda_ext.ctypes.c_float()
+            cuda_ext.check(lib.eas_event_elapsed_ms(e0, e1, cuda_ext.ctypes.byref(ms)), "elapsed")
+        finally:
+            lib.eas_event_destroy(e0)
+            lib.eas_event_destroy(e1)
+        self._check_native_status(device)
+        return float(ms.value) * 1e-3 / repeat
+
     def benchmark(self, ck: Any, runtime_args: Mapping[str, Any], meta: Mapping[str, Any], *, repeat: int,
                   warmup: int = 0, nthreads: int | None = None, grid: tuple[int, int, int] | None = None,
                   tptg: tuple[int, int, int] | None = None, shape: tuple[int, ...] | None = None,

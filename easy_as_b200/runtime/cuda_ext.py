@@ -79,8 +79,12 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "eas_gemm_f16": (_int, [_vp, _vp, _vp, _u32, _u32, _u32, _u32, ctypes.c_uint64, ctypes.c_uint64,
                             ctypes.c_uint64, ctypes.c_uint64, _int, ctypes.c_uint64, ctypes.c_uint64, _int, _vp]),
     "eas_gemm_status": (_int, [_int, _PINT]),
-    "eas_gemm_last_config": (_int, [_PINT, _PINT, _PINT, _PINT, _PINT]),
-    "eas_gemm_f16_plan": (_int, [_u32, _u32, _u32, _u32, _int, _int, _int, _int, _PINT, _PINT, _PINT, _PINT, _PINT]),
+    "eas_gemm_f16_tile": (_int, [_vp, _vp, _vp, _u32, _u32, _u32, _u32, ctypes.c_uint64, ctypes.c_uint64,
+                                 ctypes.c_uint64, ctypes.c_uint64, _int, ctypes.c_uint64, ctypes.c_uint64, _int, _int,
+                                 _int, _vp]),
+    "eas_gemm_last_config": (_int, [_PINT, _PINT, _PINT, _PINT, _PINT, _PINT]),
+    "eas_gemm_f16_plan": (_int, [_u32, _u32, _u32, _u32, _int, _int, _int, _int, _int, _int, _PINT, _PINT, _PINT,
+                                 _PINT, _PINT, _PINT]),
     "eas_gemm_tf32": (_int, [_vp, _vp, _vp, _u32, _u32, _u32, _u32, ctypes.c_uint64, ctypes.c_uint64,
                              ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64, _int, _vp]),
     "eas_gemm_3xtf32": (_int, [_vp, _vp, _vp, _u32, _u32, _u32, _u32, ctypes.c_uint64, ctypes.c_uint64,

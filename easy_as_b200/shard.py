@@ -39,26 +39,44 @@ def run_shard(kernel: Any, *args: Any, _rank: int, _world: int, _axis: int = 0,
     """Run this rank's share of ``kernel(*args, **kwargs)``; returns the program range it ran.
 
     Launch options (``_grid``, ``_nthreads``, ``_shape``) describe the *whole*
-    launch, exactly as for a single-GPU call.
+    launch, exactly as for a single-GPU call.  An autotuned kernel is tuned on
+    this rank's own range (its buffers may hold only their slice, so the whole
+    launch cannot be timed here); the choice is cached per range.
     """
     from .runtime import get_runtime
+    from .runtime.cuda import launch_geometry
 
+    rt = get_runtime()
     raw = kernel._extract_runtime_options(kwargs)
     meta, runtime_args = kernel._bind_and_split(*args, **kwargs)
+
+    def share(ck: Any, opts: Mapping[str, Any]) -> tuple[int, int] | None:
+        geo = launch_geometry(ck, runtime_args, nthreads=opts["nthreads"], grid=opts["grid"], tptg=None,
+                              shape=opts["shape"])
+        return None if geo is None else program_range(geo[0][_axis], _rank, _world)
+
     if kernel._autotune_spec is not None:
-        meta, opts = kernel._autotune_select(kernel._autotune_spec, meta, runtime_args, raw)
+        spec = kernel._autotune_spec
+
+        def timer(ck: Any, m: Mapping[str, Any], opts: Mapping[str, Any]) -> float:
+            r = share(ck, opts)
+            if r is None:
+                return 0.0
+            return rt.benchmark_range(ck, runtime_args, m, axis=_axis, lo=r[0], hi=r[1], grid=opts["grid"],
+                                      nthreads=opts["nthreads"], shape=opts["shape"], buffer_base=_buffer_base,
+                                      repeat=spec.repeat, warmup=spec.warmup)
+
+        extra = ("range", _axis, _rank, _world, tuple(sorted((_buffer_base or {}).items())))
+        meta, opts = kernel._autotune_select(spec, meta, runtime_args, raw, timer=timer, key_extra=extra)
     else:
         opts = kernel._normalize_runtime_options(raw, meta, runtime_args)
     ck = kernel._compile_from_split(meta, runtime_args)
-    from .runtime.cuda import launch_geometry
-
-    geo = launch_geometry(ck, runtime_args, nthreads=opts["nthreads"], grid=opts["grid"], tptg=None,
-                          shape=opts["shape"])
-    if geo is None:
+    r = share(ck, opts)
+    if r is None:
         return (0, 0)
-    lo, hi = program_range(geo[0][_axis], _rank, _world)
-    get_runtime().run_range(ck, runtime_args, meta, axis=_axis, lo=lo, hi=hi, grid=opts["grid"],
-                            nthreads=opts["nthreads"], shape=opts["shape"], buffer_base=_buffer_base, sync=_sync)
+    lo, hi = r
+    rt.run_range(ck, runtime_args, meta, axis=_axis, lo=lo, hi=hi, grid=opts["grid"], nthreads=opts["nthreads"],
+                 shape=opts["shape"], buffer_base=_buffer_base, sync=_sync)
     return lo, hi
 
 

@@ -5,9 +5,12 @@ accumulation and an f32 output; A is ``[batch, M, K]`` and B ``[batch, K, N]``,
 both row-major and contiguous, K is a runtime scalar.  Each DSL thread owns one
 output element; ``program_id(0)`` tiles N, ``program_id(1)`` is the row and
 ``program_id(2)`` the batch.  The CUDA backend recognises this shape and runs
-it on the tcgen05 tensor-core GEMM; ``BLOCK_N`` picks that kernel's N tile,
-``BLOCK_M``/``BLOCK_K`` are the tile hints of the autotune space named in the
-benchmark configuration (the current native kernel uses 128 x BLOCK_N x 64).
+it on the tcgen05 tensor-core GEMM (``eas_gemm_f16_tile``).  ``BLOCK_N`` is
+the N tile of a CTA; ``BLOCK_M`` 128 runs the 1-SM kernel (128 x BLOCK_N
+tiles) and 256 a CTA pair (256 x 2 BLOCK_N tiles); ``BLOCK_K`` 64 or 128 is
+the K depth of one pipeline stage.  The default ``BLOCK_M = BLOCK_K = 0``
+leaves the M tile and stage depth to the library.  ``CONFIGS`` is the
+autotune space of benchmark configuration C4: eight distinct kernels.
 
 Run as a script for a quick check against torch (needs a GPU).
 """
@@ -26,8 +29,8 @@ def _cdiv(a, b):
 
 
 @eas.kernel
-def matmul_dot_f16(a, b, c, M, N, K, BLOCK_M: eas.constexpr = 128, BLOCK_N: eas.constexpr = 256,
-                   BLOCK_K: eas.constexpr = 64):
+def matmul_dot_f16(a, b, c, M, N, K, BLOCK_M: eas.constexpr = 0, BLOCK_N: eas.constexpr = 256,
+                   BLOCK_K: eas.constexpr = 0):
     col = mk.program_id(0) * BLOCK_N + mk.tid(0, BLOCK_N)
     row = mk.program_id(1)
     bat = mk.program_id(2)
@@ -50,7 +53,7 @@ def matmul(a, b, c, batch, M, N, K, *, block_n=256, tuned=False, sync=True):
     if tuned:
         matmul_dot_f16_tuned(a, b, c, M, N, K, _grid=grid(batch), _sync=sync)
     else:
-        matmul_dot_f16(a, b, c, M, N, K, BLOCK_M=128, BLOCK_N=block_n, BLOCK_K=64, _grid=grid(batch), _sync=sync)
+        matmul_dot_f16(a, b, c, M, N, K, BLOCK_N=block_n, _grid=grid(batch), _sync=sync)
 
 
 def main():

@@ -163,12 +163,33 @@ int eas_event_elapsed_ms(void* start, void* end, float* ms);
  *   C at c + b*c_bstride + m*ldc + n
  * A and B must be 16-byte aligned with strides that are multiples of 8
  * elements (TMA); otherwise EAS_ERR_VALUE (the caller then runs the generic
- * kernel).  block_n is the N tile (128 or 256).  Asynchronous on `stream`.
+ * kernel).  block_n is the N tile (128 or 256); the library picks the rest
+ * of the tile (eas_gemm_f16_tile with tile_m = 0).  Asynchronous on `stream`.
  * A pipeline wait that exceeds its budget ends the kernel early and is
- * reported by eas_gemm_status(). */
+ * reported by eas_gemm_status().  Launches that leave most SMs idle split K
+ * into at most 2 parts by default (see eas_gemm_f16_plan), which keeps every
+ * result bit-reproducible; EAS_GEMM_SPLITK=4 allows 4 parts, whose order of
+ * summation (and so the last bits) may vary from run to run. */
 int eas_gemm_f16(const void* a, const void* b, float* c, uint32_t M, uint32_t N, uint32_t K, uint32_t batch,
                  uint64_t lda, uint64_t a_bstride, uint64_t ldb, uint64_t b_bstride, int b_kmajor, uint64_t ldc,
                  uint64_t c_bstride, int block_n, void* stream);
+
+/* eas_gemm_f16 with an explicit tile configuration: the native meaning of the
+ * autotune space BLOCK_M x BLOCK_N x BLOCK_K of a DSL dot GEMM (the reference
+ * times each Config and keeps the fastest, eas/kernel.py:73-127; its Metal
+ * kernel uses the values as threadgroup tile sizes).
+ *   tile_m  0: the library's choice (as eas_gemm_f16);
+ *           128: the 1-SM kernel, output tile 128 x block_n;
+ *           256: a CTA pair (tcgen05 cta_group::2, M = 256), each CTA staging
+ *                block_n columns of B per k-block: pair tile 256 x 2*block_n
+ *                (256 x 512 only when C is TMA-storable, else 256 x 256).
+ *   block_k 0 or 64: one 64-deep k-block per pipeline stage; 128: two, with
+ *           half as many stages in the same shared memory.
+ * Every (tile_m, block_n, block_k) in {128, 256} x {128, 256} x {64, 128}
+ * launches a different kernel.  Other values: EAS_ERR_VALUE. */
+int eas_gemm_f16_tile(const void* a, const void* b, float* c, uint32_t M, uint32_t N, uint32_t K, uint32_t batch,
+                      uint64_t lda, uint64_t a_bstride, uint64_t ldb, uint64_t b_bstride, int b_kmajor,
+                      uint64_t ldc, uint64_t c_bstride, int tile_m, int block_n, int block_k, void* stream);
 
 /* Strided batched fp32 GEMM with per-K-tile partial sums, true fp32 FFMA on
  * the CUDA cores.  Replaces the launch of the generated kernel for the
@@ -215,20 +236,23 @@ int eas_cast_f32_f16_2d(const float* src, void* dst, uint32_t rows, uint32_t col
  * Nothing faults or hangs; the context stays usable.  Asynchronous. */
 int eas_wait_selftest(long long budget_cycles, void* stream);
 
-/* What eas_gemm_f16 would launch, without a device: the CTA-pair or 1-SM
- * kernel (*pair), the output tile (tile_m x tile_n per CTA pair or CTA),
- * pipeline stages and split-K parts, for a C that TMA can store (c_tma_ok:
- * 16-byte aligned base and strides) on a GPU with num_sms SMs of which
- * resident_pairs CTA pairs are co-resident (cudaOccupancyMaxActiveClusters).
- * Composes the same rules the launcher applies (no reference counterpart). */
-int eas_gemm_f16_plan(uint32_t M, uint32_t N, uint32_t K, uint32_t batch, int block_n, int c_tma_ok, int num_sms,
-                      int resident_pairs, int* tile_m, int* tile_n, int* stages, int* ksplit, int* pair);
+/* What eas_gemm_f16_tile (tile_m, block_n, block_k; tile_m = block_k = 0 is
+ * eas_gemm_f16) would launch, without a device: the CTA-pair or 1-SM kernel
+ * (*pair), the output tile (out_tile_m x out_tile_n per CTA pair or CTA),
+ * pipeline stages, split-K parts and the K depth of a stage (out_block_k),
+ * for a C that TMA can store (c_tma_ok: 16-byte aligned base and strides) on
+ * a GPU with num_sms SMs of which resident_pairs CTA pairs are co-resident
+ * (cudaOccupancyMaxActiveClusters).  Composes the same rules the launcher
+ * applies (no reference counterpart). */
+int eas_gemm_f16_plan(uint32_t M, uint32_t N, uint32_t K, uint32_t batch, int block_n, int tile_m, int block_k,
+                      int c_tma_ok, int num_sms, int resident_pairs, int* out_tile_m, int* out_tile_n, int* stages,
+                      int* ksplit, int* pair, int* out_block_k);
 
 /* Tile configuration the most recent eas_gemm_* launch in this process used:
  * output tile (tile_m x tile_n per CTA, or per CTA pair when *pair is 1),
- * pipeline stages and split-K parts.  Reporting only (no reference
- * counterpart). */
-int eas_gemm_last_config(int* tile_m, int* tile_n, int* stages, int* ksplit, int* pair);
+ * pipeline stages, split-K parts and K depth of a stage.  Reporting only (no
+ * reference counterpart). */
+int eas_gemm_last_config(int* tile_m, int* tile_n, int* stages, int* ksplit, int* pair, int* block_k);
 
 /* Strided batched GEMM on tcgen05 with TF32 operands (kind::tf32, f32
  * accumulate): C[b][m][n] = sum_k A[b][m][k] * B[b][n][k] with A at
@@ -272,7 +296,13 @@ int eas_gemm_status(int dev, int* code);
  * device allocator or a fixed memory budget), or code that must not allocate
  * at the point where it launches work.  No counterpart in the reference.
  *
- * Same arguments and results as eas_gemm_f16.  The kernel's only scratch, one
+ * Same arguments as eas_gemm_f16, and the same sums, but it launches only the
+ * 1-SM kernels (128 x block_n tiles, one k-block per stage), never the CTA-pair
+ * or 256 x 512 tiles that eas_gemm_f16 takes for M > 128: slower on large
+ * shapes, and the results agree with eas_gemm_f16 to f32 rounding, not bit for
+ * bit (the tensor core may sum a different tile shape in another order).
+ * eas_gemm_f16_plan and eas_gemm_last_config do not describe its launch
+ * choice beyond that.  The kernel's only scratch, one
  * 4-byte status word, lives in a file-scope __device__ array of this library
  * (one word per GPU that loads it, held until the process exits) instead of
  * memory allocated on first use; this call never calls cudaMalloc, cudaFree
@@ -284,9 +314,13 @@ int eas_gemm_status(int dev, int* code);
  * (cudaGetSymbolAddress) with that device current; make that first call
  * before any stream capture.  Every call clears the word, then runs the
  * kernel.  All calls on a device share the word, so calls that overlap on the
- * GPU race on it.  With status_out != NULL the call waits for the kernel and
- * stores the status there (0 = ok, EAS_ERR_TIMEOUT = a bounded wait expired);
- * with NULL it returns at once. */
+ * GPU race on it.  The stream must belong to the current device (the word is
+ * looked up for the current device).  With status_out != NULL the call
+ * copies the word out and synchronises the stream, then stores the status
+ * there (0 = ok, EAS_ERR_TIMEOUT = a bounded wait expired).  With NULL it
+ * returns at once and the status is lost: nothing reads the word back, and
+ * the next call clears it, so a wait that expired then goes unreported and C
+ * may be incomplete.  Pass status_out wherever the result matters. */
 int eas_gemm_f16_noalloc(const void* a, const void* b, float* c, uint32_t M, uint32_t N, uint32_t K,
                          uint32_t batch, uint64_t lda, uint64_t a_bstride, uint64_t ldb, uint64_t b_bstride,
                          int b_kmajor, uint64_t ldc, uint64_t c_bstride, int block_n, void* stream,

@@ -29,7 +29,7 @@ def _run(cuda_rt, batch, M, N, K, bn, seed=0):
     a, b = _inputs(batch, M, N, K, seed)
     c = np.zeros((batch, M, N), np.float32)
     before = cuda_rt.native_launches
-    matmul_dot_f16(a.reshape(-1), b.reshape(-1), c.reshape(-1), M, N, K, BLOCK_M=128, BLOCK_N=bn, BLOCK_K=64,
+    matmul_dot_f16(a.reshape(-1), b.reshape(-1), c.reshape(-1), M, N, K, BLOCK_N=bn,
                    _grid=grid(batch))
     return a, b, c, cuda_rt.native_launches - before
 
@@ -121,7 +121,7 @@ def test_torch_tensors_zero_copy_and_async(cuda_rt):
     a = (torch.randn(batch, M, K, device="cuda", generator=g) / K ** 0.5).half()
     b = (torch.randn(batch, K, N, device="cuda", generator=g) / K ** 0.5).half()
     c = torch.empty(batch, M, N, device="cuda")
-    matmul_dot_f16(a.reshape(-1), b.reshape(-1), c.reshape(-1), M, N, K, BLOCK_M=128, BLOCK_N=256, BLOCK_K=64,
+    matmul_dot_f16(a.reshape(-1), b.reshape(-1), c.reshape(-1), M, N, K, BLOCK_N=256,
                    _grid=grid(batch), _sync=False)
     cuda_rt.synchronize()
     ref = torch.bmm(a.double(), b.double())

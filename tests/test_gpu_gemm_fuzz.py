@@ -49,7 +49,7 @@ def test_random_gemm_shapes(cuda_rt, i):
         cuda_ext.check(lib.eas_gemm_status(0, ctypes.byref(code)), "status")
         assert code.value == 0
     else:
-        matmul_dot_f16(a.reshape(-1), b.reshape(-1), c.reshape(-1), M, N, K, BLOCK_M=128, BLOCK_N=bn, BLOCK_K=64,
+        matmul_dot_f16(a.reshape(-1), b.reshape(-1), c.reshape(-1), M, N, K, BLOCK_N=bn,
                        _grid=grid(batch), _sync=True)
     ref = torch.bmm(a.double(), b.double())
     assert not torch.isnan(c).any(), (batch, M, N, K, bn, kmajor)

@@ -29,7 +29,7 @@ def test_fully_stored_output_is_not_copied_in(cuda_rt):
     a, b = _inputs(batch, M, N, K)
     c = np.full(batch * M * N, np.nan, np.float32)
     before = cuda_rt.skipped_copy_bytes
-    matmul_dot_f16(a, b, c, M, N, K, BLOCK_M=128, BLOCK_N=256, BLOCK_K=64, _grid=grid(batch))
+    matmul_dot_f16(a, b, c, M, N, K, BLOCK_N=256, _grid=grid(batch))
     assert cuda_rt.skipped_copy_bytes - before == c.nbytes
     ref = _ref(a, b, batch, M, N, K)
     assert not np.isnan(c).any()
@@ -42,12 +42,12 @@ def test_partly_stored_outputs_keep_their_other_elements(cuda_rt):
     # a larger C buffer: elements past M*N are never stored
     c = np.full(M * N + 4096, 7.0, np.float32)
     before = cuda_rt.skipped_copy_bytes
-    matmul_dot_f16(a, b, c, M, N, K, BLOCK_M=128, BLOCK_N=256, BLOCK_K=64, _grid=grid(batch))
+    matmul_dot_f16(a, b, c, M, N, K, BLOCK_N=256, _grid=grid(batch))
     assert cuda_rt.skipped_copy_bytes == before
     assert np.all(c[M * N:] == 7.0)
     # a grid over the first 300 rows only: rows 300.. keep their values
     c2 = np.full(M * N, 5.0, np.float32)
-    matmul_dot_f16(a, b, c2, M, N, K, BLOCK_M=128, BLOCK_N=256, BLOCK_K=64, _grid=(N // 256, 300, 1))
+    matmul_dot_f16(a, b, c2, M, N, K, BLOCK_N=256, _grid=(N // 256, 300, 1))
     assert cuda_rt.skipped_copy_bytes == before
     assert np.all(c2.reshape(M, N)[300:] == 5.0)
     ref = _ref(a, b, 1, M, N, K)[0]
@@ -72,7 +72,7 @@ def test_batched_gemm_on_pinned_host_tensors_is_pipelined(cuda_rt, monkeypatch):
                                             "M": M, "N": N, "K": K}, ((N // 256 + (N % 256 > 0), M, batch),
                                                                       0xFFFFFFFF)) is not None
     before = cuda_rt.native_launches
-    matmul_dot_f16(a.reshape(-1), b.reshape(-1), c.reshape(-1), M, N, K, BLOCK_M=128, BLOCK_N=256, BLOCK_K=64,
+    matmul_dot_f16(a.reshape(-1), b.reshape(-1), c.reshape(-1), M, N, K, BLOCK_N=256,
                    _grid=grid(batch))
     assert cuda_rt.native_launches - before >= 2           # one native launch per slice
     ref = torch.bmm(a.double(), b.double())

@@ -21,7 +21,7 @@ def test_f16_dot_gemm_shards_run_natively(cuda_rt, world, axis):
     a = (torch.randn(batch * M * K, device="cuda", generator=g) / K ** 0.5).half()
     b = (torch.randn(batch * K * N, device="cuda", generator=g) / K ** 0.5).half()
     full = torch.zeros(batch * M * N, device="cuda")
-    meta = dict(BLOCK_M=128, BLOCK_N=256, BLOCK_K=64)
+    meta = dict(BLOCK_N=256)
     matmul_dot_f16(a, b, full, M, N, K, **meta, _grid=grid(batch))
     parts = torch.zeros_like(full)
     before = cuda_rt.native_launches

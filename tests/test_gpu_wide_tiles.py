@@ -37,9 +37,9 @@ for batch, M, N, K in [(1, 300, 704, 136), (2, 512, 1024, 200), (1, 257, 520, 72
     b = (torch.randn(batch, K, N, device="cuda", generator=g) / K ** 0.5).half()
     c = torch.full((batch, M, N), float("nan"), device="cuda")
     before = rt.native_launches
-    matmul_dot_f16(a.reshape(-1), b.reshape(-1), c.reshape(-1), M, N, K, BLOCK_M=128, BLOCK_N=256, BLOCK_K=64,
+    matmul_dot_f16(a.reshape(-1), b.reshape(-1), c.reshape(-1), M, N, K, BLOCK_N=256,
                    _grid=grid(batch), _sync=True)
-    vals = [ctypes.c_int() for _ in range(5)]
+    vals = [ctypes.c_int() for _ in range(6)]
     lib.eas_gemm_last_config(*(ctypes.byref(x) for x in vals))
     tn = vals[1].value
     ref = torch.bmm(a.double(), b.double())

@@ -16,7 +16,7 @@ def _ck(M, N, K, batch, bn=256):
     a = np.zeros(1, np.float16)
     b = np.zeros(1, np.float16)
     c = np.zeros(1, np.float32)
-    return matmul_dot_f16.compile(a, b, c, M, N, K, BLOCK_M=128, BLOCK_N=bn, BLOCK_K=64)
+    return matmul_dot_f16.compile(a, b, c, M, N, K, BLOCK_N=bn)
 
 
 def _scal(M, N, K):

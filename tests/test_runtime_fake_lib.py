@@ -188,6 +188,13 @@ class FakeLib:
         self.pdl_launches = getattr(self, "pdl_launches", 0) + 1
         return self.eas_launch(*args)
 
+    def eas_gemm_f16_tile(self, a, b, c, M, N, K, batch, lda, a_bs, ldb, b_bs, b_kmajor, ldc, c_bs, tile_m, block_n,
+                          block_k, stream):
+        """The explicit-tile entry: same sums as eas_gemm_f16 (the tile only changes speed)."""
+        if tile_m not in (0, 128, 256) or block_k not in (0, 64, 128):
+            return 4
+        return self.eas_gemm_f16(a, b, c, M, N, K, batch, lda, a_bs, ldb, b_bs, b_kmajor, ldc, c_bs, block_n, stream)
+
     def eas_gemm_f16(self, a, b, c, M, N, K, batch, lda, a_bs, ldb, b_bs, b_kmajor, ldc, c_bs, block_n, stream):
         """numpy stand-in for the tcgen05 GEMM over the fake device memory."""
         self.calls.append(("gemm", M, N, K, batch))
@@ -396,7 +403,7 @@ def test_host_output_stored_in_full_is_not_copied_in(fake):
     a = rng.standard_normal(M * K).astype(np.float16)
     b = rng.standard_normal(K * N).astype(np.float16)
     c = np.full(M * N, np.nan, np.float32)
-    _run(lib, rt, matmul_dot_f16, (a, b, c, M, N, K), grid=(1, M, 1), BLOCK_M=128, BLOCK_N=256, BLOCK_K=64)
+    _run(lib, rt, matmul_dot_f16, (a, b, c, M, N, K), grid=(1, M, 1), BLOCK_N=256)
     h2d = [k[1] for k in lib.calls if k[0] == "h2d"]
     assert sorted(h2d) == sorted([a.nbytes, b.nbytes])          # no copy of c
     assert rt.skipped_copy_bytes == c.nbytes
@@ -405,7 +412,7 @@ def test_host_output_stored_in_full_is_not_copied_in(fake):
 
     lib.calls.clear()
     c2 = np.full(M * N + 8, 3.0, np.float32)
-    _run(lib, rt, matmul_dot_f16, (a, b, c2, M, N, K), grid=(1, M, 1), BLOCK_M=128, BLOCK_N=256, BLOCK_K=64)
+    _run(lib, rt, matmul_dot_f16, (a, b, c2, M, N, K), grid=(1, M, 1), BLOCK_N=256)
     assert sorted(k[1] for k in lib.calls if k[0] == "h2d") == sorted([a.nbytes, b.nbytes, c2.nbytes])
     assert np.all(c2[M * N:] == 3.0)
 
@@ -430,7 +437,7 @@ def test_elementwise_launch_on_host_arrays_is_zero_copy(fake):
     y = rng.standard_normal(K * N).astype(np.float16)
     z = np.zeros(M * N, np.float32)
     lib.calls.clear()
-    _run(lib, rt, matmul_dot_f16, (x, y, z, M, N, K), grid=(1, M, 1), BLOCK_M=128, BLOCK_N=256, BLOCK_K=64)
+    _run(lib, rt, matmul_dot_f16, (x, y, z, M, N, K), grid=(1, M, 1), BLOCK_N=256)
     assert any(k[0] == "h2d_async" for k in lib.calls) and any(k[0] == "d2h_async" for k in lib.calls)
 
 
@@ -448,7 +455,7 @@ def test_batched_gemm_on_pinned_host_arrays_is_pipelined(fake, monkeypatch):
     b = rng.standard_normal(batch * K * N).astype(np.float16)
     c = np.full(batch * M * N, np.nan, np.float32)
     lib.pinned_ranges = [(x.ctypes.data, x.ctypes.data + x.nbytes) for x in (a, b, c)]
-    _run(lib, rt, matmul_dot_f16, (a, b, c, M, N, K), grid=(1, M, batch), BLOCK_M=128, BLOCK_N=256, BLOCK_K=64)
+    _run(lib, rt, matmul_dot_f16, (a, b, c, M, N, K), grid=(1, M, batch), BLOCK_N=256)
     gemms = [k for k in lib.calls if k[0] == "gemm"]
     assert [g[4] for g in gemms] == [2, 2, 1]                       # slices of 2, 2 and 1 batches
     copies_in = [k[1] for k in lib.calls if k[0] == "h2d_async"]
@@ -548,7 +555,7 @@ def test_checked_kernels_run_as_generated(fake, checked):
     a = np.ones(M * K, np.float16)
     b = np.ones(K * N, np.float16)
     c = np.zeros(M * N, np.float32)
-    ck = matmul_dot_f16.compile(a, b, c, M, N, K, BLOCK_M=128, BLOCK_N=256, BLOCK_K=64)
+    ck = matmul_dot_f16.compile(a, b, c, M, N, K, BLOCK_N=256)
     assert ck.plan.checked and ck.plan.native is None
     ck2 = add_kernel.compile(c, c, c, M * N, BLOCK=256)
     assert ck2.plan.checked and ck2.plan.elementwise is None
