@@ -31,12 +31,33 @@ def sources() -> list[Path]:
     return sorted(CSRC.glob("*.cu"))
 
 
-def needs_build() -> bool:
-    if not LIB.exists():
-        return True
-    t = LIB.stat().st_mtime
+def _flags(ptxas_verbose: bool = False) -> list[str]:
+    return [*ARCH, "-O3", "-lineinfo", "-std=c++17", "-shared", "-Xcompiler", "-fPIC", "-cudart", "static",
+            *(["-Xptxas", "-v"] if ptxas_verbose else [])]
+
+
+def source_hash() -> str:
+    """sha256 over every source and header the library is built from, and the nvcc flags."""
+    import hashlib
+
+    h = hashlib.sha256()
     deps = sources() + sorted(CSRC.glob("*.h")) + sorted(CSRC.glob("*.cuh")) + [PKG.parent / "include" / "eas_cuda.h"]
-    return any(p.stat().st_mtime > t for p in deps if p.exists())
+    for p in deps:
+        if p.exists():
+            h.update(p.name.encode() + b"\0" + p.read_bytes() + b"\0")
+    h.update(" ".join(_flags()).encode())
+    return h.hexdigest()
+
+
+STAMP = LIB.with_name(LIB.name + ".sha256")
+
+
+def needs_build() -> bool:
+    """Rebuild unless the library exists and its stamp (written beside it by the build that made it)
+    matches the current sources and flags; file times play no part."""
+    if not LIB.exists() or not STAMP.exists():
+        return True
+    return STAMP.read_text().strip() != source_hash()
 
 
 def build(verbose: bool = False, force: bool = False, ptxas_verbose: bool = False) -> Path:
@@ -44,9 +65,8 @@ def build(verbose: bool = False, force: bool = False, ptxas_verbose: bool = Fals
         return LIB
     LIB_DIR.mkdir(parents=True, exist_ok=True)
     tmp = LIB.with_suffix(".so.tmp")
-    cmd = [nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "-shared", "-Xcompiler", "-fPIC",
-           "-cudart", "static", "-I", str(PKG.parent / "include"), "-I", str(CSRC),
-           *(["-Xptxas", "-v"] if ptxas_verbose else []),
+    digest = source_hash()
+    cmd = [nvcc(), *_flags(ptxas_verbose), "-I", str(PKG.parent / "include"), "-I", str(CSRC),
            *map(str, sources()), "-o", str(tmp), "-ldl", "-lpthread"]
     if verbose:
         print(" ".join(cmd), flush=True)
@@ -56,6 +76,7 @@ def build(verbose: bool = False, force: bool = False, ptxas_verbose: bool = Fals
     if verbose or ptxas_verbose:
         sys.stdout.write(res.stdout + res.stderr)
     os.replace(tmp, LIB)
+    STAMP.write_text(digest + "\n")
     return LIB
 
 

@@ -111,9 +111,18 @@ def load(*, require: bool = True) -> ctypes.CDLL | None:
     if _lib is not None:
         return _lib
     path = Path(os.environ.get("EAS_CUDA_LIB", str(LIB_PATH)))
+    stale = None
+    if path == LIB_PATH and path.exists():
+        from .. import build as _build
+
+        if _build.STAMP.exists() and _build.STAMP.read_text().strip() != _build.source_hash():
+            stale = (f"native library {path} was built from other sources than the ones beside it; "
+                     "rebuild with `python -m easy_as_b200.build`")
     if not path.exists():
         _load_error = (f"native library {path} is not built; run `python -m easy_as_b200.build` "
                        "(nvcc for sm_100a)")
+    elif stale:
+        _load_error = stale
     else:
         try:
             lib = ctypes.CDLL(str(path))

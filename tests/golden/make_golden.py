@@ -1,9 +1,8 @@
 """Generate tests/golden/reference_ir.json(.gz) from the reference front end.
 
-Run where the reference checkout is readable (its location in
-$EAS_REFERENCE, else the default below):
+Run where a reference checkout is readable, its location in $EAS_REFERENCE:
 
-    python tests/golden/make_golden.py
+    EAS_REFERENCE=<path to the easy_as checkout> python tests/golden/make_golden.py
 
 For every case below this script imports the reference package ``eas`` and
 the reference module that defines the kernel (examples/*.py, tests/*.py),
@@ -30,7 +29,9 @@ import sys
 from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
-REF = Path(os.environ.get("EAS_REFERENCE", "/root/reference"))
+if not os.environ.get("EAS_REFERENCE"):
+    raise SystemExit("make_golden.py: set EAS_REFERENCE to a checkout of the reference (easy_as)")
+REF = Path(os.environ["EAS_REFERENCE"])
 
 
 def B(dtype: str, n: int) -> dict:

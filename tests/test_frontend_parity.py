@@ -54,7 +54,7 @@ def _ref_kernel(c):
     return getattr(mod, attr)
 
 
-@pytest.mark.skipif(not REFERENCE.exists(), reason="reference checkout not present")
+@pytest.mark.skipif(REFERENCE is None or not REFERENCE.exists(), reason="EAS_REFERENCE not set to a reference checkout")
 @pytest.mark.parametrize("c", CASES, ids=[c["id"] for c in CASES])
 def test_tracer_reproduces_reference(c):
     kern = _ref_kernel(c)

@@ -4,6 +4,7 @@ compiles generated CUDA with NVRTC for sm_100a, and honours host-side fault inje
 from __future__ import annotations
 
 import ctypes
+import os
 import re
 from pathlib import Path
 
@@ -80,3 +81,15 @@ def test_check_maps_status_to_exception_types():
     with pytest.raises(RuntimeError):
         cuda_ext.check(cuda_ext.EAS_ERR_LAUNCH)
 
+
+
+def test_build_is_keyed_on_a_source_hash():
+    """The library's stamp records the sha256 of the sources and nvcc flags it was built from; a
+    changed source (not a newer file time) is what makes ``needs_build`` true."""
+    from easy_as_b200 import build
+
+    assert build.STAMP.exists(), "build() writes the stamp beside the library"
+    assert build.STAMP.read_text().strip() == build.source_hash()
+    assert not build.needs_build()
+    os.utime(build.sources()[0])          # touching a file changes nothing
+    assert not build.needs_build()
