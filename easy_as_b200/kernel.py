@@ -20,10 +20,14 @@ import inspect
 import os as _os
 from typing import Any, Callable, Mapping
 
+import numpy as _np
+
 from .autotune import AutotuneSpec, Config
 from .compiler import CompiledKernel, compile as _compile, fast_arg_sig, runtime_arg_signature
 from .meta import constexpr
+from .compiler import _torch
 from .runtime import get_runtime
+from .tensor import Tensor as _Tensor
 
 _LAUNCH_OPTIONS = ("_sync", "_shape", "_grid", "_tptg", "_nthreads")
 
@@ -62,6 +66,12 @@ class Kernel:
         self._autotune_spec: AutotuneSpec | None = None
         self._tuned_cache: dict[tuple[Any, ...], Config] = {}
         self._tuned_times: dict[tuple[Any, ...], list[tuple[dict[str, Any], float]]] = {}
+        # prepared launches of repeated calls (runtime fast path); EAS_FAST_LAUNCH=0 turns it off
+        self._fast: dict[tuple[Any, ...], Any] | None = (
+            None if _os.environ.get("EAS_FAST_LAUNCH", "1") in ("0", "off") else {})
+        runtime_names = [n for n in self._names if n not in self.meta_params]
+        self._positions = {n: i for i, n in enumerate(runtime_names)}
+        self._runtime_first = tuple(self._names[:len(runtime_names)]) == tuple(runtime_names)
 
     def _set_autotune_spec(self, spec: AutotuneSpec) -> None:
         self._autotune_spec = spec
@@ -244,9 +254,60 @@ class Kernel:
     def compile(self, /, *args: Any, **kwargs: Any) -> CompiledKernel:
         return self._prepare(args, dict(kwargs))[0]
 
+    def _fast_key(self, args: tuple[Any, ...], kwargs: dict[str, Any]) -> tuple[Any, ...] | None:
+        """Key of a call that a prepared launch can repeat: the scalar values, the kind, dtype,
+        device and size of every buffer (and which arguments are the same host array), the
+        keyword arguments and the bounds-check switch.  None for calls the fast path does not
+        take (autotuned kernels, callable grids, other argument types)."""
+        if self._autotune_spec is not None or not self._runtime_first or len(args) != len(self._positions):
+            return None
+        parts: list[Any] = []
+        for i, v in enumerate(args):
+            t = type(v)
+            if t is int or t is float or t is bool:
+                parts.append((t, v))
+            elif t is _Tensor:
+                if v._device != "cuda":
+                    return None
+                parts.append((v._dtype, v._cuda_device(), v.nbytes))
+            elif t is _np.ndarray:
+                alias = next((j for j in range(i) if args[j] is v), i)
+                parts.append((v.dtype, v.shape, alias, v.flags.c_contiguous))
+            elif t.__name__ == "Tensor" and (tm := _torch()) is not None and t is tm.Tensor:
+                parts.append((v.dtype, v.device, v.numel(), v.is_contiguous(), v.requires_grad))
+            else:
+                return None
+        for k, v in kwargs.items():
+            if k == "_sync":
+                continue
+            if callable(v) or isinstance(v, (list, dict)):
+                return None
+            parts.append((k, v))
+        parts.append(_os.environ.get("EAS_BOUNDS_CHECK"))
+        try:
+            return tuple(parts)
+        except TypeError:
+            return None
+
     def __call__(self, /, *args: Any, **kwargs: Any) -> None:
+        key = self._fast_key(args, kwargs) if self._fast is not None else None
+        if key is not None:
+            fl = self._fast.get(key)
+            if fl is not None:
+                rt = get_runtime()
+                if fl.rt is rt and rt.fast_run(fl, args, kwargs.get("_sync", True)):
+                    return
         ck, meta, runtime_args, opts = self._prepare(args, dict(kwargs))
-        get_runtime().run(ck, runtime_args, meta, **opts)
+        rt = get_runtime()
+        rt.run(ck, runtime_args, meta, **opts)
+        if key is not None and len(self._fast) < 64:
+            prep = getattr(rt, "fast_prepare", None)
+            fl = prep(ck, runtime_args, opts, self._positions) if prep is not None else None
+            if fl is not None:
+                try:
+                    self._fast[key] = fl
+                except TypeError:   # an unhashable keyword value
+                    pass
 
     def to_cuda(self, /, *args: Any, **kwargs: Any) -> str:
         """Generated CUDA C++ source for this specialisation."""

@@ -103,6 +103,7 @@ class DeviceBuffer:
 # kernel parameter packing
 # ---------------------------------------------------------------------------
 
+_PACK_PTR = struct.Struct("<Q").pack_into
 _SCALAR_FMT = {DType.U32: ("<I", 4), DType.F32: ("<f", 4), DType.F16: ("<H", 2), DType.BOOL: ("<?", 1)}
 
 
@@ -249,6 +250,22 @@ class _Arg:
         self.deferred = False  # copy-in not made yet (a write-only host output; see _settle_deferred)
         self.zero_copy = False  # the kernel works on the page-locked bounce buffer in place
 
+
+class _FastLaunch:
+    """A launch prepared once for repeated calls whose inputs differ only in buffer contents or
+    pointers (the same kernel, meta, scalars, grid and buffer kinds, shapes and dtypes): the
+    pipeline, grid, block and the packed parameter block are fixed, so a call patches the buffer
+    pointers into the block and makes one driver call.
+
+    mode ``"device"``: every buffer is a contiguous CUDA torch tensor or a CUDA eas.Tensor;
+    ``ptr_slots`` holds (byte offset, argument position, is torch tensor).
+    mode ``"zerocopy"``: every buffer is a small host numpy array of an elementwise kernel; the
+    kernel works on the pinned bounce buffer in place (pointers fixed), ``copy_in`` /
+    ``copy_out`` hold (argument position, bounce offset, bytes).
+    """
+
+    __slots__ = ("rt", "lib", "mode", "pipe", "grid", "block", "dyn", "buf", "offsets", "count", "launch",
+                 "device", "torch_stream", "ptr_slots", "bounce", "copy_in", "copy_out", "bounds_env")
 
 class _Bounce:
     """Page-locked host buffer and its device twin, for launches with small host arrays."""
@@ -757,6 +774,163 @@ class CudaRuntime:
             if not self._pending:
                 self._close_bucket()
             self._wait_one()
+
+    # -- prepared repeated launches (Kernel.__call__ fast path) ------------------------
+    def fast_prepare(self, ck: Any, runtime_args: Mapping[str, Any], opts: Mapping[str, Any],
+                     positions: Mapping[str, int]) -> _FastLaunch | None:
+        """A :class:`_FastLaunch` for this launch, or None when it needs the general path (a
+        native plan, a bounds-checked kernel, host arrays other than small elementwise ones, a
+        grid split into several launches, ...).  Call after an identical :meth:`run` succeeded."""
+        plan = ck.plan
+        if plan.checked or getattr(plan, "native", None) is not None or not self._available:
+            return None
+        geo = launch_geometry(ck, runtime_args, nthreads=opts.get("nthreads"), grid=opts.get("grid"),
+                              tptg=opts.get("tptg"), shape=opts.get("shape"))
+        if geo is None:
+            return None
+        (gx, gy, gz), ntx = geo
+        if gy > MAX_GRID_YZ or gz > MAX_GRID_YZ:
+            return None
+        torch = _torch()
+        fl = _FastLaunch()
+        bufs = [a for a in ck.ir.args if a.kind == "buffer"]
+        if any(a.name not in positions for a in bufs):
+            return None
+        kinds = set()
+        device = None
+        slots: dict[str, tuple[int, bool]] = {}
+        for a in bufs:
+            v = runtime_args[a.name]
+            want_np = np.float32 if a.dtype == DType.F32 else np.float16
+            if type(v) is Tensor and v._device == "cuda" and v._dtype == want_np:
+                kinds.add("device")
+                dev = v._cuda_device()
+                slots[a.name] = (positions[a.name], False)
+            elif (torch is not None and type(v) is torch.Tensor and v.is_cuda and not v.requires_grad
+                  and v.is_contiguous() and v.dtype == (torch.float32 if a.dtype == DType.F32 else torch.float16)):
+                kinds.add("device")
+                kinds.add("torch")
+                dev = v.get_device()
+                slots[a.name] = (positions[a.name], True)
+            elif type(v) is np.ndarray and v.dtype == want_np and v.flags.c_contiguous:
+                kinds.add("host")
+                dev = self.default_device()
+            else:
+                return None
+            if device is not None and dev != device:
+                return None
+            device = dev
+        if device is None or ("host" in kinds and "device" in kinds):
+            return None
+        layout = plan.layout
+        if layout is None:
+            layout = plan.layout = ParamLayout(plan.params)
+            layout.block = (cuda_ext.ctypes.c_uint32 * 3)(plan.cuda_threads, 1, 1)
+        hidden = {"eas_ntx": ntx, "eas_pid_x": 0, "eas_pid_y": 0, "eas_pid_z": 0}
+        if "host" in kinds:
+            # small elementwise launches on the pinned bounce buffer, in place (as _bounce_resolve)
+            if (getattr(plan, "elementwise", None) is None
+                    or os.environ.get("EAS_ZERO_COPY", "1") in ("0", "off")):
+                return None
+            bb = self._bounce.get(device)
+            if bb is None or not bb.mapped:
+                return None
+            al = self._BOUNCE_ALIGN
+            offs: dict[int, int] = {}
+            cur = 0
+            copy_in = []
+            for a in bufs:
+                arr = runtime_args[a.name]
+                if id(arr) in offs:
+                    continue
+                offs[id(arr)] = cur
+                copy_in.append((positions[a.name], cur, arr.nbytes))
+                cur += -(-max(arr.nbytes, 1) // al) * al
+            if cur > self.ZERO_COPY_MAX_BYTES or cur > bb.nbytes:
+                return None
+            ptrs = {a.name: bb.mapped + offs[id(runtime_args[a.name])] for a in bufs}
+            seen = set()
+            copy_out = []
+            for a in bufs:
+                arr = runtime_args[a.name]
+                if a.name in ck.writes and id(arr) not in seen:
+                    seen.add(id(arr))
+                    copy_out.append((positions[a.name], offs[id(arr)], arr.nbytes))
+            fl.mode, fl.bounce, fl.copy_in, fl.copy_out, fl.ptr_slots = "zerocopy", bb, copy_in, copy_out, ()
+        else:
+            ptrs = {a.name: 0 for a in bufs}
+            fl.mode, fl.bounce, fl.copy_in, fl.copy_out = "device", None, (), ()
+            fl.ptr_slots = tuple((off, slots[p.arg][0], slots[p.arg][1]) for p, off, _f in layout.entries
+                                 if p.kind == "buffer")
+        fl.rt, fl.lib = self, self.lib()
+        fl.pipe = self._pipeline_for(ck, device)
+        fl.grid = (cuda_ext.ctypes.c_uint32 * 3)(gx, gy, gz)
+        fl.block = layout.block
+        fl.dyn = plan.dyn_smem
+        blob = layout.pack(runtime_args, ptrs, hidden)
+        fl.buf = cuda_ext.ctypes.create_string_buffer(blob, len(blob))
+        fl.offsets, fl.count = layout.offsets, layout.count
+        fl.launch = fl.lib.eas_launch_pdl if self._pdl() else fl.lib.eas_launch
+        fl.device = device
+        fl.torch_stream = "torch" in kinds
+        return fl
+
+    def fast_run(self, fl: _FastLaunch, args: tuple[Any, ...], sync: bool) -> bool:
+        """Launch ``fl`` with the buffers of ``args``; False (nothing done) when the general path
+        must take the call (the runtime's library or bounce buffer changed since it was prepared,
+        or the stream is being captured)."""
+        lib = fl.lib
+        if cuda_ext._lib is not lib:
+            return False
+        buf = fl.buf
+        if fl.mode == "device":
+            for off, pos, is_torch in fl.ptr_slots:
+                v = args[pos]
+                _PACK_PTR(buf, off, v.data_ptr() if is_torch else v._cuda_ptr())
+            stream = 0
+            if fl.torch_stream:
+                stream = int(_torch()._C._cuda_getCurrentRawStream(fl.device))
+                if stream:
+                    cap = cuda_ext.ctypes.c_int(0)
+                    lib.eas_stream_is_capturing(stream, cuda_ext.ctypes.byref(cap))
+                    if cap.value:
+                        return False
+            rc = fl.launch(fl.pipe, fl.grid, fl.block, fl.dyn, stream, buf, fl.offsets, fl.count)
+            if rc:
+                cuda_ext.check(rc, "launch")
+            self.launch_count += 1
+            if sync:
+                cuda_ext.check(lib.eas_stream_synchronize(stream), "kernel execution")
+                return True
+            if self._bucket_n and stream != self._bucket_stream:
+                self._close_bucket()
+            self._bucket_keep.append(args)
+            self._bucket_n += 1
+            self._bucket_stream = stream
+            limit = self._max_flight()
+            if self._bucket_n >= (max(1, limit // 16) if limit else 64):
+                self._close_bucket()
+            while limit and self.in_flight() > limit:
+                if not self._pending:
+                    self._close_bucket()
+                self._wait_one()
+            return True
+        bb = fl.bounce
+        if self._bounce.get(fl.device) is not bb:
+            return False
+        view = bb.view
+        for pos, off, n in fl.copy_in:
+            if n:
+                view[off:off + n] = args[pos].reshape(-1).view(np.uint8)
+        rc = fl.launch(fl.pipe, fl.grid, fl.block, fl.dyn, 0, buf, fl.offsets, fl.count)
+        if rc:
+            cuda_ext.check(rc, "launch")
+        self.launch_count += 1
+        cuda_ext.check(lib.eas_stream_synchronize(0), "kernel execution")
+        for pos, off, n in fl.copy_out:
+            if n:
+                args[pos].reshape(-1).view(np.uint8)[:] = view[off:off + n]
+        return True
 
     def _close_bucket(self) -> None:
         if not self._bucket_n:

@@ -680,3 +680,85 @@ def test_program_id_shards_on_slice_buffers(fake, monkeypatch):
         buf, at = lib._find(sl["c"]._cuda_ptr())
         out[e0:e1] = np.frombuffer(buf, np.float32, e1 - e0, at)
     np.testing.assert_array_equal(out, a + b)
+
+
+# -- prepared repeated launches (Kernel.__call__ fast path) -------------------------------------
+
+
+@pytest.fixture
+def fast(fake, monkeypatch):
+    """The fake runtime as the process runtime, so kernel calls reach it."""
+    import easy_as_b200.runtime as runtime_mod
+
+    lib, rt = fake
+    rt._available = True
+    monkeypatch.setattr(runtime_mod, "_cuda", rt)
+    lib.eas_event_create = lambda p: (setattr(p._obj, "value", 4096), 0)[1]
+    lib.eas_event_record = lambda ev, s: 0
+    lib.eas_event_synchronize = lambda ev: 0
+    lib.eas_stream_is_capturing = lambda s, p: 0
+    lib.eas_set_device = lambda d: 0
+    return lib, rt
+
+
+@eas.kernel
+def axpy_kernel(x, y, out, N, alpha, BLOCK: eas.constexpr):
+    offs = mk.program_id(0) * BLOCK + mk.arange(0, BLOCK)
+    m = offs < N
+    mk.store(out, offs, mk.load(x, offs, m) * alpha + mk.load(y, offs, m), m)
+
+
+def test_repeated_device_calls_take_the_prepared_launch(fast):
+    """Device buffers: the second and later identical calls make one launch each without
+    re-resolving their arguments, with the buffer pointers of each call patched in."""
+    lib, rt = fast
+    n = 1000
+    k = eas.kernel(axpy_kernel.fn)
+    xs = [eas.tensor(np.random.default_rng(i).standard_normal(n).astype(np.float32), device="cuda") for i in range(3)]
+    y = eas.tensor(np.ones(n, np.float32), device="cuda")
+    out = eas.empty_like(y)
+    lib.current = k.compile(xs[0], y, out, n, 2.0, BLOCK=256)
+    calls = []
+    orig_resolve = rt._resolve
+    rt._resolve = lambda *a, **kw: (calls.append(1), orig_resolve(*a, **kw))[1]
+
+    def want(x, alpha):
+        w = np.zeros(n, np.float32)
+        execute(lib.current.ir, {"x": x.numpy(), "y": y.numpy(), "out": w, "N": n, "alpha": alpha})
+        return w
+
+    for x in xs:
+        k(x, y, out, n, 2.0, BLOCK=256, _sync=False)
+        rt.synchronize()
+        np.testing.assert_array_equal(out.numpy(), want(x, 2.0))
+    assert len(calls) == 1 and len(k._fast) == 1
+    # a different scalar is a different prepared launch; its result uses the new value
+    k(xs[0], y, out, n, 3.0, BLOCK=256)
+    np.testing.assert_array_equal(out.numpy(), want(xs[0], 3.0))
+    assert len(k._fast) == 2
+
+
+def test_repeated_small_host_calls_use_the_bounce_buffer_in_place(fast):
+    """Small numpy arrays of an elementwise kernel: each call copies its inputs into the pinned
+    buffer, launches on it in place and copies the written array back; arrays passed twice
+    (aliases) get their own prepared launch."""
+    lib, rt = fast
+    n = 1031
+    k = eas.kernel(add_kernel.fn)
+    rng = np.random.default_rng(0)
+    a, b = rng.standard_normal(n, dtype=np.float32), rng.standard_normal(n, dtype=np.float32)
+    c = np.zeros(n, np.float32)
+    lib.current = k.compile(a, b, c, n, BLOCK=256)
+    for i in range(3):
+        a = rng.standard_normal(n, dtype=np.float32)
+        k(a, b, c, n, BLOCK=256)
+        np.testing.assert_array_equal(c, a + b)
+    assert len(k._fast) == 1
+    k(a, a, a, n, BLOCK=256)          # in place: a = a + a
+    assert len(k._fast) == 2
+
+
+def test_fast_launch_can_be_switched_off(fast, monkeypatch):
+    monkeypatch.setenv("EAS_FAST_LAUNCH", "0")
+    k = eas.kernel(add_kernel.fn)
+    assert k._fast is None
