@@ -260,13 +260,13 @@ def run_gemm(name: str, args, world: int, rank: int, rt) -> dict:
                   _buffer_base=base, _sync=sync)
 
     native0 = rt.native_launches
-    keys0 = set(kern._tuned_times)
+    keys0 = set(kern._tuned_cache)
     step(sync=True)                      # first call tunes (8 configs timed on this rank's range)
     if rt.native_launches == native0:
         raise SystemExit(f"bench: {name} did not take the tcgen05 path")
-    new = [k for k in kern._tuned_times if k not in keys0]
-    times = kern._tuned_times[new[0]] if new else []
-    best = min(times, key=lambda t: t[1])[0] if times else {}
+    new = [k for k in kern._tuned_cache if k not in keys0]
+    best = dict(kern._tuned_cache[new[0]].meta) if new else {}
+    times = kern._tuned_times.get(new[0], []) if new else []
     ref = a[0, :4].double() @ b[0].double()
     err = ((c[0, :4].double() - ref).abs().max() / ref.abs().max()).item()
     if err > 1e-4:
@@ -311,7 +311,7 @@ def run_gemm(name: str, args, world: int, rank: int, rt) -> dict:
             lib_tf = None
     flops_total = 2.0 * batch * M * N * K
     local_tf = 2.0 * lb * lm * N * K / (ms * 1e-3) / 1e12
-    e2e = None if args.quick else gemm_e2e(name, a, b, c, step, world, flops_total)
+    e2e = None if args.quick else gemm_e2e(name, a, b, c, step, world, flops_total, best)
     pk = peaks()
     out = {
         "value": round(flops_total / (ms_max * 1e-3) / 1e12, 1), "unit": "TFLOP/s", "ms_per_step": round(ms_max, 4),
@@ -331,13 +331,14 @@ def run_gemm(name: str, args, world: int, rank: int, rt) -> dict:
     return out
 
 
-def gemm_e2e(name, a, b, c, step, world, flops_total) -> dict:
+def gemm_e2e(name, a, b, c, step, world, flops_total, best: dict) -> dict:
     """The GEMM end to end with pinned host tensors, synchronised per step, wall clock, max over ranks.
-    One GPU: the public call with host tensors (the runtime pipelines the copies with the kernel).
+    One GPU: the public call with host tensors and the tuned tile configuration (the runtime
+    pipelines the copies with the kernel).
     N GPUs: every rank copies its slices in, runs its range (``run_shard``) and copies its C out."""
     import torch
 
-    from examples.matmul_dot_f16 import grid, matmul_dot_f16_tuned
+    from examples.matmul_dot_f16 import grid, matmul_dot_f16
 
     batch, M, N, K, _ = GEMM_CONFIGS[name]
     ha, hb = a.cpu().pin_memory(), b.cpu().pin_memory()
@@ -347,7 +348,7 @@ def gemm_e2e(name, a, b, c, step, world, flops_total) -> dict:
     rt = get_runtime()
     if world == 1:
         def e2e_step():
-            matmul_dot_f16_tuned(ha.reshape(-1), hb.reshape(-1), hc.reshape(-1), M, N, K, _grid=grid(batch))
+            matmul_dot_f16(ha.reshape(-1), hb.reshape(-1), hc.reshape(-1), M, N, K, **best, _grid=grid(batch))
     else:
         def e2e_step():
             a.copy_(ha, non_blocking=True)

@@ -777,10 +777,13 @@ class CudaRuntime:
 
     # -- prepared repeated launches (Kernel.__call__ fast path) ------------------------
     def fast_prepare(self, ck: Any, runtime_args: Mapping[str, Any], opts: Mapping[str, Any],
-                     positions: Mapping[str, int]) -> _FastLaunch | None:
+                     positions: Mapping[str, int], axis: int = 0, lo: int | None = None, hi: int | None = None,
+                     buffer_base: Mapping[str, int] | None = None) -> _FastLaunch | None:
         """A :class:`_FastLaunch` for this launch, or None when it needs the general path (a
         native plan, a bounds-checked kernel, host arrays other than small elementwise ones, a
-        grid split into several launches, ...).  Call after an identical :meth:`run` succeeded."""
+        grid split into several launches, ...).  Call after an identical :meth:`run` succeeded.
+        With ``lo``/``hi`` it is the :meth:`run_range` launch of programs ``[lo, hi)`` on ``axis``
+        (device buffers only; ``buffer_base`` as there)."""
         plan = ck.plan
         if plan.checked or getattr(plan, "native", None) is not None or not self._available:
             return None
@@ -789,6 +792,15 @@ class CudaRuntime:
         if geo is None:
             return None
         (gx, gy, gz), ntx = geo
+        pid = [0, 0, 0]
+        if lo is not None:
+            dims = [gx, gy, gz]
+            lo, hi = max(0, int(lo)), min(int(hi), dims[axis])
+            if hi <= lo:
+                return None
+            dims[axis] = hi - lo
+            pid[axis] = lo
+            gx, gy, gz = dims
         if gy > MAX_GRID_YZ or gz > MAX_GRID_YZ:
             return None
         torch = _torch()
@@ -820,13 +832,13 @@ class CudaRuntime:
             if device is not None and dev != device:
                 return None
             device = dev
-        if device is None or ("host" in kinds and "device" in kinds):
+        if device is None or ("host" in kinds and "device" in kinds) or ("host" in kinds and lo is not None):
             return None
         layout = plan.layout
         if layout is None:
             layout = plan.layout = ParamLayout(plan.params)
             layout.block = (cuda_ext.ctypes.c_uint32 * 3)(plan.cuda_threads, 1, 1)
-        hidden = {"eas_ntx": ntx, "eas_pid_x": 0, "eas_pid_y": 0, "eas_pid_z": 0}
+        hidden = {"eas_ntx": ntx, "eas_pid_x": pid[0], "eas_pid_y": pid[1], "eas_pid_z": pid[2]}
         if "host" in kinds:
             # small elementwise launches on the pinned bounce buffer, in place (as _bounce_resolve)
             if (getattr(plan, "elementwise", None) is None
@@ -860,8 +872,10 @@ class CudaRuntime:
         else:
             ptrs = {a.name: 0 for a in bufs}
             fl.mode, fl.bounce, fl.copy_in, fl.copy_out = "device", None, (), ()
-            fl.ptr_slots = tuple((off, slots[p.arg][0], slots[p.arg][1]) for p, off, _f in layout.entries
-                                 if p.kind == "buffer")
+            base = buffer_base or {}
+            item = {a.name: (4 if a.dtype == DType.F32 else 2) for a in bufs}
+            fl.ptr_slots = tuple((off, slots[p.arg][0], slots[p.arg][1], int(base.get(p.arg, 0)) * item[p.arg])
+                                 for p, off, _f in layout.entries if p.kind == "buffer")
         fl.rt, fl.lib = self, self.lib()
         fl.pipe = self._pipeline_for(ck, device)
         fl.grid = (cuda_ext.ctypes.c_uint32 * 3)(gx, gy, gz)
@@ -884,9 +898,9 @@ class CudaRuntime:
             return False
         buf = fl.buf
         if fl.mode == "device":
-            for off, pos, is_torch in fl.ptr_slots:
+            for off, pos, is_torch, back in fl.ptr_slots:
                 v = args[pos]
-                _PACK_PTR(buf, off, v.data_ptr() if is_torch else v._cuda_ptr())
+                _PACK_PTR(buf, off, (v.data_ptr() if is_torch else v._cuda_ptr()) - back)
             stream = 0
             if fl.torch_stream:
                 stream = int(_torch()._C._cuda_getCurrentRawStream(fl.device))

@@ -47,6 +47,17 @@ def run_shard(kernel: Any, *args: Any, _rank: int, _world: int, _axis: int = 0,
     from .runtime.cuda import launch_geometry
 
     rt = get_runtime()
+    fast = getattr(kernel, "_fast", None)
+    key = None
+    if fast is not None:
+        key = kernel._fast_key(args, kwargs)
+        if key is not None:
+            key = ("shard", _rank, _world, _axis, tuple(sorted((_buffer_base or {}).items()))) + key
+            hit = fast.get(key)
+            if hit is not None:
+                fl, r = hit
+                if fl.rt is rt and rt.fast_run(fl, args, _sync):
+                    return r
     raw = kernel._extract_runtime_options(kwargs)
     meta, runtime_args = kernel._bind_and_split(*args, **kwargs)
 
@@ -77,6 +88,12 @@ def run_shard(kernel: Any, *args: Any, _rank: int, _world: int, _axis: int = 0,
     lo, hi = r
     rt.run_range(ck, runtime_args, meta, axis=_axis, lo=lo, hi=hi, grid=opts["grid"], nthreads=opts["nthreads"],
                  shape=opts["shape"], buffer_base=_buffer_base, sync=_sync)
+    if key is not None and len(fast) < 64:
+        prep = getattr(rt, "fast_prepare", None)
+        fl = prep(ck, runtime_args, opts, kernel._positions, axis=_axis, lo=lo, hi=hi,
+                  buffer_base=_buffer_base) if prep is not None else None
+        if fl is not None:
+            fast[key] = (fl, r)
     return lo, hi
 
 

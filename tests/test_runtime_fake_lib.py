@@ -762,3 +762,29 @@ def test_fast_launch_can_be_switched_off(fast, monkeypatch):
     monkeypatch.setenv("EAS_FAST_LAUNCH", "0")
     k = eas.kernel(add_kernel.fn)
     assert k._fast is None
+
+
+def test_repeated_shard_calls_take_the_prepared_range_launch(fast):
+    """run_shard's later identical calls reuse the prepared range launch: the same program range,
+    the hidden program-id base and slice pointers moved back by the buffer base."""
+    from easy_as_b200.shard import element_range, run_shard
+
+    lib, rt = fast
+    n, world, rank = 1 << 15, 4, 2
+    k = eas.kernel(add_kernel.fn)
+    lo, hi = element_range(n, 256, rank, world)
+    base = {"a": lo, "b": lo, "c": lo}
+    c = eas.tensor(np.zeros(hi - lo, np.float32), device="cuda")
+    b = eas.tensor(np.ones(hi - lo, np.float32), device="cuda")
+    calls = []
+    orig_resolve = rt._resolve
+    rt._resolve = lambda *a, **kw: (calls.append(1), orig_resolve(*a, **kw))[1]
+    for i in range(3):
+        a = eas.tensor(np.random.default_rng(i).standard_normal(hi - lo).astype(np.float32), device="cuda")
+        lib.current = k.compile(a, b, c, n, BLOCK=256)
+        assert run_shard(k, a, b, c, n, BLOCK=256, _rank=rank, _world=world, _buffer_base=base) == (lo // 256,
+                                                                                                   hi // 256)
+        np.testing.assert_array_equal(c.numpy(), a.numpy() + 1.0)
+    assert len(calls) == 1
+    (fl, _r), = [v for kk, v in k._fast.items() if kk[0] == "shard"]
+    assert [o[3] for o in fl.ptr_slots] == [4 * lo] * 3
