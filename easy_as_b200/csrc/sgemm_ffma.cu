@@ -39,6 +39,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <cstdlib>
 #include <type_traits>
 
 #include "eas_internal.h"
@@ -63,6 +64,29 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
 
+// Packed fp32 pairs (sm_100 fma.rn.f32x2 / add.rn.f32x2): each lane is exactly one fma.rn.f32
+// (add.rn.f32), so a pair computes the same two results as two scalar instructions, in one issue
+// slot.  d = {a, a} * b + d.
+__device__ __forceinline__ void fma2_bcast(float2& d, float a, float2 b) {
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %2};\n\t"
+      "mov.b64 rb, {%3, %4};\n\t"
+      "mov.b64 rd, {%0, %1};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rd;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "+f"(d.x), "+f"(d.y)
+      : "f"(a), "f"(b.x), "f"(b.y));
+}
+__device__ __forceinline__ void add2(float2& d, float2 p) {
+  asm("{\n\t.reg .b64 rp, rd;\n\t"
+      "mov.b64 rp, {%2, %3};\n\t"
+      "mov.b64 rd, {%0, %1};\n\t"
+      "add.rn.f32x2 rd, rd, rp;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "+f"(d.x), "+f"(d.y)
+      : "f"(p.x), "f"(p.y));
+}
+
 template <int BM, int BN, int BKS, int STAGES, int TM, int TN>
 struct SgemmCfg {
   static constexpr int kTX = BN / TN, kTY = BM / TM, kThreads = kTX * kTY, kCG = TN / 4;
@@ -75,7 +99,7 @@ struct SgemmCfg {
   static_assert(BKS % 4 == 0, "BKS must be a multiple of 4");
 };
 
-template <int BM, int BN, int BKS, int STAGES, int TM, int TN, int MINB, bool VEC>
+template <int BM, int BN, int BKS, int STAGES, int TM, int TN, int MINB, bool VEC, bool F2 = false>
 __global__ void __launch_bounds__(SgemmCfg<BM, BN, BKS, STAGES, TM, TN>::kThreads, MINB)
 sgemm_ffma_kernel(const float* __restrict__ A, const float* __restrict__ B, float* __restrict__ C, uint32_t M,
                   uint32_t N, uint32_t K, uint32_t stages_per_tile, uint64_t lda, uint64_t ldb, uint64_t ldc,
@@ -142,6 +166,7 @@ sgemm_ffma_kernel(const float* __restrict__ A, const float* __restrict__ B, floa
     cp_async_commit();
   };
 
+  static_assert(!F2 || TN % 2 == 0, "packed pairs need an even TN");
   float acc[TM][TN], p[TM][TN];
   const float init = zero_init ? 0.0f : -0.0f;
 #pragma unroll
@@ -175,11 +200,23 @@ sgemm_ffma_kernel(const float* __restrict__ A, const float* __restrict__ B, floa
         float av[TM];
 #pragma unroll
         for (int i = 0; i < TM; ++i) av[i] = kk == 0 ? af[i].x : kk == 1 ? af[i].y : kk == 2 ? af[i].z : af[i].w;
+        if constexpr (F2) {
 #pragma unroll
-        for (int i = 0; i < TM; ++i)
+          for (int i = 0; i < TM; ++i)
 #pragma unroll
-          for (int j = 0; j < TN; ++j)
-            p[i][j] = (kFirst && kb == 0 && kk == 0) ? fmaf(av[i], bv[j], 0.0f) : fmaf(av[i], bv[j], p[i][j]);
+            for (int j = 0; j < TN; j += 2) {
+              float2 d = (kFirst && kb == 0 && kk == 0) ? make_float2(0.0f, 0.0f) : make_float2(p[i][j], p[i][j + 1]);
+              fma2_bcast(d, av[i], make_float2(bv[j], bv[j + 1]));
+              p[i][j] = d.x;
+              p[i][j + 1] = d.y;
+            }
+        } else {
+#pragma unroll
+          for (int i = 0; i < TM; ++i)
+#pragma unroll
+            for (int j = 0; j < TN; ++j)
+              p[i][j] = (kFirst && kb == 0 && kk == 0) ? fmaf(av[i], bv[j], 0.0f) : fmaf(av[i], bv[j], p[i][j]);
+        }
       }
     }
   };
@@ -196,10 +233,22 @@ sgemm_ffma_kernel(const float* __restrict__ A, const float* __restrict__ B, floa
       compute(buf, std::false_type{});
     if (++in_tile == stages_per_tile) {  // end of a K tile: fold its partial sums, in order
       in_tile = 0;
+      if constexpr (F2) {
 #pragma unroll
-      for (int i = 0; i < TM; ++i)
+        for (int i = 0; i < TM; ++i)
 #pragma unroll
-        for (int j = 0; j < TN; ++j) acc[i][j] = __fadd_rn(acc[i][j], p[i][j]);
+          for (int j = 0; j < TN; j += 2) {
+            float2 d = make_float2(acc[i][j], acc[i][j + 1]);
+            add2(d, make_float2(p[i][j], p[i][j + 1]));
+            acc[i][j] = d.x;
+            acc[i][j + 1] = d.y;
+          }
+      } else {
+#pragma unroll
+        for (int i = 0; i < TM; ++i)
+#pragma unroll
+          for (int j = 0; j < TN; ++j) acc[i][j] = __fadd_rn(acc[i][j], p[i][j]);
+      }
     }
   }
   cp_async_wait<0>();
@@ -223,7 +272,7 @@ sgemm_ffma_kernel(const float* __restrict__ A, const float* __restrict__ B, floa
   }
 }
 
-template <int BM, int BN, int BKS, int STAGES, int TM, int TN, int MINB, bool VEC>
+template <int BM, int BN, int BKS, int STAGES, int TM, int TN, int MINB, bool VEC, bool F2 = false>
 int launch_sgemm(const float* a, const float* b, float* c, uint32_t M, uint32_t N, uint32_t K, uint32_t k_tile,
                  uint32_t batch, uint64_t lda, uint64_t a_bs, uint64_t ldb, uint64_t b_bs, uint64_t ldc,
                  uint64_t c_bs, int zero_init, SgemmValid valid, cudaStream_t s) {
@@ -231,7 +280,7 @@ int launch_sgemm(const float* a, const float* b, float* c, uint32_t M, uint32_t 
   const uint32_t gy = (M + BM - 1) / BM;
   if (gy > 65535) return eas_fail(EAS_ERR_VALUE, "eas_sgemm_f32_tiled: M too large");
   const size_t smem = Cfg::kSmemFloats * sizeof(float);
-  auto kern = sgemm_ffma_kernel<BM, BN, BKS, STAGES, TM, TN, MINB, VEC>;
+  auto kern = sgemm_ffma_kernel<BM, BN, BKS, STAGES, TM, TN, MINB, VEC, F2>;
   static int attr_done[64];
   int dev = 0;
   cudaGetDevice(&dev);
@@ -277,10 +326,18 @@ extern "C" int eas_sgemm_f32_tiled(const float* a, const float* b, float* c, uin
   const uint64_t big_tiles = (uint64_t)((M + 127) / 128) * ((N + 127) / 128) * batch;
   const bool small = big_tiles < 4ull * (uint64_t)sms;
 #define EAS_SG(BM, BN, BKS, ST, TM, TN, MINB)                                                                    \
-  (vec ? launch_sgemm<BM, BN, BKS, ST, TM, TN, MINB, true>(a, b, c, M, N, K, k_tile, batch, lda, a_bstride, ldb,    \
-                                                           b_bstride, ldc, c_bstride, zero_init, valid, s)        \
+  (vec ? (f2 ? launch_sgemm<BM, BN, BKS, ST, TM, TN, MINB, true, true>(a, b, c, M, N, K, k_tile, batch, lda,       \
+                                                                       a_bstride, ldb, b_bstride, ldc, c_bstride,  \
+                                                                       zero_init, valid, s)                        \
+              : launch_sgemm<BM, BN, BKS, ST, TM, TN, MINB, true>(a, b, c, M, N, K, k_tile, batch, lda, a_bstride, \
+                                                                  ldb, b_bstride, ldc, c_bstride, zero_init, valid, s)) \
        : launch_sgemm<BM, BN, BKS, ST, TM, TN, MINB, false>(a, b, c, M, N, K, k_tile, batch, lda, a_bstride, ldb,   \
                                                             b_bstride, ldc, c_bstride, zero_init, valid, s))
+  // EAS_SGEMM_F2=1: packed fma.rn.f32x2 pairs (the same fp32 operations, half the issue slots)
+  static const bool f2 = [] {
+    const char* e = getenv("EAS_SGEMM_F2");
+    return e && e[0] == '1';
+  }();
   if (small) {
     if (k_tile % 32 == 0) return EAS_SG(64, 64, 32, 2, 8, 4, 4);
     if (k_tile % 16 == 0) return EAS_SG(64, 64, 16, 2, 8, 4, 4);
