@@ -992,13 +992,17 @@ int launch_2sm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& 
 // keep one accumulator (no epilogue overlap) and halve the tile count.  Taken when they need no
 // more tile-rounds of work over the CTA pairs: 2 * ceil(wide tiles / pairs) <= ceil(tiles / pairs)
 // (C4 8192^3: 512 wide tiles = 7 rounds vs 1024 = 14; M = N = 768: 6 wide tiles pay a half-empty
-// column of tiles and lose).  EAS_GEMM_WIDE=0 / 1 forces the choice.
-bool use_wide(uint32_t M, uint32_t N, uint32_t batch, int num_sms) {
+// column of tiles and lose).  The exposed part of a wide tile's epilogue is a fixed cost per
+// tile, so short K loops lose with them: below 64 k-blocks (K < 4096) the 256 x 256 tiles with two
+// accumulators win (C5, K = 2088: 3.60 ms against 4.42 ms wide, measured by the autotuner on one
+// B200; C4, K = 8192: 0.736 ms wide against 0.786 ms).  EAS_GEMM_WIDE=0 / 1 forces the choice.
+bool use_wide(uint32_t M, uint32_t N, uint32_t K, uint32_t batch, int num_sms) {
   static const int forced = [] {
     const char* e = getenv("EAS_GEMM_WIDE");
     return e && (e[0] == '0' || e[0] == '1') ? e[0] - '0' : -1;
   }();
   if (forced >= 0) return forced == 1;
+  if (K < 64u * BK) return false;
   const long long pairs = num_sms / 2 > 0 ? num_sms / 2 : 1;
   const long long mt = (M + 255) / 256;
   const long long t1 = mt * ((N + 255) / 256) * batch, t2 = mt * ((N + 511) / 512) * batch;
@@ -1030,13 +1034,13 @@ struct F16Choice {
   int stages;
 };
 
-F16Choice choose_f16(uint32_t M, uint32_t N, uint32_t batch, int block_n, int tile_m, int block_k, bool tma_c,
-                     int num_sms) {
+F16Choice choose_f16(uint32_t M, uint32_t N, uint32_t K, uint32_t batch, int block_n, int tile_m, int block_k,
+                     bool tma_c, int num_sms) {
   F16Choice ch{};
   ch.ks = block_k == 128 ? 2 : 1;
   ch.pair = tile_m == 0 ? use_2sm(block_n, M) : tile_m == 256;
   if (ch.pair) {
-    const bool wide = tma_c && (tile_m == 0 ? (N >= 512 && use_wide(M, N, batch, num_sms)) : block_n == 256);
+    const bool wide = tma_c && (tile_m == 0 ? (N >= 512 && use_wide(M, N, K, batch, num_sms)) : block_n == 256);
     ch.nh = wide ? 2 : 1;
     ch.tile_n = 256 * ch.nh;
     ch.stages = wide ? 4 / ch.ks : (tma_c ? 6 / ch.ks : (ch.ks == 1 ? 7 : 3));
@@ -1169,7 +1173,7 @@ int gemm_entry(const char* who, const void* a, const void* b, float* c, uint32_t
   // C through TMA stores when its rows/batches are 16-byte strided and the base is aligned
   const bool tma_c = (reinterpret_cast<uintptr_t>(c) & 15) == 0 && (ldc * 4) % 16 == 0 &&
                      (batch == 1 || (c_bstride * 4) % 16 == 0) && ldc >= N;
-  const F16Choice ch = choose_f16(M, N, batch, block_n, TF ? 0 : tile_m, TF ? 0 : block_k, tma_c, num_sms);
+  const F16Choice ch = choose_f16(M, N, K, batch, block_n, TF ? 0 : tile_m, TF ? 0 : block_k, tma_c, num_sms);
   const bool pair = ch.pair;
   if (b_mn)
     rc = encode_map(&mb, b, N, K, batch, ldb * kElem, bb ? bb : 16, 64, kBoxK, dt);
@@ -1219,7 +1223,7 @@ extern "C" int eas_gemm_f16_plan(uint32_t M, uint32_t N, uint32_t K, uint32_t ba
   if (M == 0 || N == 0 || K == 0 || batch == 0 || num_sms <= 0)
     return eas_fail(EAS_ERR_VALUE, "eas_gemm_f16_plan: empty launch");
   const int kblocks = (int)((K + BK - 1) / BK);
-  const F16Choice ch = choose_f16(M, N, batch, block_n, tile_m, block_k, c_tma_ok != 0, num_sms);
+  const F16Choice ch = choose_f16(M, N, K, batch, block_n, tile_m, block_k, c_tma_ok != 0, num_sms);
   *pair = ch.pair ? 1 : 0;
   *out_tile_m = ch.pair ? 256 : BM;
   *out_tile_n = ch.tile_n;
