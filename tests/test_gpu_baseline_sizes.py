@@ -65,6 +65,32 @@ def test_c3_tiled_fp32_full_size(cuda_rt):
 
 
 @pytest.mark.parametrize("batch,M,N,K", [(1, 8192, 8192, 8192), (64, 4096, 4096, 2088)])
+def test_fp16_gemm_full_size_every_output_vs_float64(cuda_rt, batch, M, N, K):
+    """Configs C4 and C5 at full size: EVERY output of the library's launch against a float64
+    product computed on the GPU (cuBLAS DGEMM, batch by batch), at the north-star bound
+    (rtol 2e-2) and at the normwise f32-accumulation bound the sampled check uses."""
+    import torch
+
+    g = torch.Generator(device="cuda").manual_seed(5)
+    a = (torch.randn(batch, M, K, device="cuda", generator=g) / K ** 0.5).half()
+    b = (torch.randn(batch, K, N, device="cuda", generator=g) / K ** 0.5).half()
+    c = torch.empty(batch, M, N, device="cuda")
+    before = cuda_rt.native_launches
+    matmul_dot_f16(a.reshape(-1), b.reshape(-1), c.reshape(-1), M, N, K, _grid=grid(batch))
+    assert cuda_rt.native_launches == before + 1
+    worst = 0.0
+    for bi in range(batch):
+        ref = a[bi].double() @ b[bi].double()
+        got = c[bi].double()
+        scale = ref.abs().max().item()
+        err = (got - ref).abs()
+        assert bool((err <= 2e-2 * ref.abs() + 2e-2 * scale).all()), f"batch {bi}"
+        worst = max(worst, err.max().item() / scale)
+        del ref, got, err
+    assert worst <= 1e-5 * max(1.0, (K / 2048) ** 0.5), worst
+
+
+@pytest.mark.parametrize("batch,M,N,K", [(1, 8192, 8192, 8192), (64, 4096, 4096, 2088)])
 def test_fp16_gemm_full_size_sampled(cuda_rt, batch, M, N, K):
     import torch
 
