@@ -284,6 +284,8 @@ class Kernel:
                 return None
             parts.append((k, v))
         parts.append(_os.environ.get("EAS_BOUNDS_CHECK"))
+        if any(type(v) is _np.ndarray for v in args):
+            parts.append(_os.environ.get("EAS_ZERO_COPY"))   # host arrays: in place on pinned memory or not
         try:
             return tuple(parts)
         except TypeError:
