@@ -196,30 +196,6 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// Split form of tmem_ld32: the load is issued now and its registers are valid only after
-// tmem_wait32 on the same array (whose "+r" operands keep every use of r after the wait).
-__device__ __forceinline__ void tmem_ld32_issue(uint32_t taddr, uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
-        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
-        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-}
-__device__ __forceinline__ void tmem_wait32(uint32_t (&r)[32]) {
-  asm volatile("tcgen05.wait::ld.sync.aligned;"
-               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
-                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
-                 "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
-                 "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
-                 "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
-               :
-               : "memory");
-}
-
 struct TileCoord {
   int b, m0, n0;
 };
@@ -555,7 +531,7 @@ struct Smem2 {
   static constexpr int kTotal = kBarOffset + (2 * kStages2 + 4) * 8 + 16 + 1024;
 };
 
-template <int kStages2, bool B_MN, bool TMA_C, bool TF = false, int NH = 1, int KS = 1, bool EPF = false>
+template <int kStages2, bool B_MN, bool TMA_C, bool TF = false, int NH = 1, int KS = 1>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_f16_tcgen05_2sm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                                 const __grid_constant__ CUtensorMap map_c, float* __restrict__ c, int M, int N, int K,
@@ -846,30 +822,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           }
         }
       };
-      if constexpr (EPF) {
-        // the next chunk's TMEM load is in flight while this chunk is staged and stored
-        constexpr int kCh = BN / 32;  // even
-        uint32_t ra[32], rb[32];
-        tmem_ld32_issue(tbase, ra);
-        tmem_wait32(ra);
 #pragma unroll 1
-        for (int cc = 0; cc < kCh; cc += 2) {
-          tmem_ld32_issue(tbase + (cc + 1) * 32, rb);
-          put(ra, cc);
-          tmem_wait32(rb);
-          if (NH == 2 && cc + 1 == 256 / 32 - 1) release_half0();
-          if (cc + 2 < kCh) tmem_ld32_issue(tbase + (cc + 2) * 32, ra);
-          put(rb, cc + 1);
-          if (cc + 2 < kCh) tmem_wait32(ra);
-        }
-      } else {
-#pragma unroll 1
-        for (int cc = 0; cc < BN / 32; ++cc) {
-          uint32_t r[32];
-          tmem_ld32(tbase + cc * 32, r);
-          if (NH == 2 && cc == 256 / 32 - 1) release_half0();
-          put(r, cc);
-        }
+      for (int cc = 0; cc < BN / 32; ++cc) {
+        uint32_t r[32];
+        tmem_ld32(tbase + cc * 32, r);
+        if (NH == 2 && cc == 256 / 32 - 1) release_half0();
+        put(r, cc);
       }
       tc_fence_before();
       __syncwarp();
@@ -995,13 +953,13 @@ int launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorM
   return eas_cuda_check(cudaGetLastError(), "gemm: launch", EAS_ERR_LAUNCH);
 }
 
-template <int STAGES, bool B_MN, bool TMA_C, bool TF = false, int NH = 1, int KS = 1, bool EPF = false>
+template <int STAGES, bool B_MN, bool TMA_C, bool TF = false, int NH = 1, int KS = 1>
 int launch_2sm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, float* c, int M, int N, int K,
                int batch, long long ldc, long long cbs, int* status, cudaStream_t stream, int num_sms, int seg_kb = 0) {
   using L = Smem2<STAGES, TMA_C, NH, KS>;
   static_assert(L::kTotal <= 232448, "shared memory over the 227 KB per-CTA limit");
-  auto kern = gemm_f16_tcgen05_2sm_kernel<STAGES, B_MN, TMA_C, TF, NH, KS, EPF>;
-  int rc = set_smem_once<gemm_f16_tcgen05_2sm_kernel<STAGES, B_MN, TMA_C, TF, NH, KS, EPF>>(
+  auto kern = gemm_f16_tcgen05_2sm_kernel<STAGES, B_MN, TMA_C, TF, NH, KS>;
+  int rc = set_smem_once<gemm_f16_tcgen05_2sm_kernel<STAGES, B_MN, TMA_C, TF, NH, KS>>(
       L::kTotal, "gemm(2sm): set smem attribute");
   if (rc) return rc;
   const long long tiles = (long long)((M + 255) / 256) * ((N + 256 * NH - 1) / (256 * NH)) * batch;
@@ -1107,17 +1065,6 @@ int launch_f16_choice(const F16Choice& ch, bool b_mn, bool tma_c, const CUtensor
   constexpr int kS1w = 4 / KS, kS1 = 6 / KS, kS1d = KS == 1 ? 7 : 3;  // pair: wide, 256-wide, direct-store C
   constexpr int kSs256 = 4 / KS, kSs128 = 6 / KS;                    // 1-SM: BN = 256, 128
 #define EAS_ARGS ma, mb, mc, c, M, N, K, batch, ldc, cbs, status, s, num_sms
-  static const bool epf = [] {
-    const char* e = getenv("EAS_GEMM_EPF");
-    return e && e[0] == '1';
-  }();
-  if (ch.pair && epf && tma_c && KS == 1) {
-    if (ch.nh == 2)
-      return b_mn ? launch_2sm<kS1w, true, true, false, 2, KS, true>(EAS_ARGS)
-                  : launch_2sm<kS1w, false, true, false, 2, KS, true>(EAS_ARGS);
-    return b_mn ? launch_2sm<kS1, true, true, false, 1, KS, true>(EAS_ARGS)
-                : launch_2sm<kS1, false, true, false, 1, KS, true>(EAS_ARGS);
-  }
   if (ch.pair) {
     if (ch.nh == 2)  // TMA-storable C only
       return b_mn ? launch_2sm<kS1w, true, true, false, 2, KS>(EAS_ARGS)
