@@ -342,6 +342,18 @@ extern "C" int eas_sgemm_f32_tiled(const float* a, const float* b, float* c, uin
     const char* e = getenv("EAS_SGEMM_F2");
     return !(e && e[0] == '0');
   }();
+  static const int probe = [] {  // exploration switch (measurements only)
+    const char* e = getenv("EAS_SGEMM_PROBE");
+    return e ? atoi(e) : 0;
+  }();
+  if (small && k_tile % 32 == 0 && vec && probe) {
+    switch (probe) {
+      case 1: return EAS_SG(64, 64, 32, 2, 8, 4, 5);
+      case 2: return EAS_SG(64, 64, 32, 2, 8, 4, 6);
+      case 3: return EAS_SG(64, 64, 16, 3, 8, 4, 5);
+      default: break;
+    }
+  }
   if (small) {
     if (k_tile % 32 == 0) return EAS_SG(64, 64, 32, 2, 8, 4, 4);
     if (k_tile % 16 == 0) return EAS_SG(64, 64, 16, 2, 8, 4, 4);
