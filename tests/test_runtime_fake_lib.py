@@ -788,3 +788,48 @@ def test_repeated_shard_calls_take_the_prepared_range_launch(fast):
     assert len(calls) == 1
     (fl, _r), = [v for kk, v in k._fast.items() if kk[0] == "shard"]
     assert [o[3] for o in fl.ptr_slots] == [4 * lo] * 3
+
+
+@eas.kernel
+def add_default_block(a, b, c, N, BLOCK: eas.constexpr = 256):
+    offs = mk.program_id(0) * BLOCK + mk.arange(0, BLOCK)
+    m = offs < N
+    mk.store(c, offs, mk.load(a, offs, m) + mk.load(b, offs, m), m)
+
+
+def test_run_shard_tunes_an_autotuned_kernel_on_its_own_range(fast, monkeypatch):
+    """An autotuned kernel under run_shard is timed on this rank's program range (the whole launch
+    may not fit the slice buffers), keeps the fastest config per range, and then launches it."""
+    from easy_as_b200.shard import element_range, run_shard
+
+    lib, rt = fast
+    n, world, rank = 1 << 14, 2, 1
+    tuned = eas.autotune(configs=[eas.Config(meta={"BLOCK": 256}), eas.Config(meta={"BLOCK": 512})],
+                         key=["N"], warmup=1, repeat=2)(eas.kernel(add_default_block.fn))
+    lo, hi = element_range(n, 512, rank, world)           # both configs split at the same element
+    a = eas.tensor(np.arange(hi - lo, dtype=np.float32), device="cuda")
+    b = eas.tensor(np.ones(hi - lo, np.float32), device="cuda")
+    c = eas.tensor(np.zeros(hi - lo, np.float32), device="cuda")
+    timed = []
+
+    def fake_bench(ck, runtime_args, meta, *, axis, lo, hi, repeat, warmup, **kw):
+        timed.append((meta["BLOCK"], axis, lo, hi))
+        return 1.0 if meta["BLOCK"] == 256 else 0.5      # BLOCK 512 "wins"
+
+    monkeypatch.setattr(rt, "benchmark_range", fake_bench)
+    monkeypatch.setenv("EAS_AUTOTUNE_CACHE", "0")
+    orig_raw = rt._launch_generic_raw
+
+    def raw(ck, *a_, **kw):      # the fake decodes each launch with the kernel being launched
+        lib.current = ck
+        return orig_raw(ck, *a_, **kw)
+
+    monkeypatch.setattr(rt, "_launch_generic_raw", raw)
+    r = run_shard(tuned, a, b, c, n, _rank=rank, _world=world, _buffer_base={"a": lo, "b": lo, "c": lo})
+    assert timed == [(256, 0, 32, 64), (512, 0, 16, 32)]     # each config's own range of rank 1
+    assert r == (16, 32)
+    np.testing.assert_array_equal(c.numpy(), a.numpy() + 1.0)
+    (best,) = tuned._tuned_cache.values()
+    assert best.meta == {"BLOCK": 512}
+    (times,) = tuned._tuned_times.values()
+    assert times == [({"BLOCK": 256}, 1.0), ({"BLOCK": 512}, 0.5)]
