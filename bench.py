@@ -282,6 +282,7 @@ def run_gemm(name: str, args, world: int, rank: int, rt) -> dict:
     stream = torch.cuda.current_stream()
     e0, e1 = _events()
     with ClockSampler(torch.cuda.current_device()) as clk:
+        torch.cuda._sleep(100_000)      # the first step is queued before the start event is reached
         e0.record(stream)
         for _ in range(steps):
             step()
@@ -682,6 +683,10 @@ def run_add(args, world: int, rank: int, local: int, rt) -> dict:
     launches0 = rt.launch_count
     e0, e1 = _events()
     with ClockSampler(local) as clk:
+        # a ~50 us device sleep ahead of the start event, so the first step is already queued when
+        # the event is reached (the timed region holds the K steps back to back, not the host's
+        # latency to launch the first one)
+        torch.cuda._sleep(100_000)
         e0.record(stream)
         t0 = time.perf_counter()
         for _ in range(args.steps):

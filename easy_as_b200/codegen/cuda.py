@@ -54,8 +54,6 @@ tested on its own.
 """
 
 from __future__ import annotations
-
-import os
 import struct
 from dataclasses import dataclass, field
 from typing import Any
@@ -300,8 +298,7 @@ class _Emitter:
                                      "(use mk.tid for thread-level kernels)")
             self.V = 4 if self.block % 4 == 0 else 1
             per_chunk = self.block // self.V
-            tmax = int(os.environ.get("EAS_SPMD_MAX_THREADS", "256"))   # exploration knob (measurements)
-            self.T = per_chunk if per_chunk <= tmax else tmax
+            self.T = per_chunk if per_chunk <= 256 else 256
             self.J = -(-per_chunk // self.T)
             self.L = self.J * self.V
             self.lane_guard = (self.J * self.T * self.V) != self.block

@@ -348,9 +348,9 @@ extern "C" int eas_sgemm_f32_tiled(const float* a, const float* b, float* c, uin
   }();
   if (small && k_tile % 32 == 0 && vec && probe) {
     switch (probe) {
-      case 1: return EAS_SG(64, 64, 32, 2, 8, 4, 5);
-      case 2: return EAS_SG(64, 64, 32, 2, 8, 4, 6);
-      case 3: return EAS_SG(64, 64, 16, 3, 8, 4, 5);
+      case 1: return EAS_SG(64, 64, 32, 2, 8, 4, 3);
+      case 2: return EAS_SG(64, 64, 32, 3, 8, 4, 3);
+      case 3: return EAS_SG(128, 64, 32, 2, 8, 4, 2);
       default: break;
     }
   }
