@@ -54,6 +54,8 @@ tested on its own.
 """
 
 from __future__ import annotations
+
+import os
 import struct
 from dataclasses import dataclass, field
 from typing import Any
