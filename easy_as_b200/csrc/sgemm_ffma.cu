@@ -343,19 +343,6 @@ extern "C" int eas_sgemm_f32_tiled(const float* a, const float* b, float* c, uin
     const char* e = getenv("EAS_SGEMM_F2");
     return !(e && e[0] == '0');
   }();
-  static const int probe = [] {  // exploration switch (measurements only)
-    const char* e = getenv("EAS_SGEMM_PROBE");
-    return e ? atoi(e) : 0;
-  }();
-  if (small && k_tile % 32 == 0 && vec && probe) {
-    switch (probe) {
-      case 1: return EAS_SG(64, 64, 32, 2, 8, 8, 4);
-      case 2: return EAS_SG(64, 64, 32, 3, 8, 8, 4);
-      case 3: return EAS_SG(64, 64, 32, 2, 8, 8, 3);
-      case 4: return EAS_SG(64, 64, 32, 2, 8, 4, 2);
-      default: break;
-    }
-  }
   if (small) {
     // 3 CTAs per SM (up to 168 registers; 156 used) rather than 4 at 128: 46.4 TFLOP/s against
     // 44.4 on C3 with packed pairs (the spare registers go to deeper operand prefetch)
