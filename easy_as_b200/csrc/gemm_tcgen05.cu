@@ -218,49 +218,6 @@ struct Sched {
 };
 
 // KS k-blocks of 64 per pipeline stage (BLOCK_K = 64 KS): stage = KS A boxes then KS B boxes.
-// The work of one CTA (pair) as a sequence of segments: pipeline stages [kb0, kb1) of one tile.
-//   units mode: unit u (from `first`, step `step`) is K part (u % ks) of tile (u / ks); ks = 1 is
-//               one whole tile per unit (data-parallel), ks > 1 is split-K;
-//   stream-K:   the concatenation of every tile's stages, total `sk_total`, cut into `step` equal
-//               ranges; range `first` may begin with the tail of a tile and end with the head of
-//               another (each split tile has exactly one head and one tail when tiles >= ranges).
-struct Work {
-  int tile, kb0, kb1;
-};
-struct WorkIter {
-  long long pos, end;  // stream-K: stage positions; units mode: pos = u, end = units
-  int step, ks, kstages;
-  bool sk;
-  __device__ WorkIter(int first, int step_, int units, int ks_, int kstages_, long long sk_total)
-      : step(step_), ks(ks_), kstages(kstages_), sk(sk_total > 0) {
-    if (sk) {
-      pos = sk_total * first / step_;
-      end = sk_total * (first + 1) / step_;
-    } else {
-      pos = first;
-      end = units;
-    }
-  }
-  __device__ bool next(Work& w) {
-    if (pos >= end) return false;
-    if (!sk) {
-      const int u = (int)pos;
-      w.tile = u / ks;
-      const int part = u % ks;
-      w.kb0 = (int)((long long)part * kstages / ks);
-      w.kb1 = (int)((long long)(part + 1) * kstages / ks);
-      pos += step;
-      return true;
-    }
-    w.tile = (int)(pos / kstages);
-    w.kb0 = (int)(pos - (long long)w.tile * kstages);
-    const long long rest = end - pos;
-    w.kb1 = rest < kstages - w.kb0 ? w.kb0 + (int)rest : kstages;
-    pos += w.kb1 - w.kb0;
-    return true;
-  }
-};
-
 template <int BN, int STAGES, bool B_MN, int KS = 1>
 struct Smem {
   static constexpr int kA1 = BM * BK * 2;  // one k-block of A
@@ -579,7 +536,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_f16_tcgen05_2sm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                                 const __grid_constant__ CUtensorMap map_c, float* __restrict__ c, int M, int N, int K,
                                 int batch, long long ldc, long long c_bstride, int* status, int seg_kb,
-                                int ksplit, float* __restrict__ sk_ws, unsigned* sk_flags, long long sk_total) {
+                                int ksplit) {
   static_assert(!(TF && B_MN), "tf32 operands are K-major here");
   constexpr int kBKe = TF ? 32 : BK;  // elements per 128-byte K row of a stage
   // NH = 2: 256 x 512 pair tiles (two 256-column halves, one MMA each per k step) in ONE 512-column
@@ -644,24 +601,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const int cid = blockIdx.x >> 1;
   const int ncl = gridDim.x >> 1;
   const int units = sched.total * ks;
-  // stream-K (sk_total > 0): pair cid runs stages [cid, cid + 1) * sk_total / ncl of all tiles.  A
-  // tile split between pairs p and p + 1 is finished by p (its head, k from 0, is p's last
-  // segment): p + 1 computes the tail first, writes that partial tile to its slot of sk_ws and
-  // counts its 8 epilogue warps into sk_flags[p + 1]; p adds the partial to its own accumulator,
-  // always in the order head + tail, and stores C.  Deterministic, no reduce-adds, no zeroing.
-  const long long skt = ks == 1 ? sk_total : 0;
+  auto k_range = [&](int u, int& kb0, int& kb1) {  // stage range of work unit u
+    const int part = u % ks;
+    kb0 = (int)((long long)part * kstages / ks);
+    kb1 = (int)((long long)(part + 1) * kstages / ks);
+  };
 
   if (warp == 0) {
     if (lane == 0) {
       int s = 0;
       uint32_t ph = 0;
-      WorkIter it(cid, ncl, units, ks, kstages, skt);
-      Work w;
-      while (!*abort_flag && it.next(w)) {
-        const TileCoord tc = sched.at(w.tile);  // m0 in units of 128: pair tiles are 256 rows
+      for (int u = cid; u < units && !*abort_flag; u += ncl) {
+        const TileCoord tc = sched.at(u / ks);  // m0 in units of 128: pair tiles are 256 rows
         const int m0 = (tc.m0 / BM) * 256 + 128 * (int)rank;
         const int n0 = tc.n0 * BN + 128 * (int)rank;
-        const int kb_lo = w.kb0, kb_hi = w.kb1;
+        int kb_lo, kb_hi;
+        k_range(u, kb_lo, kb_hi);
         for (int kb = kb_lo; kb < kb_hi; ++kb) {
           if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) break;
           const uint32_t fl = mapa_rank(smem_u32(&full[s]), 0);
@@ -746,16 +701,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           ph ^= 1;
         }
       };
-      WorkIter it(cid, ncl, units, ks, kstages, skt);
-      Work w;
-      for (; !*abort_flag && it.next(w); ++local) {
+      for (int u = cid; u < units && !*abort_flag; u += ncl, ++local) {
         const int buf = NBUF == 2 ? (local & 1) : 0;
         const uint32_t acc_ph = NBUF == 2 ? (local >> 1) & 1 : local & 1;
         if (!mbar_wait_cl(&acc_empty[buf], acc_ph ^ 1, abort_flag)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * BN;
         bool ok = true;
-        const int kb_lo = w.kb0, kb_hi = w.kb1;
+        int kb_lo, kb_hi;
+        k_range(u, kb_lo, kb_hi);
         int kb = kb_lo;
         if constexpr (NH == 2) {
           // the epilogue frees the accumulator by halves (acc_empty[0]: columns 0-255, [1]: 256-511):
@@ -811,35 +765,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const bool vec_ok = ((ldc & 3) == 0) && ((c_bstride & 3) == 0) && ((reinterpret_cast<uintptr_t>(c) & 15) == 0);
     const uint32_t acc_empty_leader[2] = {mapa_rank(smem_u32(&acc_empty[0]), 0), mapa_rank(smem_u32(&acc_empty[1]), 0)};
     int local = 0;
-    WorkIter it(cid, ncl, units, ks, kstages, skt);
-    Work w;
-    for (; !*abort_flag && it.next(w); ++local) {
+    for (int u = cid; u < units && !*abort_flag; u += ncl, ++local) {
       const int buf = NBUF == 2 ? (local & 1) : 0;
       const uint32_t acc_ph = NBUF == 2 ? (local >> 1) & 1 : local & 1;
       if (!mbar_wait(&acc_full[buf], acc_ph, abort_flag)) break;
       tc_fence_after();
-      const TileCoord tc = sched.at(w.tile);
-      // stream-K roles of this segment (see above); `slot` is this warp's chunk area of a slot
-      const bool sk_tail = skt > 0 && w.kb0 > 0;
-      const bool sk_head = skt > 0 && w.kb0 == 0 && w.kb1 < kstages;
-      auto slot_chunk = [&](int slot, int cc) {
-        return sk_ws + (((long long)slot * 2 + rank) * (BN / 32) + cc) * 4096 + (q * 32 + lane) * 32;
-      };
-      if (sk_head) {  // the partner's tail partial must be complete before it is added
-        const unsigned* flag = sk_flags + cid + 1;
-        const long long t0 = clock64();
-        while (true) {
-          unsigned v;
-          asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
-          if (v >= 8u) break;
-          if (*abort_flag) break;
-          if (clock64() - t0 > kWaitBudget) {
-            *abort_flag = 1;
-            break;
-          }
-          __nanosleep(64);
-        }
-      }
+      const TileCoord tc = sched.at(u / ks);
       const int n0 = tc.n0 * BN;
       const int mrow0 = (tc.m0 / BM) * 256 + 128 * (int)rank + q * 32;
       const int m = mrow0 + lane;
@@ -896,31 +827,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         uint32_t r[32];
         tmem_ld32(tbase + cc * 32, r);
         if (NH == 2 && cc == 256 / 32 - 1) release_half0();
-        if (sk_tail) {  // the partial goes to this pair's slot, not to C
-          float4* dst = reinterpret_cast<float4*>(slot_chunk(cid, cc));
-#pragma unroll
-          for (int j = 0; j < 8; ++j)
-            dst[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
-                                 __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
-          continue;
-        }
-        if (sk_head) {  // head + tail, in that order
-          const float4* src = reinterpret_cast<const float4*>(slot_chunk(cid + 1, cc));
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const float4 t = __ldcg(src + j);  // from L2: written by another SM in this launch
-            r[4 * j] = __float_as_uint(__fadd_rn(__uint_as_float(r[4 * j]), t.x));
-            r[4 * j + 1] = __float_as_uint(__fadd_rn(__uint_as_float(r[4 * j + 1]), t.y));
-            r[4 * j + 2] = __float_as_uint(__fadd_rn(__uint_as_float(r[4 * j + 2]), t.z));
-            r[4 * j + 3] = __float_as_uint(__fadd_rn(__uint_as_float(r[4 * j + 3]), t.w));
-          }
-        }
         put(r, cc);
-      }
-      if (sk_tail) {  // publish: the partial's stores happen before this warp's arrival
-        __threadfence();
-        __syncwarp();
-        if (lane == 0) asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(sk_flags + cid) : "memory");
       }
       tc_fence_before();
       __syncwarp();
@@ -1024,52 +931,6 @@ int zero_c_for_split(float* c, int M, int N, int batch, long long ldc, long long
   return EAS_OK;
 }
 
-// Stream-K for the CTA-pair kernel.  When the data-parallel schedule's last round would leave
-// more than 5 % of the pairs idle (tiles not a near multiple of the resident pairs; e.g. the
-// per-GPU shards of C4 at 4 and 8 GPUs: 128 or 256 tiles of 256 x 256 on 74 pairs end at 86.5 %),
-// every pair takes an equal share of all tiles' k-blocks instead.  Needs tiles >= pairs (so each
-// split tile has one head and one tail) and no split-K.  EAS_GEMM_STREAMK=0 turns it off.
-bool use_streamk(long long tiles, long long pairs, int ksplit) {
-  static const bool enabled = [] {
-    const char* e = getenv("EAS_GEMM_STREAMK");
-    return !(e && e[0] == '0');
-  }();
-  if (!enabled || ksplit > 1 || pairs <= 1 || tiles < pairs) return false;
-  const long long rounds = (tiles + pairs - 1) / pairs;
-  return (double)tiles / (double)(rounds * pairs) < 0.95;
-}
-
-// Per-device stream-K scratch: one partial-tile slot per CTA pair (2 CTAs x 128 rows x up to 512
-// f32 columns = 512 KB) and one arrival counter per pair, allocated on first use and kept.
-constexpr int kSkMaxPairs = 96;
-struct SkScratch {
-  float* ws = nullptr;
-  unsigned* flags = nullptr;
-};
-SkScratch g_sk[64];
-std::mutex g_sk_mu;
-
-int streamk_scratch(int dev, SkScratch* out) {
-  if (dev < 0 || dev >= 64) return eas_fail(EAS_ERR_VALUE, "gemm: device index out of range");
-  std::lock_guard<std::mutex> lock(g_sk_mu);
-  if (!g_sk[dev].ws) {
-    void* w = nullptr;
-    void* f = nullptr;
-    int rc = eas_cuda_check(cudaMalloc(&w, (size_t)kSkMaxPairs * 2 * 128 * 512 * sizeof(float)),
-                            "gemm: stream-K workspace", EAS_ERR_MEMORY);
-    if (rc) return rc;
-    rc = eas_cuda_check(cudaMalloc(&f, kSkMaxPairs * sizeof(unsigned)), "gemm: stream-K flags", EAS_ERR_MEMORY);
-    if (rc) {
-      cudaFree(w);
-      return rc;
-    }
-    g_sk[dev].ws = static_cast<float*>(w);
-    g_sk[dev].flags = static_cast<unsigned*>(f);
-  }
-  *out = g_sk[dev];
-  return EAS_OK;
-}
-
 template <int BN, int STAGES, bool B_MN, bool TMA_C, bool TF = false, int KS = 1>
 int launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, float* c, int M, int N, int K,
                    int batch, long long ldc, long long cbs, int* status, cudaStream_t stream, int num_sms, int seg_kb = 0) {
@@ -1125,23 +986,10 @@ int launch_2sm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& 
     rc = zero_c_for_split(c, M, N, batch, ldc, cbs, stream);
     if (rc) return rc;
   }
-  long long sk_total = 0;
-  SkScratch sk;
-  if (!TF && use_streamk(tiles, pairs, ksplit) && pairs <= kSkMaxPairs) {
-    rc = streamk_scratch(dev, &sk);
-    if (rc) return rc;
-    // every arrival counter starts the launch at zero (stream-ordered before the kernel)
-    rc = eas_cuda_check(cudaMemsetAsync(sk.flags, 0, (size_t)pairs * sizeof(unsigned), stream),
-                        "gemm: clear stream-K counters", EAS_ERR_LAUNCH);
-    if (rc) return rc;
-    const int kstages = (((K + BK - 1) / BK) + KS - 1) / KS;
-    sk_total = tiles * kstages;
-  }
-  const long long units = sk_total ? pairs : tiles * ksplit;
+  const long long units = tiles * ksplit;
   const int grid = 2 * (int)(units < pairs ? units : pairs);
-  g_last_config = {256, 256 * NH, STAGES, sk_total ? 0 : ksplit, 1, KS * BK};
-  kern<<<grid, kThreads, L::kTotal, stream>>>(ma, mb, mc, c, M, N, K, batch, ldc, cbs, status, seg_kb, ksplit,
-                                              sk.ws, sk.flags, sk_total);
+  g_last_config = {256, 256 * NH, STAGES, ksplit, 1, KS * BK};
+  kern<<<grid, kThreads, L::kTotal, stream>>>(ma, mb, mc, c, M, N, K, batch, ldc, cbs, status, seg_kb, ksplit);
   return eas_cuda_check(cudaGetLastError(), "gemm(2sm): launch", EAS_ERR_LAUNCH);
 }
 
@@ -1163,9 +1011,6 @@ bool use_wide(uint32_t M, uint32_t N, uint32_t K, uint32_t batch, int num_sms) {
   const long long pairs = num_sms / 2 > 0 ? num_sms / 2 : 1;
   const long long mt = (M + 255) / 256;
   const long long t1 = mt * ((N + 255) / 256) * batch, t2 = mt * ((N + 511) / 512) * batch;
-  // wide tiles that cannot fill one round while 256 x 256 ones can take stream-K: the latter (the
-  // per-GPU shard of C4 at 8 GPUs: 64 wide tiles or 128 narrow ones on 74 pairs)
-  if (t2 < pairs && use_streamk(t1, pairs, 1)) return false;
   return 2 * ((t2 + pairs - 1) / pairs) <= (t1 + pairs - 1) / pairs;
 }
 
@@ -1391,7 +1236,6 @@ extern "C" int eas_gemm_f16_plan(uint32_t M, uint32_t N, uint32_t K, uint32_t ba
   *out_block_k = BK * ch.ks;
   const long long tiles = (long long)((M + *out_tile_m - 1) / *out_tile_m) * ((N + ch.tile_n - 1) / ch.tile_n) * batch;
   *ksplit = c_tma_ok ? choose_ksplit(tiles, ch.pair ? resident_pairs : num_sms, kblocks, (int)batch) : 1;
-  if (ch.pair && use_streamk(tiles, resident_pairs, *ksplit) && resident_pairs <= kSkMaxPairs) *ksplit = 0;
   return EAS_OK;
 }
 

@@ -27,10 +27,8 @@ def plan(M, N, K, batch=1, block_n=256, tma=True, sms=148, pairs=74, tile_m=0, b
     # C4 on 1, 2, 4, 8 GPUs (M split across ranks)
     ((8192, 8192, 8192), {"pair": True, "tile": (256, 512), "stages": 4, "ksplit": 1}),
     ((4096, 8192, 8192), {"pair": True, "tile": (256, 256), "stages": 6, "ksplit": 1}),   # wide adds a round
-    # 4 and 8 GPUs: the data-parallel schedule would end at 86.5 % of the pairs: stream-K (ksplit 0);
-    # at 8 GPUs 64 wide tiles cannot fill one round, so 128 tiles of 256 x 256 take it
-    ((2048, 8192, 8192), {"pair": True, "tile": (256, 512), "stages": 4, "ksplit": 0}),
-    ((1024, 8192, 8192), {"pair": True, "tile": (256, 256), "stages": 6, "ksplit": 0}),
+    ((2048, 8192, 8192), {"pair": True, "tile": (256, 512), "stages": 4, "ksplit": 1}),
+    ((1024, 8192, 8192), {"pair": True, "tile": (256, 512), "stages": 4, "ksplit": 1}),
     # C5 on 1 GPU (batch 64) and on 8 (batch 8): K = 2088 is too short a loop for wide tiles
     ((4096, 4096, 2088, 64), {"pair": True, "tile": (256, 256), "stages": 6, "ksplit": 1}),
     ((4096, 4096, 2088, 8), {"pair": True, "tile": (256, 256), "stages": 6, "ksplit": 1}),
@@ -91,12 +89,3 @@ def test_library_choice_is_unchanged_by_zero_hints():
 def test_bad_tile_requests(tile_m, block_k):
     with pytest.raises(ValueError):
         plan(256, 256, 256, tile_m=tile_m, block_k=block_k)
-
-
-def test_stream_k_needs_a_tile_per_pair_and_a_poor_last_round():
-    # 80 tiles on 74 pairs (2 rounds, 54 %): stream-K; 74 tiles: one full round; 36 tiles: split-K
-    assert plan(512, 1024, 1000, 10, block_n=256)["ksplit"] == 0
-    assert plan(256 * 37, 512, 1000, 1, block_n=256)["ksplit"] == 1
-    assert plan(600, 1000, 1100, 3, block_n=256)["ksplit"] == 2
-    # 1-SM tiles never take it
-    assert plan(1024, 8192, 8192, tile_m=128, block_n=256)["ksplit"] != 0
