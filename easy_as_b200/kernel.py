@@ -26,7 +26,7 @@ from .autotune import AutotuneSpec, Config
 from .compiler import CompiledKernel, compile as _compile, fast_arg_sig, runtime_arg_signature
 from .meta import constexpr
 from .compiler import _torch
-from .runtime import get_runtime
+from .runtime import env_bytes, get_runtime
 from .tensor import Tensor as _Tensor
 
 _LAUNCH_OPTIONS = ("_sync", "_shape", "_grid", "_tptg", "_nthreads")
@@ -283,9 +283,9 @@ class Kernel:
             if callable(v) or isinstance(v, (list, dict)):
                 return None
             parts.append((k, v))
-        parts.append(_os.environ.get("EAS_BOUNDS_CHECK"))
+        parts.append(env_bytes(b"EAS_BOUNDS_CHECK"))
         if any(type(v) is _np.ndarray for v in args):
-            parts.append(_os.environ.get("EAS_ZERO_COPY"))   # host arrays: in place on pinned memory or not
+            parts.append(env_bytes(b"EAS_ZERO_COPY"))   # host arrays: in place on pinned memory or not
         try:
             return tuple(parts)
         except TypeError:

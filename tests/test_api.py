@@ -202,3 +202,16 @@ def test_interval_lt_fold(limit, folded):
     src = np.arange(limit, dtype=np.float32)
     ck = _in_tile_store_kernel.compile(src, np.zeros_like(src), LIMIT=limit, NT=16)
     assert ("lt" in [i.op for i in ck.ir.insts]) is not folded
+
+
+def test_launch_path_environment_lookups_follow_os_environ(monkeypatch):
+    """The launch path reads EAS_* switches through runtime.env_bytes, which must see every change
+    made through os.environ (as monkeypatch, or a user, makes them)."""
+    from easy_as_b200.runtime import env_bytes
+
+    monkeypatch.delenv("EAS_BOUNDS_CHECK", raising=False)
+    assert env_bytes(b"EAS_BOUNDS_CHECK") is None
+    monkeypatch.setenv("EAS_BOUNDS_CHECK", "1")
+    assert env_bytes(b"EAS_BOUNDS_CHECK") == b"1"
+    monkeypatch.setenv("EAS_BOUNDS_CHECK", "0")
+    assert env_bytes(b"EAS_BOUNDS_CHECK") == b"0"
