@@ -269,6 +269,31 @@ class DotGemmPlan:
                 return False
         return True
 
+    def _restage(self, rt: Any, lib: Any, m: dict[str, Any], a: int, b: int, device: int,
+                 stream: int) -> tuple[int, int, int, int, int, int, list] | None:
+        """A and B as the tcgen05 kernel will read them: in place when TMA can (16-byte aligned base
+        and pitches), else re-pitched into scratch rows padded to 8 elements (the GEMM still reads
+        only K columns of A and K rows or columns of B, so the padding never enters a sum)."""
+        M, N, K, B = m["M"], m["N"], m["K"], m["batch"]
+        lda, a_bs, ldb, b_bs = m["lda"], m["a_bs"], m["ldb"], m["b_bs"]
+        keep: list = []
+        if not _tma_rows_ok(a, lda, a_bs, B):
+            got = _restage_operand(rt, lib, a, M, K, lda, a_bs, B, device, stream, "dot_a16")
+            if got is None:
+                self.last_reason = "A re-pitch scratch unavailable (CUDA-graph capture)"
+                return None
+            a, lda, a_bs, owner = got
+            keep.append(owner)
+        if not _tma_rows_ok(b, ldb, b_bs, B):
+            rows, cols = (N, K) if m["b_kmajor"] else (K, N)
+            got = _restage_operand(rt, lib, b, rows, cols, ldb, b_bs, B, device, stream, "dot_b16")
+            if got is None:
+                self.last_reason = "B re-pitch scratch unavailable (CUDA-graph capture)"
+                return None
+            b, ldb, b_bs, owner = got
+            keep.append(owner)
+        return a, lda, a_bs if B > 1 else 0, b, ldb, b_bs if B > 1 else 0, keep
+
     def covers(self, runtime_args: dict[str, Any], programs: tuple[int, int, int], ntx: int, name: str,
                numel: int) -> bool:
         """True when this launch stores every element of buffer ``name`` (numel elements from index 0):
@@ -313,9 +338,12 @@ class DotGemmPlan:
         b = args[self.b_arg].ptr + 2 * m["b0"]
         c = args[self.c_arg].ptr + 4 * m["c0"]
         lib = rt.lib()
-        rc = lib.eas_gemm_f16_tile(a, b, c, m["M"], m["N"], m["K"], m["batch"], m["lda"], m["a_bs"], m["ldb"],
-                                   m["b_bs"], m["b_kmajor"], m["ldc"], m["c_bs"], self.tile_m, self.block_n,
-                                   self.block_k, stream)
+        staged = self._restage(rt, lib, m, a, b, device, stream)
+        if staged is None:
+            return False
+        a, lda, a_bs, b, ldb, b_bs, _keep = staged
+        rc = lib.eas_gemm_f16_tile(a, b, c, m["M"], m["N"], m["K"], m["batch"], lda, a_bs, ldb, b_bs,
+                                   m["b_kmajor"], m["ldc"], m["c_bs"], self.tile_m, self.block_n, self.block_k, stream)
         if rc == 4:  # EAS_ERR_VALUE: layout the native kernel does not take (alignment, sizes)
             from ..runtime import cuda_ext
 
@@ -327,6 +355,29 @@ class DotGemmPlan:
         rt.launch_count += 1
         rt.native_launches += 1
         return True
+
+
+def _tma_rows_ok(ptr: int, ld: int, bs: int, batch: int) -> bool:
+    """f16 rows TMA reads in place: 16-byte aligned base, row and batch pitches multiples of 8 elements."""
+    return ptr % 16 == 0 and ld % 8 == 0 and (batch == 1 or bs % 8 == 0)
+
+
+def _restage_operand(rt: Any, lib: Any, ptr: int, rows: int, cols: int, ld: int, bs: int, batch: int, device: int,
+                     stream: int, tag: str) -> tuple[int, int, int, Any] | None:
+    """Copy f16 rows [batch][rows][cols] (pitch ld, batch pitch bs) to scratch rows padded to a
+    multiple of 8 elements (``eas_pad_f16_2d``); (pointer, ld', bs', owner) or None when no scratch
+    can be had (inside a CUDA-graph capture without torch)."""
+    from ..runtime import cuda_ext
+
+    cols_pad = -(-cols // 8) * 8
+    got = rt.scratch(device, stream, tag, 2 * batch * rows * cols_pad)
+    if got is None:
+        return None
+    dst, owner = got
+    cuda_ext.check(lib.eas_pad_f16_2d(ptr, dst, rows, cols_pad, ld, cols_pad, rows, cols, batch, bs, rows * cols_pad,
+                                      stream), f"re-pitch {tag}")
+    rt.launch_count += 1
+    return dst, cols_pad, rows * cols_pad, owner
 
 
 def _numel(v: Any) -> int:

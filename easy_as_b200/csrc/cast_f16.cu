@@ -1,5 +1,7 @@
 // cast_f16.cu — operand staging for native GEMMs on tcgen05:
 //   * f32 -> f16 for the proven simdgroup-MMA GEMM;
+//   * f16 -> f16 re-pitching for fp16 dot GEMMs whose rows TMA cannot read in place (a row
+//     pitch or base that is not a multiple of 16 bytes);
 //   * f32 -> (hi, lo) TF32 pairs for the opt-in 3xTF32 mode of proven fp32 matmuls.
 //
 // The reference's matmul_simdgroup kernel (easy_as examples/matmul_simdgroup.py:29-127) casts
@@ -26,7 +28,11 @@ __device__ __forceinline__ uint16_t f2h_rn(float f) {
   return h;
 }
 
-__global__ void cast_f32_f16_kernel(const float* __restrict__ src, uint16_t* __restrict__ dst, uint32_t rows,
+__device__ __forceinline__ uint16_t to_f16_bits(float f) { return f2h_rn(f); }
+__device__ __forceinline__ uint16_t to_f16_bits(uint16_t h) { return h; }  // f16 source: bits copied
+
+template <typename Src>
+__global__ void cast_f32_f16_kernel(const Src* __restrict__ src, uint16_t* __restrict__ dst, uint32_t rows,
                                     uint32_t groups, uint64_t ld_src, uint64_t ld_dst, uint32_t rows_valid,
                                     uint32_t cols_valid, uint32_t batch, uint64_t bs_src, uint64_t bs_dst) {
   const uint64_t total = (uint64_t)batch * rows * groups;
@@ -37,11 +43,11 @@ __global__ void cast_f32_f16_kernel(const float* __restrict__ src, uint16_t* __r
     const uint32_t b = br / rows;
     const uint32_t c0 = g * 8;
     uint16_t h[8];
-    const float* s = src + b * bs_src + (uint64_t)r * ld_src;
+    const Src* s = src + b * bs_src + (uint64_t)r * ld_src;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const uint32_t c = c0 + j;
-      h[j] = (r < rows_valid && c < cols_valid) ? f2h_rn(s[c]) : (uint16_t)0;
+      h[j] = (r < rows_valid && c < cols_valid) ? to_f16_bits(s[c]) : (uint16_t)0;
     }
     uint4 v;
     v.x = h[0] | ((uint32_t)h[1] << 16);
@@ -165,8 +171,30 @@ extern "C" int eas_cast_f32_f16_2d(const float* src, void* dst, uint32_t rows, u
   const uint64_t total = (uint64_t)batch * rows * (cols_pad / 8);
   const uint64_t want = (total + 255) / 256;
   const unsigned grid = (unsigned)(want < (uint64_t)sms * 16 ? want : (uint64_t)sms * 16);
-  cast_f32_f16_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+  cast_f32_f16_kernel<float><<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       src, static_cast<uint16_t*>(dst), rows, cols_pad / 8, ld_src, ld_dst, rows_valid, cols_valid, batch, bs_src,
       bs_dst);
   return eas_cuda_check(cudaGetLastError(), "cast_f32_f16 launch", EAS_ERR_LAUNCH);
+}
+
+extern "C" int eas_pad_f16_2d(const void* src, void* dst, uint32_t rows, uint32_t cols_pad, uint64_t ld_src,
+                              uint64_t ld_dst, uint32_t rows_valid, uint32_t cols_valid, uint32_t batch,
+                              uint64_t bs_src, uint64_t bs_dst, void* stream) {
+  if (!src || !dst) return eas_fail(EAS_ERR_VALUE, "eas_pad_f16_2d: null pointer");
+  if (rows == 0 || cols_pad == 0 || batch == 0) return EAS_OK;
+  if (reinterpret_cast<uintptr_t>(src) & 1) return eas_fail(EAS_ERR_VALUE, "eas_pad_f16_2d: source not 2-byte aligned");
+  if (cols_pad % 8 || ld_dst % 8 || ld_dst < cols_pad || (batch > 1 && bs_dst % 8) ||
+      (reinterpret_cast<uintptr_t>(dst) & 15))
+    return eas_fail(EAS_ERR_VALUE, "eas_pad_f16_2d: destination rows must be 16-byte aligned");
+  if (cols_valid > cols_pad) return eas_fail(EAS_ERR_VALUE, "eas_pad_f16_2d: cols_valid exceeds cols_pad");
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const uint64_t total = (uint64_t)batch * rows * (cols_pad / 8);
+  const uint64_t want = (total + 255) / 256;
+  const unsigned grid = (unsigned)(want < (uint64_t)sms * 16 ? want : (uint64_t)sms * 16);
+  cast_f32_f16_kernel<uint16_t><<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint16_t*>(src), static_cast<uint16_t*>(dst), rows, cols_pad / 8, ld_src, ld_dst, rows_valid,
+      cols_valid, batch, bs_src, bs_dst);
+  return eas_cuda_check(cudaGetLastError(), "pad_f16 launch", EAS_ERR_LAUNCH);
 }

@@ -93,6 +93,8 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "eas_wait_selftest": (_int, [ctypes.c_longlong, _vp]),
     "eas_cast_f32_f16_2d": (_int, [_vp, _vp, _u32, _u32, ctypes.c_uint64, ctypes.c_uint64, _u32, _u32, _u32,
                                    ctypes.c_uint64, ctypes.c_uint64, _vp]),
+    "eas_pad_f16_2d": (_int, [_vp, _vp, _u32, _u32, ctypes.c_uint64, ctypes.c_uint64, _u32, _u32, _u32,
+                                   ctypes.c_uint64, ctypes.c_uint64, _vp]),
     "eas_sgemm_f32_tiled": (_int, [_vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, ctypes.c_uint64, ctypes.c_uint64,
                                    ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64, _int,
                                    _u32, _u32, _u32, _u32, _vp]),

@@ -227,6 +227,17 @@ int eas_cast_f32_f16_2d(const float* src, void* dst, uint32_t rows, uint32_t col
                         uint64_t ld_dst, uint32_t rows_valid, uint32_t cols_valid, uint32_t batch, uint64_t bs_src,
                         uint64_t bs_dst, void* stream);
 
+/* f16 -> f16 re-pitching, the same layout rules as eas_cast_f32_f16_2d with an
+ * f16 source (bits copied, zero outside the valid extent; source 2-byte
+ * aligned, any pitch).  The runtime stages through it the operands of an fp16
+ * `mk.dot` GEMM whose row pitch or base TMA cannot read in place (not a
+ * multiple of 16 bytes), so the launch still runs on eas_gemm_f16_tile (the
+ * reference has no such constraint: Metal kernels read any pitch,
+ * msl.py:920-952). */
+int eas_pad_f16_2d(const void* src, void* dst, uint32_t rows, uint32_t cols_pad, uint64_t ld_src, uint64_t ld_dst,
+                   uint32_t rows_valid, uint32_t cols_valid, uint32_t batch, uint64_t bs_src, uint64_t bs_dst,
+                   void* stream);
+
 /* Self-test of the bounded waits of the native kernels (no counterpart in
  * the reference): launches one warp that waits, with the same bounded
  * mbarrier wait the GEMM uses, on a barrier that nothing ever completes.  The

@@ -76,19 +76,39 @@ def test_generic_path_equals_oracle_bitwise(cuda_rt, monkeypatch):
     np.testing.assert_array_equal(c.reshape(-1), want)
 
 
-def test_unaligned_n_falls_back_to_generic(cuda_rt):
-    """N = 300: B rows are 600 bytes apart, not a TMA stride; the generic kernel runs."""
+def test_unaligned_n_is_repitched_and_runs_natively(cuda_rt):
+    """N = 300: B rows are 600 bytes apart, not a TMA stride; B is re-pitched into scratch rows of 304
+    elements (``eas_pad_f16_2d``) and the tcgen05 GEMM runs on the copy."""
     a, b, c, native = _run(cuda_rt, 3, 20, 300, 136, 256, seed=4)
-    assert native == 0
-    np.testing.assert_allclose(c, _ref64(a, b), rtol=1e-4, atol=1e-5)
-
-
-def test_unaligned_k_falls_back_to_generic(cuda_rt):
-    """K = 45: A rows are 90 bytes apart, not a TMA stride; the generic kernel runs and stays correct."""
-    a, b, c, native = _run(cuda_rt, 1, 40, 96, 45, 128, seed=3)
-    assert native == 0
+    assert native == 1
     ref = _ref64(a, b)
-    np.testing.assert_allclose(c, ref, rtol=1e-4, atol=1e-5)
+    assert np.abs(c - ref).max() <= 1e-5 * np.abs(ref).max()
+
+
+def test_unaligned_k_is_repitched_and_runs_natively(cuda_rt):
+    """K = 45: A rows are 90 bytes apart; A (and B's 45 rows) are re-pitched; the padding is never
+    read by the GEMM, which still runs K = 45."""
+    a, b, c, native = _run(cuda_rt, 1, 40, 96, 45, 128, seed=3)
+    assert native == 1
+    ref = _ref64(a, b)
+    assert np.abs(c - ref).max() <= 1e-5 * np.abs(ref).max()
+
+
+@pytest.mark.parametrize("batch,M,N,K", [(4, 300, 1000, 1044), (2, 129, 203, 77)])
+def test_unaligned_batched_shapes_match_float64(cuda_rt, batch, M, N, K):
+    """Batched launches whose pitches TMA cannot use (K = 1044: 2088-byte A rows; odd N) run natively
+    on re-pitched operands."""
+    import torch
+
+    g = torch.Generator(device="cuda").manual_seed(K)
+    a = (torch.randn(batch, M, K, device="cuda", generator=g) / K ** 0.5).half()
+    b = (torch.randn(batch, K, N, device="cuda", generator=g) / K ** 0.5).half()
+    c = torch.full((batch, M, N), float("nan"), device="cuda")
+    before = cuda_rt.native_launches
+    matmul_dot_f16(a.reshape(-1), b.reshape(-1), c.reshape(-1), M, N, K, BLOCK_N=256, _grid=grid(batch))
+    assert cuda_rt.native_launches == before + 1
+    ref = torch.bmm(a.double(), b.double())
+    assert ((c.double() - ref).abs().max() / ref.abs().max()).item() <= 1e-5
 
 
 @eas.kernel

@@ -188,6 +188,22 @@ class FakeLib:
         self.pdl_launches = getattr(self, "pdl_launches", 0) + 1
         return self.eas_launch(*args)
 
+    def eas_pad_f16_2d(self, src, dst, rows, cols_pad, ld_src, ld_dst, rows_valid, cols_valid, batch, bs_src, bs_dst,
+                       stream):
+        """numpy stand-in for the f16 re-pitching kernel (zero outside the valid extent)."""
+        if int(dst) % 16 or cols_pad % 8 or ld_dst % 8:
+            return 4
+        self.calls.append(("pad_f16", rows, cols_pad, batch))
+        for z in range(batch):
+            for r in range(rows):
+                out = np.zeros(cols_pad, np.float16)
+                if r < rows_valid:
+                    buf, at = self._find(int(src) + 2 * (z * bs_src + r * ld_src))
+                    out[:cols_valid] = np.frombuffer(buf, np.float16, count=cols_valid, offset=at)
+                dbuf, dat = self._find(int(dst) + 2 * (z * bs_dst + r * ld_dst))
+                ctypes.memmove(ctypes.addressof(dbuf) + dat, out.ctypes.data, 2 * cols_pad)
+        return 0
+
     def eas_gemm_f16_tile(self, a, b, c, M, N, K, batch, lda, a_bs, ldb, b_bs, b_kmajor, ldc, c_bs, tile_m, block_n,
                           block_k, stream):
         """The explicit-tile entry: same sums as eas_gemm_f16 (the tile only changes speed)."""
@@ -833,3 +849,27 @@ def test_run_shard_tunes_an_autotuned_kernel_on_its_own_range(fast, monkeypatch)
     assert best.meta == {"BLOCK": 512}
     (times,) = tuned._tuned_times.values()
     assert times == [({"BLOCK": 256}, 1.0), ({"BLOCK": 512}, 0.5)]
+
+
+
+def test_unaligned_dot_gemm_operands_are_repitched_then_run_natively(fast):
+    """K = 45 (A rows 90 bytes apart) and N = 300 (B rows 600 bytes apart): TMA cannot read them in
+    place, so the launch re-pitches them into scratch rows padded to 8 elements and runs the native
+    GEMM on the copies; the result equals the float64 product of the original operands."""
+    from examples.matmul_dot_f16 import grid, matmul_dot_f16
+
+    lib, rt = fast
+    batch, M, N, K = 2, 20, 300, 45
+    rng = np.random.default_rng(3)
+    a = eas.tensor((rng.standard_normal(batch * M * K) / K ** 0.5).astype(np.float16), device="cuda")
+    b = eas.tensor((rng.standard_normal(batch * K * N) / K ** 0.5).astype(np.float16), device="cuda")
+    c = eas.tensor(np.zeros(batch * M * N, np.float32), device="cuda")
+    ck = matmul_dot_f16.compile(a, b, c, M, N, K, BLOCK_N=128)
+    lib.current = ck
+    rt.run(ck, {"a": a, "b": b, "c": c, "M": M, "N": N, "K": K}, {"BLOCK_N": 128}, sync=True, grid=grid(batch)(
+        {"BLOCK_N": 128}, {"N": N, "M": M}))
+    pads = [x for x in lib.calls if x[0] == "pad_f16"]
+    assert [x[1:] for x in pads] == [(M, 48, batch), (K, 304, batch)]      # A rows, then B rows
+    assert [x for x in lib.calls if x[0] == "gemm"]
+    want = np.matmul(a.numpy().reshape(batch, M, K).astype(np.float64), b.numpy().reshape(batch, K, N).astype(np.float64))
+    np.testing.assert_allclose(c.numpy().reshape(batch, M, N), want, rtol=1e-5, atol=1e-5)
