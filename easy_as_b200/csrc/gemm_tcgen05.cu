@@ -136,7 +136,6 @@ __device__ __forceinline__ void tma_reduce_add_3d(const CUtensorMap* map, const 
 
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
-__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
@@ -532,15 +531,8 @@ struct Smem2 {
   static constexpr int kTotal = kBarOffset + (2 * kStages2 + 4) * 8 + 16 + 1024;
 };
 
-// EW epilogue warps per CTA: 4 (one per TMEM lane quarter, two staging boxes each) or 8 (two per
-// quarter, taking alternate 32-column chunks, one box each; the same 32 KB of staging)
-template <int EW>
-constexpr int pair_threads() {
-  return 64 + 32 * EW;
-}
-
-template <int kStages2, bool B_MN, bool TMA_C, bool TF = false, int NH = 1, int KS = 1, int EW = 4>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<EW>(), 1)
+template <int kStages2, bool B_MN, bool TMA_C, bool TF = false, int NH = 1, int KS = 1>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_f16_tcgen05_2sm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                                 const __grid_constant__ CUtensorMap map_c, float* __restrict__ c, int M, int N, int K,
                                 int batch, long long ldc, long long c_bstride, int* status, int seg_kb,
@@ -581,7 +573,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<EW>(), 
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], 2 * EW);  // EW epilogue warps x 2 CTAs (leader's copy is used)
+      mbar_init(&acc_empty[i], 8);  // 4 epilogue warps x 2 CTAs (leader's copy is used)
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -767,12 +759,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<EW>(), 
       }
     }
   } else {
-    static_assert(EW == 4 || EW == 8, "4 or 8 epilogue warps");
-    constexpr int kBoxes = EW == 4 ? 2 : 1;  // staging boxes per epilogue warp (32 KB in all)
-    constexpr int kGroups = EW / 4;          // warps per TMEM lane quarter
     const int q = warp & 3;
-    const int grp = (warp - 2) / 4;          // this warp takes the chunks cc with cc % kGroups == grp
-    uint8_t* boxes = smem + L::kEpiOffset + (warp - 2) * (kBoxes * 32 * 32 * 4);
+    uint8_t* boxes = smem + L::kEpiOffset + q * (2 * 32 * 32 * 4);
     int nbox = 0;
     const bool vec_ok = ((ldc & 3) == 0) && ((c_bstride & 3) == 0) && ((reinterpret_cast<uintptr_t>(c) & 15) == 0);
     const uint32_t acc_empty_leader[2] = {mapa_rank(smem_u32(&acc_empty[0]), 0), mapa_rank(smem_u32(&acc_empty[1]), 0)};
@@ -799,13 +787,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<EW>(), 
         const int nb = n0 + cc * 32;
         if (TMA_C) {
           if (nb < N && mrow0 < M) {
-            uint8_t* box = boxes + (nbox & (kBoxes - 1)) * (32 * 32 * 4);
-            if (lane == 0) {  // the store that last used this box has read it
-              if (kBoxes == 2)
-                bulk_wait_read1();
-              else
-                bulk_wait_read0();
-            }
+            uint8_t* box = boxes + (nbox & 1) * (32 * 32 * 4);
+            if (lane == 0) bulk_wait_read1();
             __syncwarp();
             uint8_t* row = box + lane * 128;
 #pragma unroll
@@ -840,10 +823,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<EW>(), 
         }
       };
 #pragma unroll 1
-      for (int cc = grp; cc < BN / 32; cc += kGroups) {
+      for (int cc = 0; cc < BN / 32; ++cc) {
         uint32_t r[32];
         tmem_ld32(tbase + cc * 32, r);
-        if (NH == 2 && cc == 256 / 32 - kGroups + grp) release_half0();  // this warp's last chunk of half 0
+        if (NH == 2 && cc == 256 / 32 - 1) release_half0();
         put(r, cc);
       }
       tc_fence_before();
@@ -970,13 +953,13 @@ int launch_variant(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorM
   return eas_cuda_check(cudaGetLastError(), "gemm: launch", EAS_ERR_LAUNCH);
 }
 
-template <int STAGES, bool B_MN, bool TMA_C, bool TF = false, int NH = 1, int KS = 1, int EW = 4>
+template <int STAGES, bool B_MN, bool TMA_C, bool TF = false, int NH = 1, int KS = 1>
 int launch_2sm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, float* c, int M, int N, int K,
                int batch, long long ldc, long long cbs, int* status, cudaStream_t stream, int num_sms, int seg_kb = 0) {
   using L = Smem2<STAGES, TMA_C, NH, KS>;
   static_assert(L::kTotal <= 232448, "shared memory over the 227 KB per-CTA limit");
-  auto kern = gemm_f16_tcgen05_2sm_kernel<STAGES, B_MN, TMA_C, TF, NH, KS, EW>;
-  int rc = set_smem_once<gemm_f16_tcgen05_2sm_kernel<STAGES, B_MN, TMA_C, TF, NH, KS, EW>>(
+  auto kern = gemm_f16_tcgen05_2sm_kernel<STAGES, B_MN, TMA_C, TF, NH, KS>;
+  int rc = set_smem_once<gemm_f16_tcgen05_2sm_kernel<STAGES, B_MN, TMA_C, TF, NH, KS>>(
       L::kTotal, "gemm(2sm): set smem attribute");
   if (rc) return rc;
   const long long tiles = (long long)((M + 255) / 256) * ((N + 256 * NH - 1) / (256 * NH)) * batch;
@@ -988,7 +971,7 @@ int launch_2sm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& 
   if (resident_pairs[dev] == 0) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * (num_sms / 2), 1, 1);
-    cfg.blockDim = dim3(pair_threads<EW>(), 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
     cfg.dynamicSmemBytes = L::kTotal;
     int n = 0;
     if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
@@ -1006,8 +989,7 @@ int launch_2sm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& 
   const long long units = tiles * ksplit;
   const int grid = 2 * (int)(units < pairs ? units : pairs);
   g_last_config = {256, 256 * NH, STAGES, ksplit, 1, KS * BK};
-  kern<<<grid, pair_threads<EW>(), L::kTotal, stream>>>(ma, mb, mc, c, M, N, K, batch, ldc, cbs, status, seg_kb,
-                                                         ksplit);
+  kern<<<grid, kThreads, L::kTotal, stream>>>(ma, mb, mc, c, M, N, K, batch, ldc, cbs, status, seg_kb, ksplit);
   return eas_cuda_check(cudaGetLastError(), "gemm(2sm): launch", EAS_ERR_LAUNCH);
 }
 
@@ -1083,17 +1065,6 @@ int launch_f16_choice(const F16Choice& ch, bool b_mn, bool tma_c, const CUtensor
   constexpr int kS1w = 4 / KS, kS1 = 6 / KS, kS1d = KS == 1 ? 7 : 3;  // pair: wide, 256-wide, direct-store C
   constexpr int kSs256 = 4 / KS, kSs128 = 6 / KS;                    // 1-SM: BN = 256, 128
 #define EAS_ARGS ma, mb, mc, c, M, N, K, batch, ldc, cbs, status, s, num_sms
-  static const bool epi8 = [] {  // measurement switch: 8 epilogue warps in the pair kernel
-    const char* e = getenv("EAS_GEMM_EPI8");
-    return e && e[0] == '1';
-  }();
-  if (ch.pair && epi8 && tma_c && KS == 1) {
-    if (ch.nh == 2)
-      return b_mn ? launch_2sm<kS1w, true, true, false, 2, KS, 8>(EAS_ARGS)
-                  : launch_2sm<kS1w, false, true, false, 2, KS, 8>(EAS_ARGS);
-    return b_mn ? launch_2sm<kS1, true, true, false, 1, KS, 8>(EAS_ARGS)
-                : launch_2sm<kS1, false, true, false, 1, KS, 8>(EAS_ARGS);
-  }
   if (ch.pair) {
     if (ch.nh == 2)  // TMA-storable C only
       return b_mn ? launch_2sm<kS1w, true, true, false, 2, KS>(EAS_ARGS)
